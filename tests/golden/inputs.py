@@ -1,0 +1,124 @@
+"""Seeded inputs shared by ``make_golden.py`` and the tests.
+
+Golden fixtures store the reference's OUTPUTS and a SHA-256 digest of the
+inputs; the inputs themselves are regenerated here from their seeds
+(``torch.Generator`` on the CPU), so fixtures stay small.  A digest mismatch
+means the generator changed and the fixtures must be regenerated.
+"""
+from __future__ import annotations
+
+import hashlib
+import os
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+# name: (B, H, H_kv, T, D, chunk, dtype, seed) -- T_q = 1 chunk walks
+WALK_CASES = {
+    "walk_f32_gqa4": (2, 8, 2, 300, 64, 64, torch.float32, 1),
+    "walk_f32_mha": (1, 4, 4, 128, 32, 16, torch.float32, 2),
+    "walk_f32_t1": (1, 4, 2, 1, 32, 16, torch.float32, 3),
+    "walk_bf16_gqa4": (2, 16, 4, 520, 128, 128, torch.bfloat16, 4),
+    "walk_bf16_gqa8": (1, 16, 2, 1000, 128, 256, torch.bfloat16, 5),
+    "walk_f16_gqa4": (1, 8, 2, 256, 64, 64, torch.float16, 6),
+}
+
+# name: (B, H, H_kv, T_cold, T_gpu, D, chunk, dtype, seed) -- compute_attention T_q = 1
+DECODE_CASES = {
+    "decode_f32": (1, 8, 2, 700, 90, 32, 128, torch.float32, 21),
+    "decode_bf16": (2, 8, 2, 1024, 64, 64, 256, torch.bfloat16, 22),
+}
+
+# name: (B, H, H_kv, T_cold, T_gpu, T_q, D, chunk, dtype, seed) -- T_q > 1 causal
+PREFILL_CASES = {
+    "prefill_f32": (1, 4, 2, 192, 80, 48, 32, 64, torch.float32, 11),
+    "prefill_bf16": (1, 8, 2, 256, 128, 96, 64, 64, torch.bfloat16, 12),
+}
+
+# name: (shape, dtype, bits, seed)
+KIVI_CASES = {
+    "kivi_f16_b2": ((2, 3, 70, 128), torch.float16, 2, 31),
+    "kivi_f16_b4": ((1, 2, 40, 64), torch.float16, 4, 32),
+    "kivi_bf16_b2": ((1, 4, 50, 128), torch.bfloat16, 2, 33),
+}
+
+# name: (B, H, H_kv, T, D, page, dtype, seed, memory_ratio, min_pages)
+SCORER_CASES = {
+    "quest_f32_gqa4": (2, 8, 2, 130, 32, 16, torch.float32, 41, 4.0, 2),
+    "quest_bf16_gqa4": (2, 16, 4, 512, 128, 32, torch.bfloat16, 42, 4.0, 4),
+    "quest_bf16_gqa3": (1, 6, 2, 256, 64, 16, torch.bfloat16, 43, 2.0, 1),
+}
+
+
+def digest(*ts) -> str:
+    h = hashlib.sha256()
+    for t in ts:
+        h.update(t.contiguous().view(torch.uint8).numpy().tobytes())
+    return h.hexdigest()
+
+
+def qkv(B, H, H_kv, T, D, dtype, seed, T_q=1):
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(B, H, T_q, D, generator=g).to(dtype)
+    k = torch.randn(B, H_kv, T, D, generator=g).to(dtype)
+    v = torch.randn(B, H_kv, T, D, generator=g).to(dtype)
+    return q, k, v
+
+
+def walk_inputs(name):
+    B, H, H_kv, T, D, chunk, dtype, seed = WALK_CASES[name]
+    return qkv(B, H, H_kv, T, D, dtype, seed), chunk
+
+
+def decode_inputs(name):
+    B, H, H_kv, T_cold, T_gpu, D, chunk, dtype, seed = DECODE_CASES[name]
+    return qkv(B, H, H_kv, T_cold + T_gpu, D, dtype, seed), T_cold, chunk
+
+
+def prefill_inputs(name):
+    B, H, H_kv, T_cold, T_gpu, T_q, D, chunk, dtype, seed = PREFILL_CASES[name]
+    return qkv(B, H, H_kv, T_cold + T_gpu, D, dtype, seed, T_q=T_q), T_cold, chunk
+
+
+def config1_inputs():
+    """fp32, B1, H32/H_kv8, D128, T8192, seed 0."""
+    g = torch.Generator().manual_seed(0)
+    q = torch.randn(1, 32, 1, 128, generator=g)
+    k = torch.randn(1, 8, 8192, 128, generator=g)
+    v = torch.randn(1, 8, 8192, 128, generator=g)
+    return q, k, v
+
+
+def kivi_inputs(name):
+    shape, dtype, bits, seed = KIVI_CASES[name]
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(*shape, generator=g)
+    x[..., 3] *= 10.0                       # outlier channels
+    x[..., 77 % shape[-1]] *= 10.0
+    x[0, 0, 0, :32] = 0.5                   # constant group
+    x[0, 0, 1, :32] = torch.linspace(0, 1e-3, 32)    # tiny range
+    x[0, 0, 2, 32:64] = 6.0e4 * torch.sign(torch.randn(32, generator=g))  # huge range
+    return x.to(dtype), bits
+
+
+def scorer_inputs(name):
+    B, H, H_kv, T, D, page, dtype, seed, mr, mp = SCORER_CASES[name]
+    g = torch.Generator().manual_seed(seed)
+    K = torch.randn(B, H_kv, T, D, generator=g)
+    idx = torch.randperm(D, generator=g)[:4]
+    K[..., idx] *= 10.0                     # 4 outlier channels x10
+    K = K.to(dtype)
+    q = torch.randn(B, H, 1, D, generator=g).to(dtype)
+    return K, q, page, mr, mp
+
+
+def load(name: str) -> dict:
+    """Load ``tests/golden/<name>.npz`` as ``{case: {key: array}}``."""
+    out: dict = {}
+    with np.load(os.path.join(HERE, name), allow_pickle=False) as z:
+        for full in z.files:
+            case, key = full.split("/", 1)
+            out.setdefault(case, {})[key] = z[full]
+    return out
