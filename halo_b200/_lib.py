@@ -1,0 +1,121 @@
+"""ctypes binding of ``libhalo_sm100.so`` (declared in ``include/halo_b200.h``).
+
+The library is required: importing an op without it raises ``HaloError``.
+There is no CPU fallback anywhere in the package.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+import torch  # noqa: F401  -- loads the CUDA runtime the library shares with torch
+
+LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libhalo_sm100.so")
+
+HALO_OK = 0
+HALO_ERR_INVALID_ARG = -1
+HALO_ERR_UNSUPPORTED = -2
+HALO_ERR_MISALIGNED = -3
+HALO_ERR_CUDA = -4
+HALO_ERR_TIMEOUT = -5
+HALO_ERR_WORKSPACE = -6
+
+DTYPE_F32, DTYPE_BF16, DTYPE_F16 = 0, 1, 2
+MERGE_FINALIZE, MERGE_ACCUMULATE = 0, 1
+
+_TORCH_TO_HALO = {torch.float32: DTYPE_F32, torch.bfloat16: DTYPE_BF16, torch.float16: DTYPE_F16}
+
+
+class HaloError(RuntimeError):
+    """A libhalo_sm100 call failed (status code in ``.code``)."""
+
+    def __init__(self, msg: str, code: int = 0):
+        super().__init__(msg)
+        self.code = code
+
+
+def halo_dtype(dt: torch.dtype) -> int:
+    try:
+        return _TORCH_TO_HALO[dt]
+    except KeyError:
+        raise HaloError(f"unsupported dtype {dt}", HALO_ERR_UNSUPPORTED) from None
+
+
+class KVChunk(ctypes.Structure):
+    _fields_ = [("k", ctypes.c_void_p), ("v", ctypes.c_void_p),
+                ("k_stride_b", ctypes.c_int64), ("k_stride_h", ctypes.c_int64),
+                ("k_stride_t", ctypes.c_int64),
+                ("v_stride_b", ctypes.c_int64), ("v_stride_h", ctypes.c_int64),
+                ("v_stride_t", ctypes.c_int64),
+                ("start", ctypes.c_int64), ("len", ctypes.c_int32), ("causal", ctypes.c_int32)]
+
+
+class DecodeProblem(ctypes.Structure):
+    _fields_ = [("B", ctypes.c_int32), ("H", ctypes.c_int32), ("H_kv", ctypes.c_int32),
+                ("D", ctypes.c_int32), ("Dv", ctypes.c_int32), ("dtype", ctypes.c_int32),
+                ("q", ctypes.c_void_p), ("q_stride_b", ctypes.c_int64),
+                ("q_stride_h", ctypes.c_int64), ("q_pos", ctypes.c_void_p),
+                ("scale", ctypes.c_float), ("max_split_rows", ctypes.c_int32)]
+
+
+class MergeArgs(ctypes.Structure):
+    _fields_ = [("mode", ctypes.c_int32), ("out_dtype", ctypes.c_int32),
+                ("out", ctypes.c_void_p), ("out_stride_b", ctypes.c_int64),
+                ("out_stride_h", ctypes.c_int64), ("lse", ctypes.c_void_p),
+                ("m", ctypes.c_void_p), ("l", ctypes.c_void_p), ("o", ctypes.c_void_p)]
+
+
+# name -> (restype, argtypes); must match include/halo_b200.h
+SIGNATURES = {
+    "halo_decode_workspace_bytes": (ctypes.c_int64, [ctypes.POINTER(DecodeProblem),
+                                                     ctypes.POINTER(KVChunk), ctypes.c_int32]),
+    "halo_chunked_decode": (ctypes.c_int32, [ctypes.POINTER(DecodeProblem), ctypes.POINTER(KVChunk),
+                                             ctypes.c_int32, ctypes.c_void_p, ctypes.c_int64,
+                                             ctypes.POINTER(MergeArgs), ctypes.c_void_p]),
+    "halo_lse_merge": (ctypes.c_int32, [ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                                        ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p,
+                                        ctypes.c_void_p, ctypes.POINTER(MergeArgs),
+                                        ctypes.c_void_p]),
+    "halo_last_error_string": (ctypes.c_char_p, []),
+    "halo_device_error": (ctypes.c_int32, [ctypes.POINTER(ctypes.c_int32), ctypes.c_int32]),
+    "halo_version": (ctypes.c_int32, []),
+}
+
+_lib = None
+_lock = threading.Lock()
+
+
+def lib() -> ctypes.CDLL:
+    """Load ``libhalo_sm100.so`` once; raise ``HaloError`` if it is missing."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not os.path.exists(LIB_PATH):
+                raise HaloError(f"{LIB_PATH} not built; run `python -m halo_b200.build`")
+            handle = ctypes.CDLL(LIB_PATH)
+            for name, (res, args) in SIGNATURES.items():
+                fn = getattr(handle, name)
+                fn.restype = res
+                fn.argtypes = args
+            _lib = handle
+    return _lib
+
+
+def check(rc: int, what: str) -> None:
+    if rc != HALO_OK:
+        msg = lib().halo_last_error_string()
+        raise HaloError(f"{what} failed ({rc}): {msg.decode() if msg else ''}", rc)
+
+
+def device_error(clear: bool = True) -> int:
+    """Read (and clear) the device error word; 0 or a HALO_ERR_* code."""
+    code = ctypes.c_int32(0)
+    check(lib().halo_device_error(ctypes.byref(code), int(clear)), "halo_device_error")
+    return code.value
+
+
+def stream_handle(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream

@@ -1,0 +1,1212 @@
+// Split-KV chunked decode attention + log-sum-exp merge for B200 (sm_100a).
+//
+// Replaces the reference's per-chunk Triton kernel (halo/triton_chunked.py:47-138,
+// one program per (b, q-head), one launch per chunk, K/V re-read by every
+// q-head of a GQA group) with:
+//   * kd: one CTA per (work item, kv-head, batch row).  A work item is a
+//     contiguous row range of one chunk.  A producer warp streams 64-row K/V
+//     tiles into a 3-stage shared-memory ring with per-row async bulk copies
+//     (cp.async.bulk + mbarrier transaction counts); four consumer warps
+//     each own 16 rows of every tile and attend ALL q-heads of the GQA group
+//     at once, so every K/V byte is read from HBM exactly once.
+//       - bf16/fp16: S = Q K^T and O += P V on tensor cores (mma.m16n8k16,
+//         fp32 accumulate).  P is split into a 16-bit high part and a 16-bit
+//         residual, so P V keeps ~16 mantissa bits (the reference's P is fp32).
+//       - fp32: CUDA-core FMA (exact fp32 products and sums).
+//     Online softmax in the exp2 domain with warp-shuffle row reductions.
+//     Each CTA writes one partial state (m, l, o) per q-head.
+//   * km: one warp per (b, q-head) folds all partial states (and optionally a
+//     prior running state) into the final output + LSE, or into the running
+//     (m, l, o) accumulators of update_chunk.
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "halo_common.cuh"
+
+namespace halo {
+
+__device__ unsigned int g_device_error = 0;
+
+unsigned int* device_error_ptr() {
+  static std::mutex mu;
+  static unsigned int* cache[64] = {nullptr};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lk(mu);
+  if (!cache[dev]) {
+    void* ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_device_error) == cudaSuccess)
+      cache[dev] = static_cast<unsigned int*>(ptr);
+  }
+  return cache[dev];
+}
+
+// ---------------------------------------------------------------- config
+constexpr int kBlockN = 64;          // K/V rows per pipeline stage (one TMA box high)
+constexpr int kConsumerWarps = 4;    // each owns 16 rows of every stage
+constexpr int kThreads = (kConsumerWarps + 1) * 32;
+constexpr int kMaxSegs = 48;         // tensor-map pairs per launch
+constexpr int kMaxItems = 512;       // work items per launch
+
+// A work item: `rows` consecutive rows of one segment (a K/V view with its
+// own pair of tensor maps), starting at segment row `row0`, whose first row
+// sits at global position `start`.
+struct Item {
+  int64_t start;
+  int32_t seg;
+  int32_t row0;
+  int32_t rows;
+  int32_t slot;     // first partial slot; warp w writes slot + w
+  int32_t causal;
+  int32_t b_bcast;  // batch stride 0: every batch row reads batch 0
+};
+
+struct alignas(64) DecodeParams {
+  CUtensorMap maps[2 * kMaxSegs];  // K, V tensor map per segment
+  CUtensorMap qmap;                // q as {D, H, B}
+  Item items[kMaxItems];
+  const int64_t* q_pos;
+  float* m_part;
+  float* l_part;
+  float* o_part;
+  unsigned int* err;  // device error word
+  int32_t B, H, H_kv, G, gblocks;
+  int32_t S;          // partial slots per (b, h) row
+  int32_t n_items, n_units;
+  float scale_log2;   // softmax scale * log2(e)
+};
+
+template <typename T, int D, int STAGES>
+struct Geom {
+  static constexpr int kElt = sizeof(T);
+  static constexpr int kRowBytes = D * kElt;
+  static constexpr int kBoxElems = 128 / kElt;         // inner box: 128 bytes
+  static constexpr int kNBox = kRowBytes / 128;        // boxes per row
+  static constexpr int kBoxBytes = kBlockN * 128;
+  static constexpr int kTileBytes = kNBox * kBoxBytes;
+  static constexpr int kStageBytes = 2 * kTileBytes;
+  static constexpr int kGpb = (kElt == 4 ? 8 : 16);   // q-heads per unit
+  static constexpr int kQSlotBytes = kNBox * kGpb * 128;
+  static constexpr int kPBytes = (kElt == 4 ? kConsumerWarps * 16 * 8 * 4 : 0);
+  static constexpr int kBarBytes = 128;
+  // ring | q ring (2 slots) | P | barriers ; +1024 for manual alignment
+  static constexpr int kSmemBytes =
+      STAGES * kStageBytes + 2 * kQSlotBytes + kPBytes + kBarBytes + 1024;
+  static_assert(kRowBytes % 128 == 0, "row must be a whole number of 128-byte boxes");
+  static_assert(kQSlotBytes % 1024 == 0, "q slot must keep 1024-byte alignment");
+};
+
+struct Unit {
+  int item, b, h_kv, gbase, gcount;
+};
+
+__device__ __forceinline__ Unit decode_unit(const DecodeParams& p, int u, int gpb) {
+  Unit r;
+  r.item = u % p.n_items;
+  int pair = u / p.n_items;
+  const int gb = pair % p.gblocks;
+  pair /= p.gblocks;
+  r.h_kv = pair % p.H_kv;
+  r.b = pair / p.H_kv;
+  r.gbase = gb * gpb;
+  r.gcount = min(gpb, p.G - r.gbase);
+  return r;
+}
+
+// Write one warp's partial state for q-head rows [gbase, gbase+gcount).
+__device__ __forceinline__ void write_partial_meta(const DecodeParams& p, const Unit& un,
+                                                   const Item& it, int warp, int g, float m_log2,
+                                                   float l) {
+  const int h = un.h_kv * p.G + un.gbase + g;
+  const int64_t row = ((int64_t)un.b * p.H + h) * p.S + it.slot + warp;
+  p.m_part[row] = (m_log2 == -INFINITY) ? -INFINITY : m_log2 * kLn2;
+  p.l_part[row] = l;
+}
+
+// ---------------------------------------------------------------- consumers
+// 16-bit inputs: tensor-core path.  Warp `w` handles rows [16w, 16w+16) of
+// every stage; the 16 query rows of the MMA are the unit's q-heads.
+template <typename T, int D, int STAGES>
+__device__ __forceinline__ bool consume_mma(const DecodeParams& p, const Unit& un, const Item& it,
+                                            char* ring, const char* qslot, uint64_t* full,
+                                            uint64_t* empty, uint64_t* qempty, int n_tiles,
+                                            int& gt, int64_t qpos) {
+  using Gm = Geom<T, D, STAGES>;
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+
+  // Q fragments (A operand) for all k-steps, loaded once per unit.
+  uint32_t qf[D / 16][4];
+  {
+    const uint32_t qb = smem_addr(qslot);
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk) {
+      const int row = lane & 15;
+      const int c16 = kk * 2 + (lane >> 4);
+      ldsm_x4(qb + swz128<Gm::kGpb>(row, c16), qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3]);
+    }
+  }
+  __syncwarp();
+  if (lane == 0) mbar_arrive(qempty);
+
+  float o[D / 8][4];
+#pragma unroll
+  for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+  const int c = lane & 3;
+  const int item_end = it.row0 + it.rows;
+  const int wrow = warp * 16;
+  bool ok = true;
+
+  for (int t = 0; t < n_tiles; ++t, ++gt) {
+    const int s = gt % STAGES;
+    if (!mbar_wait(&full[s], (gt / STAGES) & 1, p.err)) { ok = false; ++gt; break; }
+    const uint32_t kbase = smem_addr(ring + s * Gm::kStageBytes);
+    const uint32_t vbase = kbase + Gm::kTileBytes;
+
+    // ---- S = Q K^T (16 q-heads x 16 keys)
+    float sacc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    {
+      const int key = wrow + (lane & 7) + ((lane >> 4) << 3);
+#pragma unroll
+      for (int kk = 0; kk < D / 16; ++kk) {
+        const int c16 = kk * 2 + ((lane >> 3) & 1);
+        uint32_t b00, b01, b10, b11;
+        ldsm_x4(kbase + swz128(key, c16), b00, b01, b10, b11);
+        mma_16816(sacc[0], qf[kk], b00, b01, (T*)nullptr);
+        mma_16816(sacc[1], qf[kk], b10, b11, (T*)nullptr);
+      }
+    }
+
+    // ---- scale + mask (rows beyond the item, or causally hidden)
+    const int row_base = it.row0 + t * kBlockN + wrow;
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int row = row_base + nt * 8 + 2 * c + e;
+        const bool valid =
+            row < item_end && (!it.causal || it.start + (row - it.row0) <= qpos);
+        sacc[nt][e] = valid ? sacc[nt][e] * p.scale_log2 : -INFINITY;
+        sacc[nt][e + 2] = valid ? sacc[nt][e + 2] * p.scale_log2 : -INFINITY;
+      }
+
+    // ---- online softmax (rows g0 = lane/4, g1 = lane/4 + 8)
+    float r0 = fmaxf(fmaxf(sacc[0][0], sacc[0][1]), fmaxf(sacc[1][0], sacc[1][1]));
+    float r1 = fmaxf(fmaxf(sacc[0][2], sacc[0][3]), fmaxf(sacc[1][2], sacc[1][3]));
+    r0 = fmaxf(r0, __shfl_xor_sync(0xffffffffu, r0, 1));
+    r0 = fmaxf(r0, __shfl_xor_sync(0xffffffffu, r0, 2));
+    r1 = fmaxf(r1, __shfl_xor_sync(0xffffffffu, r1, 1));
+    r1 = fmaxf(r1, __shfl_xor_sync(0xffffffffu, r1, 2));
+    const float mn0 = fmaxf(m0, r0), mn1 = fmaxf(m1, r1);
+    const float mu0 = (mn0 == -INFINITY) ? 0.f : mn0;
+    const float mu1 = (mn1 == -INFINITY) ? 0.f : mn1;
+    const float a0 = exp2f(m0 - mu0), a1 = exp2f(m1 - mu1);
+    m0 = mn0;
+    m1 = mn1;
+    float pr[2][4];
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      pr[nt][0] = exp2f(sacc[nt][0] - mu0);
+      pr[nt][1] = exp2f(sacc[nt][1] - mu0);
+      pr[nt][2] = exp2f(sacc[nt][2] - mu1);
+      pr[nt][3] = exp2f(sacc[nt][3] - mu1);
+    }
+    l0 = l0 * a0 + (pr[0][0] + pr[0][1] + pr[1][0] + pr[1][1]);
+    l1 = l1 * a1 + (pr[0][2] + pr[0][3] + pr[1][2] + pr[1][3]);
+    if (__any_sync(0xffffffffu, a0 != 1.f || a1 != 1.f)) {
+#pragma unroll
+      for (int i = 0; i < D / 8; ++i) {
+        o[i][0] *= a0;
+        o[i][1] *= a0;
+        o[i][2] *= a1;
+        o[i][3] *= a1;
+      }
+    }
+
+    // ---- O += P V with P = hi + lo (two 16-bit MMAs)
+    uint32_t ph[4], pl[4];
+    {
+      const float v[4][2] = {{pr[0][0], pr[0][1]}, {pr[0][2], pr[0][3]},
+                             {pr[1][0], pr[1][1]}, {pr[1][2], pr[1][3]}};
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        ph[r] = Elem<T>::pack(v[r][0], v[r][1]);
+        float h0, h1;
+        Elem<T>::unpack(ph[r], h0, h1);
+        pl[r] = Elem<T>::pack(v[r][0] - h0, v[r][1] - h1);
+      }
+    }
+    {
+      const int key = wrow + (lane & 7) + (((lane >> 3) & 1) << 3);
+#pragma unroll
+      for (int j = 0; j < D / 16; ++j) {
+        const int c16 = j * 2 + (lane >> 4);
+        uint32_t v0, v1, v2, v3;
+        ldsm_x4_t(vbase + swz128(key, c16), v0, v1, v2, v3);
+        mma_16816(o[2 * j], ph, v0, v1, (T*)nullptr);
+        mma_16816(o[2 * j], pl, v0, v1, (T*)nullptr);
+        mma_16816(o[2 * j + 1], ph, v2, v3, (T*)nullptr);
+        mma_16816(o[2 * j + 1], pl, v2, v3, (T*)nullptr);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+  }
+
+  // ---- this warp's partial state -> global (rows < gcount only)
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+  const int g0 = lane >> 2;
+#pragma unroll
+  for (int half = 0; half < 2; ++half) {
+    const int g = g0 + 8 * half;
+    if (g < un.gcount) {
+      if (c == 0) write_partial_meta(p, un, it, warp, g, half ? m1 : m0, half ? l1 : l0);
+      const int h = un.h_kv * p.G + un.gbase + g;
+      float* op = p.o_part + (((int64_t)un.b * p.H + h) * p.S + it.slot + warp) * D;
+#pragma unroll
+      for (int i = 0; i < D / 8; ++i)
+        *reinterpret_cast<float2*>(op + i * 8 + 2 * c) =
+            make_float2(o[i][2 * half], o[i][2 * half + 1]);
+    }
+  }
+  return ok;
+}
+
+// fp32 inputs: CUDA-core FMA path, up to 8 q-heads per unit.  For S, lane
+// pair (2k, 2k+1) owns key k of the warp's 16 rows, each lane one half of D
+// (the second half walks its 16-byte chunks rotated by 4 so both halves hit
+// different bank groups); for P V each lane owns D/32 output columns.
+template <int D, int STAGES>
+__device__ __forceinline__ bool consume_fma(const DecodeParams& p, const Unit& un, const Item& it,
+                                            char* ring, const char* qslot, float* ps_all,
+                                            uint64_t* full, uint64_t* empty, uint64_t* qempty,
+                                            int n_tiles, int& gt, int64_t qpos) {
+  using Gm = Geom<float, D, STAGES>;
+  constexpr int GP = 8;
+  constexpr int DPL = D / 32;      // output columns per lane
+  constexpr int NCH = D / 4;       // 16-byte chunks per row
+  constexpr int HALF = NCH / 2;
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  float* ps = ps_all + warp * 16 * GP;
+  const int gcount = un.gcount;
+
+  float o[GP][DPL];
+  float m[GP], l[GP];
+#pragma unroll
+  for (int g = 0; g < GP; ++g) {
+    m[g] = -INFINITY;
+    l[g] = 0.f;
+#pragma unroll
+    for (int e = 0; e < DPL; ++e) o[g][e] = 0.f;
+  }
+  const int key = lane >> 1, half = lane & 1;
+  const int item_end = it.row0 + it.rows;
+  const int wrow = warp * 16;
+  bool ok = true;
+
+  for (int t = 0; t < n_tiles; ++t, ++gt) {
+    const int s = gt % STAGES;
+    if (!mbar_wait(&full[s], (gt / STAGES) & 1, p.err)) { ok = false; ++gt; break; }
+    const char* kt = ring + s * Gm::kStageBytes;
+    const char* vt = kt + Gm::kTileBytes;
+
+    float acc[GP];
+#pragma unroll
+    for (int g = 0; g < GP; ++g) acc[g] = 0.f;
+#pragma unroll 4
+    for (int i = 0; i < HALF; ++i) {
+      const int j = half * HALF + ((HALF >= 8 && half) ? ((i & ~7) | ((i + 4) & 7)) : i);
+      const float4 kv = *reinterpret_cast<const float4*>(kt + swz128(wrow + key, j));
+#pragma unroll
+      for (int g = 0; g < GP; ++g) {
+        if (g < gcount) {
+          const float4 qv = *reinterpret_cast<const float4*>(qslot + swz128<GP>(g, j));
+          acc[g] = fmaf(qv.x, kv.x, acc[g]);
+          acc[g] = fmaf(qv.y, kv.y, acc[g]);
+          acc[g] = fmaf(qv.z, kv.z, acc[g]);
+          acc[g] = fmaf(qv.w, kv.w, acc[g]);
+        }
+      }
+    }
+    const int row = it.row0 + t * kBlockN + wrow + key;
+    const bool valid = row < item_end && (!it.causal || it.start + (row - it.row0) <= qpos);
+    float pk[GP];
+#pragma unroll
+    for (int g = 0; g < GP; ++g) {
+      float sv = acc[g] + __shfl_xor_sync(0xffffffffu, acc[g], 1);
+      sv = valid ? sv * p.scale_log2 : -INFINITY;
+      float mt = sv;
+      mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 2));
+      mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 4));
+      mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 8));
+      mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 16));
+      const float mn = fmaxf(m[g], mt);
+      const float mu = (mn == -INFINITY) ? 0.f : mn;
+      const float a = exp2f(m[g] - mu);
+      m[g] = mn;
+      pk[g] = exp2f(sv - mu);
+      l[g] = l[g] * a + (half == 0 ? pk[g] : 0.f);
+#pragma unroll
+      for (int e = 0; e < DPL; ++e) o[g][e] *= a;
+    }
+    if (half == 0) {
+#pragma unroll
+      for (int g = 0; g < GP; ++g) ps[key * GP + g] = pk[g];
+    }
+    __syncwarp();
+    const int jv = (lane * DPL) / 4;           // this lane's 16-byte chunk
+    const int bo = ((lane * DPL) % 4) * 4;     // byte offset inside it
+#pragma unroll 4
+    for (int kr = 0; kr < 16; ++kr) {
+      const float* vrow = reinterpret_cast<const float*>(vt + swz128(wrow + kr, jv) + bo);
+      float vv[DPL];
+      if constexpr (DPL == 4) {
+        const float4 t4 = *reinterpret_cast<const float4*>(vrow);
+        vv[0] = t4.x; vv[1] = t4.y; vv[2] = t4.z; vv[3] = t4.w;
+      } else if constexpr (DPL == 2) {
+        const float2 t2 = *reinterpret_cast<const float2*>(vrow);
+        vv[0] = t2.x; vv[1] = t2.y;
+      } else {
+        vv[0] = vrow[0];
+      }
+      const float4 p03 = *reinterpret_cast<const float4*>(ps + kr * GP);
+      const float4 p47 = *reinterpret_cast<const float4*>(ps + kr * GP + 4);
+      const float pp[8] = {p03.x, p03.y, p03.z, p03.w, p47.x, p47.y, p47.z, p47.w};
+#pragma unroll
+      for (int g = 0; g < GP; ++g)
+#pragma unroll
+        for (int e = 0; e < DPL; ++e) o[g][e] = fmaf(pp[g], vv[e], o[g][e]);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+  }
+  // Q stays in shared memory for the whole unit on this path.
+  __syncwarp();
+  if (lane == 0) mbar_arrive(qempty);
+
+#pragma unroll
+  for (int g = 0; g < GP; ++g) {
+    float v = l[g];
+    v += __shfl_xor_sync(0xffffffffu, v, 1);
+    v += __shfl_xor_sync(0xffffffffu, v, 2);
+    v += __shfl_xor_sync(0xffffffffu, v, 4);
+    v += __shfl_xor_sync(0xffffffffu, v, 8);
+    v += __shfl_xor_sync(0xffffffffu, v, 16);
+    l[g] = v;
+  }
+#pragma unroll
+  for (int g = 0; g < GP; ++g) {
+    if (g < gcount) {
+      if (lane == 0) write_partial_meta(p, un, it, warp, g, m[g], l[g]);
+      const int h = un.h_kv * p.G + un.gbase + g;
+      float* op = p.o_part + (((int64_t)un.b * p.H + h) * p.S + it.slot + warp) * D + lane * DPL;
+#pragma unroll
+      for (int e = 0; e < DPL; ++e) op[e] = o[g][e];
+    }
+  }
+  return ok;
+}
+
+// ---------------------------------------------------------------- kd kernel
+// Persistent: CTA c processes units c, c + gridDim.x, ...  The producer lane
+// streams every tile of every unit through one STAGES-deep ring (and each
+// unit's q tile through a 2-slot ring) without pausing at unit boundaries.
+template <typename T, int D, int STAGES, int MINB>
+__global__ void __launch_bounds__(kThreads, MINB) kd_kernel(const __grid_constant__ DecodeParams p) {
+  using Gm = Geom<T, D, STAGES>;
+  extern __shared__ char smem_raw[];
+  char* ring = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                       ~uintptr_t(1023));
+  char* qring = ring + STAGES * Gm::kStageBytes;
+  float* ps = reinterpret_cast<float*>(qring + 2 * Gm::kQSlotBytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(qring + 2 * Gm::kQSlotBytes + Gm::kPBytes);
+  uint64_t* empty = full + STAGES;
+  uint64_t* qfull = empty + STAGES;
+  uint64_t* qempty = qfull + 2;
+
+  const int tid = threadIdx.x;
+  if (tid == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kConsumerWarps);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&qfull[s], 1);
+      mbar_init(&qempty[s], kConsumerWarps);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+  const int warp = tid >> 5, lane = tid & 31;
+
+  if (warp == kConsumerWarps) {
+    // ---------------- producer warp: lane 0 issues every TMA load
+    if (lane == 0) {
+      int gt = 0, ut = 0;
+      for (int u = blockIdx.x; u < p.n_units; u += gridDim.x, ++ut) {
+        const Unit un = decode_unit(p, u, Gm::kGpb);
+        const Item& it = p.items[un.item];
+        const int qs = ut & 1;
+        if (ut >= 2 && !mbar_wait(&qempty[qs], ((ut >> 1) & 1) ^ 1, p.err)) return;
+        mbar_arrive_expect_tx(&qfull[qs], Gm::kQSlotBytes);
+#pragma unroll
+        for (int bx = 0; bx < Gm::kNBox; ++bx)
+          tma_load_3d(qring + qs * Gm::kQSlotBytes + bx * Gm::kGpb * 128, &p.qmap,
+                      bx * Gm::kBoxElems, un.h_kv * p.G + un.gbase, un.b, &qfull[qs]);
+        const CUtensorMap* kmap = &p.maps[2 * it.seg];
+        const CUtensorMap* vmap = &p.maps[2 * it.seg + 1];
+        const int bc = it.b_bcast ? 0 : un.b;
+        const int n_tiles = (it.rows + kBlockN - 1) / kBlockN;
+        for (int t = 0; t < n_tiles; ++t, ++gt) {
+          const int s = gt % STAGES;
+          if (gt >= STAGES && !mbar_wait(&empty[s], ((gt / STAGES) & 1) ^ 1, p.err)) return;
+          const int r0 = it.row0 + t * kBlockN;
+          char* kd = ring + s * Gm::kStageBytes;
+          char* vd = kd + Gm::kTileBytes;
+          mbar_arrive_expect_tx(&full[s], 2u * Gm::kTileBytes);
+#pragma unroll
+          for (int bx = 0; bx < Gm::kNBox; ++bx) {
+            tma_load_4d(kd + bx * Gm::kBoxBytes, kmap, bx * Gm::kBoxElems, r0, un.h_kv, bc, &full[s]);
+            tma_load_4d(vd + bx * Gm::kBoxBytes, vmap, bx * Gm::kBoxElems, r0, un.h_kv, bc, &full[s]);
+          }
+        }
+      }
+    }
+    return;
+  }
+
+  // ---------------- consumer warps
+  int gt = 0, ut = 0;
+  for (int u = blockIdx.x; u < p.n_units; u += gridDim.x, ++ut) {
+    const Unit un = decode_unit(p, u, Gm::kGpb);
+    const Item& it = p.items[un.item];
+    const int qs = ut & 1;
+    if (!mbar_wait(&qfull[qs], (ut >> 1) & 1, p.err)) return;
+    const int64_t qpos = (it.causal && p.q_pos != nullptr) ? p.q_pos[un.b] : INT64_MAX;
+    const int n_tiles = (it.rows + kBlockN - 1) / kBlockN;
+    bool ok;
+    if constexpr (sizeof(T) == 4)
+      ok = consume_fma<D, STAGES>(p, un, it, ring, qring + qs * Gm::kQSlotBytes, ps, full, empty,
+                                  &qempty[qs], n_tiles, gt, qpos);
+    else
+      ok = consume_mma<T, D, STAGES>(p, un, it, ring, qring + qs * Gm::kQSlotBytes, full, empty,
+                                     &qempty[qs], n_tiles, gt, qpos);
+    if (!ok) return;  // the error word is set; remaining units are abandoned
+  }
+}
+
+// ---------------------------------------------------------------- km kernel
+struct MergeParams {
+  const float* m_parts;
+  const float* l_parts;
+  const float* o_parts;
+  int32_t R, H, P, Dv;
+  int32_t mode, out_dtype;
+  char* out;
+  int64_t out_sb, out_sh;  // element strides
+  float* lse;
+  float* m;
+  float* l;
+  float* o;
+};
+
+// One CTA of kMergeWarps warps per (b, h) row.  Pass 1: the row max M over
+// every partial (and the prior state).  Pass 2: warp w folds partials
+// s = w, w + kMergeWarps, ... with weights exp(m_s - M), four partials in
+// flight per lane; the warps' sums are then combined through shared memory.
+constexpr int kMergeWarps = 8;
+
+template <int DPL>
+__global__ void __launch_bounds__(kMergeWarps * 32) km_kernel(const MergeParams mp) {
+  __shared__ float s_red[kMergeWarps];
+  __shared__ float s_l[kMergeWarps];
+  __shared__ __align__(16) float s_o[kMergeWarps][DPL * 32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x;
+  const float* mr = mp.m_parts + (int64_t)row * mp.P;
+  const float* lr = mp.l_parts + (int64_t)row * mp.P;
+  const float* orow = mp.o_parts + (int64_t)row * mp.P * mp.Dv;
+  const bool have_prior = mp.m != nullptr;
+
+  // ---- pass 1: row max
+  float M = -INFINITY;
+  for (int s = threadIdx.x; s < mp.P; s += blockDim.x) M = fmaxf(M, mr[s]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+  if (lane == 0) s_red[warp] = M;
+  __syncthreads();
+  M = have_prior ? mp.m[row] : -INFINITY;
+#pragma unroll
+  for (int w = 0; w < kMergeWarps; ++w) M = fmaxf(M, s_red[w]);
+
+  // ---- pass 2: weighted sums, this warp's share of the partials
+  const int d0 = lane * DPL;
+  const bool active = d0 < mp.Dv;
+  float L = 0.f;
+  float acc[DPL];
+#pragma unroll
+  for (int e = 0; e < DPL; ++e) acc[e] = 0.f;
+  if (M != -INFINITY) {
+    int s = warp;
+    for (; s + 3 * kMergeWarps < mp.P; s += 4 * kMergeWarps) {
+      float ms[4], ls[4], w[4];
+      float ov[4][DPL];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        ms[j] = mr[s + j * kMergeWarps];
+        ls[j] = lr[s + j * kMergeWarps];
+        if (active) {
+          const float* src = orow + (int64_t)(s + j * kMergeWarps) * mp.Dv + d0;
+#pragma unroll
+          for (int e = 0; e < DPL; ++e) ov[j][e] = src[e];
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        w[j] = (ms[j] == -INFINITY) ? 0.f : expf(ms[j] - M);
+        L = fmaf(ls[j], w[j], L);
+        if (active)
+#pragma unroll
+          for (int e = 0; e < DPL; ++e) acc[e] = fmaf(ov[j][e], w[j], acc[e]);
+      }
+    }
+    for (; s < mp.P; s += kMergeWarps) {
+      const float ms = mr[s];
+      if (ms == -INFINITY) continue;
+      const float w = expf(ms - M);
+      L = fmaf(lr[s], w, L);
+      if (active) {
+        const float* src = orow + (int64_t)s * mp.Dv + d0;
+#pragma unroll
+        for (int e = 0; e < DPL; ++e) acc[e] = fmaf(src[e], w, acc[e]);
+      }
+    }
+  }
+  if (lane == 0) s_l[warp] = L;
+#pragma unroll
+  for (int e = 0; e < DPL; ++e) s_o[warp][d0 + e] = acc[e];
+  __syncthreads();
+  if (warp != 0) return;
+
+  // ---- warp 0: combine the warps (plus the prior state) and write
+  L = 0.f;
+#pragma unroll
+  for (int w = 0; w < kMergeWarps; ++w) L += s_l[w];
+#pragma unroll
+  for (int e = 0; e < DPL; ++e) {
+    float v = 0.f;
+#pragma unroll
+    for (int w = 0; w < kMergeWarps; ++w) v += s_o[w][d0 + e];
+    acc[e] = v;
+  }
+  if (have_prior && M != -INFINITY) {
+    const float mw = mp.m[row];
+    const float w = (mw == -INFINITY) ? 0.f : expf(mw - M);
+    L = fmaf(mp.l[row], w, L);
+    if (active)
+#pragma unroll
+      for (int e = 0; e < DPL; ++e) acc[e] = fmaf(mp.o[(int64_t)row * mp.Dv + d0 + e], w, acc[e]);
+  }
+
+  if (mp.mode == HALO_MERGE_ACCUMULATE) {
+    if (lane == 0) {
+      mp.m[row] = M;
+      mp.l[row] = L;
+    }
+    if (active)
+#pragma unroll
+      for (int e = 0; e < DPL; ++e) mp.o[(int64_t)row * mp.Dv + d0 + e] = acc[e];
+    return;
+  }
+  const int b = row / mp.H, h = row % mp.H;
+  if (lane == 0 && mp.lse != nullptr) mp.lse[row] = (L > 0.f) ? M + logf(L) : -INFINITY;
+  if (!active) return;
+  const float inv = (L > 0.f) ? 1.f / L : 0.f;
+  const int64_t off = (int64_t)b * mp.out_sb + (int64_t)h * mp.out_sh + d0;
+#pragma unroll
+  for (int e = 0; e < DPL; ++e) {
+    const float v = (L > 0.f) ? acc[e] * inv : 0.f;
+    if (mp.out_dtype == HALO_DTYPE_F32)
+      reinterpret_cast<float*>(mp.out)[off + e] = v;
+    else if (mp.out_dtype == HALO_DTYPE_BF16)
+      reinterpret_cast<__nv_bfloat16*>(mp.out)[off + e] = __float2bfloat16_rn(v);
+    else
+      reinterpret_cast<__half*>(mp.out)[off + e] = __float2half_rn(v);
+  }
+}
+
+// ================================================================ host side
+thread_local std::string t_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  t_last_error = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(HALO_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+int device_sms() {
+  static std::mutex mu;
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  std::lock_guard<std::mutex> lk(mu);
+  if (cache[dev] == 0) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cache[dev] = n > 0 ? n : 148;
+  }
+  return cache[dev];
+}
+
+static int elt_size(int dtype) {
+  return dtype == HALO_DTYPE_F32 ? 4 : (dtype == HALO_DTYPE_BF16 || dtype == HALO_DTYPE_F16) ? 2 : 0;
+}
+
+// ---------------------------------------------------------------- tensor maps
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess && q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  });
+  return fn;
+}
+
+struct MapKey {
+  uintptr_t ptr;
+  int64_t dims[4];
+  int64_t strides[3];
+  int dtype;
+  bool operator==(const MapKey& o) const {
+    return ptr == o.ptr && dtype == o.dtype && std::memcmp(dims, o.dims, sizeof(dims)) == 0 &&
+           std::memcmp(strides, o.strides, sizeof(strides)) == 0;
+  }
+};
+struct MapKeyHash {
+  size_t operator()(const MapKey& k) const {
+    uint64_t h = 1469598103934665603ull ^ k.ptr;
+    auto mix = [&](uint64_t v) { h = (h ^ v) * 1099511628211ull; };
+    for (int i = 0; i < 4; ++i) mix(static_cast<uint64_t>(k.dims[i]));
+    for (int i = 0; i < 3; ++i) mix(static_cast<uint64_t>(k.strides[i]));
+    mix(static_cast<uint64_t>(k.dtype));
+    return static_cast<size_t>(h);
+  }
+};
+
+// Encode (or fetch from a small host cache) the 4-D tiled tensor map of one
+// K or V view: dims {D, rows, H_kv, B}, 128-byte inner box x 64 rows, 128B
+// swizzle, out-of-bounds rows zero-filled.
+static int encode_view(const void* base, int64_t rows, int H_kv, int B, int D, int dtype,
+                       int64_t sb_el, int64_t sh_el, int64_t st_el, CUtensorMap* out) {
+  const int elt = elt_size(dtype);
+  MapKey key;
+  key.ptr = reinterpret_cast<uintptr_t>(base);
+  const bool bcast = sb_el == 0;
+  key.dims[0] = D;
+  key.dims[1] = rows;
+  key.dims[2] = H_kv;
+  key.dims[3] = bcast ? 1 : B;
+  key.strides[0] = st_el * elt;
+  key.strides[1] = sh_el * elt;
+  key.strides[2] = bcast ? sh_el * elt * H_kv : sb_el * elt;
+  key.dtype = dtype;
+  static std::mutex mu;
+  static std::unordered_map<MapKey, CUtensorMap, MapKeyHash> cache;
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    auto itc = cache.find(key);
+    if (itc != cache.end()) {
+      *out = itc->second;
+      return HALO_OK;
+    }
+  }
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(HALO_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  if (key.strides[2] == 0) key.strides[2] = key.strides[1] > 0 ? key.strides[1] : 16;
+  cuuint64_t gdim[4] = {(cuuint64_t)key.dims[0], (cuuint64_t)key.dims[1], (cuuint64_t)key.dims[2],
+                        (cuuint64_t)key.dims[3]};
+  cuuint64_t gstr[3] = {(cuuint64_t)key.strides[0], (cuuint64_t)key.strides[1],
+                        (cuuint64_t)key.strides[2]};
+  cuuint32_t box[4] = {(cuuint32_t)(128 / elt), (cuuint32_t)kBlockN, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUtensorMapDataType dt = dtype == HALO_DTYPE_F32    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                 : dtype == HALO_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                            : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUresult r = fn(out, dt, 4, const_cast<void*>(base), gdim, gstr, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(HALO_ERR_INVALID_ARG,
+                "cuTensorMapEncodeTiled failed (%d): dims {%lld,%lld,%lld,%lld} strides "
+                "{%lld,%lld,%lld} bytes",
+                (int)r, (long long)key.dims[0], (long long)key.dims[1], (long long)key.dims[2],
+                (long long)key.dims[3], (long long)key.strides[0], (long long)key.strides[1],
+                (long long)key.strides[2]);
+  std::lock_guard<std::mutex> lk(mu);
+  if (cache.size() > 8192) cache.clear();
+  cache.emplace(key, *out);
+  return HALO_OK;
+}
+
+
+static int64_t align256(int64_t x) { return (x + 255) & ~int64_t(255); }
+
+static int validate_problem(const halo_decode_problem_t* p, const halo_kv_chunk_t* chunks,
+                            int n_chunks) {
+  if (!p) return fail(HALO_ERR_INVALID_ARG, "problem is NULL");
+  if (p->B <= 0 || p->H <= 0 || p->H_kv <= 0 || p->D <= 0 || p->Dv <= 0)
+    return fail(HALO_ERR_INVALID_ARG, "non-positive dimension (B=%d H=%d H_kv=%d D=%d Dv=%d)",
+                p->B, p->H, p->H_kv, p->D, p->Dv);
+  if (p->H % p->H_kv != 0)
+    return fail(HALO_ERR_INVALID_ARG, "H=%d not divisible by H_kv=%d", p->H, p->H_kv);
+  if (elt_size(p->dtype) == 0) return fail(HALO_ERR_INVALID_ARG, "bad dtype %d", p->dtype);
+  if (p->Dv != p->D) return fail(HALO_ERR_UNSUPPORTED, "Dv (%d) != D (%d)", p->Dv, p->D);
+  const bool d_ok = (p->dtype == HALO_DTYPE_F32) ? (p->D == 32 || p->D == 64 || p->D == 128)
+                                                 : (p->D == 64 || p->D == 128);
+  if (!d_ok) return fail(HALO_ERR_UNSUPPORTED, "head_dim %d unsupported for dtype %d", p->D, p->dtype);
+  if (n_chunks < 0 || (n_chunks > 0 && !chunks))
+    return fail(HALO_ERR_INVALID_ARG, "bad chunk list");
+  if (n_chunks > 0 && !p->q) return fail(HALO_ERR_INVALID_ARG, "q is NULL");
+  const int elt = elt_size(p->dtype);
+  for (int i = 0; i < n_chunks; ++i) {
+    const halo_kv_chunk_t& c = chunks[i];
+    if (c.len < 0) return fail(HALO_ERR_INVALID_ARG, "chunk %d: negative length", i);
+    if (c.len == 0) continue;
+    if (!c.k || !c.v) return fail(HALO_ERR_INVALID_ARG, "chunk %d: NULL k/v", i);
+    if (c.causal && !p->q_pos) return fail(HALO_ERR_INVALID_ARG, "chunk %d causal but q_pos NULL", i);
+    const int64_t s[6] = {c.k_stride_b, c.k_stride_h, c.k_stride_t,
+                          c.v_stride_b, c.v_stride_h, c.v_stride_t};
+    for (int j = 0; j < 6; ++j)
+      if ((s[j] * elt) % 16 != 0)
+        return fail(HALO_ERR_MISALIGNED, "chunk %d: stride %lld elements is not 16-byte aligned", i,
+                    (long long)s[j]);
+    if ((reinterpret_cast<uintptr_t>(c.k) | reinterpret_cast<uintptr_t>(c.v)) & 15)
+      return fail(HALO_ERR_MISALIGNED, "chunk %d: k/v pointer not 16-byte aligned", i);
+  }
+  return HALO_OK;
+}
+
+int launch_merge(const MergeParams& mp, cudaStream_t st) {
+  if (mp.R == 0) return HALO_OK;
+  const int threads = kMergeWarps * 32;
+  if (mp.Dv == 128) km_kernel<4><<<mp.R, threads, 0, st>>>(mp);
+  else if (mp.Dv == 64) km_kernel<2><<<mp.R, threads, 0, st>>>(mp);
+  else if (mp.Dv == 32) km_kernel<1><<<mp.R, threads, 0, st>>>(mp);
+  else if (mp.Dv <= 256) km_kernel<8><<<mp.R, threads, 0, st>>>(mp);
+  else return fail(HALO_ERR_UNSUPPORTED, "Dv %d > 256", mp.Dv);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? HALO_OK : cuda_fail(e, "km_kernel launch");
+}
+
+int validate_merge(const halo_merge_args_t* mg, int Dv) {
+  if (!mg) return fail(HALO_ERR_INVALID_ARG, "merge args NULL");
+  if (mg->mode == HALO_MERGE_ACCUMULATE) {
+    if (!mg->m || !mg->l || !mg->o) return fail(HALO_ERR_INVALID_ARG, "accumulate needs m, l, o");
+  } else if (mg->mode == HALO_MERGE_FINALIZE) {
+    if (!mg->out) return fail(HALO_ERR_INVALID_ARG, "finalize needs out");
+    if (elt_size(mg->out_dtype) == 0) return fail(HALO_ERR_INVALID_ARG, "bad out dtype");
+    if ((mg->m != nullptr) != (mg->l != nullptr) || (mg->m != nullptr) != (mg->o != nullptr))
+      return fail(HALO_ERR_INVALID_ARG, "prior state needs all of m, l, o");
+  } else {
+    return fail(HALO_ERR_INVALID_ARG, "bad merge mode %d", mg->mode);
+  }
+  (void)Dv;
+  return HALO_OK;
+}
+
+MergeParams merge_params(const halo_merge_args_t* mg, int B, int H, int Dv, int P,
+                         const float* m_parts, const float* l_parts, const float* o_parts) {
+  MergeParams mp;
+  mp.m_parts = m_parts;
+  mp.l_parts = l_parts;
+  mp.o_parts = o_parts;
+  mp.R = B * H;
+  mp.H = H;
+  mp.P = P;
+  mp.Dv = Dv;
+  mp.mode = mg->mode;
+  mp.out_dtype = mg->out_dtype;
+  mp.out = static_cast<char*>(mg->out);
+  mp.out_sb = mg->out_stride_b;
+  mp.out_sh = mg->out_stride_h;
+  mp.lse = mg->lse;
+  mp.m = mg->m;
+  mp.l = mg->l;
+  mp.o = mg->o;
+  return mp;
+}
+
+// ---------------------------------------------------------------- planning
+// A segment is a run of chunks that are contiguous in memory AND in global
+// position with one causal flag: it gets one K and one V tensor map and is
+// split into equal work items.
+struct Seg {
+  halo_kv_chunk_t view;  // k/v base, strides, start, total len, causal
+  int32_t first_chunk;
+};
+
+struct Plan {
+  std::vector<Seg> segs;
+  std::vector<Item> items;  // items[i].slot = i * kConsumerWarps
+  int32_t split_tiles = 0;
+  int32_t S = 0;            // partial slots per (b, h) row
+};
+
+static int gpb_for(int dtype) { return dtype == HALO_DTYPE_F32 ? 8 : 16; }
+
+static int ctas_per_sm(int dtype, int D);
+
+static bool continues(const halo_kv_chunk_t& a, const halo_kv_chunk_t& c, int elt) {
+  return c.causal == a.causal && c.start == a.start + a.len &&
+         c.k_stride_b == a.k_stride_b && c.k_stride_h == a.k_stride_h &&
+         c.k_stride_t == a.k_stride_t && c.v_stride_b == a.v_stride_b &&
+         c.v_stride_h == a.v_stride_h && c.v_stride_t == a.v_stride_t &&
+         static_cast<const char*>(c.k) ==
+             static_cast<const char*>(a.k) + (int64_t)a.len * a.k_stride_t * elt &&
+         static_cast<const char*>(c.v) ==
+             static_cast<const char*>(a.v) + (int64_t)a.len * a.v_stride_t * elt;
+}
+
+static Plan make_plan(const halo_decode_problem_t* p, const halo_kv_chunk_t* chunks, int n) {
+  Plan plan;
+  const int elt = elt_size(p->dtype);
+  for (int i = 0; i < n; ++i) {
+    const halo_kv_chunk_t& c = chunks[i];
+    if (c.len <= 0) continue;
+    if (!plan.segs.empty() && continues(plan.segs.back().view, c, elt)) {
+      plan.segs.back().view.len += c.len;
+    } else {
+      Seg sg;
+      sg.view = c;
+      sg.first_chunk = i;
+      plan.segs.push_back(sg);
+    }
+  }
+  if (plan.segs.empty()) return plan;
+
+  const int G = p->H / p->H_kv;
+  const int gpb = gpb_for(p->dtype);
+  const int64_t pairs = (int64_t)p->B * p->H_kv * ((G + gpb - 1) / gpb);
+  const int64_t grid = (int64_t)device_sms() * ctas_per_sm(p->dtype, p->D);
+  std::vector<int64_t> seg_tiles;
+  int64_t total_tiles = 0;
+  for (const Seg& sg : plan.segs) {
+    seg_tiles.push_back(ceil_div64(sg.view.len, kBlockN));
+    total_tiles += seg_tiles.back();
+  }
+  int64_t split = 0;
+  // Memoise the choice per layout signature: decode steps repeat layouts.
+  uint64_t sig = 1469598103934665603ull;
+  auto mix = [&](uint64_t v) { sig = (sig ^ v) * 1099511628211ull; };
+  mix((uint64_t)pairs); mix((uint64_t)grid); mix((uint64_t)p->D); mix((uint64_t)elt);
+  mix((uint64_t)p->B * p->H);
+  for (int64_t t : seg_tiles) mix((uint64_t)t);
+  static std::mutex plan_mu;
+  static std::unordered_map<uint64_t, int64_t> plan_cache;
+  if (p->max_split_rows <= 0) {
+    std::lock_guard<std::mutex> lk(plan_mu);
+    auto f = plan_cache.find(sig);
+    if (f != plan_cache.end()) split = f->second;
+  }
+  if (split > 0) {
+    // cached
+  } else if (p->max_split_rows > 0) {
+    split = std::max<int64_t>(1, p->max_split_rows / kBlockN);
+  } else {
+    // Choose the item size (in tiles) minimising the estimated time in
+    // tile-equivalents: the persistent grid's makespan
+    //   ceil(units / grid) * (tiles per item + per-unit cost)
+    // plus the merge traffic of kConsumerWarps partials per item and row,
+    // spread over the grid.  Ties go to larger items (fewer partials).
+    constexpr double kUnitCostTiles = 1.5;
+    const double tile_bytes = 2.0 * kBlockN * p->D * elt;
+    const double rows = (double)p->B * p->H;
+    double best = 1e300;
+    for (int64_t cand = std::max<int64_t>(1, total_tiles); cand >= 1; ) {
+      int64_t items = 0, longest = 0;
+      for (int64_t t : seg_tiles) {
+        items += ceil_div64(t, cand);
+        longest = std::max<int64_t>(longest, std::min<int64_t>(t, cand));
+      }
+      const int64_t units = items * pairs;
+      const double span = (double)ceil_div64(units, grid) * ((double)longest + kUnitCostTiles);
+      const double merge = rows * items * kConsumerWarps * (p->Dv + 2) * 4.0 * 2.0 /
+                           (tile_bytes * (double)grid);
+      const double cost = span + merge;
+      if (items <= 4 * kMaxItems && cost < best * (1.0 - 1e-3)) {
+        best = cost;
+        split = cand;
+      }
+      if (cand == 1) break;
+      cand = cand > 32 ? cand - std::max<int64_t>(1, cand / 32) : cand - 1;
+    }
+    if (split == 0) split = std::max<int64_t>(1, ceil_div64(total_tiles, 4 * kMaxItems));
+    std::lock_guard<std::mutex> lk(plan_mu);
+    if (plan_cache.size() > 4096) plan_cache.clear();
+    plan_cache.emplace(sig, split);
+  }
+  plan.split_tiles = (int32_t)split;
+  for (size_t si = 0; si < plan.segs.size(); ++si) {
+    const Seg& sg = plan.segs[si];
+    const int64_t split_rows = split * kBlockN;
+    for (int64_t r = 0; r < sg.view.len; r += split_rows) {
+      Item it;
+      it.seg = (int32_t)si;
+      it.row0 = (int32_t)r;
+      it.rows = (int32_t)std::min<int64_t>(split_rows, sg.view.len - r);
+      it.start = sg.view.start + r;
+      it.causal = sg.view.causal;
+      it.b_bcast = (sg.view.k_stride_b == 0 || sg.view.v_stride_b == 0) ? 1 : 0;
+      it.slot = (int32_t)plan.items.size() * kConsumerWarps;
+      plan.items.push_back(it);
+    }
+  }
+  plan.S = (int32_t)plan.items.size() * kConsumerWarps;
+  return plan;
+}
+
+static int64_t workspace_for(const halo_decode_problem_t* p, int S) {
+  const int64_t R = (int64_t)p->B * p->H;
+  return align256(R * S * 4) * 2 + align256(R * S * (int64_t)p->Dv * 4);
+}
+
+template <typename T, int D>
+struct KdConfig {
+  // 16-bit: 3 stages, 2 CTAs per SM; fp32: stages sized to one CTA per SM.
+  static constexpr int kStages = sizeof(T) == 4 ? (D == 128 ? 3 : 4) : 3;
+  static constexpr int kMinBlocks = sizeof(T) == 4 && D == 128 ? 1 : 2;
+};
+
+template <typename T, int D>
+static int kd_ctas_per_sm() {
+  using C = KdConfig<T, D>;
+  using Gm = Geom<T, D, C::kStages>;
+  static std::once_flag once[64];
+  static int cache[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::call_once(once[dev & 63], [&] {
+    cudaFuncSetAttribute(kd_kernel<T, D, C::kStages, C::kMinBlocks>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, Gm::kSmemBytes);
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+            &n, kd_kernel<T, D, C::kStages, C::kMinBlocks>, kThreads, Gm::kSmemBytes) !=
+            cudaSuccess || n <= 0)
+      n = 1;
+    cache[dev & 63] = n;
+  });
+  return cache[dev & 63];
+}
+
+static int ctas_per_sm(int dtype, int D) {
+  if (dtype == HALO_DTYPE_BF16) return D == 128 ? kd_ctas_per_sm<__nv_bfloat16, 128>()
+                                                : kd_ctas_per_sm<__nv_bfloat16, 64>();
+  if (dtype == HALO_DTYPE_F16) return D == 128 ? kd_ctas_per_sm<__half, 128>()
+                                               : kd_ctas_per_sm<__half, 64>();
+  if (D == 128) return kd_ctas_per_sm<float, 128>();
+  if (D == 64) return kd_ctas_per_sm<float, 64>();
+  return kd_ctas_per_sm<float, 32>();
+}
+
+template <typename T, int D>
+static int launch_kd(const DecodeParams& prm, cudaStream_t st) {
+  using C = KdConfig<T, D>;
+  using Gm = Geom<T, D, C::kStages>;
+  const int64_t grid_max = (int64_t)device_sms() * kd_ctas_per_sm<T, D>();
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(prm.n_units, grid_max));
+  kd_kernel<T, D, C::kStages, C::kMinBlocks><<<grid, kThreads, Gm::kSmemBytes, st>>>(prm);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? HALO_OK : cuda_fail(e, "kd_kernel launch");
+}
+
+static int dispatch_kd(int dtype, int D, const DecodeParams& prm, cudaStream_t st) {
+  if (dtype == HALO_DTYPE_BF16) {
+    if (D == 128) return launch_kd<__nv_bfloat16, 128>(prm, st);
+    if (D == 64) return launch_kd<__nv_bfloat16, 64>(prm, st);
+  } else if (dtype == HALO_DTYPE_F16) {
+    if (D == 128) return launch_kd<__half, 128>(prm, st);
+    if (D == 64) return launch_kd<__half, 64>(prm, st);
+  } else {
+    if (D == 128) return launch_kd<float, 128>(prm, st);
+    if (D == 64) return launch_kd<float, 64>(prm, st);
+    if (D == 32) return launch_kd<float, 32>(prm, st);
+  }
+  return fail(HALO_ERR_UNSUPPORTED, "no kernel for dtype %d D %d", dtype, D);
+}
+
+static int encode_q_map(const halo_decode_problem_t& pb, CUtensorMap* out) {
+  // q as a 3-D tensor {D, H, B}; box {128 bytes, q-heads per unit, 1}
+  const int elt = elt_size(pb.dtype);
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(HALO_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  if ((reinterpret_cast<uintptr_t>(pb.q) & 15) || (pb.q_stride_h * elt) % 16 ||
+      (pb.B > 1 && (pb.q_stride_b * elt) % 16))
+    return fail(HALO_ERR_MISALIGNED, "q pointer/strides must be 16-byte aligned");
+  cuuint64_t gdim[3] = {(cuuint64_t)pb.D, (cuuint64_t)pb.H, (cuuint64_t)pb.B};
+  cuuint64_t gstr[2] = {(cuuint64_t)(pb.q_stride_h * elt),
+                        (cuuint64_t)(pb.B > 1 ? pb.q_stride_b * elt : pb.q_stride_h * elt * pb.H)};
+  cuuint32_t box[3] = {(cuuint32_t)(128 / elt), (cuuint32_t)gpb_for(pb.dtype), 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  const CUtensorMapDataType dt = pb.dtype == HALO_DTYPE_F32    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                 : pb.dtype == HALO_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                               : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUresult r = fn(out, dt, 3, const_cast<void*>(pb.q), gdim, gstr, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(HALO_ERR_INVALID_ARG, "q tensor map encode failed (%d)", (int)r);
+  return HALO_OK;
+}
+
+}  // namespace halo
+
+using namespace halo;
+
+extern "C" int64_t halo_decode_workspace_bytes(const halo_decode_problem_t* problem,
+                                               const halo_kv_chunk_t* chunks, int32_t n_chunks) {
+  int rc = validate_problem(problem, chunks, n_chunks);
+  if (rc != HALO_OK) return rc;
+  Plan plan = make_plan(problem, chunks, n_chunks);
+  return workspace_for(problem, plan.S);
+}
+
+extern "C" int32_t halo_chunked_decode(const halo_decode_problem_t* problem,
+                                       const halo_kv_chunk_t* chunks, int32_t n_chunks,
+                                       void* workspace, int64_t workspace_bytes,
+                                       const halo_merge_args_t* merge, halo_stream_t stream) {
+  int rc = validate_problem(problem, chunks, n_chunks);
+  if (rc != HALO_OK) return rc;
+  rc = validate_merge(merge, problem->Dv);
+  if (rc != HALO_OK) return rc;
+  const halo_decode_problem_t& pb = *problem;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Plan plan = make_plan(problem, chunks, n_chunks);
+  const int64_t need = workspace_for(problem, plan.S);
+  if (plan.S > 0 && (!workspace || workspace_bytes < need))
+    return fail(HALO_ERR_WORKSPACE, "workspace %lld bytes < required %lld",
+                (long long)workspace_bytes, (long long)need);
+  if (reinterpret_cast<uintptr_t>(workspace) & 255)
+    return fail(HALO_ERR_MISALIGNED, "workspace must be 256-byte aligned");
+
+  const int64_t R = (int64_t)pb.B * pb.H;
+  char* ws = static_cast<char*>(workspace);
+  float* m_part = reinterpret_cast<float*>(ws);
+  float* l_part = reinterpret_cast<float*>(ws + align256(R * plan.S * 4));
+  float* o_part = reinterpret_cast<float*>(ws + 2 * align256(R * plan.S * 4));
+
+  if (plan.S > 0) {
+    const int G = pb.H / pb.H_kv;
+    const int gpb = gpb_for(pb.dtype);
+    static thread_local DecodeParams prm;  // ~29 KB; kept off the stack
+    rc = encode_q_map(pb, &prm.qmap);
+    if (rc != HALO_OK) return rc;
+    prm.q_pos = pb.q_pos;
+    prm.m_part = m_part;
+    prm.l_part = l_part;
+    prm.o_part = o_part;
+    prm.err = device_error_ptr();
+    prm.B = pb.B;
+    prm.H = pb.H;
+    prm.H_kv = pb.H_kv;
+    prm.G = G;
+    prm.gblocks = (G + gpb - 1) / gpb;
+    prm.S = plan.S;
+    prm.scale_log2 = pb.scale * kLog2e;
+    const int64_t pairs = (int64_t)pb.B * pb.H_kv * prm.gblocks;
+    // One launch unless the segment or item tables overflow the parameter block.
+    size_t i = 0;
+    while (i < plan.items.size()) {
+      int n_items = 0, n_seg = 0, last_seg = -1;
+      while (i + n_items < plan.items.size() && n_items < kMaxItems) {
+        const Item& it = plan.items[i + n_items];
+        if (it.seg != last_seg) {
+          if (n_seg == kMaxSegs) break;
+          const Seg& sg = plan.segs[it.seg];
+          rc = encode_view(sg.view.k, sg.view.len, pb.H_kv, pb.B, pb.D, pb.dtype,
+                           sg.view.k_stride_b, sg.view.k_stride_h, sg.view.k_stride_t,
+                           &prm.maps[2 * n_seg]);
+          if (rc == HALO_OK)
+            rc = encode_view(sg.view.v, sg.view.len, pb.H_kv, pb.B, pb.Dv, pb.dtype,
+                             sg.view.v_stride_b, sg.view.v_stride_h, sg.view.v_stride_t,
+                             &prm.maps[2 * n_seg + 1]);
+          if (rc != HALO_OK) return rc;
+          last_seg = it.seg;
+          ++n_seg;
+        }
+        Item li = it;
+        li.seg = n_seg - 1;
+        prm.items[n_items] = li;
+        ++n_items;
+      }
+      prm.n_items = n_items;
+      prm.n_units = (int32_t)(pairs * n_items);
+      rc = dispatch_kd(pb.dtype, pb.D, prm, st);
+      if (rc != HALO_OK) return rc;
+      i += n_items;
+    }
+  }
+  MergeParams mp = merge_params(merge, pb.B, pb.H, pb.Dv, plan.S, m_part, l_part, o_part);
+  return launch_merge(mp, st);
+}
+
+extern "C" int32_t halo_lse_merge(int32_t B, int32_t H, int32_t Dv, int32_t P,
+                                  const float* m_parts, const float* l_parts,
+                                  const float* o_parts, const halo_merge_args_t* merge,
+                                  halo_stream_t stream) {
+  if (B <= 0 || H <= 0 || Dv <= 0 || P < 0) return fail(HALO_ERR_INVALID_ARG, "bad merge shape");
+  if (P > 0 && (!m_parts || !l_parts || !o_parts))
+    return fail(HALO_ERR_INVALID_ARG, "NULL partial arrays");
+  if (Dv % 4 != 0 && Dv != 32 && Dv != 64)
+    return fail(HALO_ERR_UNSUPPORTED, "Dv %d must be a multiple of 4", Dv);
+  int rc = validate_merge(merge, Dv);
+  if (rc != HALO_OK) return rc;
+  if (Dv != 32 && Dv != 64 && Dv != 128 && (Dv > 256 || Dv % 8 != 0))
+    return fail(HALO_ERR_UNSUPPORTED, "Dv %d unsupported", Dv);
+  MergeParams mp = merge_params(merge, B, H, Dv, P, m_parts, l_parts, o_parts);
+  return launch_merge(mp, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" const char* halo_last_error_string(void) { return halo::t_last_error.c_str(); }
+
+extern "C" int32_t halo_device_error(int32_t* code_out, int32_t clear) {
+  unsigned int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, halo::g_device_error, sizeof(v));
+  if (e != cudaSuccess) return halo::cuda_fail(e, "read device error word");
+  if (clear) {
+    const unsigned int z = 0;
+    e = cudaMemcpyToSymbol(halo::g_device_error, &z, sizeof(z));
+    if (e != cudaSuccess) return halo::cuda_fail(e, "clear device error word");
+  }
+  if (code_out) *code_out = v ? -static_cast<int32_t>(v) : 0;
+  return HALO_OK;
+}
+
+extern "C" int32_t halo_version(void) { return 100; }

@@ -1,0 +1,277 @@
+"""Tensor-level entry points over the C-ABI (``include/halo_b200.h``).
+
+Every function here launches sm_100a kernels from ``libhalo_sm100.so`` on the
+current CUDA stream; there is no CPU path.  Tensors follow the reference's
+layouts: queries ``(B, H, D)`` / ``(B, H, T_q, D)`` and K/V chunks
+``(B, H_kv, T_c, D)`` with a contiguous last dimension.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+from typing import Optional, Sequence
+
+import torch
+
+from halo_b200 import _lib as L
+
+
+class _Workspaces:
+    """Grow-only device scratch per (device, stream); stream-ordered reuse."""
+
+    def __init__(self):
+        self._bufs: dict = {}
+
+    def get(self, device: torch.device, nbytes: int) -> torch.Tensor:
+        key = (device.index, torch.cuda.current_stream(device).cuda_stream)
+        buf = self._bufs.get(key)
+        if buf is None or buf.numel() < nbytes:
+            buf = torch.empty(max(nbytes, 1 << 16), dtype=torch.uint8, device=device)
+            self._bufs[key] = buf
+        return buf
+
+
+WORKSPACES = _Workspaces()
+
+
+def _require_cuda(t: torch.Tensor, name: str) -> None:
+    if not t.is_cuda:
+        raise L.HaloError(f"{name} must be a CUDA tensor (no CPU path)", L.HALO_ERR_INVALID_ARG)
+
+
+def _last_contig(t: torch.Tensor) -> torch.Tensor:
+    return t if t.stride(-1) == 1 else t.contiguous()
+
+
+def make_chunk(k: torch.Tensor, v: torch.Tensor, start: int, causal: bool,
+               *, batch_stride_zero: bool = False) -> tuple:
+    """Describe one ``(B, H_kv, T_c, D)`` chunk for the C-ABI; returns the
+    struct plus the tensors it points into (keep them alive)."""
+    k = _last_contig(k)
+    v = _last_contig(v)
+    c = L.KVChunk()
+    c.k = k.data_ptr() if k.numel() else None
+    c.v = v.data_ptr() if v.numel() else None
+    c.k_stride_b = 0 if batch_stride_zero else k.stride(0)
+    c.k_stride_h, c.k_stride_t = k.stride(1), k.stride(2)
+    c.v_stride_b = 0 if batch_stride_zero else v.stride(0)
+    c.v_stride_h, c.v_stride_t = v.stride(1), v.stride(2)
+    c.start = int(start)
+    c.len = int(k.shape[2]) if k.numel() else 0
+    c.causal = int(bool(causal))
+    return c, (k, v)
+
+
+def _problem(q3: torch.Tensor, H_kv: int, D_v: int, q_pos: Optional[torch.Tensor], scale: float,
+             max_split_rows: int = 0) -> L.DecodeProblem:
+    p = L.DecodeProblem()
+    p.B, p.H, p.D = q3.shape
+    p.H_kv = H_kv
+    p.Dv = D_v
+    p.dtype = L.halo_dtype(q3.dtype)
+    p.q = q3.data_ptr()
+    p.q_stride_b, p.q_stride_h = q3.stride(0), q3.stride(1)
+    p.q_pos = q_pos.data_ptr() if q_pos is not None else None
+    p.scale = float(scale)
+    p.max_split_rows = int(max_split_rows)
+    return p
+
+
+def decode_raw(q3: torch.Tensor, chunk_structs: Sequence[L.KVChunk], H_kv: int, D_v: int, *,
+               scale: float, q_pos: Optional[torch.Tensor], merge: L.MergeArgs,
+               max_split_rows: int = 0) -> None:
+    """Launch split-KV decode + merge for prepared chunk structs."""
+    dev = q3.device
+    prob = _problem(q3, H_kv, D_v, q_pos, scale, max_split_rows)
+    n = len(chunk_structs)
+    arr = (L.KVChunk * max(n, 1))(*chunk_structs)
+    lib = L.lib()
+    need = lib.halo_decode_workspace_bytes(ctypes.byref(prob), arr, n)
+    if need < 0:
+        L.check(int(need), "halo_decode_workspace_bytes")
+    ws = WORKSPACES.get(dev, int(need))
+    with torch.cuda.device(dev):
+        rc = lib.halo_chunked_decode(ctypes.byref(prob), arr, n, ws.data_ptr(), ws.numel(),
+                                     ctypes.byref(merge), L.stream_handle(dev))
+    L.check(rc, "halo_chunked_decode")
+
+
+class ChunkTable:
+    """A chunk list described once for repeated decode calls.
+
+    Holds the C-ABI chunk array and references to the tensors it points
+    into.  Reuse it while the chunks' storage and layout stay unchanged (the
+    steady state of a decode loop); the library additionally memoises the
+    tensor maps and the split plan for a layout it has seen.
+    """
+
+    def __init__(self, chunks: Sequence[tuple], *, batch_stride_zero: bool = False,
+                 batch: Optional[slice] = None):
+        structs, keep = [], []
+        self.H_kv = self.D_v = None
+        self.total_rows = 0
+        self.any_causal = False
+        for (k, v, start, causal) in chunks:
+            _require_cuda(k, "k")
+            _require_cuda(v, "v")
+            if batch is not None:
+                k, v = k[batch], v[batch]
+            if self.H_kv is None:
+                self.H_kv, self.D_v = int(k.shape[1]), int(v.shape[-1])
+            st, t = make_chunk(k, v, start, causal, batch_stride_zero=batch_stride_zero)
+            structs.append(st)
+            keep.append(t)
+            self.total_rows += int(k.shape[-2])
+            self.any_causal |= bool(causal)
+        self.n = len(structs)
+        self.arr = (L.KVChunk * max(self.n, 1))(*structs)
+        self._keep = keep
+
+
+def _decode_table(q3: torch.Tensor, table: ChunkTable, *, scale: float,
+                  q_pos: Optional[torch.Tensor], merge: L.MergeArgs, max_split_rows: int = 0):
+    dev = q3.device
+    H_kv = table.H_kv if table.H_kv is not None else q3.shape[1]
+    D_v = table.D_v if table.D_v is not None else q3.shape[2]
+    prob = _problem(q3, H_kv, D_v, q_pos, scale, max_split_rows)
+    lib = L.lib()
+    need = lib.halo_decode_workspace_bytes(ctypes.byref(prob), table.arr, table.n)
+    if need < 0:
+        L.check(int(need), "halo_decode_workspace_bytes")
+    ws = WORKSPACES.get(dev, int(need))
+    with torch.cuda.device(dev):
+        rc = lib.halo_chunked_decode(ctypes.byref(prob), table.arr, table.n, ws.data_ptr(),
+                                     ws.numel(), ctypes.byref(merge), L.stream_handle(dev))
+    L.check(rc, "halo_chunked_decode")
+
+
+def chunked_decode(q: torch.Tensor, chunks, *, scale: Optional[float] = None,
+                   q_pos: Optional[torch.Tensor] = None, out_dtype: Optional[torch.dtype] = None,
+                   out: Optional[torch.Tensor] = None, lse: Optional[torch.Tensor] = None,
+                   prior: Optional[tuple] = None, max_split_rows: int = 0):
+    """Attention of one decode query over ``chunks`` -- a list of
+    ``(k, v, start, causal)`` tuples or a prepared :class:`ChunkTable` --
+    merged with log-sum-exp.  Returns ``(out (B, H, D_v), lse (B, H))``.
+
+    ``prior = (m, l, o)`` folds a running fp32 state in first.  ``q_pos``
+    (device int64 ``(B,)``) defaults to ``total_T - 1`` as in
+    ``halo/triton_chunked.py:250-253`` (reference path relative to the
+    lzbaclz/HALO root).
+    """
+    q3 = q.squeeze(2) if q.dim() == 4 else q
+    _require_cuda(q3, "q")
+    q3 = q3 if q3.is_contiguous() else q3.contiguous()
+    B, H, D = q3.shape
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    table = chunks if isinstance(chunks, ChunkTable) else ChunkTable(chunks)
+    D_v = table.D_v if table.D_v is not None else D
+    if q_pos is None and table.any_causal:
+        q_pos = torch.full((B,), table.total_rows - 1, dtype=torch.int64, device=q3.device)
+    elif q_pos is not None and (q_pos.dtype != torch.int64 or q_pos.device != q3.device):
+        q_pos = q_pos.to(device=q3.device, dtype=torch.int64).contiguous()
+    if out is None:
+        out = torch.empty(B, H, D_v, dtype=out_dtype or q3.dtype, device=q3.device)
+    if lse is None:
+        lse = torch.empty(B, H, dtype=torch.float32, device=q3.device)
+    mg = L.MergeArgs()
+    mg.mode = L.MERGE_FINALIZE
+    mg.out_dtype = L.halo_dtype(out.dtype)
+    mg.out = out.data_ptr()
+    mg.out_stride_b, mg.out_stride_h = out.stride(0), out.stride(1)
+    mg.lse = lse.data_ptr()
+    if prior is not None:
+        m, l, o = prior
+        mg.m, mg.l, mg.o = m.data_ptr(), l.data_ptr(), o.data_ptr()
+    _decode_table(q3, table, scale=scale, q_pos=q_pos, merge=mg, max_split_rows=max_split_rows)
+    return out, lse
+
+
+def accumulate_decode(q: torch.Tensor, chunks: Sequence[tuple], m: torch.Tensor, l: torch.Tensor,
+                      o: torch.Tensor, *, scale: float, q_pos: Optional[torch.Tensor]) -> None:
+    """Fold ``chunks`` into running fp32 accumulators ``(m, l, o)`` in place
+    (the state ``update_chunk`` of ``halo/triton_chunked.py:151-192`` keeps)."""
+    q3 = _last_contig(q.squeeze(2) if q.dim() == 4 else q)
+    _require_cuda(q3, "q")
+    for t, name in ((m, "m"), (l, "l"), (o, "o")):
+        if t.dtype != torch.float32 or not t.is_contiguous():
+            raise L.HaloError(f"accumulator {name} must be contiguous fp32", L.HALO_ERR_INVALID_ARG)
+    structs, keep = [], []
+    H_kv, D_v = q3.shape[1], o.shape[-1]
+    for (k, v, start, causal) in chunks:
+        H_kv, D_v = int(k.shape[1]), int(v.shape[-1])
+        s, t = make_chunk(k, v, start, causal)
+        structs.append(s)
+        keep.append(t)
+    if q_pos is not None:
+        q_pos = q_pos.to(device=q3.device, dtype=torch.int64).contiguous()
+    mg = L.MergeArgs()
+    mg.mode = L.MERGE_ACCUMULATE
+    mg.m, mg.l, mg.o = m.data_ptr(), l.data_ptr(), o.data_ptr()
+    decode_raw(q3, structs, H_kv, D_v, scale=scale, q_pos=q_pos, merge=mg)
+
+
+def multi_query_attention(q: torch.Tensor, chunks: Sequence[tuple], *, scale: Optional[float] = None,
+                          query_pos_offset: int, out_dtype: Optional[torch.dtype] = None):
+    """``T_q > 1`` queries (a chunked-prefill slice) over causal chunks: query
+    row ``i`` sits at global position ``query_pos_offset + i``
+    (``halo/kv_cache_chunked.py:873-942``).  Each query row is one decode
+    problem whose K/V batch stride is zero, so every row reuses the same
+    chunk memory.  Returns ``(out (B, H, T_q, D_v), lse (B, H, T_q))``."""
+    _require_cuda(q, "q")
+    B, H, T_q, D = q.shape
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    D_v = int(chunks[0][1].shape[-1]) if chunks else D
+    H_kv = int(chunks[0][0].shape[1]) if chunks else H
+    out = torch.empty(B, H, T_q, D_v, dtype=out_dtype or q.dtype, device=q.device)
+    lse = torch.empty(B, H, T_q, dtype=torch.float32, device=q.device)
+    qp = torch.arange(T_q, dtype=torch.int64, device=q.device) + int(query_pos_offset)
+    for b in range(B):
+        qb = q[b].transpose(0, 1).contiguous()   # (T_q, H, D)
+        structs, keep = [], []
+        for (k, v, start, causal) in chunks:
+            s, t = make_chunk(k[b:b + 1], v[b:b + 1], start, causal, batch_stride_zero=True)
+            structs.append(s)
+            keep.append(t)
+        ob = out[b].transpose(0, 1)          # (T_q, H, D_v) view
+        lb = torch.empty(T_q, H, dtype=torch.float32, device=q.device)
+        mg = L.MergeArgs()
+        mg.mode = L.MERGE_FINALIZE
+        mg.out_dtype = L.halo_dtype(ob.dtype)
+        mg.out = ob.data_ptr()
+        mg.out_stride_b, mg.out_stride_h = ob.stride(0), ob.stride(1)
+        mg.lse = lb.data_ptr()
+        decode_raw(qb, structs, H_kv, D_v, scale=scale, q_pos=qp, merge=mg)
+        lse[b] = lb.transpose(0, 1)
+    return out, lse
+
+
+def lse_merge(m_parts: torch.Tensor, l_parts: torch.Tensor, o_parts: torch.Tensor, *,
+              out_dtype: torch.dtype = torch.float32, out: Optional[torch.Tensor] = None,
+              lse: Optional[torch.Tensor] = None):
+    """Merge ``P`` partial states ``m/l (B, H, P)``, ``o (B, H, P, D_v)`` (fp32,
+    contiguous) into ``(out (B, H, D_v), lse (B, H))``; the P-way form of
+    ``halo/kv_cache_chunked.py:194-239``."""
+    B, H, P = m_parts.shape
+    D_v = o_parts.shape[-1]
+    for t in (m_parts, l_parts, o_parts):
+        _require_cuda(t, "partial")
+        if t.dtype != torch.float32 or not t.is_contiguous():
+            raise L.HaloError("partials must be contiguous fp32", L.HALO_ERR_INVALID_ARG)
+    dev = m_parts.device
+    if out is None:
+        out = torch.empty(B, H, D_v, dtype=out_dtype, device=dev)
+    if lse is None:
+        lse = torch.empty(B, H, dtype=torch.float32, device=dev)
+    mg = L.MergeArgs()
+    mg.mode = L.MERGE_FINALIZE
+    mg.out_dtype = L.halo_dtype(out.dtype)
+    mg.out = out.data_ptr()
+    mg.out_stride_b, mg.out_stride_h = out.stride(0), out.stride(1)
+    mg.lse = lse.data_ptr()
+    with torch.cuda.device(dev):
+        rc = L.lib().halo_lse_merge(B, H, D_v, P, m_parts.data_ptr(), l_parts.data_ptr(),
+                                    o_parts.data_ptr(), ctypes.byref(mg), L.stream_handle(dev))
+    L.check(rc, "halo_lse_merge")
+    return out, lse

@@ -1,0 +1,143 @@
+/*
+ * halo_b200.h -- C ABI of libhalo_sm100.so, the B200 (sm_100a) kernels of
+ * HALO's chunked-attention hot path.
+ *
+ * Conventions
+ *  - Every entry point returns 0 (HALO_OK) or a negative HALO_ERR_* code;
+ *    halo_last_error_string() describes the last failure of the calling
+ *    thread.
+ *  - Pointers marked "device" are CUDA device pointers; strides are in
+ *    ELEMENTS; the innermost (head_dim) dimension is always contiguous.
+ *  - All work is enqueued on the given stream; nothing synchronises the host.
+ *  - The library allocates no device memory: callers pass workspaces sized by
+ *    the matching *_workspace_bytes() query.
+ *  - Kernels never wait without a limit: a wait that exceeds ~2 s records
+ *    HALO_ERR_TIMEOUT in the per-device error word (halo_device_error) and
+ *    the kernel returns.
+ *
+ * Reference interfaces replaced (paths relative to the lzbaclz/HALO root):
+ *  - halo/triton_chunked.py:47-138   _chunked_lse_merge_kernel (Triton)
+ *  - halo/triton_chunked.py:141-207  init_acc / update_chunk / finalize
+ *  - halo/kv_cache_chunked.py:194-276 _lse_merge / _chunk_attention
+ */
+#ifndef HALO_B200_H_
+#define HALO_B200_H_
+
+#include <stdint.h>
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------ status */
+#define HALO_OK 0
+#define HALO_ERR_INVALID_ARG (-1)   /* bad shape, null pointer, bad enum     */
+#define HALO_ERR_UNSUPPORTED (-2)   /* valid but not implemented (e.g. D)    */
+#define HALO_ERR_MISALIGNED (-3)    /* pointer/stride not 16-byte aligned    */
+#define HALO_ERR_CUDA (-4)          /* a CUDA runtime call failed            */
+#define HALO_ERR_TIMEOUT (-5)       /* a device-side bounded wait expired    */
+#define HALO_ERR_WORKSPACE (-6)     /* workspace missing or too small        */
+
+/* ------------------------------------------------------------------ dtypes */
+#define HALO_DTYPE_F32 0
+#define HALO_DTYPE_BF16 1
+#define HALO_DTYPE_F16 2
+
+/* Opaque CUDA stream (cudaStream_t); 0 = legacy default stream. */
+typedef void* halo_stream_t;
+
+/* One KV chunk: element (b, h, t, d) of K lives at
+ *   k + b*k_stride_b + h*k_stride_h + t*k_stride_t + d      (elements)
+ * and likewise for V.  `start` is the global position of row t = 0; when
+ * `causal` is nonzero, key t is visible to batch row b iff
+ * start + t <= q_pos[b].  Mirrors one (k, v, chunk_start, apply_causal)
+ * tuple of triton_chunked_attention (halo/triton_chunked.py:210-267). */
+typedef struct halo_kv_chunk {
+  const void* k;
+  const void* v;
+  int64_t k_stride_b, k_stride_h, k_stride_t;
+  int64_t v_stride_b, v_stride_h, v_stride_t;
+  int64_t start;
+  int32_t len;
+  int32_t causal;
+} halo_kv_chunk_t;
+
+/* The decode query and its shape.  q is (B, H, D) with strides
+ * (q_stride_b, q_stride_h, 1).  Query head h reads KV head h / (H / H_kv)
+ * (GQA, halo/triton_chunked.py:73).  q_pos is a device int64 (B,) array of
+ * global query positions, required when any chunk is causal. */
+typedef struct halo_decode_problem {
+  int32_t B, H, H_kv, D, Dv;
+  int32_t dtype;               /* HALO_DTYPE_* of q, k and v */
+  const void* q;
+  int64_t q_stride_b, q_stride_h;
+  const int64_t* q_pos;
+  float scale;                 /* softmax scale, e.g. 1/sqrt(D) */
+  int32_t max_split_rows;      /* 0 = automatic split size */
+} halo_decode_problem_t;
+
+/* Where the merged result goes.
+ * mode HALO_MERGE_FINALIZE: out (B, H, Dv) in out_dtype with strides
+ *   (out_stride_b, out_stride_h, 1) gets softmax(qk) @ v (zeros where no key
+ *   is visible, halo/triton_chunked.py:195-207); lse (B, H) fp32 contiguous,
+ *   optional, gets the natural-log log-sum-exp (-inf where no key is visible).
+ *   If m/l/o are non-NULL they are folded in first as a prior running state.
+ * mode HALO_MERGE_ACCUMULATE: the running fp32 accumulators m (B, H),
+ *   l (B, H), o (B, H, Dv) (contiguous) of halo/triton_chunked.py:141-148 are
+ *   updated in place: m = running max score, l = sum exp(s - m),
+ *   o = sum exp(s - m) v, exactly the state update_chunk maintains. */
+#define HALO_MERGE_FINALIZE 0
+#define HALO_MERGE_ACCUMULATE 1
+typedef struct halo_merge_args {
+  int32_t mode;
+  int32_t out_dtype;
+  void* out;
+  int64_t out_stride_b, out_stride_h;
+  float* lse;
+  float* m;
+  float* l;
+  float* o;
+} halo_merge_args_t;
+
+/* ------------------------------------------------------------------ decode */
+
+/* Bytes of device workspace halo_chunked_decode needs for this problem and
+ * chunk list (partial (m, l, o) per split).  Returns < 0 on invalid input. */
+int64_t halo_decode_workspace_bytes(const halo_decode_problem_t* problem,
+                                    const halo_kv_chunk_t* chunks, int32_t n_chunks);
+
+/* Split-KV chunked decode attention with a fused log-sum-exp merge.
+ * Replaces the per-chunk Triton launches of update_chunk
+ * (halo/triton_chunked.py:151-192, kernel :47-138) and the torch loop of
+ * _chunk_attention + _lse_merge (halo/kv_cache_chunked.py:194-276) with one
+ * split-KV launch over every chunk plus one merge launch.  `chunks` is a
+ * HOST array; K/V rows are staged through the async-copy engine, so every
+ * row address must be 16-byte aligned. */
+int32_t halo_chunked_decode(const halo_decode_problem_t* problem,
+                            const halo_kv_chunk_t* chunks, int32_t n_chunks,
+                            void* workspace, int64_t workspace_bytes,
+                            const halo_merge_args_t* merge, halo_stream_t stream);
+
+/* Merge P partial states laid out as m[R][P], l[R][P] (fp32) and
+ * o[R][P][Dv] (fp32) into R rows, with the semantics of `merge` (rows are
+ * (b, h) pairs, R = B*H).  This is the LSE merge of
+ * halo/kv_cache_chunked.py:194-239 generalised to P parts; also the merge
+ * step of the sequence-sharded decode (parts gathered from several GPUs). */
+int32_t halo_lse_merge(int32_t B, int32_t H, int32_t Dv, int32_t P,
+                       const float* m_parts, const float* l_parts, const float* o_parts,
+                       const halo_merge_args_t* merge, halo_stream_t stream);
+
+/* ------------------------------------------------------------------ misc */
+const char* halo_last_error_string(void);
+/* Read (and optionally clear) the device error word of the current device.
+ * Synchronises the current device. */
+int32_t halo_device_error(int32_t* code_out, int32_t clear);
+/* ABI version: major*10000 + minor*100 + patch. */
+int32_t halo_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* HALO_B200_H_ */

@@ -1,0 +1,257 @@
+"""GPU parity: split-KV decode + LSE merge (sm_100a) vs the CPU oracle and the
+reference's golden vectors.
+
+Tolerances: attention output within 2e-3 max-abs of the
+fp32 reference for 16-bit inputs (compared on the fp32 output, before any
+rounding to the storage dtype), LSE within 1e-4; fp32 inputs within 1e-5.
+"""
+from __future__ import annotations
+
+import math
+import random
+
+import numpy as np
+import pytest
+import torch
+
+import inputs as I
+from oracle import attention as OA
+
+pytestmark = pytest.mark.gpu
+
+OUT_TOL_16 = 2e-3
+LSE_TOL = 1e-4
+OUT_TOL_32 = 1e-5
+
+
+def _tol(dtype):
+    return OUT_TOL_32 if dtype == torch.float32 else OUT_TOL_16
+
+
+def _ops():
+    from halo_b200 import ops
+    return ops
+
+
+def _gpu_chunks(k, v, bounds, causal=False, dev="cuda"):
+    kd, vd = k.to(dev), v.to(dev)
+    return [(kd[..., a:b, :], vd[..., a:b, :], a, causal) for a, b in bounds]
+
+
+def _bounds(T, chunk):
+    return [(c0, min(c0 + chunk, T)) for c0 in range(0, T, chunk)]
+
+
+@pytest.mark.parametrize("name", list(I.WALK_CASES))
+def test_decode_matches_reference_golden(cuda_device, name):
+    ops = _ops()
+    (q, k, v), chunk = I.walk_inputs(name)
+    g = I.load("attention.npz")[name]
+    chunks = _gpu_chunks(k, v, _bounds(k.shape[-2], chunk))
+    out, lse = ops.chunked_decode(q.to(cuda_device), chunks, out_dtype=torch.float32)
+    ref_o = torch.from_numpy(g["out"])[:, :, 0]
+    ref_l = torch.from_numpy(g["lse"])[:, :, 0]
+    assert (out.cpu() - ref_o).abs().max().item() <= _tol(q.dtype)
+    assert (lse.cpu() - ref_l).abs().max().item() <= LSE_TOL
+    # output in q.dtype equals the fp32 result rounded once
+    out_q, _ = ops.chunked_decode(q.to(cuda_device), chunks)
+    assert out_q.dtype == q.dtype
+    torch.testing.assert_close(out_q.float(), out.to(q.dtype).float(), rtol=0, atol=0)
+
+
+def test_decode_config1_full(cuda_device):
+    """BASELINE config 1 (fp32, B1, H32/8, D128, T8192, 16 x 512, hot {0,13,14,15})."""
+    ops = _ops()
+    g = I.load("config1.npz")["config1"]
+    q, k, v = I.config1_inputs()
+    order = [int(c) for c in g["order"]]
+    chunks = _gpu_chunks(k, v, [(c * 512, (c + 1) * 512) for c in order])
+    out, lse = ops.chunked_decode(q.to(cuda_device), chunks)
+    assert (out.cpu() - torch.from_numpy(g["out"])).abs().max().item() <= OUT_TOL_32 * 10
+    assert (lse.cpu() - torch.from_numpy(g["lse"])).abs().max().item() <= LSE_TOL
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("chunk_size", [128, 512])
+def test_decode_small_gqa(cuda_device, dtype, chunk_size):
+    """Mirrors the reference Triton test (1K cache, GQA 4:1, D 64) with the
+    reference's relative-L2 bounds, plus the absolute/LSE bounds."""
+    ops = _ops()
+    torch.manual_seed(0)
+    B, H, H_kv, D, T = 1, 8, 2, 64, 1024
+    q = (torch.randn(B, H, 1, D) * 0.1).to(dtype)
+    k = (torch.randn(B, H_kv, T, D) * 0.1).to(dtype)
+    v = (torch.randn(B, H_kv, T, D) * 0.1).to(dtype)
+    ref_o, ref_l = OA.full_attention_f64(q, k, v, q_pos=T - 1)
+    chunks = _gpu_chunks(k, v, _bounds(T, chunk_size), causal=True)
+    qp = torch.tensor([T - 1], device=cuda_device)
+    out, lse = ops.chunked_decode(q.to(cuda_device), chunks, q_pos=qp, out_dtype=torch.float32)
+    rel = ((out.cpu().double() - ref_o[:, :, 0]).norm() / ref_o.norm()).item()
+    assert rel <= (1e-4 if dtype == torch.float32 else 5e-3)
+    assert (out.cpu().double() - ref_o[:, :, 0]).abs().max().item() <= _tol(dtype)
+    assert (lse.cpu().double() - ref_l[:, :, 0]).abs().max().item() <= LSE_TOL
+
+
+@pytest.mark.parametrize("chunk_size", [256, 512])
+def test_decode_causal_mask_and_truncation(cuda_device, chunk_size):
+    ops = _ops()
+    torch.manual_seed(1)
+    B, H, H_kv, D, T = 1, 4, 1, 64, 2048
+    q = torch.randn(B, H, 1, D) * 0.1
+    k = torch.randn(B, H_kv, T, D) * 0.1
+    v = torch.randn(B, H_kv, T, D) * 0.1
+    qp = torch.tensor([T // 2], device=cuda_device)
+    ref_o, _ = OA.full_attention_f64(q, k, v, q_pos=T // 2)
+    out, _ = ops.chunked_decode(q.to(cuda_device), _gpu_chunks(k, v, _bounds(T, chunk_size), True),
+                                q_pos=qp)
+    assert ((out.cpu().double() - ref_o[:, :, 0]).norm() / ref_o.norm()).item() <= 1e-4
+    half, _ = ops.chunked_decode(q.to(cuda_device), _gpu_chunks(k, v, [(0, T // 2 + 1)], True),
+                                 q_pos=qp)
+    assert ((out - half).norm() / out.norm()).item() <= 1e-5
+
+
+def test_decode_noncontiguous_partition_and_permutation(cuda_device):
+    ops = _ops()
+    torch.manual_seed(4)
+    B, H, H_kv, D, T = 1, 8, 2, 64, 2048
+    q = torch.randn(B, H, 1, D) * 0.1
+    k = torch.randn(B, H_kv, T, D) * 0.1
+    v = torch.randn(B, H_kv, T, D) * 0.1
+    intervals = [(0, 256), (768, 1024), (1280, 1408), (1536, 1664), (1856, 2048)]
+    keep = torch.zeros(T, dtype=torch.bool)
+    for a, b in intervals:
+        keep[a:b] = True
+    ref_o, ref_l = OA.full_attention_f64(q, k, v, q_pos=T - 1, keep=keep)
+    qp = torch.tensor([T - 1], device=cuda_device)
+    chunks = _gpu_chunks(k, v, intervals, True)
+    out, lse = ops.chunked_decode(q.to(cuda_device), chunks, q_pos=qp)
+    assert ((out.cpu().double() - ref_o[:, :, 0]).norm() / ref_o.norm()).item() <= 1e-4
+    random.seed(0)
+    perm = chunks.copy()
+    random.shuffle(perm)
+    out_p, lse_p = ops.chunked_decode(q.to(cuda_device), perm, q_pos=qp)
+    assert ((out_p.cpu().double() - ref_o[:, :, 0]).norm() / ref_o.norm()).item() <= 1e-4
+    assert (lse_p - lse).abs().max().item() <= 1e-5
+
+
+def test_decode_per_batch_q_pos_and_fully_masked_rows(cuda_device):
+    """Per-row causal positions, including a row that sees no key at all
+    (output zeros, lse -inf, like finalize's safe divide)."""
+    ops = _ops()
+    torch.manual_seed(5)
+    B, H, H_kv, D, T = 3, 8, 2, 128, 700
+    q = torch.randn(B, H, 1, D).bfloat16()
+    k = torch.randn(B, H_kv, T, D).bfloat16()
+    v = torch.randn(B, H_kv, T, D).bfloat16()
+    qpos = [T - 1, 333, -1]
+    chunks = _gpu_chunks(k, v, [(100, T)], True)   # keys start at 100 -> row 2 sees nothing
+    out, lse = ops.chunked_decode(q.to(cuda_device), chunks,
+                                  q_pos=torch.tensor(qpos, device=cuda_device),
+                                  out_dtype=torch.float32)
+    for b in range(2):
+        keep = torch.zeros(T, dtype=torch.bool)
+        keep[100:] = True
+        ro, rl = OA.full_attention_f64(q[b:b + 1], k[b:b + 1], v[b:b + 1], q_pos=qpos[b], keep=keep)
+        assert (out[b].cpu().double() - ro[0, :, 0]).abs().max().item() <= OUT_TOL_16
+        assert (lse[b].cpu().double() - rl[0, :, 0]).abs().max().item() <= LSE_TOL
+    assert torch.all(out[2] == 0)
+    assert torch.all(torch.isneginf(lse[2]))
+
+
+def test_decode_empty_inputs(cuda_device):
+    ops = _ops()
+    q = torch.randn(2, 4, 1, 64, device=cuda_device, dtype=torch.bfloat16)
+    out, lse = ops.chunked_decode(q, [])
+    assert torch.all(out == 0) and torch.all(torch.isneginf(lse))
+    k = torch.empty(2, 2, 0, 64, device=cuda_device, dtype=torch.bfloat16)
+    out, lse = ops.chunked_decode(q, [(k, k, 0, True)])
+    assert torch.all(out == 0) and torch.all(torch.isneginf(lse))
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_accumulate_matches_triton_state(cuda_device, dtype):
+    """ACCUMULATE mode keeps the (m, l, o) state of halo/triton_chunked.py."""
+    ops = _ops()
+    (q, k, v), chunk = I.walk_inputs("walk_f32_gqa4")
+    q, k, v = q.to(dtype), k.to(dtype), v.to(dtype)
+    bounds = _bounds(k.shape[-2], chunk)
+    qp = torch.full((q.shape[0],), 150, device=cuda_device)
+    B, H, D = q.shape[0], q.shape[1], q.shape[-1]
+    m = torch.full((B, H), float("-inf"), device=cuda_device)
+    l = torch.zeros(B, H, device=cuda_device)
+    o = torch.zeros(B, H, D, device=cuda_device)
+    for a, b in bounds:
+        ops.accumulate_decode(q.to(cuda_device), _gpu_chunks(k, v, [(a, b)], True), m, l, o,
+                              scale=1 / math.sqrt(D), q_pos=qp)
+    rm, rl, ro = OA.acc_state_from_chunks(q, [(k[..., a:b, :], v[..., a:b, :], a, True)
+                                              for a, b in bounds], q_pos=150)
+    assert (m.cpu() - rm[..., 0]).abs().max().item() <= 1e-5
+    finite = torch.isfinite(rm[..., 0])
+    torch.testing.assert_close((o / l.unsqueeze(-1)).cpu()[finite],
+                               (ro / rl.unsqueeze(-1))[..., 0, :][finite],
+                               atol=_tol(dtype), rtol=0)
+
+
+@pytest.mark.parametrize("name", list(I.PREFILL_CASES))
+def test_multi_query_causal_matches_reference(cuda_device, name):
+    ops = _ops()
+    (q, k, v), T_cold, chunk = I.prefill_inputs(name)
+    g = I.load("attention.npz")[name]
+    T, T_q = k.shape[-2], q.shape[-2]
+    chunks = _gpu_chunks(k, v, _bounds(T, chunk), True)
+    out, lse = ops.multi_query_attention(q.to(cuda_device), chunks, query_pos_offset=T - T_q,
+                                         out_dtype=torch.float32)
+    assert (out.cpu() - torch.from_numpy(g["out"])).abs().max().item() <= _tol(q.dtype)
+    assert (lse.cpu() - torch.from_numpy(g["lse"])).abs().max().item() <= LSE_TOL
+
+
+def test_lse_merge_parts(cuda_device):
+    ops = _ops()
+    torch.manual_seed(9)
+    B, H, D, T = 2, 8, 128, 1500
+    q = torch.randn(B, H, 1, D)
+    k = torch.randn(B, 2, T, D)
+    v = torch.randn(B, 2, T, D)
+    parts = [(0, 400), (400, 401), (401, 1500)]
+    ms, ls, os_ = [], [], []
+    for a, b in parts:
+        m, l, o = OA.acc_state_from_chunks(q, [(k[..., a:b, :], v[..., a:b, :], a, False)])
+        ms.append(m[..., 0]); ls.append(l[..., 0]); os_.append(o[..., 0, :])
+    # a fully masked part contributes nothing
+    ms.append(torch.full((B, H), float("-inf"))); ls.append(torch.zeros(B, H)); os_.append(torch.zeros(B, H, D))
+    mp = torch.stack(ms, -1).contiguous().to(cuda_device)
+    lp = torch.stack(ls, -1).contiguous().to(cuda_device)
+    op = torch.stack(os_, -2).contiguous().to(cuda_device)
+    out, lse = ops.lse_merge(mp, lp, op)
+    ro, rl = OA.full_attention_f64(q, k, v)
+    assert (out.cpu().double() - ro[:, :, 0]).abs().max().item() <= 1e-5
+    assert (lse.cpu().double() - rl[:, :, 0]).abs().max().item() <= 1e-5
+
+
+def test_large_context_properties(cuda_device):
+    """Config-5-like context at reduced heads: chunk-order invariance and
+    linearity in V (attention is linear in V for fixed q, k)."""
+    ops = _ops()
+    torch.manual_seed(12)
+    B, H, H_kv, D, T, chunk = 1, 16, 2, 128, 131072, 4096
+    dev = cuda_device
+    q = torch.randn(B, H, 1, D, device=dev).bfloat16()
+    k = torch.randn(B, H_kv, T, D, device=dev).bfloat16()
+    v = torch.randn(B, H_kv, T, D, device=dev).bfloat16()
+    ch = [(k[..., a:b, :], v[..., a:b, :], a, False) for a, b in _bounds(T, chunk)]
+    o1, l1 = ops.chunked_decode(q, ch, out_dtype=torch.float32)
+    o2, l2 = ops.chunked_decode(q, ch[::-1], out_dtype=torch.float32)
+    assert (o1 - o2).abs().max().item() <= 1e-5 and (l1 - l2).abs().max().item() <= 1e-5
+    v2 = (v.float() * 2).bfloat16()     # exact doubling
+    ch2 = [(k[..., a:b, :], v2[..., a:b, :], a, False) for a, b in _bounds(T, chunk)]
+    o3, l3 = ops.chunked_decode(q, ch2, out_dtype=torch.float32)
+    assert (o3 - 2 * o1).abs().max().item() <= 1e-5 and torch.equal(l3, l1)
+    # spot-check one kv-head group against the fp64 oracle
+    ro, rl = OA.full_attention_f64(q[:, :8].cpu(), k[:, :1].cpu(), v[:, :1].cpu())
+    assert (o1[:, :8].cpu().double() - ro[:, :, 0]).abs().max().item() <= OUT_TOL_16
+    assert (l1[:, :8].cpu().double() - rl[:, :, 0]).abs().max().item() <= LSE_TOL
+
+
+def test_device_error_word_clear(cuda_device):
+    from halo_b200 import _lib as L
+    assert L.device_error(clear=True) == 0
