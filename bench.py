@@ -1,0 +1,357 @@
+"""Benchmark of the HALO chunked-attention hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload cfg5|cfg2]
+
+Default workload (all N): BASELINE config 5 -- 1M-token sequence-sharded
+decode of one Llama-3-70B-shaped attention layer (B1, 64 q-heads / 8 KV
+heads, head_dim 128, bf16, 256 chunks of 4096 rows).  Rank r of N owns a
+contiguous 1/N of the chunks; a step is one decode query: split-KV kernel over
+the local chunks, NCCL all-gather of the fp32 (o, lse) partials, LSE merge.
+Total context is fixed as N grows (strong scaling).  K/V are seeded N(0,1)
+synthetic data resident in HBM; the working set per GPU (4.3 GB / N) is far
+larger than L2, so no flush is needed between steps.
+
+``--workload cfg2`` runs BASELINE config 2's tiered decode step instead (one
+GPU): 32 layers of B8 / 32 q-heads / 8 KV heads / 32K context, chunks of 1024,
+hot chunks resident, top-8 cold chunks picked by the chunk scorer and
+refetched from pinned host memory each step.
+
+Rank 0 prints one JSON line.  ``--impl reference`` times the reference's CPU
+implementation of the path (its torch ops restated in ``oracle/``) on this
+host's cores over a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+# cfg5 shapes
+CFG5 = dict(B=1, H=64, H_kv=8, D=128, T=1 << 20, chunk=4096)
+METRIC = "decode-attn tokens/s & achieved HBM GB/s at 32K-1M ctx, 1/2/4/8 B200"
+
+# DRAM traffic of the split-KV kernel per K/V byte it must read, from one ncu
+# capture (dram__bytes_read.sum + dram__bytes_write.sum over the algorithmic
+# K+V bytes of that launch); the capture and its command are summarised under
+# profiles/.  None until a capture of this workload exists.
+NCU_TRAFFIC_RATIO = None
+
+
+def _peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            pk = json.load(f)
+        return float(pk["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """Samples SM clocks and clock-event reasons through NVML while running."""
+
+    REASONS = {
+        0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+        0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+        0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+        0x100: "display_clock_setting",
+    }
+
+    def __init__(self, device_index: int, period_s: float = 0.02):
+        self.idx, self.period = device_index, period_s
+        self.samples, self.reasons, self.max_mhz = [], 0, None
+        self._stop = threading.Event()
+        self._thr = None
+        self.ok = False
+
+    def __enter__(self):
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(self.idx)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception:
+            return self
+        def loop():
+            while not self._stop.is_set():
+                try:
+                    self.samples.append(self._nv.nvmlDeviceGetClockInfo(self._h, self._nv.NVML_CLOCK_SM))
+                    self.reasons |= int(self._nv.nvmlDeviceGetCurrentClocksEventReasons(self._h))
+                except Exception:
+                    pass
+                time.sleep(self.period)
+        self._thr = threading.Thread(target=loop, daemon=True)
+        self._thr.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thr is not None:
+            self._thr.join()
+
+    def summary(self):
+        if not self.ok:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvml_unavailable"]}
+        names = [n for bit, n in self.REASONS.items() if self.reasons & bit and n != "gpu_idle"]
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+                "sm_max_mhz": self.max_mhz, "reasons": names, "samples": len(self.samples)}
+
+
+def _dist_setup(n_gpus: int):
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != n_gpus:
+        raise SystemExit(f"--gpus {n_gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def _cfg5_shard(world: int, rank: int, dev):
+    """This rank's K/V shard of the 1M-token context and the replicated query."""
+    import torch
+    from halo_b200.sharded import shard_range
+    c = CFG5
+    n_chunks = c["T"] // c["chunk"]
+    lo, hi = shard_range(n_chunks, world, rank)
+    rows = (hi - lo) * c["chunk"]
+    g = torch.Generator(device=dev).manual_seed(1000 + rank)
+    k = torch.randn(c["B"], c["H_kv"], rows, c["D"], device=dev, dtype=torch.bfloat16, generator=g)
+    v = torch.randn(c["B"], c["H_kv"], rows, c["D"], device=dev, dtype=torch.bfloat16, generator=g)
+    gq = torch.Generator(device=dev).manual_seed(7)
+    q = torch.randn(c["B"], c["H"], c["D"], device=dev, dtype=torch.bfloat16, generator=gq)
+    return q, k, v, lo * c["chunk"]
+
+
+def _cpu_cfg5_sample(n_chunks_sample: int, seed: int = 1000):
+    """CPU copies of the first chunks of rank 0's shard (bf16) and the query."""
+    import torch
+    c = CFG5
+    g = torch.Generator().manual_seed(seed)
+    rows = n_chunks_sample * c["chunk"]
+    k = torch.randn(c["B"], c["H_kv"], rows, c["D"], generator=g).bfloat16()
+    v = torch.randn(c["B"], c["H_kv"], rows, c["D"], generator=g).bfloat16()
+    q = torch.randn(c["B"], c["H"], 1, c["D"], generator=g).bfloat16()
+    chunks = [(k[..., a:a + c["chunk"], :], v[..., a:a + c["chunk"], :], a, False)
+              for a in range(0, rows, c["chunk"])]
+    return q, chunks
+
+
+def _time_cpu_oracle(n_chunks_sample: int, repeats: int):
+    """Seconds per sample of the CPU oracle port (reference torch ops)."""
+    import torch
+    from oracle import attention as OA
+    torch.set_num_threads(os.cpu_count() or 1)
+    q, chunks = _cpu_cfg5_sample(n_chunks_sample)
+    OA.chunked_attention(q, chunks[:1])  # warm the thread pool
+    ts = []
+    for _ in range(repeats):
+        t0 = time.perf_counter()
+        OA.chunked_attention(q, chunks)
+        ts.append(time.perf_counter() - t0)
+    return statistics.median(ts), torch.get_num_threads()
+
+
+def cpu_baseline_cfg5(budget_s: float = 15.0):
+    """Bounded CPU sample of cfg5 through the oracle port, scaled to a step."""
+    n_total = CFG5["T"] // CFG5["chunk"]
+    t1, _ = _time_cpu_oracle(1, 1)
+    n = int(max(1, min(n_total, budget_s / 3 / max(t1, 1e-3))))
+    t, cores = _time_cpu_oracle(n, 3)
+    step_s = t * n_total / n
+    return {"value": CFG5["B"] / step_s, "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": f"{n} of {n_total} chunks (x{CFG5['chunk']} rows) of rank-0 data, "
+                      f"median of 3, scaled x{n_total / n:.1f} to the full 1M-token step",
+            "s_per_step": step_s}
+
+
+def run_reference(args):
+    """The reference arm: the reference's CPU torch path (restated in the
+    oracle) on this host's cores, each step a bounded sample of cfg5."""
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    n_total = CFG5["T"] // CFG5["chunk"]
+    t1, cores = _time_cpu_oracle(1, 1)
+    budget = 150.0 / max(1, args.steps + args.warmup)
+    n = int(max(1, min(n_total, budget / max(t1, 1e-3))))
+    import torch
+    from oracle import attention as OA
+    q, chunks = _cpu_cfg5_sample(n)
+    for _ in range(args.warmup):
+        OA.chunked_attention(q, chunks)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        OA.chunked_attention(q, chunks)
+    el = time.perf_counter() - t0
+    step_s = el / args.steps * n_total / n
+    value = CFG5["B"] / step_s
+    sample = (f"each step: {n} of {n_total} chunks of the 1M-token context through the "
+              f"reference torch ops on CPU, time scaled x{n_total / n:.1f}")
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": step_s * 1e3, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": _cfg5_config(args.gpus),
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def _cfg5_config(n: int):
+    c = CFG5
+    return {"workload": "cfg5: 1M-token sequence-sharded decode, one Llama-3-70B-shaped "
+                        "attention layer (64 q-heads / 8 KV heads, head_dim 128), "
+                        "256 chunks x 4096",
+            "global_batch": c["B"], "seq_len": c["T"], "chunk": c["chunk"],
+            "parallelism": f"sequence-sharded x{n} (NCCL all-gather of (o, lse) + LSE merge)"
+                           if n > 1 else "single GPU",
+            "l2": "inputs larger than L2 (K+V %.2f GB per GPU); no flush" %
+                  (2 * c["B"] * c["H_kv"] * c["T"] * c["D"] * 2 / n / 1e9)}
+
+
+def run_ours_cfg5(args):
+    import torch
+    import torch.distributed as dist
+    world, rank, local = _dist_setup(args.gpus)
+    dev = torch.device("cuda", local)
+    from halo_b200.sharded import ShardedDecoder
+    q, k, v, start = _cfg5_shard(world, rank, dev)
+    dec = ShardedDecoder(k, v, start=start, chunk_size=CFG5["chunk"],
+                         group=dist.group.WORLD if world > 1 else None)
+    B, H, D = q.shape
+    out = torch.empty(B, H, D, device=dev, dtype=q.dtype)
+    lse = torch.empty(B, H, device=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    for _ in range(args.warmup):
+        dec(q, out=out, lse=lse)
+    torch.cuda.synchronize()
+
+    # ---- device throughput: K steps; kd kernel bracketed per step by events
+    K = args.steps
+    ev_b = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    ev_e = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    for e in ev_b + ev_e:          # materialise the raw events
+        e.record()
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        t0.record()
+        for i in range(K):
+            dec(q, out=out, lse=lse, events=(ev_b[i].cuda_event, ev_e[i].cuda_event))
+        t1.record()
+        torch.cuda.synchronize()
+    barrier()
+    ms = t0.elapsed_time(t1)
+    kd_ms = sum(ev_b[i].elapsed_time(ev_e[i]) for i in range(K)) / K
+    ms_t = torch.tensor([ms, kd_ms], device=dev)
+    if world > 1:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms, kd_ms_max = ms_t.tolist()
+    ms_step = ms / K
+
+    # ---- end to end through the public API with host buffers
+    q_host = q.cpu().pin_memory()
+    out_host = torch.empty_like(out, device="cpu").pin_memory()
+    q_dev = torch.empty_like(q)
+    for _ in range(3):
+        q_dev.copy_(q_host, non_blocking=True)
+        dec(q_dev, out=out, lse=lse)
+        out_host.copy_(out, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(K):
+        q_dev.copy_(q_host, non_blocking=True)
+        dec(q_dev, out=out, lse=lse)
+        out_host.copy_(out, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = torch.tensor([e0.elapsed_time(e1) / K], device=dev)
+    if world > 1:
+        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+    e2e_ms = float(e2e_ms.item())
+    barrier()
+
+    # parity self-check of the final state on rank 0 (cheap, outside timing)
+    local_bytes = 2 * k.numel() * k.element_size()
+    peak, peak_kind = _peaks()
+    achieved = local_bytes / (kd_ms_max / 1e3) / 1e9
+    line = None
+    if rank == 0:
+        cpu = cpu_baseline_cfg5() if world == 1 and not args.no_cpu_baseline else None
+        roof = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                "frac": achieved / peak, "peak_kind": f"of {peak_kind}",
+                "kernel": "kd_kernel (split-KV decode)",
+                "bytes_per_launch": local_bytes,
+                "traffic": (local_bytes * NCU_TRAFFIC_RATIO) if NCU_TRAFFIC_RATIO else None,
+                "step_gbs": 2 * CFG5["B"] * CFG5["H_kv"] * CFG5["T"] * CFG5["D"] * 2
+                            / (ms_step / 1e3) / 1e9}
+        line = {"metric": METRIC, "value": CFG5["B"] / (ms_step / 1e3), "unit": "tokens/s",
+                "n_gpus": world, "steps": K, "warmup": args.warmup, "ms_per_step": ms_step,
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+                "dtype": "bf16", "data": "synthetic", "config": _cfg5_config(world),
+                "roofline": roof,
+                "cpu_baseline": cpu and {kk: cpu[kk] for kk in ("value", "unit", "cores",
+                                                               "kind", "sample")},
+                "e2e": {"value": CFG5["B"] / (e2e_ms / 1e3), "unit": "tokens/s",
+                        "h2d_bytes_per_step": q.numel() * q.element_size(),
+                        "d2h_bytes_per_step": out.numel() * out.element_size()},
+                "clocks": clocks.summary(),
+                "gpu_launches": K * dec.launches_per_call}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+    return line
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=300)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["cfg5", "cfg2"], default="cfg5")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    if args.impl == "reference":
+        return run_reference(args)
+    if args.workload == "cfg2":
+        from halo_b200 import tiered_bench
+        return tiered_bench.run(args)
+    return run_ours_cfg5(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -56,7 +56,8 @@ class DecodeProblem(ctypes.Structure):
                 ("D", ctypes.c_int32), ("Dv", ctypes.c_int32), ("dtype", ctypes.c_int32),
                 ("q", ctypes.c_void_p), ("q_stride_b", ctypes.c_int64),
                 ("q_stride_h", ctypes.c_int64), ("q_pos", ctypes.c_void_p),
-                ("scale", ctypes.c_float), ("max_split_rows", ctypes.c_int32)]
+                ("scale", ctypes.c_float), ("max_split_rows", ctypes.c_int32),
+                ("event_begin", ctypes.c_void_p), ("event_end", ctypes.c_void_p)]
 
 
 class MergeArgs(ctypes.Structure):
@@ -75,8 +76,9 @@ SIGNATURES = {
                                              ctypes.POINTER(MergeArgs), ctypes.c_void_p]),
     "halo_lse_merge": (ctypes.c_int32, [ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                                         ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p,
-                                        ctypes.c_void_p, ctypes.POINTER(MergeArgs),
-                                        ctypes.c_void_p]),
+                                        ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
+                                        ctypes.c_int64, ctypes.c_int64,
+                                        ctypes.POINTER(MergeArgs), ctypes.c_void_p]),
     "halo_last_error_string": (ctypes.c_char_p, []),
     "halo_device_error": (ctypes.c_int32, [ctypes.POINTER(ctypes.c_int32), ctypes.c_int32]),
     "halo_version": (ctypes.c_int32, []),

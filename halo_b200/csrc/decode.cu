@@ -510,8 +510,10 @@ __global__ void __launch_bounds__(kThreads, MINB) kd_kernel(const __grid_constan
 // ---------------------------------------------------------------- km kernel
 struct MergeParams {
   const float* m_parts;
-  const float* l_parts;
+  const float* l_parts;   // NULL: every part has l = 1
   const float* o_parts;
+  int64_t ps, rs;         // m/l: part stride, row stride (elements)
+  int64_t ops, ors;       // o: part stride, row stride (elements)
   int32_t R, H, P, Dv;
   int32_t mode, out_dtype;
   char* out;
@@ -535,14 +537,14 @@ __global__ void __launch_bounds__(kMergeWarps * 32) km_kernel(const MergeParams 
   __shared__ __align__(16) float s_o[kMergeWarps][DPL * 32];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = blockIdx.x;
-  const float* mr = mp.m_parts + (int64_t)row * mp.P;
-  const float* lr = mp.l_parts + (int64_t)row * mp.P;
-  const float* orow = mp.o_parts + (int64_t)row * mp.P * mp.Dv;
+  const float* mr = mp.m_parts + (int64_t)row * mp.rs;
+  const float* lr = mp.l_parts ? mp.l_parts + (int64_t)row * mp.rs : nullptr;
+  const float* orow = mp.o_parts + (int64_t)row * mp.ors;
   const bool have_prior = mp.m != nullptr;
 
   // ---- pass 1: row max
   float M = -INFINITY;
-  for (int s = threadIdx.x; s < mp.P; s += blockDim.x) M = fmaxf(M, mr[s]);
+  for (int s = threadIdx.x; s < mp.P; s += blockDim.x) M = fmaxf(M, mr[s * mp.ps]);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
   if (lane == 0) s_red[warp] = M;
@@ -565,10 +567,10 @@ __global__ void __launch_bounds__(kMergeWarps * 32) km_kernel(const MergeParams 
       float ov[4][DPL];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        ms[j] = mr[s + j * kMergeWarps];
-        ls[j] = lr[s + j * kMergeWarps];
+        ms[j] = mr[(int64_t)(s + j * kMergeWarps) * mp.ps];
+        ls[j] = lr ? lr[(int64_t)(s + j * kMergeWarps) * mp.ps] : 1.f;
         if (active) {
-          const float* src = orow + (int64_t)(s + j * kMergeWarps) * mp.Dv + d0;
+          const float* src = orow + (int64_t)(s + j * kMergeWarps) * mp.ops + d0;
 #pragma unroll
           for (int e = 0; e < DPL; ++e) ov[j][e] = src[e];
         }
@@ -583,12 +585,12 @@ __global__ void __launch_bounds__(kMergeWarps * 32) km_kernel(const MergeParams 
       }
     }
     for (; s < mp.P; s += kMergeWarps) {
-      const float ms = mr[s];
+      const float ms = mr[(int64_t)s * mp.ps];
       if (ms == -INFINITY) continue;
       const float w = expf(ms - M);
-      L = fmaf(lr[s], w, L);
+      L = fmaf(lr ? lr[(int64_t)s * mp.ps] : 1.f, w, L);
       if (active) {
-        const float* src = orow + (int64_t)s * mp.Dv + d0;
+        const float* src = orow + (int64_t)s * mp.ops + d0;
 #pragma unroll
         for (int e = 0; e < DPL; ++e) acc[e] = fmaf(src[e], w, acc[e]);
       }
@@ -844,11 +846,16 @@ int validate_merge(const halo_merge_args_t* mg, int Dv) {
 }
 
 MergeParams merge_params(const halo_merge_args_t* mg, int B, int H, int Dv, int P,
-                         const float* m_parts, const float* l_parts, const float* o_parts) {
+                         const float* m_parts, const float* l_parts, const float* o_parts,
+                         int64_t ps, int64_t rs, int64_t ops, int64_t ors) {
   MergeParams mp;
   mp.m_parts = m_parts;
   mp.l_parts = l_parts;
   mp.o_parts = o_parts;
+  mp.ps = ps;
+  mp.rs = rs;
+  mp.ops = ops;
+  mp.ors = ors;
   mp.R = B * H;
   mp.H = H;
   mp.P = P;
@@ -1141,6 +1148,10 @@ extern "C" int32_t halo_chunked_decode(const halo_decode_problem_t* problem,
     prm.S = plan.S;
     prm.scale_log2 = pb.scale * kLog2e;
     const int64_t pairs = (int64_t)pb.B * pb.H_kv * prm.gblocks;
+    if (pb.event_begin) {
+      cudaError_t e = cudaEventRecord(static_cast<cudaEvent_t>(pb.event_begin), st);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaEventRecord(event_begin)");
+    }
     // One launch unless the segment or item tables overflow the parameter block.
     size_t i = 0;
     while (i < plan.items.size()) {
@@ -1172,25 +1183,29 @@ extern "C" int32_t halo_chunked_decode(const halo_decode_problem_t* problem,
       if (rc != HALO_OK) return rc;
       i += n_items;
     }
+    if (pb.event_end) {
+      cudaError_t e = cudaEventRecord(static_cast<cudaEvent_t>(pb.event_end), st);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaEventRecord(event_end)");
+    }
   }
-  MergeParams mp = merge_params(merge, pb.B, pb.H, pb.Dv, plan.S, m_part, l_part, o_part);
+  MergeParams mp = merge_params(merge, pb.B, pb.H, pb.Dv, plan.S, m_part, l_part, o_part, 1,
+                                plan.S, pb.Dv, (int64_t)plan.S * pb.Dv);
   return launch_merge(mp, st);
 }
 
 extern "C" int32_t halo_lse_merge(int32_t B, int32_t H, int32_t Dv, int32_t P,
                                   const float* m_parts, const float* l_parts,
-                                  const float* o_parts, const halo_merge_args_t* merge,
-                                  halo_stream_t stream) {
+                                  const float* o_parts, int64_t part_stride, int64_t row_stride,
+                                  int64_t o_part_stride, int64_t o_row_stride,
+                                  const halo_merge_args_t* merge, halo_stream_t stream) {
   if (B <= 0 || H <= 0 || Dv <= 0 || P < 0) return fail(HALO_ERR_INVALID_ARG, "bad merge shape");
-  if (P > 0 && (!m_parts || !l_parts || !o_parts))
-    return fail(HALO_ERR_INVALID_ARG, "NULL partial arrays");
-  if (Dv % 4 != 0 && Dv != 32 && Dv != 64)
-    return fail(HALO_ERR_UNSUPPORTED, "Dv %d must be a multiple of 4", Dv);
-  int rc = validate_merge(merge, Dv);
-  if (rc != HALO_OK) return rc;
+  if (P > 0 && (!m_parts || !o_parts)) return fail(HALO_ERR_INVALID_ARG, "NULL partial arrays");
   if (Dv != 32 && Dv != 64 && Dv != 128 && (Dv > 256 || Dv % 8 != 0))
     return fail(HALO_ERR_UNSUPPORTED, "Dv %d unsupported", Dv);
-  MergeParams mp = merge_params(merge, B, H, Dv, P, m_parts, l_parts, o_parts);
+  int rc = validate_merge(merge, Dv);
+  if (rc != HALO_OK) return rc;
+  MergeParams mp = merge_params(merge, B, H, Dv, P, m_parts, l_parts, o_parts, part_stride,
+                                row_stride, o_part_stride, o_row_stride);
   return launch_merge(mp, static_cast<cudaStream_t>(stream));
 }
 

@@ -129,11 +129,14 @@ class ChunkTable:
 
 
 def _decode_table(q3: torch.Tensor, table: ChunkTable, *, scale: float,
-                  q_pos: Optional[torch.Tensor], merge: L.MergeArgs, max_split_rows: int = 0):
+                  q_pos: Optional[torch.Tensor], merge: L.MergeArgs, max_split_rows: int = 0,
+                  events: Optional[tuple] = None):
     dev = q3.device
     H_kv = table.H_kv if table.H_kv is not None else q3.shape[1]
     D_v = table.D_v if table.D_v is not None else q3.shape[2]
     prob = _problem(q3, H_kv, D_v, q_pos, scale, max_split_rows)
+    if events is not None:
+        prob.event_begin, prob.event_end = events
     lib = L.lib()
     need = lib.halo_decode_workspace_bytes(ctypes.byref(prob), table.arr, table.n)
     if need < 0:
@@ -148,7 +151,8 @@ def _decode_table(q3: torch.Tensor, table: ChunkTable, *, scale: float,
 def chunked_decode(q: torch.Tensor, chunks, *, scale: Optional[float] = None,
                    q_pos: Optional[torch.Tensor] = None, out_dtype: Optional[torch.dtype] = None,
                    out: Optional[torch.Tensor] = None, lse: Optional[torch.Tensor] = None,
-                   prior: Optional[tuple] = None, max_split_rows: int = 0):
+                   prior: Optional[tuple] = None, max_split_rows: int = 0,
+                   events: Optional[tuple] = None):
     """Attention of one decode query over ``chunks`` -- a list of
     ``(k, v, start, causal)`` tuples or a prepared :class:`ChunkTable` --
     merged with log-sum-exp.  Returns ``(out (B, H, D_v), lse (B, H))``.
@@ -156,7 +160,8 @@ def chunked_decode(q: torch.Tensor, chunks, *, scale: Optional[float] = None,
     ``prior = (m, l, o)`` folds a running fp32 state in first.  ``q_pos``
     (device int64 ``(B,)``) defaults to ``total_T - 1`` as in
     ``halo/triton_chunked.py:250-253`` (reference path relative to the
-    lzbaclz/HALO root).
+    lzbaclz/HALO root).  ``events = (begin, end)`` are raw ``cudaEvent_t``
+    handles recorded around the split-KV kernel launches (profiling).
     """
     q3 = q.squeeze(2) if q.dim() == 4 else q
     _require_cuda(q3, "q")
@@ -183,7 +188,8 @@ def chunked_decode(q: torch.Tensor, chunks, *, scale: Optional[float] = None,
     if prior is not None:
         m, l, o = prior
         mg.m, mg.l, mg.o = m.data_ptr(), l.data_ptr(), o.data_ptr()
-    _decode_table(q3, table, scale=scale, q_pos=q_pos, merge=mg, max_split_rows=max_split_rows)
+    _decode_table(q3, table, scale=scale, q_pos=q_pos, merge=mg, max_split_rows=max_split_rows,
+                  events=events)
     return out, lse
 
 
@@ -247,18 +253,40 @@ def multi_query_attention(q: torch.Tensor, chunks: Sequence[tuple], *, scale: Op
     return out, lse
 
 
-def lse_merge(m_parts: torch.Tensor, l_parts: torch.Tensor, o_parts: torch.Tensor, *,
+def lse_merge(m_parts: torch.Tensor, l_parts: Optional[torch.Tensor], o_parts: torch.Tensor, *,
               out_dtype: torch.dtype = torch.float32, out: Optional[torch.Tensor] = None,
-              lse: Optional[torch.Tensor] = None):
-    """Merge ``P`` partial states ``m/l (B, H, P)``, ``o (B, H, P, D_v)`` (fp32,
-    contiguous) into ``(out (B, H, D_v), lse (B, H))``; the P-way form of
-    ``halo/kv_cache_chunked.py:194-239``."""
-    B, H, P = m_parts.shape
+              lse: Optional[torch.Tensor] = None, parts_major: bool = False):
+    """Merge ``P`` partial states into ``(out (B, H, D_v), lse (B, H))``; the
+    P-way form of ``halo/kv_cache_chunked.py:194-239``.
+
+    Row-major (default): ``m/l (B, H, P)``, ``o (B, H, P, D_v)``.
+    ``parts_major``: ``m/l (P, B, H)``, ``o (P, B, H, D_v)`` (e.g. gathered
+    from P GPUs).  ``l_parts=None`` means every part is normalised (l = 1,
+    ``m`` is its LSE).  All fp32.
+    """
+    if parts_major:
+        P, B, H = m_parts.shape
+    else:
+        B, H, P = m_parts.shape
     D_v = o_parts.shape[-1]
+    R = B * H
     for t in (m_parts, l_parts, o_parts):
+        if t is None:
+            continue
         _require_cuda(t, "partial")
-        if t.dtype != torch.float32 or not t.is_contiguous():
-            raise L.HaloError("partials must be contiguous fp32", L.HALO_ERR_INVALID_ARG)
+        if t.dtype != torch.float32 or t.stride(-1) != 1:
+            raise L.HaloError("partials must be fp32 with a contiguous last dim",
+                              L.HALO_ERR_INVALID_ARG)
+    if parts_major:
+        ps, rs = m_parts.stride(0), 1
+        ops_, ors = o_parts.stride(0), D_v
+        if m_parts.stride(2) != 1 or m_parts.stride(1) != H or o_parts.stride(1) != H * D_v:
+            raise L.HaloError("parts-major partials need contiguous (B, H) rows", L.HALO_ERR_INVALID_ARG)
+    else:
+        m_parts = m_parts.contiguous()
+        o_parts = o_parts.contiguous()
+        l_parts = l_parts.contiguous() if l_parts is not None else None
+        ps, rs, ops_, ors = 1, P, D_v, P * D_v
     dev = m_parts.device
     if out is None:
         out = torch.empty(B, H, D_v, dtype=out_dtype, device=dev)
@@ -271,7 +299,9 @@ def lse_merge(m_parts: torch.Tensor, l_parts: torch.Tensor, o_parts: torch.Tenso
     mg.out_stride_b, mg.out_stride_h = out.stride(0), out.stride(1)
     mg.lse = lse.data_ptr()
     with torch.cuda.device(dev):
-        rc = L.lib().halo_lse_merge(B, H, D_v, P, m_parts.data_ptr(), l_parts.data_ptr(),
-                                    o_parts.data_ptr(), ctypes.byref(mg), L.stream_handle(dev))
+        rc = L.lib().halo_lse_merge(B, H, D_v, P, m_parts.data_ptr(),
+                                    l_parts.data_ptr() if l_parts is not None else None,
+                                    o_parts.data_ptr(), ps, rs, ops_, ors, ctypes.byref(mg),
+                                    L.stream_handle(dev))
     L.check(rc, "halo_lse_merge")
     return out, lse

@@ -75,6 +75,11 @@ typedef struct halo_decode_problem {
   const int64_t* q_pos;
   float scale;                 /* softmax scale, e.g. 1/sqrt(D) */
   int32_t max_split_rows;      /* 0 = automatic split size */
+  /* Optional profiling hooks (cudaEvent_t or NULL): recorded on `stream`
+   * right before the first and right after the last split-KV launch, so a
+   * caller can time the decode kernel apart from the merge. */
+  void* event_begin;
+  void* event_end;
 } halo_decode_problem_t;
 
 /* Where the merged result goes.
@@ -119,13 +124,17 @@ int32_t halo_chunked_decode(const halo_decode_problem_t* problem,
                             void* workspace, int64_t workspace_bytes,
                             const halo_merge_args_t* merge, halo_stream_t stream);
 
-/* Merge P partial states laid out as m[R][P], l[R][P] (fp32) and
- * o[R][P][Dv] (fp32) into R rows, with the semantics of `merge` (rows are
- * (b, h) pairs, R = B*H).  This is the LSE merge of
- * halo/kv_cache_chunked.py:194-239 generalised to P parts; also the merge
- * step of the sequence-sharded decode (parts gathered from several GPUs). */
+/* Merge P partial states into R = B*H rows with the semantics of `merge`.
+ * Part s of row r has max-score/LSE m_parts[s*part_stride + r*row_stride],
+ * weight l_parts[same index] (l_parts NULL: every part is normalised, l = 1,
+ * so m is its LSE) and output o_parts[s*o_part_stride + r*o_row_stride + d]
+ * (fp32).  This is the LSE merge of halo/kv_cache_chunked.py:194-239
+ * generalised to P parts; with (o, lse) parts gathered from several GPUs it
+ * is the merge step of the sequence-sharded decode. */
 int32_t halo_lse_merge(int32_t B, int32_t H, int32_t Dv, int32_t P,
                        const float* m_parts, const float* l_parts, const float* o_parts,
+                       int64_t part_stride, int64_t row_stride,
+                       int64_t o_part_stride, int64_t o_row_stride,
                        const halo_merge_args_t* merge, halo_stream_t stream);
 
 /* ------------------------------------------------------------------ misc */
