@@ -74,6 +74,9 @@ SIGNATURES = {
     "halo_chunked_decode": (ctypes.c_int32, [ctypes.POINTER(DecodeProblem), ctypes.POINTER(KVChunk),
                                              ctypes.c_int32, ctypes.c_void_p, ctypes.c_int64,
                                              ctypes.POINTER(MergeArgs), ctypes.c_void_p]),
+    "halo_chunked_decode_noalloc": (ctypes.c_int32, [ctypes.POINTER(DecodeProblem),
+                                                     ctypes.POINTER(KVChunk), ctypes.c_int32,
+                                                     ctypes.POINTER(MergeArgs), ctypes.c_void_p]),
     "halo_lse_merge": (ctypes.c_int32, [ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                                         ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p,
                                         ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,

@@ -137,6 +137,22 @@ int32_t halo_lse_merge(int32_t B, int32_t H, int32_t Dv, int32_t P,
                        int64_t o_part_stride, int64_t o_row_stride,
                        const halo_merge_args_t* merge, halo_stream_t stream);
 
+/* Same as halo_chunked_decode, but allocates nothing and takes no workspace:
+ * the partial (m, l, o) scratch lives in a fixed 8 MiB device array inside
+ * the library.  No counterpart in the reference (its Triton path allocates
+ * through torch); this exists for callers that cannot allocate device memory
+ * when they need attention -- code whose framework owns every device
+ * allocation, plugin hosts that forbid cudaMalloc on the hot path, C/FFI
+ * callers without an allocator.  Problems needing more than 8 MiB of scratch
+ * (halo_decode_workspace_bytes) are rejected with HALO_ERR_WORKSPACE.  Every
+ * GPU that loads the library holds the array until exit.  All calls on a
+ * device share it, so calls that overlap on the GPU race: serialise them.
+ * The first call on each device looks up the array's address (make it before
+ * any stream capture). */
+int32_t halo_chunked_decode_noalloc(const halo_decode_problem_t* problem,
+                                    const halo_kv_chunk_t* chunks, int32_t n_chunks,
+                                    const halo_merge_args_t* merge, halo_stream_t stream);
+
 /* ------------------------------------------------------------------ misc */
 const char* halo_last_error_string(void);
 /* Read (and optionally clear) the device error word of the current device.
