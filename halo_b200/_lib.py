@@ -82,6 +82,9 @@ SIGNATURES = {
                                         ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
                                         ctypes.c_int64, ctypes.c_int64,
                                         ctypes.POINTER(MergeArgs), ctypes.c_void_p]),
+    "halo_copy2d_async": (ctypes.c_int32, [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p,
+                                           ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                           ctypes.c_void_p]),
     "halo_last_error_string": (ctypes.c_char_p, []),
     "halo_device_error": (ctypes.c_int32, [ctypes.POINTER(ctypes.c_int32), ctypes.c_int32]),
     "halo_version": (ctypes.c_int32, []),

@@ -87,20 +87,23 @@ template <typename T, int D, int STAGES>
 struct Geom {
   static constexpr int kElt = sizeof(T);
   static constexpr int kRowBytes = D * kElt;
-  static constexpr int kBoxElems = 128 / kElt;         // inner box: 128 bytes
-  static constexpr int kNBox = kRowBytes / 128;        // boxes per row
-  static constexpr int kBoxBytes = kBlockN * 128;
+  // TMA inner box: the largest of 128/64/32 bytes dividing a row; swizzle
+  // mode of the same width.
+  static constexpr int kInner = kRowBytes % 128 == 0 ? 128 : (kRowBytes % 64 == 0 ? 64 : 32);
+  static constexpr int kBoxElems = kInner / kElt;
+  static constexpr int kNBox = kRowBytes / kInner;     // boxes per row
+  static constexpr int kBoxBytes = kBlockN * kInner;
   static constexpr int kTileBytes = kNBox * kBoxBytes;
   static constexpr int kStageBytes = 2 * kTileBytes;
   static constexpr int kGpb = (kElt == 4 ? 8 : 16);   // q-heads per unit
-  static constexpr int kQSlotBytes = kNBox * kGpb * 128;
+  static constexpr int kQSlotBytes = ((kNBox * kGpb * kInner) + 1023) / 1024 * 1024;
   static constexpr int kPBytes = (kElt == 4 ? kConsumerWarps * 16 * 8 * 4 : 0);
   static constexpr int kBarBytes = 128;
   // ring | q ring (2 slots) | P | barriers ; +1024 for manual alignment
   static constexpr int kSmemBytes =
       STAGES * kStageBytes + 2 * kQSlotBytes + kPBytes + kBarBytes + 1024;
-  static_assert(kRowBytes % 128 == 0, "row must be a whole number of 128-byte boxes");
-  static_assert(kQSlotBytes % 1024 == 0, "q slot must keep 1024-byte alignment");
+  static_assert(kRowBytes % 32 == 0, "row must be a whole number of 32-byte TMA boxes");
+  static_assert(kTileBytes % 1024 == 0, "tiles must keep 1024-byte alignment");
 };
 
 struct Unit {
@@ -150,7 +153,7 @@ __device__ __forceinline__ bool consume_mma(const DecodeParams& p, const Unit& u
     for (int kk = 0; kk < D / 16; ++kk) {
       const int row = lane & 15;
       const int c16 = kk * 2 + (lane >> 4);
-      ldsm_x4(qb + swz128<Gm::kGpb>(row, c16), qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3]);
+      ldsm_x4(qb + swz<Gm::kInner, Gm::kGpb>(row, c16), qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3]);
     }
   }
   __syncwarp();
@@ -179,7 +182,7 @@ __device__ __forceinline__ bool consume_mma(const DecodeParams& p, const Unit& u
       for (int kk = 0; kk < D / 16; ++kk) {
         const int c16 = kk * 2 + ((lane >> 3) & 1);
         uint32_t b00, b01, b10, b11;
-        ldsm_x4(kbase + swz128(key, c16), b00, b01, b10, b11);
+        ldsm_x4(kbase + swz<Gm::kInner>(key, c16), b00, b01, b10, b11);
         mma_16816(sacc[0], qf[kk], b00, b01, (T*)nullptr);
         mma_16816(sacc[1], qf[kk], b10, b11, (T*)nullptr);
       }
@@ -250,7 +253,7 @@ __device__ __forceinline__ bool consume_mma(const DecodeParams& p, const Unit& u
       for (int j = 0; j < D / 16; ++j) {
         const int c16 = j * 2 + (lane >> 4);
         uint32_t v0, v1, v2, v3;
-        ldsm_x4_t(vbase + swz128(key, c16), v0, v1, v2, v3);
+        ldsm_x4_t(vbase + swz<Gm::kInner>(key, c16), v0, v1, v2, v3);
         mma_16816(o[2 * j], ph, v0, v1, (T*)nullptr);
         mma_16816(o[2 * j], pl, v0, v1, (T*)nullptr);
         mma_16816(o[2 * j + 1], ph, v2, v3, (T*)nullptr);
@@ -284,9 +287,8 @@ __device__ __forceinline__ bool consume_mma(const DecodeParams& p, const Unit& u
 }
 
 // fp32 inputs: CUDA-core FMA path, up to 8 q-heads per unit.  For S, lane
-// pair (2k, 2k+1) owns key k of the warp's 16 rows, each lane one half of D
-// (the second half walks its 16-byte chunks rotated by 4 so both halves hit
-// different bank groups); for P V each lane owns D/32 output columns.
+// pair (2k, 2k+1) owns key k of the warp's 16 rows, each lane one half of
+// the row's 16-byte chunks; for P V lane l owns output columns l, l+32, ...
 template <int D, int STAGES>
 __device__ __forceinline__ bool consume_fma(const DecodeParams& p, const Unit& un, const Item& it,
                                             char* ring, const char* qslot, float* ps_all,
@@ -294,9 +296,9 @@ __device__ __forceinline__ bool consume_fma(const DecodeParams& p, const Unit& u
                                             int n_tiles, int& gt, int64_t qpos) {
   using Gm = Geom<float, D, STAGES>;
   constexpr int GP = 8;
-  constexpr int DPL = D / 32;      // output columns per lane
-  constexpr int NCH = D / 4;       // 16-byte chunks per row
-  constexpr int HALF = NCH / 2;
+  constexpr int DPL = (D + 31) / 32;   // output columns per lane (strided by 32)
+  constexpr int NCH = D / 4;           // 16-byte chunks per row
+  constexpr int HALF = (NCH + 1) / 2;
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   float* ps = ps_all + warp * 16 * GP;
@@ -327,16 +329,19 @@ __device__ __forceinline__ bool consume_fma(const DecodeParams& p, const Unit& u
     for (int g = 0; g < GP; ++g) acc[g] = 0.f;
 #pragma unroll 4
     for (int i = 0; i < HALF; ++i) {
-      const int j = half * HALF + ((HALF >= 8 && half) ? ((i & ~7) | ((i + 4) & 7)) : i);
-      const float4 kv = *reinterpret_cast<const float4*>(kt + swz128(wrow + key, j));
+      const int j = half * HALF + i;
+      if (j < NCH) {
+        const float4 kv = *reinterpret_cast<const float4*>(kt + swz<Gm::kInner>(wrow + key, j));
 #pragma unroll
-      for (int g = 0; g < GP; ++g) {
-        if (g < gcount) {
-          const float4 qv = *reinterpret_cast<const float4*>(qslot + swz128<GP>(g, j));
-          acc[g] = fmaf(qv.x, kv.x, acc[g]);
-          acc[g] = fmaf(qv.y, kv.y, acc[g]);
-          acc[g] = fmaf(qv.z, kv.z, acc[g]);
-          acc[g] = fmaf(qv.w, kv.w, acc[g]);
+        for (int g = 0; g < GP; ++g) {
+          if (g < gcount) {
+            const float4 qv =
+                *reinterpret_cast<const float4*>(qslot + swz<Gm::kInner, GP>(g, j));
+            acc[g] = fmaf(qv.x, kv.x, acc[g]);
+            acc[g] = fmaf(qv.y, kv.y, acc[g]);
+            acc[g] = fmaf(qv.z, kv.z, acc[g]);
+            acc[g] = fmaf(qv.w, kv.w, acc[g]);
+          }
         }
       }
     }
@@ -366,20 +371,15 @@ __device__ __forceinline__ bool consume_fma(const DecodeParams& p, const Unit& u
       for (int g = 0; g < GP; ++g) ps[key * GP + g] = pk[g];
     }
     __syncwarp();
-    const int jv = (lane * DPL) / 4;           // this lane's 16-byte chunk
-    const int bo = ((lane * DPL) % 4) * 4;     // byte offset inside it
 #pragma unroll 4
     for (int kr = 0; kr < 16; ++kr) {
-      const float* vrow = reinterpret_cast<const float*>(vt + swz128(wrow + kr, jv) + bo);
       float vv[DPL];
-      if constexpr (DPL == 4) {
-        const float4 t4 = *reinterpret_cast<const float4*>(vrow);
-        vv[0] = t4.x; vv[1] = t4.y; vv[2] = t4.z; vv[3] = t4.w;
-      } else if constexpr (DPL == 2) {
-        const float2 t2 = *reinterpret_cast<const float2*>(vrow);
-        vv[0] = t2.x; vv[1] = t2.y;
-      } else {
-        vv[0] = vrow[0];
+#pragma unroll
+      for (int e = 0; e < DPL; ++e) {
+        const int d = lane + 32 * e;
+        vv[e] = d < D ? *reinterpret_cast<const float*>(vt + swz<Gm::kInner>(wrow + kr, d >> 2) +
+                                                       ((d & 3) << 2))
+                      : 0.f;
       }
       const float4 p03 = *reinterpret_cast<const float4*>(ps + kr * GP);
       const float4 p47 = *reinterpret_cast<const float4*>(ps + kr * GP + 4);
@@ -411,9 +411,10 @@ __device__ __forceinline__ bool consume_fma(const DecodeParams& p, const Unit& u
     if (g < gcount) {
       if (lane == 0) write_partial_meta(p, un, it, warp, g, m[g], l[g]);
       const int h = un.h_kv * p.G + un.gbase + g;
-      float* op = p.o_part + (((int64_t)un.b * p.H + h) * p.S + it.slot + warp) * D + lane * DPL;
+      float* op = p.o_part + (((int64_t)un.b * p.H + h) * p.S + it.slot + warp) * D;
 #pragma unroll
-      for (int e = 0; e < DPL; ++e) op[e] = o[g][e];
+      for (int e = 0; e < DPL; ++e)
+        if (lane + 32 * e < D) op[lane + 32 * e] = o[g][e];
     }
   }
   return ok;
@@ -460,10 +461,10 @@ __global__ void __launch_bounds__(kThreads, MINB) kd_kernel(const __grid_constan
         const Item& it = p.items[un.item];
         const int qs = ut & 1;
         if (ut >= 2 && !mbar_wait(&qempty[qs], ((ut >> 1) & 1) ^ 1, p.err)) return;
-        mbar_arrive_expect_tx(&qfull[qs], Gm::kQSlotBytes);
+        mbar_arrive_expect_tx(&qfull[qs], Gm::kNBox * Gm::kGpb * Gm::kInner);
 #pragma unroll
         for (int bx = 0; bx < Gm::kNBox; ++bx)
-          tma_load_3d(qring + qs * Gm::kQSlotBytes + bx * Gm::kGpb * 128, &p.qmap,
+          tma_load_3d(qring + qs * Gm::kQSlotBytes + bx * Gm::kGpb * Gm::kInner, &p.qmap,
                       bx * Gm::kBoxElems, un.h_kv * p.G + un.gbase, un.b, &qfull[qs]);
         const CUtensorMap* kmap = &p.maps[2 * it.seg];
         const CUtensorMap* vmap = &p.maps[2 * it.seg + 1];
@@ -685,6 +686,17 @@ static int elt_size(int dtype) {
 }
 
 // ---------------------------------------------------------------- tensor maps
+// TMA inner box width (bytes) for rows of D elements: the largest of
+// 128/64/32 dividing the row, with the swizzle mode of the same width.
+static int inner_bytes(int D, int elt) {
+  const int rb = D * elt;
+  return rb % 128 == 0 ? 128 : (rb % 64 == 0 ? 64 : 32);
+}
+static CUtensorMapSwizzle swizzle_for(int inner) {
+  return inner == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                      : (inner == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B);
+}
+
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
@@ -758,13 +770,14 @@ static int encode_view(const void* base, int64_t rows, int H_kv, int B, int D, i
                         (cuuint64_t)key.dims[3]};
   cuuint64_t gstr[3] = {(cuuint64_t)key.strides[0], (cuuint64_t)key.strides[1],
                         (cuuint64_t)key.strides[2]};
-  cuuint32_t box[4] = {(cuuint32_t)(128 / elt), (cuuint32_t)kBlockN, 1, 1};
+  const int inner = inner_bytes(D, elt);
+  cuuint32_t box[4] = {(cuuint32_t)(inner / elt), (cuuint32_t)kBlockN, 1, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
   const CUtensorMapDataType dt = dtype == HALO_DTYPE_F32    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
                                  : dtype == HALO_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                                             : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   CUresult r = fn(out, dt, 4, const_cast<void*>(base), gdim, gstr, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle_for(inner),
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return fail(HALO_ERR_INVALID_ARG,
@@ -782,6 +795,12 @@ static int encode_view(const void* base, int64_t rows, int H_kv, int B, int D, i
 
 static int64_t align256(int64_t x) { return (x + 255) & ~int64_t(255); }
 
+// Head dims with a compiled kernel (rows must be whole 32-byte TMA boxes).
+static bool supported_head_dim(int dtype, int D) {
+  if (dtype == HALO_DTYPE_F32) return D == 16 || D == 32 || D == 64 || D == 80 || D == 96 || D == 128;
+  return D == 16 || D == 32 || D == 64 || D == 80 || D == 96 || D == 128;
+}
+
 static int validate_problem(const halo_decode_problem_t* p, const halo_kv_chunk_t* chunks,
                             int n_chunks) {
   if (!p) return fail(HALO_ERR_INVALID_ARG, "problem is NULL");
@@ -792,8 +811,7 @@ static int validate_problem(const halo_decode_problem_t* p, const halo_kv_chunk_
     return fail(HALO_ERR_INVALID_ARG, "H=%d not divisible by H_kv=%d", p->H, p->H_kv);
   if (elt_size(p->dtype) == 0) return fail(HALO_ERR_INVALID_ARG, "bad dtype %d", p->dtype);
   if (p->Dv != p->D) return fail(HALO_ERR_UNSUPPORTED, "Dv (%d) != D (%d)", p->Dv, p->D);
-  const bool d_ok = (p->dtype == HALO_DTYPE_F32) ? (p->D == 32 || p->D == 64 || p->D == 128)
-                                                 : (p->D == 64 || p->D == 128);
+  const bool d_ok = supported_head_dim(p->dtype, p->D);
   if (!d_ok) return fail(HALO_ERR_UNSUPPORTED, "head_dim %d unsupported for dtype %d", p->D, p->dtype);
   if (n_chunks < 0 || (n_chunks > 0 && !chunks))
     return fail(HALO_ERR_INVALID_ARG, "bad chunk list");
@@ -820,11 +838,11 @@ static int validate_problem(const halo_decode_problem_t* p, const halo_kv_chunk_
 int launch_merge(const MergeParams& mp, cudaStream_t st) {
   if (mp.R == 0) return HALO_OK;
   const int threads = kMergeWarps * 32;
-  if (mp.Dv == 128) km_kernel<4><<<mp.R, threads, 0, st>>>(mp);
-  else if (mp.Dv == 64) km_kernel<2><<<mp.R, threads, 0, st>>>(mp);
-  else if (mp.Dv == 32) km_kernel<1><<<mp.R, threads, 0, st>>>(mp);
-  else if (mp.Dv <= 256) km_kernel<8><<<mp.R, threads, 0, st>>>(mp);
-  else return fail(HALO_ERR_UNSUPPORTED, "Dv %d > 256", mp.Dv);
+  if (mp.Dv <= 32) km_kernel<1><<<mp.R, threads, 0, st>>>(mp);
+  else if (mp.Dv <= 64 && mp.Dv % 2 == 0) km_kernel<2><<<mp.R, threads, 0, st>>>(mp);
+  else if (mp.Dv <= 128 && mp.Dv % 4 == 0) km_kernel<4><<<mp.R, threads, 0, st>>>(mp);
+  else if (mp.Dv <= 256 && mp.Dv % 8 == 0) km_kernel<8><<<mp.R, threads, 0, st>>>(mp);
+  else return fail(HALO_ERR_UNSUPPORTED, "Dv %d unsupported by the merge", mp.Dv);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? HALO_OK : cuda_fail(e, "km_kernel launch");
 }
@@ -1008,9 +1026,10 @@ static int64_t workspace_for(const halo_decode_problem_t* p, int S) {
 
 template <typename T, int D>
 struct KdConfig {
-  // 16-bit: 3 stages, 2 CTAs per SM; fp32: stages sized to one CTA per SM.
-  static constexpr int kStages = sizeof(T) == 4 ? (D == 128 ? 3 : 4) : 3;
-  static constexpr int kMinBlocks = sizeof(T) == 4 && D == 128 ? 1 : 2;
+  // 3 stages; 2 CTAs per SM unless a stage is larger than 32 KB (fp32 with
+  // D > 64), then one.
+  static constexpr int kStages = 3;
+  static constexpr int kMinBlocks = (2 * 64 * D * (int)sizeof(T)) > 32768 ? 1 : 2;
 };
 
 template <typename T, int D>
@@ -1035,13 +1054,29 @@ static int kd_ctas_per_sm() {
 }
 
 static int ctas_per_sm(int dtype, int D) {
-  if (dtype == HALO_DTYPE_BF16) return D == 128 ? kd_ctas_per_sm<__nv_bfloat16, 128>()
-                                                : kd_ctas_per_sm<__nv_bfloat16, 64>();
-  if (dtype == HALO_DTYPE_F16) return D == 128 ? kd_ctas_per_sm<__half, 128>()
-                                               : kd_ctas_per_sm<__half, 64>();
-  if (D == 128) return kd_ctas_per_sm<float, 128>();
-  if (D == 64) return kd_ctas_per_sm<float, 64>();
-  return kd_ctas_per_sm<float, 32>();
+  if (dtype == HALO_DTYPE_BF16) {
+    if (D == 16) return kd_ctas_per_sm<__nv_bfloat16, 16>();
+    if (D == 32) return kd_ctas_per_sm<__nv_bfloat16, 32>();
+    if (D == 64) return kd_ctas_per_sm<__nv_bfloat16, 64>();
+    if (D == 80) return kd_ctas_per_sm<__nv_bfloat16, 80>();
+    if (D == 96) return kd_ctas_per_sm<__nv_bfloat16, 96>();
+    if (D == 128) return kd_ctas_per_sm<__nv_bfloat16, 128>();
+  } else if (dtype == HALO_DTYPE_F16) {
+    if (D == 16) return kd_ctas_per_sm<__half, 16>();
+    if (D == 32) return kd_ctas_per_sm<__half, 32>();
+    if (D == 64) return kd_ctas_per_sm<__half, 64>();
+    if (D == 80) return kd_ctas_per_sm<__half, 80>();
+    if (D == 96) return kd_ctas_per_sm<__half, 96>();
+    if (D == 128) return kd_ctas_per_sm<__half, 128>();
+  } else {
+    if (D == 16) return kd_ctas_per_sm<float, 16>();
+    if (D == 32) return kd_ctas_per_sm<float, 32>();
+    if (D == 64) return kd_ctas_per_sm<float, 64>();
+    if (D == 80) return kd_ctas_per_sm<float, 80>();
+    if (D == 96) return kd_ctas_per_sm<float, 96>();
+    if (D == 128) return kd_ctas_per_sm<float, 128>();
+  }
+  return 1;
 }
 
 template <typename T, int D>
@@ -1057,15 +1092,26 @@ static int launch_kd(const DecodeParams& prm, cudaStream_t st) {
 
 static int dispatch_kd(int dtype, int D, const DecodeParams& prm, cudaStream_t st) {
   if (dtype == HALO_DTYPE_BF16) {
-    if (D == 128) return launch_kd<__nv_bfloat16, 128>(prm, st);
+    if (D == 16) return launch_kd<__nv_bfloat16, 16>(prm, st);
+    if (D == 32) return launch_kd<__nv_bfloat16, 32>(prm, st);
     if (D == 64) return launch_kd<__nv_bfloat16, 64>(prm, st);
+    if (D == 80) return launch_kd<__nv_bfloat16, 80>(prm, st);
+    if (D == 96) return launch_kd<__nv_bfloat16, 96>(prm, st);
+    if (D == 128) return launch_kd<__nv_bfloat16, 128>(prm, st);
   } else if (dtype == HALO_DTYPE_F16) {
-    if (D == 128) return launch_kd<__half, 128>(prm, st);
+    if (D == 16) return launch_kd<__half, 16>(prm, st);
+    if (D == 32) return launch_kd<__half, 32>(prm, st);
     if (D == 64) return launch_kd<__half, 64>(prm, st);
+    if (D == 80) return launch_kd<__half, 80>(prm, st);
+    if (D == 96) return launch_kd<__half, 96>(prm, st);
+    if (D == 128) return launch_kd<__half, 128>(prm, st);
   } else {
-    if (D == 128) return launch_kd<float, 128>(prm, st);
-    if (D == 64) return launch_kd<float, 64>(prm, st);
+    if (D == 16) return launch_kd<float, 16>(prm, st);
     if (D == 32) return launch_kd<float, 32>(prm, st);
+    if (D == 64) return launch_kd<float, 64>(prm, st);
+    if (D == 80) return launch_kd<float, 80>(prm, st);
+    if (D == 96) return launch_kd<float, 96>(prm, st);
+    if (D == 128) return launch_kd<float, 128>(prm, st);
   }
   return fail(HALO_ERR_UNSUPPORTED, "no kernel for dtype %d D %d", dtype, D);
 }
@@ -1081,13 +1127,14 @@ static int encode_q_map(const halo_decode_problem_t& pb, CUtensorMap* out) {
   cuuint64_t gdim[3] = {(cuuint64_t)pb.D, (cuuint64_t)pb.H, (cuuint64_t)pb.B};
   cuuint64_t gstr[2] = {(cuuint64_t)(pb.q_stride_h * elt),
                         (cuuint64_t)(pb.B > 1 ? pb.q_stride_b * elt : pb.q_stride_h * elt * pb.H)};
-  cuuint32_t box[3] = {(cuuint32_t)(128 / elt), (cuuint32_t)gpb_for(pb.dtype), 1};
+  const int inner = inner_bytes(pb.D, elt);
+  cuuint32_t box[3] = {(cuuint32_t)(inner / elt), (cuuint32_t)gpb_for(pb.dtype), 1};
   cuuint32_t estr[3] = {1, 1, 1};
   const CUtensorMapDataType dt = pb.dtype == HALO_DTYPE_F32    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
                                  : pb.dtype == HALO_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                                                : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   CUresult r = fn(out, dt, 3, const_cast<void*>(pb.q), gdim, gstr, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle_for(inner),
                   CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(HALO_ERR_INVALID_ARG, "q tensor map encode failed (%d)", (int)r);
   return HALO_OK;
@@ -1200,7 +1247,7 @@ extern "C" int32_t halo_lse_merge(int32_t B, int32_t H, int32_t Dv, int32_t P,
                                   const halo_merge_args_t* merge, halo_stream_t stream) {
   if (B <= 0 || H <= 0 || Dv <= 0 || P < 0) return fail(HALO_ERR_INVALID_ARG, "bad merge shape");
   if (P > 0 && (!m_parts || !o_parts)) return fail(HALO_ERR_INVALID_ARG, "NULL partial arrays");
-  if (Dv != 32 && Dv != 64 && Dv != 128 && (Dv > 256 || Dv % 8 != 0))
+  if (Dv > 256 || (Dv > 32 && Dv % ((Dv + 31) / 32 > 2 ? ((Dv + 31) / 32 > 4 ? 8 : 4) : 2)))
     return fail(HALO_ERR_UNSUPPORTED, "Dv %d unsupported", Dv);
   int rc = validate_merge(merge, Dv);
   if (rc != HALO_OK) return rc;

@@ -128,13 +128,19 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, i
 }
 
 // Byte offset of 16-byte chunk `c16` (along the row) of row `row` in a tile
-// written by 128B-swizzled TMA boxes of BOX_ROWS rows x 128 bytes (box
-// = c16 / 8, boxes stacked); inside each 8-row x 128-byte atom, chunk j of
-// row r sits at j ^ (r % 8).  The tile base must be 1024-byte aligned.
-template <int BOX_ROWS = 64>
-__device__ __forceinline__ uint32_t swz128(int row, int c16) {
-  return static_cast<uint32_t>((c16 >> 3) * (BOX_ROWS * 128) + row * 128 +
-                               (((c16 & 7) ^ (row & 7)) << 4));
+// written by swizzled TMA boxes of BOX_ROWS rows x INNER bytes (INNER = 32,
+// 64 or 128 with the matching 32B/64B/128B swizzle mode; boxes stacked along
+// the row).  The TMA swizzle XORs address bits [4, 4+b) with bits [7, 7+b),
+// b = log2(INNER/16); with INNER-byte rows that is chunk j of row r stored at
+// j ^ ((r >> (7 - log2 INNER)) % (INNER/16)).  The tile base must be
+// 1024-byte aligned.
+template <int INNER = 128, int BOX_ROWS = 64>
+__device__ __forceinline__ uint32_t swz(int row, int c16) {
+  constexpr int kCpb = INNER / 16;
+  constexpr int kShift = INNER == 128 ? 0 : (INNER == 64 ? 1 : 2);
+  const int box = c16 / kCpb, c = c16 % kCpb;
+  const int x = (row >> kShift) & (kCpb - 1);
+  return static_cast<uint32_t>(box * (BOX_ROWS * INNER) + row * INNER + ((c ^ x) << 4));
 }
 
 // ---------------------------------------------------------------- fragments

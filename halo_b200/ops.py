@@ -253,6 +253,25 @@ def multi_query_attention(q: torch.Tensor, chunks: Sequence[tuple], *, scale: Op
     return out, lse
 
 
+def multi_query_accumulate(q: torch.Tensor, chunks: Sequence[tuple], m: torch.Tensor,
+                           l: torch.Tensor, o: torch.Tensor, *, scale: float,
+                           query_pos_offset: int) -> None:
+    """Fold ``chunks`` into running fp32 state for ``T_q > 1`` queries: query
+    row ``i`` sits at position ``query_pos_offset + i``; causal chunks hide
+    keys after it.  State layout ``m, l (B, T_q, H)``, ``o (B, T_q, H, D_v)``
+    (contiguous), i.e. rows ordered (query row, head) per batch."""
+    _require_cuda(q, "q")
+    B, H, T_q, D = q.shape
+    qp = torch.arange(T_q, dtype=torch.int64, device=q.device) + int(query_pos_offset)
+    for b in range(B):
+        table = ChunkTable(chunks, batch_stride_zero=True, batch=slice(b, b + 1))
+        qb = q[b].transpose(0, 1).contiguous()          # (T_q, H, D)
+        mg = L.MergeArgs()
+        mg.mode = L.MERGE_ACCUMULATE
+        mg.m, mg.l, mg.o = m[b].data_ptr(), l[b].data_ptr(), o[b].data_ptr()
+        _decode_table(qb, table, scale=scale, q_pos=qp, merge=mg)
+
+
 def lse_merge(m_parts: torch.Tensor, l_parts: Optional[torch.Tensor], o_parts: torch.Tensor, *,
               out_dtype: torch.dtype = torch.float32, out: Optional[torch.Tensor] = None,
               lse: Optional[torch.Tensor] = None, parts_major: bool = False):

@@ -153,6 +153,16 @@ int32_t halo_chunked_decode_noalloc(const halo_decode_problem_t* problem,
                                     const halo_kv_chunk_t* chunks, int32_t n_chunks,
                                     const halo_merge_args_t* merge, halo_stream_t stream);
 
+/* ------------------------------------------------------------------ tiers */
+
+/* Pitched async copy of `height` rows of `width_bytes` between any two of
+ * pinned host / device memory (cudaMemcpyDefault), on `stream`.  Moves a
+ * (B, H_kv, rows, D) slice of a (B, H_kv, T_cap, D) tier in one DMA.
+ * Replaces the strided slice copies of halo/kv_cache_chunked.py:441-446,
+ * :469-483 (peel to host) and :716-717, :884-885 (refetch to HBM). */
+int32_t halo_copy2d_async(void* dst, int64_t dst_pitch, const void* src, int64_t src_pitch,
+                          int64_t width_bytes, int64_t height, halo_stream_t stream);
+
 /* ------------------------------------------------------------------ misc */
 const char* halo_last_error_string(void);
 /* Read (and optionally clear) the device error word of the current device.

@@ -48,7 +48,7 @@ def test_invalid_arguments_are_reported_without_gpu():
     rc = lib.halo_decode_workspace_bytes(ctypes.byref(prob), None, 0)
     assert rc == L.HALO_ERR_INVALID_ARG
     assert b"not divisible" in lib.halo_last_error_string()
-    prob.H, prob.D, prob.Dv = 8, 96, 96
+    prob.H, prob.D, prob.Dv = 8, 40, 40
     assert lib.halo_decode_workspace_bytes(ctypes.byref(prob), None, 0) == L.HALO_ERR_UNSUPPORTED
     prob.D = prob.Dv = 128
     prob.q = 0x2000

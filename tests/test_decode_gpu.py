@@ -255,3 +255,23 @@ def test_large_context_properties(cuda_device):
 def test_device_error_word_clear(cuda_device):
     from halo_b200 import _lib as L
     assert L.device_error(clear=True) == 0
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("D", [16, 32, 64, 80, 96, 128])
+def test_decode_head_dims(cuda_device, dtype, D):
+    """Every compiled head_dim (32/64/128-byte swizzle widths, 1..5 TMA
+    boxes per row) against the fp64 oracle, with a ragged causal tail."""
+    ops = _ops()
+    g = torch.Generator().manual_seed(D)
+    B, H, H_kv, T = 2, 8, 2, 777
+    q = torch.randn(B, H, 1, D, generator=g).to(dtype)
+    k = torch.randn(B, H_kv, T, D, generator=g).to(dtype)
+    v = torch.randn(B, H_kv, T, D, generator=g).to(dtype)
+    qp = torch.tensor([T - 1, 500], device=cuda_device)
+    out, lse = ops.chunked_decode(q.to(cuda_device), _gpu_chunks(k, v, _bounds(T, 300), True),
+                                  q_pos=qp, out_dtype=torch.float32)
+    for b, p in enumerate((T - 1, 500)):
+        ro, rl = OA.full_attention_f64(q[b:b + 1], k[b:b + 1], v[b:b + 1], q_pos=p)
+        assert (out[b].cpu().double() - ro[0, :, 0]).abs().max().item() <= _tol(dtype)
+        assert (lse[b].cpu().double() - rl[0, :, 0]).abs().max().item() <= LSE_TOL
