@@ -82,6 +82,20 @@ SIGNATURES = {
                                         ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
                                         ctypes.c_int64, ctypes.c_int64,
                                         ctypes.POINTER(MergeArgs), ctypes.c_void_p]),
+    "halo_page_summary": (ctypes.c_int32, [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
+                                           ctypes.c_int64, ctypes.c_int32, ctypes.c_int32,
+                                           ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                                           ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p,
+                                           ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
+                                           ctypes.c_int64, ctypes.c_void_p]),
+    "halo_page_score_topk": (ctypes.c_int32, [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
+                                              ctypes.c_int64, ctypes.c_int32, ctypes.c_int32,
+                                              ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                                              ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p,
+                                              ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                              ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p,
+                                              ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p,
+                                              ctypes.c_void_p]),
     "halo_copy2d_async": (ctypes.c_int32, [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p,
                                            ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
                                            ctypes.c_void_p]),

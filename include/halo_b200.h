@@ -153,6 +153,35 @@ int32_t halo_chunked_decode_noalloc(const halo_decode_problem_t* problem,
                                     const halo_kv_chunk_t* chunks, int32_t n_chunks,
                                     const halo_merge_args_t* merge, halo_stream_t stream);
 
+/* ------------------------------------------------------------------ scorer */
+
+/* Per-page channel-wise min/max of K (B, H_kv, T, D) for pages
+ * [page_begin, page_begin + n_pages) of `page_size` rows, written to
+ * kmin/kmax at element (b, h, page, d) = b*o_sb + h*o_sh + page*o_sp + d, in
+ * K's dtype (exact).  Replaces _QuestScorerAdapter.observe_keys
+ * (baselines/quest_path_d.py:125-150). */
+int32_t halo_page_summary(const void* k, int64_t k_sb, int64_t k_sh, int64_t k_st,
+                          int32_t B, int32_t H_kv, int32_t D, int32_t dtype,
+                          int32_t page_size, int32_t page_begin, int32_t n_pages,
+                          void* kmin, void* kmax, int64_t o_sb, int64_t o_sh, int64_t o_sp,
+                          halo_stream_t stream);
+
+/* Quest upper-bound page scores and top-k.  q is (B, H, T_q, D) with element
+ * strides (q_sb, q_sh, q_st, 1); it is mean-pooled over each GQA group in
+ * fp32 and rounded once to its dtype, then scores[b][h_kv][t][p] =
+ * sum_d max(q_d * kmin_d, q_d * kmax_d) in fp32 (contiguous (B, H_kv, T_q, P)
+ * output).  With k > 0, per_page (optional, (P,)) gets the max over
+ * (b, h_kv, t) and topk ((k,) int64) the k best pages, largest first, ties
+ * to the lower index, skipping pages with exclude[p] != 0 (optional).
+ * P <= 16384 when k > 0.  Replaces _QuestScorerAdapter.score_pages and
+ * select_hot_pages (baselines/quest_path_d.py:153-205). */
+int32_t halo_page_score_topk(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_st,
+                             int32_t B, int32_t H, int32_t T_q, int32_t H_kv, int32_t D,
+                             int32_t dtype, const void* kmin, const void* kmax, int64_t o_sb,
+                             int64_t o_sh, int64_t o_sp, int32_t P, float* scores,
+                             const uint8_t* exclude, int32_t k, float* per_page, int64_t* topk,
+                             halo_stream_t stream);
+
 /* ------------------------------------------------------------------ tiers */
 
 /* Pitched async copy of `height` rows of `width_bytes` between any two of
