@@ -67,6 +67,13 @@ class MergeArgs(ctypes.Structure):
                 ("m", ctypes.c_void_p), ("l", ctypes.c_void_p), ("o", ctypes.c_void_p)]
 
 
+class KiviTensor(ctypes.Structure):
+    _fields_ = [("codes", ctypes.c_void_p), ("scale", ctypes.c_void_p), ("zero", ctypes.c_void_p),
+                ("codes_stride_b", ctypes.c_int64), ("codes_stride_h", ctypes.c_int64),
+                ("sz_stride_b", ctypes.c_int64), ("sz_stride_h", ctypes.c_int64),
+                ("t_cap", ctypes.c_int64)]
+
+
 # name -> (restype, argtypes); must match include/halo_b200.h
 SIGNATURES = {
     "halo_decode_workspace_bytes": (ctypes.c_int64, [ctypes.POINTER(DecodeProblem),
@@ -82,6 +89,27 @@ SIGNATURES = {
                                         ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
                                         ctypes.c_int64, ctypes.c_int64,
                                         ctypes.POINTER(MergeArgs), ctypes.c_void_p]),
+    "halo_kivi_quantize": (ctypes.c_int32, [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
+                                            ctypes.c_int64, ctypes.c_int32, ctypes.c_int32,
+                                            ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                                            ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p,
+                                            ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                            ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64,
+                                            ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p]),
+    "halo_kivi_dequantize": (ctypes.c_int32, [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
+                                              ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p,
+                                              ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                              ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                                              ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                                              ctypes.c_int32, ctypes.c_void_p, ctypes.c_int64,
+                                              ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p]),
+    "halo_kivi_decode_workspace_bytes": (ctypes.c_int64, [ctypes.POINTER(DecodeProblem),
+                                                          ctypes.c_int32]),
+    "halo_kivi_decode": (ctypes.c_int32, [ctypes.POINTER(DecodeProblem), ctypes.POINTER(KiviTensor),
+                                          ctypes.POINTER(KiviTensor), ctypes.c_int32, ctypes.c_int32,
+                                          ctypes.c_int64, ctypes.c_int32, ctypes.c_void_p,
+                                          ctypes.c_int64, ctypes.POINTER(MergeArgs),
+                                          ctypes.c_void_p]),
     "halo_page_summary": (ctypes.c_int32, [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
                                            ctypes.c_int64, ctypes.c_int32, ctypes.c_int32,
                                            ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,

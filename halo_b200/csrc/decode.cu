@@ -110,7 +110,8 @@ struct Unit {
   int item, b, h_kv, gbase, gcount;
 };
 
-__device__ __forceinline__ Unit decode_unit(const DecodeParams& p, int u, int gpb) {
+template <class P>
+__device__ __forceinline__ Unit decode_unit(const P& p, int u, int gpb) {
   Unit r;
   r.item = u % p.n_items;
   int pair = u / p.n_items;
@@ -124,7 +125,8 @@ __device__ __forceinline__ Unit decode_unit(const DecodeParams& p, int u, int gp
 }
 
 // Write one warp's partial state for q-head rows [gbase, gbase+gcount).
-__device__ __forceinline__ void write_partial_meta(const DecodeParams& p, const Unit& un,
+template <class P>
+__device__ __forceinline__ void write_partial_meta(const P& p, const Unit& un,
                                                    const Item& it, int warp, int g, float m_log2,
                                                    float l) {
   const int h = un.h_kv * p.G + un.gbase + g;
@@ -136,10 +138,31 @@ __device__ __forceinline__ void write_partial_meta(const DecodeParams& p, const 
 // ---------------------------------------------------------------- consumers
 // 16-bit inputs: tensor-core path.  Warp `w` handles rows [16w, 16w+16) of
 // every stage; the 16 query rows of the MMA are the unit's q-heads.
-template <typename T, int D, int STAGES>
-__device__ __forceinline__ bool consume_mma(const DecodeParams& p, const Unit& un, const Item& it,
-                                            char* ring, const char* qslot, uint64_t* full,
-                                            uint64_t* empty, uint64_t* qempty, int n_tiles,
+// K/V tiles from the TMA ring: wait for stage `gt % STAGES`, hand out its
+// K and V tile addresses, release the stage after the tile is consumed.
+template <int STAGES, int STAGE_BYTES, int TILE_BYTES>
+struct RingTiles {
+  char* ring;
+  uint64_t* full;
+  uint64_t* empty;
+  unsigned int* err;
+  __device__ __forceinline__ bool acquire(int t, int gt, uint32_t& kbase, uint32_t& vbase) {
+    const int s = gt % STAGES;
+    if (!mbar_wait(&full[s], (gt / STAGES) & 1, err)) return false;
+    kbase = smem_addr(ring + s * STAGE_BYTES);
+    vbase = kbase + TILE_BYTES;
+    return true;
+  }
+  __device__ __forceinline__ void release(int gt) {
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) mbar_arrive(&empty[gt % STAGES]);
+  }
+};
+
+template <typename T, int D, int STAGES, class P, class Tiles>
+__device__ __forceinline__ bool consume_mma(const P& p, const Unit& un, const Item& it,
+                                            Tiles& tiles, const char* qslot,
+                                            uint64_t* qempty, int n_tiles,
                                             int& gt, int64_t qpos) {
   using Gm = Geom<T, D, STAGES>;
   const int lane = threadIdx.x & 31;
@@ -169,10 +192,8 @@ __device__ __forceinline__ bool consume_mma(const DecodeParams& p, const Unit& u
   bool ok = true;
 
   for (int t = 0; t < n_tiles; ++t, ++gt) {
-    const int s = gt % STAGES;
-    if (!mbar_wait(&full[s], (gt / STAGES) & 1, p.err)) { ok = false; ++gt; break; }
-    const uint32_t kbase = smem_addr(ring + s * Gm::kStageBytes);
-    const uint32_t vbase = kbase + Gm::kTileBytes;
+    uint32_t kbase, vbase;
+    if (!tiles.acquire(t, gt, kbase, vbase)) { ok = false; ++gt; break; }
 
     // ---- S = Q K^T (16 q-heads x 16 keys)
     float sacc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
@@ -260,8 +281,7 @@ __device__ __forceinline__ bool consume_mma(const DecodeParams& p, const Unit& u
         mma_16816(o[2 * j + 1], pl, v2, v3, (T*)nullptr);
       }
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[s]);
+    tiles.release(gt);
   }
 
   // ---- this warp's partial state -> global (rows < gcount only)
@@ -501,10 +521,237 @@ __global__ void __launch_bounds__(kThreads, MINB) kd_kernel(const __grid_constan
     if constexpr (sizeof(T) == 4)
       ok = consume_fma<D, STAGES>(p, un, it, ring, qring + qs * Gm::kQSlotBytes, ps, full, empty,
                                   &qempty[qs], n_tiles, gt, qpos);
-    else
-      ok = consume_mma<T, D, STAGES>(p, un, it, ring, qring + qs * Gm::kQSlotBytes, full, empty,
-                                     &qempty[qs], n_tiles, gt, qpos);
+    else {
+      RingTiles<STAGES, Gm::kStageBytes, Gm::kTileBytes> tiles{ring, full, empty, p.err};
+      ok = consume_mma<T, D, STAGES>(p, un, it, tiles, qring + qs * Gm::kQSlotBytes, &qempty[qs],
+                                     n_tiles, gt, qpos);
+    }
     if (!ok) return;  // the error word is set; remaining units are abandoned
+  }
+}
+
+// ---------------------------------------------------------------- KIVI decode
+// Fused dequantise-and-attend over a KIVI-packed prefix.  Same persistent
+// producer / consumer structure and the same tensor-core attention math as
+// kd_kernel; the tiles are different: the producer streams each 64-row tile's
+// packed codes, scales and zero points (cp.async.bulk, ~0.375 B/element at
+// 2 bits) and each consumer warp dequantises its own 16 rows into a swizzled
+// 16-bit tile in shared memory, bit-identical to the reference's
+// `q.float() * scale.float() + zero.float()` rounded to the cache dtype
+// (baselines/kivi_cache.py:72-78 in lzbaclz/HALO), before attending.
+struct KiviView {
+  const uint8_t* codes;
+  const char* scale;
+  const char* zero;
+  int64_t c_sb, c_sh;  // bytes
+  int64_t s_sb, s_sh;  // bytes
+};
+
+struct alignas(64) KiviParams {
+  CUtensorMap qmap;
+  Item items[kMaxItems];
+  KiviView kv[2];
+  const int64_t* q_pos;
+  float* m_part;
+  float* l_part;
+  float* o_part;
+  unsigned int* err;
+  int32_t B, H, H_kv, G, gblocks;
+  int32_t S;
+  int32_t n_items, n_units;
+  float scale_log2;
+};
+
+template <typename T, int D, int BITS>
+struct KGeom {
+  using Gm = Geom<T, D, 1>;
+  static constexpr int kCB = D * BITS / 8;        // code bytes per row
+  static constexpr int kGS = D / 32;              // groups per row
+  static constexpr int kCodeTile = 64 * kCB;
+  static constexpr int kSZTile = 64 * kGS * 2;
+  static constexpr int kPackBytes = kCodeTile + 2 * kSZTile;
+  static constexpr int kStages = 4;
+  static constexpr int kStageBytes = 2 * kPackBytes;
+  static constexpr int kDqBytes = 2 * Gm::kTileBytes;
+  static constexpr int kSmemBytes =
+      kDqBytes + 2 * Gm::kQSlotBytes + kStages * kStageBytes + 128 + 1024;
+  static_assert(kPackBytes % 16 == 0, "bulk copies need 16-byte multiples");
+};
+
+template <typename T>
+__device__ __forceinline__ uint32_t bits16(float x) {
+  const T h = Elem<T>::from_f32(x);
+  return static_cast<uint32_t>(*reinterpret_cast<const unsigned short*>(&h));
+}
+
+// rnd(fl32(c * s) + z): the reference's dequantisation of one code.
+template <typename T>
+__device__ __forceinline__ uint32_t dq1(uint32_t c, float s, float z) {
+  return bits16<T>(__fadd_rn(__fmul_rn((float)c, s), z));
+}
+
+// Warp w dequantises rows [16w, 16w+16) of one packed K or V tile into the
+// swizzled 64-row 16-bit tile `dq`.  Lane: row 16w + lane/2, half of the
+// row's columns by lane parity; one group (32 columns) at a time.
+template <typename T, int D, int BITS>
+__device__ __forceinline__ void dequant_rows(const char* pack, char* dq) {
+  using KG = KGeom<T, D, BITS>;
+  using Gm = typename KG::Gm;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int row = warp * 16 + (lane >> 1);
+  const int half = lane & 1;
+  constexpr int kCols = D / 2;
+  constexpr int kGroups = kCols / 32;
+  const uint8_t* codes = reinterpret_cast<const uint8_t*>(pack) + row * KG::kCB;
+  const T* sc = reinterpret_cast<const T*>(pack + KG::kCodeTile) + row * KG::kGS;
+  const T* ze = reinterpret_cast<const T*>(pack + KG::kCodeTile + KG::kSZTile) + row * KG::kGS;
+#pragma unroll
+  for (int j = 0; j < kGroups; ++j) {
+    const int col0 = half * kCols + j * 32;
+    const int g = col0 / 32;
+    const float s = Elem<T>::to_f32(sc[g]);
+    const float z = Elem<T>::to_f32(ze[g]);
+    uint32_t out[16];
+    if constexpr (BITS == 2) {
+      // 4-entry table of this group's values, selected per code with prmt
+      const uint32_t t01 = dq1<T>(0, s, z) | (dq1<T>(1, s, z) << 16);
+      const uint32_t t23 = dq1<T>(2, s, z) | (dq1<T>(3, s, z) << 16);
+      const uint2 cw = *reinterpret_cast<const uint2*>(codes + col0 / 4);
+      const uint32_t words[2] = {cw.x, cw.y};
+#pragma unroll
+      for (int w = 0; w < 2; ++w)
+#pragma unroll
+        for (int bb = 0; bb < 4; ++bb) {
+          const uint32_t B = (words[w] >> (8 * bb)) & 0xFFu;
+          const uint32_t y = (B & 3u) | ((B & 0xCu) << 6) | ((B & 0x30u) << 12) | ((B & 0xC0u) << 18);
+          out[w * 8 + bb * 2] = __byte_perm(t01, t23, (y & 0xFFFFu) * 0x22u + 0x1010u);
+          out[w * 8 + bb * 2 + 1] = __byte_perm(t01, t23, (y >> 16) * 0x22u + 0x1010u);
+        }
+    } else {
+      constexpr uint32_t kMask = (1u << BITS) - 1u;
+      constexpr int kPer = 8 / BITS;
+#pragma unroll
+      for (int e = 0; e < 32; e += 2) {
+        const int i0 = col0 + e, i1 = col0 + e + 1;
+        const uint32_t c0 = (codes[i0 / kPer] >> ((i0 % kPer) * BITS)) & kMask;
+        const uint32_t c1 = (codes[i1 / kPer] >> ((i1 % kPer) * BITS)) & kMask;
+        out[e / 2] = dq1<T>(c0, s, z) | (dq1<T>(c1, s, z) << 16);
+      }
+    }
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+      *reinterpret_cast<uint4*>(dq + swz<Gm::kInner>(row, col0 / 8 + c)) =
+          make_uint4(out[4 * c], out[4 * c + 1], out[4 * c + 2], out[4 * c + 3]);
+  }
+}
+
+// Tile provider: wait for a packed stage, dequantise this warp's rows of K
+// and V into the 16-bit tiles, free the packed stage at once.
+template <typename T, int D, int BITS>
+struct DequantTiles {
+  using KG = KGeom<T, D, BITS>;
+  char* stages;
+  char* kdq;
+  char* vdq;
+  uint64_t* full;
+  uint64_t* empty;
+  unsigned int* err;
+  __device__ __forceinline__ bool acquire(int t, int gt, uint32_t& kbase, uint32_t& vbase) {
+    const int s = gt % KG::kStages;
+    if (!mbar_wait(&full[s], (gt / KG::kStages) & 1, err)) return false;
+    const char* st = stages + s * KG::kStageBytes;
+    dequant_rows<T, D, BITS>(st, kdq);
+    dequant_rows<T, D, BITS>(st + KG::kPackBytes, vdq);
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) mbar_arrive(&empty[s]);
+    kbase = smem_addr(kdq);
+    vbase = smem_addr(vdq);
+    return true;
+  }
+  __device__ __forceinline__ void release(int) { __syncwarp(); }
+};
+
+template <typename T, int D, int BITS>
+__global__ void __launch_bounds__(kThreads, 2) kk_kernel(const __grid_constant__ KiviParams p) {
+  using KG = KGeom<T, D, BITS>;
+  using Gm = typename KG::Gm;
+  constexpr int STAGES = KG::kStages;
+  extern __shared__ char smem_raw[];
+  char* kdq = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                      ~uintptr_t(1023));
+  char* vdq = kdq + Gm::kTileBytes;
+  char* qring = kdq + KG::kDqBytes;
+  char* stages = qring + 2 * Gm::kQSlotBytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(stages + STAGES * KG::kStageBytes);
+  uint64_t* empty = full + STAGES;
+  uint64_t* qfull = empty + STAGES;
+  uint64_t* qempty = qfull + 2;
+
+  const int tid = threadIdx.x;
+  if (tid == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kConsumerWarps);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&qfull[s], 1);
+      mbar_init(&qempty[s], kConsumerWarps);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+  const int warp = tid >> 5, lane = tid & 31;
+
+  if (warp == kConsumerWarps) {
+    if (lane == 0) {
+      int gt = 0, ut = 0;
+      for (int u = blockIdx.x; u < p.n_units; u += gridDim.x, ++ut) {
+        const Unit un = decode_unit(p, u, Gm::kGpb);
+        const Item& it = p.items[un.item];
+        const int qs = ut & 1;
+        if (ut >= 2 && !mbar_wait(&qempty[qs], ((ut >> 1) & 1) ^ 1, p.err)) return;
+        mbar_arrive_expect_tx(&qfull[qs], Gm::kNBox * Gm::kGpb * Gm::kInner);
+#pragma unroll
+        for (int bx = 0; bx < Gm::kNBox; ++bx)
+          tma_load_3d(qring + qs * Gm::kQSlotBytes + bx * Gm::kGpb * Gm::kInner, &p.qmap,
+                      bx * Gm::kBoxElems, un.h_kv * p.G + un.gbase, un.b, &qfull[qs]);
+        const int n_tiles = (it.rows + kBlockN - 1) / kBlockN;
+        for (int t = 0; t < n_tiles; ++t, ++gt) {
+          const int s = gt % STAGES;
+          if (gt >= STAGES && !mbar_wait(&empty[s], ((gt / STAGES) & 1) ^ 1, p.err)) return;
+          const int64_t r0 = it.row0 + t * kBlockN;
+          char* dst = stages + s * KG::kStageBytes;
+          mbar_arrive_expect_tx(&full[s], KG::kStageBytes);
+#pragma unroll
+          for (int w = 0; w < 2; ++w) {
+            const KiviView& kv = p.kv[w];
+            char* d = dst + w * KG::kPackBytes;
+            bulk_g2s(d, kv.codes + un.b * kv.c_sb + un.h_kv * kv.c_sh + r0 * KG::kCB,
+                     KG::kCodeTile, &full[s]);
+            bulk_g2s(d + KG::kCodeTile, kv.scale + un.b * kv.s_sb + un.h_kv * kv.s_sh + r0 * KG::kGS * 2,
+                     KG::kSZTile, &full[s]);
+            bulk_g2s(d + KG::kCodeTile + KG::kSZTile,
+                     kv.zero + un.b * kv.s_sb + un.h_kv * kv.s_sh + r0 * KG::kGS * 2,
+                     KG::kSZTile, &full[s]);
+          }
+        }
+      }
+    }
+    return;
+  }
+
+  int gt = 0, ut = 0;
+  for (int u = blockIdx.x; u < p.n_units; u += gridDim.x, ++ut) {
+    const Unit un = decode_unit(p, u, Gm::kGpb);
+    const Item& it = p.items[un.item];
+    const int qs = ut & 1;
+    if (!mbar_wait(&qfull[qs], (ut >> 1) & 1, p.err)) return;
+    const int64_t qpos = (it.causal && p.q_pos != nullptr) ? p.q_pos[un.b] : INT64_MAX;
+    const int n_tiles = (it.rows + kBlockN - 1) / kBlockN;
+    DequantTiles<T, D, BITS> tiles{stages, kdq, vdq, full, empty, p.err};
+    if (!consume_mma<T, D, STAGES>(p, un, it, tiles, qring + qs * Gm::kQSlotBytes, &qempty[qs],
+                                   n_tiles, gt, qpos))
+      return;
   }
 }
 
@@ -1140,6 +1387,99 @@ static int encode_q_map(const halo_decode_problem_t& pb, CUtensorMap* out) {
   return HALO_OK;
 }
 
+// ---------------------------------------------------------------- KIVI host side
+template <typename T, int D, int BITS>
+static int kk_ctas_per_sm() {
+  using KG = KGeom<T, D, BITS>;
+  static std::once_flag once[64];
+  static int cache[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::call_once(once[dev & 63], [&] {
+    cudaFuncSetAttribute(kk_kernel<T, D, BITS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         KG::kSmemBytes);
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kk_kernel<T, D, BITS>, kThreads,
+                                                      KG::kSmemBytes) != cudaSuccess || n <= 0)
+      n = 1;
+    cache[dev & 63] = n;
+  });
+  return cache[dev & 63];
+}
+
+template <typename T, int D, int BITS>
+static int launch_kk(const KiviParams& prm, cudaStream_t st) {
+  using KG = KGeom<T, D, BITS>;
+  const int64_t grid_max = (int64_t)device_sms() * kk_ctas_per_sm<T, D, BITS>();
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(prm.n_units, grid_max));
+  kk_kernel<T, D, BITS><<<grid, kThreads, KG::kSmemBytes, st>>>(prm);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? HALO_OK : cuda_fail(e, "kk_kernel launch");
+}
+
+template <typename T>
+static int dispatch_kk_t(int D, int bits, const KiviParams& prm, cudaStream_t st) {
+  if (D == 128) {
+    if (bits == 2) return launch_kk<T, 128, 2>(prm, st);
+    if (bits == 4) return launch_kk<T, 128, 4>(prm, st);
+    if (bits == 8) return launch_kk<T, 128, 8>(prm, st);
+  } else if (D == 64) {
+    if (bits == 2) return launch_kk<T, 64, 2>(prm, st);
+    if (bits == 4) return launch_kk<T, 64, 4>(prm, st);
+    if (bits == 8) return launch_kk<T, 64, 8>(prm, st);
+  }
+  return fail(HALO_ERR_UNSUPPORTED, "KIVI decode: D %d bits %d", D, bits);
+}
+
+// Rows per work item for the KIVI decode: the same cost model as the plain
+// decode planner (persistent makespan + merge traffic), one segment.
+static int64_t kivi_split_tiles(const halo_decode_problem_t* p, int64_t rows) {
+  const int G = p->H / p->H_kv;
+  const int64_t pairs = (int64_t)p->B * p->H_kv * ((G + 15) / 16);
+  const int64_t grid = (int64_t)device_sms() * 2;
+  const int64_t tiles = ceil_div64(rows, kBlockN);
+  if (p->max_split_rows > 0) return std::max<int64_t>(1, p->max_split_rows / kBlockN);
+  double best = 1e300;
+  int64_t split = tiles;
+  for (int64_t cand = std::max<int64_t>(1, tiles); cand >= 1;) {
+    const int64_t items = ceil_div64(tiles, cand);
+    const double span = (double)ceil_div64(items * pairs, grid) * ((double)std::min(cand, tiles) + 1.5);
+    const double merge = (double)p->B * p->H * items * kConsumerWarps * (p->Dv + 2) * 8.0 /
+                         (2.0 * kBlockN * p->D * 0.375 * (double)grid);
+    if (items <= kMaxItems && span + merge < best * (1.0 - 1e-3)) {
+      best = span + merge;
+      split = cand;
+    }
+    if (cand == 1) break;
+    cand = cand > 32 ? cand - std::max<int64_t>(1, cand / 32) : cand - 1;
+  }
+  return split;
+}
+
+static int validate_kivi(const halo_decode_problem_t* p, const halo_kivi_tensor_t* k,
+                         const halo_kivi_tensor_t* v, int32_t rows, int32_t bits) {
+  if (!p || !k || !v) return fail(HALO_ERR_INVALID_ARG, "NULL argument");
+  if (p->B <= 0 || p->H <= 0 || p->H_kv <= 0 || p->H % p->H_kv || rows < 0)
+    return fail(HALO_ERR_INVALID_ARG, "bad KIVI decode shape");
+  if (p->dtype != HALO_DTYPE_F16 && p->dtype != HALO_DTYPE_BF16)
+    return fail(HALO_ERR_UNSUPPORTED, "KIVI decode needs fp16/bf16");
+  if ((p->D != 64 && p->D != 128) || p->Dv != p->D)
+    return fail(HALO_ERR_UNSUPPORTED, "KIVI decode supports head_dim 64 and 128");
+  if (bits != 2 && bits != 4 && bits != 8) return fail(HALO_ERR_UNSUPPORTED, "bits %d", bits);
+  for (const halo_kivi_tensor_t* t : {k, v}) {
+    if (rows > 0 && (!t->codes || !t->scale || !t->zero))
+      return fail(HALO_ERR_INVALID_ARG, "NULL KIVI tensor");
+    if (t->t_cap % kBlockN || t->t_cap < ceil_div64(rows, kBlockN) * kBlockN)
+      return fail(HALO_ERR_INVALID_ARG, "t_cap must be a multiple of 64 covering the rows");
+    if ((reinterpret_cast<uintptr_t>(t->codes) | reinterpret_cast<uintptr_t>(t->scale) |
+         reinterpret_cast<uintptr_t>(t->zero)) & 15 ||
+        t->codes_stride_b % 16 || t->codes_stride_h % 16 || (t->sz_stride_b * 2) % 16 ||
+        (t->sz_stride_h * 2) % 16)
+      return fail(HALO_ERR_MISALIGNED, "KIVI tensors need 16-byte aligned bases and strides");
+  }
+  return HALO_OK;
+}
+
 }  // namespace halo
 
 using namespace halo;
@@ -1272,3 +1612,89 @@ extern "C" int32_t halo_device_error(int32_t* code_out, int32_t clear) {
 }
 
 extern "C" int32_t halo_version(void) { return 100; }
+
+extern "C" int64_t halo_kivi_decode_workspace_bytes(const halo_decode_problem_t* problem,
+                                                    int32_t rows) {
+  if (!problem || rows < 0) return fail(HALO_ERR_INVALID_ARG, "bad arguments");
+  const int64_t split = kivi_split_tiles(problem, rows);
+  const int64_t items = rows > 0 ? ceil_div64(ceil_div64(rows, kBlockN), split) : 0;
+  return workspace_for(problem, (int)(items * kConsumerWarps));
+}
+
+extern "C" int32_t halo_kivi_decode(const halo_decode_problem_t* problem,
+                                    const halo_kivi_tensor_t* k, const halo_kivi_tensor_t* v,
+                                    int32_t rows, int32_t bits, int64_t start, int32_t causal,
+                                    void* workspace, int64_t workspace_bytes,
+                                    const halo_merge_args_t* merge, halo_stream_t stream) {
+  int rc = validate_kivi(problem, k, v, rows, bits);
+  if (rc != HALO_OK) return rc;
+  rc = validate_merge(merge, problem->Dv);
+  if (rc != HALO_OK) return rc;
+  if (causal && !problem->q_pos) return fail(HALO_ERR_INVALID_ARG, "causal needs q_pos");
+  const halo_decode_problem_t& pb = *problem;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int64_t split = kivi_split_tiles(problem, rows);
+  const int64_t tiles = ceil_div64(rows, kBlockN);
+  const int n_items = rows > 0 ? (int)ceil_div64(tiles, split) : 0;
+  if (n_items > kMaxItems) return fail(HALO_ERR_UNSUPPORTED, "too many KIVI work items");
+  const int S = n_items * kConsumerWarps;
+  const int64_t need = workspace_for(problem, S);
+  if (S > 0 && (!workspace || workspace_bytes < need))
+    return fail(HALO_ERR_WORKSPACE, "workspace %lld bytes < required %lld",
+                (long long)workspace_bytes, (long long)need);
+  if (reinterpret_cast<uintptr_t>(workspace) & 255)
+    return fail(HALO_ERR_MISALIGNED, "workspace must be 256-byte aligned");
+  const int64_t R = (int64_t)pb.B * pb.H;
+  char* ws = static_cast<char*>(workspace);
+  float* m_part = reinterpret_cast<float*>(ws);
+  float* l_part = reinterpret_cast<float*>(ws + align256(R * S * 4));
+  float* o_part = reinterpret_cast<float*>(ws + 2 * align256(R * S * 4));
+  if (S > 0) {
+    static thread_local KiviParams prm;
+    rc = encode_q_map(pb, &prm.qmap);
+    if (rc != HALO_OK) return rc;
+    const int G = pb.H / pb.H_kv;
+    prm.q_pos = pb.q_pos;
+    prm.m_part = m_part;
+    prm.l_part = l_part;
+    prm.o_part = o_part;
+    prm.err = device_error_ptr();
+    prm.B = pb.B;
+    prm.H = pb.H;
+    prm.H_kv = pb.H_kv;
+    prm.G = G;
+    prm.gblocks = (G + 15) / 16;
+    prm.S = S;
+    prm.scale_log2 = pb.scale * kLog2e;
+    prm.n_items = n_items;
+    prm.n_units = (int32_t)((int64_t)pb.B * pb.H_kv * prm.gblocks * n_items);
+    const halo_kivi_tensor_t* src[2] = {k, v};
+    for (int w = 0; w < 2; ++w) {
+      prm.kv[w].codes = src[w]->codes;
+      prm.kv[w].scale = static_cast<const char*>(src[w]->scale);
+      prm.kv[w].zero = static_cast<const char*>(src[w]->zero);
+      prm.kv[w].c_sb = src[w]->codes_stride_b;
+      prm.kv[w].c_sh = src[w]->codes_stride_h;
+      prm.kv[w].s_sb = src[w]->sz_stride_b * 2;
+      prm.kv[w].s_sh = src[w]->sz_stride_h * 2;
+    }
+    for (int i = 0; i < n_items; ++i) {
+      Item& it = prm.items[i];
+      it.seg = 0;
+      it.row0 = (int32_t)(i * split * kBlockN);
+      it.rows = (int32_t)std::min<int64_t>(split * kBlockN, rows - it.row0);
+      it.start = start + it.row0;
+      it.slot = i * kConsumerWarps;
+      it.causal = causal;
+      it.b_bcast = 0;
+    }
+    if (pb.event_begin) cudaEventRecord(static_cast<cudaEvent_t>(pb.event_begin), st);
+    rc = pb.dtype == HALO_DTYPE_F16 ? dispatch_kk_t<__half>(pb.D, bits, prm, st)
+                                    : dispatch_kk_t<__nv_bfloat16>(pb.D, bits, prm, st);
+    if (rc != HALO_OK) return rc;
+    if (pb.event_end) cudaEventRecord(static_cast<cudaEvent_t>(pb.event_end), st);
+  }
+  MergeParams mp = merge_params(merge, pb.B, pb.H, pb.Dv, S, m_part, l_part, o_part, 1, S, pb.Dv,
+                                (int64_t)S * pb.Dv);
+  return launch_merge(mp, st);
+}

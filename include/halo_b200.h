@@ -153,6 +153,53 @@ int32_t halo_chunked_decode_noalloc(const halo_decode_problem_t* problem,
                                     const halo_kv_chunk_t* chunks, int32_t n_chunks,
                                     const halo_merge_args_t* merge, halo_stream_t stream);
 
+/* ------------------------------------------------------------------ KIVI */
+
+/* Per-group round-to-nearest quantisation of x (B, H, T, D) (element strides
+ * x_sb, x_sh, x_st, fp16 or bf16) along head_dim in groups of `group`, to
+ * `bits` (2/4/8) codes packed 8/bits per byte (code i of a row at byte
+ * i*bits/8, bit (i*bits)%8; byte strides c_sb/c_sh/c_st) plus per-group
+ * scale and zero in x's dtype (element strides s_sb/s_sh/s_st).  Bit-exact
+ * with _quantize_per_group (baselines/kivi_cache.py:44-69), whose every op
+ * rounds to the tensor dtype. */
+int32_t halo_kivi_quantize(const void* x, int64_t x_sb, int64_t x_sh, int64_t x_st,
+                           int32_t B, int32_t H, int32_t T, int32_t D, int32_t dtype,
+                           int32_t bits, int32_t group, uint8_t* codes, int64_t c_sb,
+                           int64_t c_sh, int64_t c_st, void* scale, void* zero, int64_t s_sb,
+                           int64_t s_sh, int64_t s_st, halo_stream_t stream);
+
+/* Inverse: x = rnd(fl32(code * scale) + zero), bit-exact with
+ * _dequantize_per_group (baselines/kivi_cache.py:72-78). */
+int32_t halo_kivi_dequantize(const uint8_t* codes, int64_t c_sb, int64_t c_sh, int64_t c_st,
+                             const void* scale, const void* zero, int64_t s_sb, int64_t s_sh,
+                             int64_t s_st, int32_t B, int32_t H, int32_t T, int32_t D,
+                             int32_t dtype, int32_t bits, int32_t group, void* x, int64_t x_sb,
+                             int64_t x_sh, int64_t x_st, halo_stream_t stream);
+
+/* A KIVI-packed K or V: codes (B, H_kv, t_cap, D*bits/8) bytes with
+ * contiguous rows, scale/zero (B, H_kv, t_cap, D/32) in the problem dtype
+ * with contiguous rows; t_cap a multiple of 64 (tiles are read whole). */
+typedef struct halo_kivi_tensor {
+  const uint8_t* codes;
+  const void* scale;
+  const void* zero;
+  int64_t codes_stride_b, codes_stride_h;   /* bytes */
+  int64_t sz_stride_b, sz_stride_h;         /* elements */
+  int64_t t_cap;
+} halo_kivi_tensor_t;
+
+int64_t halo_kivi_decode_workspace_bytes(const halo_decode_problem_t* problem, int32_t rows);
+
+/* Fused 2/4/8-bit dequantise-and-attend decode over rows [0, rows) of a
+ * KIVI-packed K/V (group 32, head_dim 64 or 128, fp16/bf16), rows at global
+ * positions start + t, then the LSE merge described by `merge`.  Replaces
+ * the per-step full dequantisation of KIVICache.update + SDPA
+ * (baselines/kivi_cache.py:187-195). */
+int32_t halo_kivi_decode(const halo_decode_problem_t* problem, const halo_kivi_tensor_t* k,
+                         const halo_kivi_tensor_t* v, int32_t rows, int32_t bits, int64_t start,
+                         int32_t causal, void* workspace, int64_t workspace_bytes,
+                         const halo_merge_args_t* merge, halo_stream_t stream);
+
 /* ------------------------------------------------------------------ scorer */
 
 /* Per-page channel-wise min/max of K (B, H_kv, T, D) for pages

@@ -29,7 +29,8 @@ def round_to(x: np.ndarray, dtype: str) -> np.ndarray:
     raise ValueError(dtype)
 
 
-def quantize_per_group(x: np.ndarray, *, bits: int, group_size: int, dtype: str):
+def quantize_per_group(x: np.ndarray, *, bits: int, group_size: int, dtype: str,
+                       unsigned_codes: bool = False):
     """Quantise along the last axis in groups of ``group_size``.
 
     Follows ``baselines/kivi_cache.py:44-69``: ``x_min/x_max`` per group
@@ -40,7 +41,9 @@ def quantize_per_group(x: np.ndarray, *, bits: int, group_size: int, dtype: str)
     group) becomes code 0 as torch's int8 cast gives it.
 
     ``x``: float32 array of fp16/bf16 values, last dim divisible by
-    ``group_size``.  Returns ``(codes int8 (..., G, gs), scale (..., G, 1),
+    ``group_size``.  The reference casts codes with ``.to(torch.int8)``, so
+    8-bit codes 128..255 wrap negative there; ``unsigned_codes=True`` keeps
+    them as uint8 0..255 (what a byte-packed store holds).  Returns ``(codes int8 (..., G, gs), scale (..., G, 1),
     zero (..., G, 1))`` with scale/zero as float32 values of ``dtype``.
     """
     qmax = (1 << bits) - 1
@@ -60,7 +63,8 @@ def quantize_per_group(x: np.ndarray, *, bits: int, group_size: int, dtype: str)
     with np.errstate(divide="ignore", invalid="ignore"):
         u = round_to(t / scale, dtype)
     r = np.rint(u)
-    codes = np.where(np.isnan(r), 0.0, np.clip(r, 0, qmax)).astype(np.int8)
+    codes = np.where(np.isnan(r), 0.0, np.clip(r, 0, qmax))
+    codes = codes.astype(np.uint8) if unsigned_codes else codes.astype(np.int16).astype(np.int8)
     return codes, scale, zero
 
 
