@@ -12,10 +12,15 @@ Total context is fixed as N grows (strong scaling).  K/V are seeded N(0,1)
 synthetic data resident in HBM; the working set per GPU (4.3 GB / N) is far
 larger than L2, so no flush is needed between steps.
 
-``--workload cfg2`` runs BASELINE config 2's tiered decode step instead (one
-GPU): 32 layers of B8 / 32 q-heads / 8 KV heads / 32K context, chunks of 1024,
-hot chunks resident, top-8 cold chunks picked by the chunk scorer and
-refetched from pinned host memory each step.
+``--seq-len T`` shrinks the cfg5 context (a multiple of 4096 x N) for small
+profiling captures; the line then names the reduced workload.
+
+``--workload cfg4`` runs BASELINE config 4 instead (one GPU): KIVI 2-bit
+decode of B4 / 32 q-heads / 8 KV heads / head_dim 128 over a 65536-token
+context -- 65408 quantised rows (packed 2-bit codes, fp16 scale and zero per
+group of 32 along head_dim) plus the 128 most recent rows in fp16 -- through
+``KIVICache.compute_attention`` (fused dequant-and-attend kernel, then the
+recent rows folded in by the split-KV kernel).
 
 Rank 0 prints one JSON line.  ``--impl reference`` times the reference's CPU
 implementation of the path (its torch ops restated in ``oracle/``) on this
@@ -219,9 +224,11 @@ def run_reference(args):
 
 def _cfg5_config(n: int):
     c = CFG5
-    return {"workload": "cfg5: 1M-token sequence-sharded decode, one Llama-3-70B-shaped "
-                        "attention layer (64 q-heads / 8 KV heads, head_dim 128), "
-                        "256 chunks x 4096",
+    n_chunks = c["T"] // c["chunk"]
+    name = ("cfg5: 1M-token sequence-sharded decode" if c["T"] == 1 << 20 else
+            f"cfg5 reduced to {c['T']} tokens (profiling case)")
+    return {"workload": f"{name}, one Llama-3-70B-shaped attention layer (64 q-heads / "
+                        f"8 KV heads, head_dim 128), {n_chunks} chunks x {c['chunk']}",
             "global_batch": c["B"], "seq_len": c["T"], "chunk": c["chunk"],
             "parallelism": f"sequence-sharded x{n} (NCCL all-gather of (o, lse) + LSE merge)"
                            if n > 1 else "single GPU",
@@ -234,6 +241,7 @@ def run_ours_cfg5(args):
     import torch.distributed as dist
     world, rank, local = _dist_setup(args.gpus)
     dev = torch.device("cuda", local)
+    from halo_b200 import _lib as L
     from halo_b200.sharded import ShardedDecoder
     q, k, v, start = _cfg5_shard(world, rank, dev)
     dec = ShardedDecoder(k, v, start=start, chunk_size=CFG5["chunk"],
@@ -260,12 +268,14 @@ def run_ours_cfg5(args):
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     torch.cuda.synchronize()
+    n0 = L.launch_count()
     with ClockSampler(local) as clocks:
         t0.record()
         for i in range(K):
             dec(q, out=out, lse=lse, events=(ev_b[i].cuda_event, ev_e[i].cuda_event))
         t1.record()
         torch.cuda.synchronize()
+    launches = L.launch_count() - n0
     barrier()
     ms = t0.elapsed_time(t1)
     kd_ms = sum(ev_b[i].elapsed_time(ev_e[i]) for i in range(K)) / K
@@ -326,12 +336,189 @@ def run_ours_cfg5(args):
                         "h2d_bytes_per_step": q.numel() * q.element_size(),
                         "d2h_bytes_per_step": out.numel() * out.element_size()},
                 "clocks": clocks.summary(),
-                "gpu_launches": K * dec.launches_per_call}
+                "gpu_launches": launches}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier(device_ids=[local])
         dist.destroy_process_group()
     return line
+
+
+# ---------------------------------------------------------------- cfg4 (KIVI)
+CFG4 = dict(B=4, H=32, H_kv=8, D=128, T=65536, bits=2, group=32, recent=128)
+METRIC4 = "KIVI 2-bit decode tokens/s & achieved HBM GB/s (packed bytes), B4 x 64K ctx, 1 B200"
+
+
+def _outlier_keys(k, seed: int):
+    """Scale 4 seeded channels of every KV head by 10 (BASELINE key outliers)."""
+    import torch
+    g = torch.Generator().manual_seed(seed)
+    for h in range(k.shape[1]):
+        idx = torch.randperm(k.shape[-1], generator=g)[:4].to(k.device)
+        k[:, h, :, idx] *= 10
+    return k
+
+
+def _cfg4_inputs(dev, rows=None, batch=None):
+    import torch
+    c = CFG4
+    B = c["B"] if batch is None else batch
+    T = c["T"] if rows is None else rows
+    g = torch.Generator(device=dev).manual_seed(4)
+    k = torch.randn(B, c["H_kv"], T, c["D"], device=dev, generator=g)
+    v = torch.randn(B, c["H_kv"], T, c["D"], device=dev, generator=g)
+    q = torch.randn(B, c["H"], 1, c["D"], device=dev, generator=g)
+    k = _outlier_keys(k, 44)
+    return q.half(), k.half(), v.half()
+
+
+def _cfg4_bytes():
+    """Packed bytes the fused kernel must read per step: 2-bit codes plus an
+    fp16 scale and zero per group of 32, for K and V, over the quantised
+    prefix."""
+    c = CFG4
+    rows = c["T"] - c["recent"]
+    per_row = c["D"] * c["bits"] // 8 + (c["D"] // c["group"]) * 2 * 2
+    return 2 * c["B"] * c["H_kv"] * rows * per_row
+
+
+def _cfg4_config():
+    c = CFG4
+    return {"workload": "cfg4: KIVI 2-bit decode, B4, 32 q-heads / 8 KV heads, head_dim 128, "
+                        "65536 ctx (65408 quantised + 128 fp16 recent), group 32, fp16 "
+                        "scale/zero, keys with 4 outlier channels x10 per head",
+            "global_batch": c["B"], "seq_len": c["T"], "parallelism": "single GPU",
+            "l2": "packed prefix %.0f MB > L2 (126 MB); no flush" % (_cfg4_bytes() / 1e6)}
+
+
+def cpu_baseline_cfg4(budget_s: float = 15.0):
+    """The reference's CPU decode step for cfg4 -- dequantise the whole
+    prefix (its update() does so on every call) and attend in fp32 -- through
+    the oracle port, on a sample of rows of one batch element, scaled."""
+    import numpy as np
+    import torch
+    from oracle import attention as OA
+    from oracle import kivi as OK
+    torch.set_num_threads(os.cpu_count() or 1)
+    c = CFG4
+
+    def prepare(rows):
+        q, k, v = _cfg4_inputs(torch.device("cpu"), rows=rows, batch=1)
+        return (q.float(),
+                OK.quantize_per_group(k.float().numpy(), bits=2, group_size=32, dtype="f16"),
+                OK.quantize_per_group(v.float().numpy(), bits=2, group_size=32, dtype="f16"))
+
+    def run(prep):
+        q, (ck, sk, zk), (cv, sv, zv) = prep
+        t0 = time.perf_counter()
+        kd = torch.from_numpy(OK.dequantize_per_group(ck, sk, zk, dtype="f16"))
+        vd = torch.from_numpy(OK.dequantize_per_group(cv, sv, zv, dtype="f16"))
+        OA.chunk_attention(q, kd, vd)
+        return time.perf_counter() - t0
+
+    t1 = run(prepare(1024))
+    rows = int(max(1024, min(c["T"], budget_s / 3 / max(t1, 1e-4) * 1024)))
+    rows = rows // 1024 * 1024
+    prep = prepare(rows)
+    t = statistics.median(run(prep) for _ in range(3))
+    step_s = t * (c["T"] / rows) * c["B"]
+    return {"value": c["B"] / step_s, "unit": "tokens/s", "cores": torch.get_num_threads(),
+            "kind": "port",
+            "sample": f"1 of {c['B']} batch rows x {rows} of {c['T']} tokens (dequantise K and "
+                      f"V + fp32 attention), median of 3, scaled x{c['B'] * c['T'] / rows:.0f}",
+            "s_per_step": step_s}
+
+
+def run_ours_cfg4(args):
+    import torch
+    from halo_b200 import _lib as L
+    from halo_b200.baselines.kivi_cache import KIVICache
+    if args.gpus != 1 or int(os.environ.get("WORLD_SIZE", "1")) != 1:
+        raise SystemExit("cfg4 runs on one GPU")
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    c = CFG4
+    q, k, v = _cfg4_inputs(dev)
+    cache = KIVICache(bits=c["bits"], group_size=c["group"], residual_length=c["recent"],
+                      fused_attention=True)
+    cache.update(k, v, layer_idx=0)
+    del k, v
+    torch.cuda.synchronize()
+    for _ in range(args.warmup):
+        cache.compute_attention(q, layer_idx=0)
+    K = args.steps
+    ev_b = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    ev_e = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    for e in ev_b + ev_e:
+        e.record()
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n0 = L.launch_count()
+    with ClockSampler(0) as clocks:
+        t0.record()
+        for i in range(K):
+            cache.compute_attention(q, layer_idx=0, events=(ev_b[i].cuda_event, ev_e[i].cuda_event))
+        t1.record()
+        torch.cuda.synchronize()
+    launches = L.launch_count() - n0
+    ms_step = t0.elapsed_time(t1) / K
+    kk_ms = sum(ev_b[i].elapsed_time(ev_e[i]) for i in range(K)) / K
+
+    q_host = q.cpu().pin_memory()
+    out_host = torch.empty(c["B"], c["H"], 1, c["D"], dtype=q.dtype).pin_memory()
+    q_dev = torch.empty_like(q)
+
+    def e2e_step():
+        q_dev.copy_(q_host, non_blocking=True)
+        o = cache.compute_attention(q_dev, layer_idx=0)
+        out_host.copy_(o, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+
+    for _ in range(3):
+        e2e_step()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(K):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / K
+
+    nbytes = _cfg4_bytes()
+    peak, peak_kind = _peaks()
+    achieved = nbytes / (kk_ms / 1e3) / 1e9
+    cpu = None if args.no_cpu_baseline else cpu_baseline_cfg4()
+    line = {"metric": METRIC4, "value": c["B"] / (ms_step / 1e3), "unit": "tokens/s",
+            "n_gpus": 1, "steps": K, "warmup": args.warmup, "ms_per_step": ms_step,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+            "data": "synthetic", "config": _cfg4_config(),
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "peak_kind": f"of {peak_kind}",
+                         "kernel": "kk_kernel (fused 2-bit dequant-and-attend)",
+                         "bytes_per_launch": nbytes, "traffic": None},
+            "cpu_baseline": cpu and {kk: cpu[kk] for kk in ("value", "unit", "cores", "kind",
+                                                           "sample")},
+            "e2e": {"value": c["B"] / (e2e_ms / 1e3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": q.numel() * q.element_size(),
+                    "d2h_bytes_per_step": out_host.numel() * out_host.element_size()},
+            "clocks": clocks.summary(), "gpu_launches": launches}
+    print(json.dumps(line), flush=True)
+    return line
+
+
+def run_reference_cfg4(args):
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    cpu = cpu_baseline_cfg4(budget_s=max(10.0, 150.0 / max(1, args.steps + args.warmup)))
+    v = cpu["value"]
+    line = {"impl": "reference", "metric": METRIC4, "value": v, "unit": "tokens/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": cpu["s_per_step"] * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f16", "data": "synthetic", "config": _cfg4_config(),
+            "cpu_baseline": {kk: cpu[kk] for kk in ("value", "unit", "cores", "kind", "sample")},
+            "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
 
 
 def main():
@@ -340,16 +527,21 @@ def main():
     ap.add_argument("--steps", type=int, default=300)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["cfg5", "cfg2"], default="cfg5")
+    ap.add_argument("--workload", choices=["cfg5", "cfg4"], default="cfg5")
+    ap.add_argument("--seq-len", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
     if args.impl == "reference":
-        return run_reference(args)
-    if args.workload == "cfg2":
-        from halo_b200 import tiered_bench
-        return tiered_bench.run(args)
+        return run_reference_cfg4(args) if args.workload == "cfg4" else run_reference(args)
+    if args.workload == "cfg4":
+        return run_ours_cfg4(args)
+    if args.seq_len:
+        n = args.gpus * CFG5["chunk"]
+        if args.seq_len % n:
+            raise SystemExit(f"--seq-len must be a multiple of {n}")
+        CFG5["T"] = args.seq_len
     return run_ours_cfg5(args)
 
 

@@ -74,6 +74,23 @@ class KiviTensor(ctypes.Structure):
                 ("t_cap", ctypes.c_int64)]
 
 
+class PrefillProblem(ctypes.Structure):
+    _fields_ = [("B", ctypes.c_int32), ("H", ctypes.c_int32), ("H_kv", ctypes.c_int32),
+                ("T_q", ctypes.c_int32), ("D", ctypes.c_int32), ("dtype", ctypes.c_int32),
+                ("q", ctypes.c_void_p), ("q_stride_b", ctypes.c_int64),
+                ("q_stride_h", ctypes.c_int64), ("q_stride_t", ctypes.c_int64),
+                ("q_pos0", ctypes.c_int64), ("scale", ctypes.c_float),
+                ("event_begin", ctypes.c_void_p), ("event_end", ctypes.c_void_p)]
+
+
+class PrefillOut(ctypes.Structure):
+    _fields_ = [("mode", ctypes.c_int32), ("out_dtype", ctypes.c_int32),
+                ("out", ctypes.c_void_p), ("out_stride_b", ctypes.c_int64),
+                ("out_stride_h", ctypes.c_int64), ("out_stride_t", ctypes.c_int64),
+                ("lse", ctypes.c_void_p), ("m", ctypes.c_void_p), ("l", ctypes.c_void_p),
+                ("o", ctypes.c_void_p)]
+
+
 # name -> (restype, argtypes); must match include/halo_b200.h
 SIGNATURES = {
     "halo_decode_workspace_bytes": (ctypes.c_int64, [ctypes.POINTER(DecodeProblem),
@@ -129,7 +146,11 @@ SIGNATURES = {
                                            ctypes.c_void_p]),
     "halo_last_error_string": (ctypes.c_char_p, []),
     "halo_device_error": (ctypes.c_int32, [ctypes.POINTER(ctypes.c_int32), ctypes.c_int32]),
+    "halo_prefill_attention": (ctypes.c_int32, [ctypes.POINTER(PrefillProblem),
+                                                ctypes.POINTER(KVChunk), ctypes.c_int32,
+                                                ctypes.POINTER(PrefillOut), ctypes.c_void_p]),
     "halo_version": (ctypes.c_int32, []),
+    "halo_launch_count": (ctypes.c_uint64, []),
 }
 
 _lib = None
@@ -165,6 +186,11 @@ def device_error(clear: bool = True) -> int:
     code = ctypes.c_int32(0)
     check(lib().halo_device_error(ctypes.byref(code), int(clear)), "halo_device_error")
     return code.value
+
+
+def launch_count() -> int:
+    """Kernels this library has launched in this process."""
+    return int(lib().halo_launch_count())
 
 
 def stream_handle(device: torch.device) -> int:

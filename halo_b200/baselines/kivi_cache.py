@@ -175,6 +175,7 @@ class KIVICache(_BaseCache):
         self._k_quant: list = []
         self._v_quant: list = []
         self._n_seen: list = []
+        self._ones_cache: dict = {}
 
     @classmethod
     def from_memory_ratio(cls, *, memory_ratio: int, **kw) -> "KIVICache":
@@ -220,10 +221,12 @@ class KIVICache(_BaseCache):
         return (torch.cat([self._k_quant[layer_idx].dequantized(), kr], dim=-2),
                 torch.cat([self._v_quant[layer_idx].dequantized(), vr], dim=-2))
 
-    def compute_attention(self, q, *, layer_idx: int, scaling: Optional[float] = None):
+    def compute_attention(self, q, *, layer_idx: int, scaling: Optional[float] = None,
+                          events: Optional[tuple] = None):
         """Attention of ``q (B, H, T_q, D)`` over the quantised prefix (its
         dequantised values, as the reference attends them) plus the recent
-        rows; decode (T_q = 1) runs the fused packed kernel."""
+        rows; decode (T_q = 1) runs the fused packed kernel.  ``events =
+        (begin, end)`` (raw ``cudaEvent_t``) bracket that kernel (profiling)."""
         B, H, T_q, D = q.shape
         scale = float(scaling) if scaling is not None else 1.0 / math.sqrt(D)
         kq, vq = self._k_quant[layer_idx], self._v_quant[layer_idx]
@@ -241,14 +244,26 @@ class KIVICache(_BaseCache):
             return out
         q3 = q.squeeze(2).contiguous()
         dev = q.device
-        m = torch.full((B, H), float("-inf"), dtype=torch.float32, device=dev)
-        l = torch.zeros(B, H, dtype=torch.float32, device=dev)
-        o = torch.zeros(B, H, D, dtype=torch.float32, device=dev)
-        if T_quant:
-            kivi_decode(q3, kq, vq, T_quant, self.bits, scale=scale, state=(m, l, o))
         recent = [(kr, vr, T_quant, False)] if (kr is not None and kr.shape[-2]) else []
-        out, _ = ops.chunked_decode(q3, recent, scale=scale, prior=(m, l, o))
+        prior = None
+        if T_quant:
+            # The prefix's normalised (out, lse) is a running state with l = 1.
+            o32 = torch.empty(B, H, D, dtype=torch.float32, device=dev)
+            lse = torch.empty(B, H, dtype=torch.float32, device=dev)
+            kivi_decode(q3, kq, vq, T_quant, self.bits, scale=scale, out=o32, lse=lse,
+                        events=events)
+            if not recent:
+                return o32.to(q.dtype).unsqueeze(2)
+            prior = (lse, self._ones(B, H, dev), o32)
+        out, _ = ops.chunked_decode(q3, recent, scale=scale, prior=prior)
         return out.unsqueeze(2)
+
+    def _ones(self, B: int, H: int, dev) -> torch.Tensor:
+        key = (B, H, str(dev))
+        t = self._ones_cache.get(key)
+        if t is None:
+            t = self._ones_cache[key] = torch.ones(B, H, dtype=torch.float32, device=dev)
+        return t
 
     def reset(self) -> None:
         self._k_recent.clear()

@@ -19,6 +19,7 @@
 //     prior running state) into the final output + LSE, or into the running
 //     (m, l, o) accumulators of update_chunk.
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -33,6 +34,10 @@
 namespace halo {
 
 __device__ unsigned int g_device_error = 0;
+
+std::atomic<uint64_t> g_launch_count{0};
+
+void count_launches(int n) { g_launch_count.fetch_add((uint64_t)n, std::memory_order_relaxed); }
 
 unsigned int* device_error_ptr() {
   static std::mutex mu;
@@ -1091,7 +1096,9 @@ int launch_merge(const MergeParams& mp, cudaStream_t st) {
   else if (mp.Dv <= 256 && mp.Dv % 8 == 0) km_kernel<8><<<mp.R, threads, 0, st>>>(mp);
   else return fail(HALO_ERR_UNSUPPORTED, "Dv %d unsupported by the merge", mp.Dv);
   cudaError_t e = cudaGetLastError();
-  return e == cudaSuccess ? HALO_OK : cuda_fail(e, "km_kernel launch");
+  if (e != cudaSuccess) return cuda_fail(e, "km_kernel launch");
+  count_launches();
+  return HALO_OK;
 }
 
 int validate_merge(const halo_merge_args_t* mg, int Dv) {
@@ -1334,7 +1341,9 @@ static int launch_kd(const DecodeParams& prm, cudaStream_t st) {
   const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(prm.n_units, grid_max));
   kd_kernel<T, D, C::kStages, C::kMinBlocks><<<grid, kThreads, Gm::kSmemBytes, st>>>(prm);
   cudaError_t e = cudaGetLastError();
-  return e == cudaSuccess ? HALO_OK : cuda_fail(e, "kd_kernel launch");
+  if (e != cudaSuccess) return cuda_fail(e, "kd_kernel launch");
+  count_launches();
+  return HALO_OK;
 }
 
 static int dispatch_kd(int dtype, int D, const DecodeParams& prm, cudaStream_t st) {
@@ -1414,7 +1423,9 @@ static int launch_kk(const KiviParams& prm, cudaStream_t st) {
   const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(prm.n_units, grid_max));
   kk_kernel<T, D, BITS><<<grid, kThreads, KG::kSmemBytes, st>>>(prm);
   cudaError_t e = cudaGetLastError();
-  return e == cudaSuccess ? HALO_OK : cuda_fail(e, "kk_kernel launch");
+  if (e != cudaSuccess) return cuda_fail(e, "kk_kernel launch");
+  count_launches();
+  return HALO_OK;
 }
 
 template <typename T>
@@ -1612,6 +1623,10 @@ extern "C" int32_t halo_device_error(int32_t* code_out, int32_t clear) {
 }
 
 extern "C" int32_t halo_version(void) { return 100; }
+
+extern "C" uint64_t halo_launch_count(void) {
+  return halo::g_launch_count.load(std::memory_order_relaxed);
+}
 
 extern "C" int64_t halo_kivi_decode_workspace_bytes(const halo_decode_problem_t* problem,
                                                     int32_t rows) {

@@ -24,6 +24,9 @@ namespace halo {
 // halo_device_error().  device_error_ptr() returns the current device's copy.
 unsigned int* device_error_ptr();
 
+// Process-wide count of kernels this library has launched (halo_launch_count).
+void count_launches(int n = 1);
+
 __device__ __forceinline__ void set_device_error(unsigned int* err, unsigned int code) {
   if (err) atomicCAS(err, 0u, code);
 }

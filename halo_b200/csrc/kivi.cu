@@ -152,7 +152,9 @@ static int kivi_launch(bool quantize, const void* x, int64_t x_sb, int64_t x_sh,
     else kivi_dequantize_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(p);
   }
   cudaError_t e = cudaGetLastError();
-  return e == cudaSuccess ? HALO_OK : cuda_fail(e, "KIVI kernel launch");
+  if (e != cudaSuccess) return cuda_fail(e, "KIVI kernel launch");
+  count_launches();
+  return HALO_OK;
 }
 
 extern "C" int32_t halo_kivi_quantize(const void* x, int64_t x_sb, int64_t x_sh, int64_t x_st,

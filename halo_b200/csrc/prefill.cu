@@ -1,0 +1,721 @@
+// Chunked-prefill attention on the Blackwell tensor cores (tcgen05 + TMEM).
+//
+// T_q > 1 query rows of one (batch, head) slice attend to a list of K/V
+// chunks (the accumulated cache of halo/kv_cache_chunked.py:873-942 and the
+// slices of halo/chunked_prefill.py:73-135 in lzbaclz/HALO).  One CTA owns a
+// tile of 128 query rows of one q-head and walks every visible 128-row K/V
+// tile of every chunk with an online softmax; there is no split over keys,
+// so the result leaves the CTA already merged.
+//
+// Warp roles (192 threads, one CTA per SM):
+//   warp 0      TMA producer: the Q tile once, then K and V tiles through
+//               two-slot rings (128B-swizzled boxes of 128 rows x 64 elements).
+//   warp 1      TMEM owner (allocates 512 columns) and, on lane 0, the MMA
+//               issuer: S_i = Q K_i^T into one of two TMEM score buffers, and
+//               O += P_i V_i into the TMEM output accumulator.
+//   warps 2-5   softmax: thread r owns query row r = TMEM lane r.  It loads
+//               its S row from TMEM, masks, keeps the running max m and sum l
+//               (log2 domain), writes P = exp2(s - m) to shared memory as a
+//               16-bit pair hi + lo (hi = rnd(p), lo = rnd(p - hi)) and
+//               rescales its O row in TMEM when the max grows by more than
+//               2^8 (the rescale is otherwise deferred: P stays <= 256).
+// O accumulates P_hi V + P_lo V, so P carries ~16 significant bits into the
+// fp32 accumulator; a single 16-bit P would put errors of up to 2^-9 |v| on
+// the output, above the 2e-3 budget for peaked rows.
+//
+// TMEM columns: S0 [0,128), S1 [128,256), O [256, 256+D).
+// Shared memory (D = 128): Q 32 KB | K x2 64 KB | V x2 64 KB | P_hi, P_lo 64 KB.
+//
+// Synchronisation (mbarriers; every wait bounded, see mbar_wait):
+//   q_full, k_full[2], v_full[2]   TMA transaction counts
+//   k_empty[2], v_empty[2]         tcgen05.commit after the MMAs reading them
+//   s_full[2]                      tcgen05.commit after S_i = Q K_i^T
+//   s_free[2]                      128 softmax threads after reading S_i
+//   p_full                         128 softmax threads after writing P_i
+//   pv_done                        tcgen05.commit after O += P_i V_i
+//   mma_done                       the MMA thread's final commit
+// The softmax of tile i waits for pv_done(i-1) before it touches P or O, so
+// one P buffer suffices; a commit tracks every earlier MMA of the issuing
+// thread, so s_full(i) also implies pv_done(i-2).
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <unordered_map>
+
+#include "halo_common.cuh"
+#include "umma.cuh"
+
+namespace halo {
+
+int fail(int code, const char* fmt, ...);
+int cuda_fail(cudaError_t e, const char* what);
+int device_sms();
+
+namespace prefill {
+
+constexpr int kBM = 128;            // query rows per CTA (TMEM lanes)
+constexpr int kBN = 128;            // keys per tile
+constexpr int kThreads = 192;
+constexpr int kMaxSegs = 48;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kColS0 = 0, kColS1 = 128, kColO = 256;
+constexpr float kRescaleLog2 = 8.f;
+
+struct Seg {
+  int64_t start;   // global position of row 0
+  int32_t len;
+  int16_t causal;
+  int16_t bcast;   // batch stride 0: every batch row reads batch 0
+};
+
+struct alignas(64) Params {
+  CUtensorMap qmap;                 // {D, T_q, H, B}
+  CUtensorMap kmap[kMaxSegs];       // {D, len, H_kv, B}
+  CUtensorMap vmap[kMaxSegs];
+  Seg seg[kMaxSegs];
+  int32_t n_seg;
+  int32_t B, H, G, T_q, n_qtiles;
+  int64_t q_pos0;
+  float scale_log2;                 // softmax scale * log2(e)
+  int32_t mode;                     // HALO_MERGE_*
+  int32_t out_dtype;
+  char* out;
+  int64_t out_sb, out_sh, out_st;   // elements
+  float* lse;
+  float* m;
+  float* l;
+  float* o;
+  unsigned int* err;
+};
+
+template <int D>
+struct Geom {
+  static constexpr int kBlocks = D / 64;                 // 64-element swizzle blocks per row
+  static constexpr int kBlockBytes = kBM * 128;          // 128 rows x 128 B
+  static constexpr int kTileBytes = kBlocks * kBlockBytes;
+  static constexpr int kPBytes = 2 * kBlockBytes;        // 128 keys = 2 blocks
+  static constexpr int kOffQ = 0;
+  static constexpr int kOffK = kOffQ + kTileBytes;
+  static constexpr int kOffV = kOffK + 2 * kTileBytes;
+  static constexpr int kOffPhi = kOffV + 2 * kTileBytes;
+  static constexpr int kOffPlo = kOffPhi + kPBytes;
+  static constexpr int kOffBar = kOffPlo + kPBytes;
+  static constexpr int kBarBytes = 256;
+  static constexpr int kSmemBytes = kOffBar + kBarBytes + 1024;  // + base alignment slack
+};
+
+struct Bars {
+  uint64_t q_full, k_full[2], v_full[2], k_empty[2], v_empty[2];
+  uint64_t s_full[2], s_free[2], p_full, pv_done, mma_done;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+// Bounded wait that also gives up once another role has aborted.
+__device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, Bars* bs,
+                                         unsigned int* err) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+    for (int i = 0; i < 32; ++i)
+      if (mbar_try_wait(bar, parity)) return true;
+    if (*reinterpret_cast<volatile int*>(&bs->abort_flag)) return false;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      set_device_error(err, static_cast<unsigned int>(-HALO_ERR_TIMEOUT));
+      *reinterpret_cast<volatile int*>(&bs->abort_flag) = 1;
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Tiles of segment `s` visible to query positions <= qmax.
+__device__ __forceinline__ int seg_tiles(const Seg& sg, int64_t qmax) {
+  int n = (sg.len + kBN - 1) / kBN;
+  if (sg.causal) {
+    const int64_t lim = qmax - sg.start;   // last visible row
+    if (lim < 0) return 0;
+    const int64_t nv = lim / kBN + 1;
+    if (nv < n) n = (int)nv;
+  }
+  return n;
+}
+
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float a, float b) {
+  return Elem<T>::pack(a, b);
+}
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kThreads, 1) kp_kernel(const __grid_constant__ Params p) {
+  using Gm = Geom<D>;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  Bars* bs = reinterpret_cast<Bars*>(smem + Gm::kOffBar);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  // heavy-first order: the last query tiles see the most keys
+  const int BH = p.B * p.H;
+  const int qt = p.n_qtiles - 1 - (int)(blockIdx.x / BH);
+  const int bh = (int)(blockIdx.x % BH);
+  const int b = bh / p.H, h = bh % p.H, hk = h / p.G;
+  const int qrow0 = qt * kBM;
+  const int q_valid = min(kBM, p.T_q - qrow0);
+  const int64_t qpos_min = p.q_pos0 + qrow0;
+  const int64_t qpos_max = qpos_min + q_valid - 1;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bs->q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bs->k_full[i], 1);
+      mbar_init(&bs->v_full[i], 1);
+      mbar_init(&bs->k_empty[i], 1);
+      mbar_init(&bs->v_empty[i], 1);
+      mbar_init(&bs->s_full[i], 1);
+      mbar_init(&bs->s_free[i], kBM);
+    }
+    mbar_init(&bs->p_full, kBM);
+    mbar_init(&bs->pv_done, 1);
+    mbar_init(&bs->mma_done, 1);
+    bs->abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    umma::tmem_alloc(&bs->tmem_base, kTmemCols);
+    umma::tmem_relinquish();
+  }
+  umma::fence_before_sync();
+  __syncthreads();
+  umma::fence_after_sync();
+  const uint32_t tmem = bs->tmem_base;
+
+  int n_tiles = 0;
+  for (int s = 0; s < p.n_seg; ++s) n_tiles += seg_tiles(p.seg[s], qpos_max);
+
+  const uint32_t sQ = smem_addr(smem + Gm::kOffQ);
+  const uint32_t sK = smem_addr(smem + Gm::kOffK);
+  const uint32_t sV = smem_addr(smem + Gm::kOffV);
+  const uint32_t sPhi = smem_addr(smem + Gm::kOffPhi);
+  const uint32_t sPlo = smem_addr(smem + Gm::kOffPlo);
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0 && n_tiles > 0) {
+      mbar_arrive_expect_tx(&bs->q_full, Gm::kTileBytes);
+      for (int blk = 0; blk < Gm::kBlocks; ++blk)
+        tma_load_4d(smem + Gm::kOffQ + blk * Gm::kBlockBytes, &p.qmap, blk * 64, qrow0, h, b,
+                    &bs->q_full);
+      int nk = 0, nv = 0;   // K and V tiles issued
+      bool ok = true;
+      for (int s = 0; s < p.n_seg && ok; ++s) {
+        const int nt = seg_tiles(p.seg[s], qpos_max);
+        const int bb = p.seg[s].bcast ? 0 : b;
+        for (int t = 0; t < nt; ++t) {
+          const int st = nk & 1, use = nk >> 1;
+          if (use > 0 && !(ok = wait_bar(&bs->k_empty[st], (use - 1) & 1, bs, p.err))) break;
+          mbar_arrive_expect_tx(&bs->k_full[st], Gm::kTileBytes);
+          for (int blk = 0; blk < Gm::kBlocks; ++blk)
+            tma_load_4d(smem + Gm::kOffK + st * Gm::kTileBytes + blk * Gm::kBlockBytes,
+                        &p.kmap[s], blk * 64, t * kBN, hk, bb, &bs->k_full[st]);
+          ++nk;
+          if (use > 0 && !(ok = wait_bar(&bs->v_empty[st], (use - 1) & 1, bs, p.err))) break;
+          mbar_arrive_expect_tx(&bs->v_full[st], Gm::kTileBytes);
+          for (int blk = 0; blk < Gm::kBlocks; ++blk)
+            tma_load_4d(smem + Gm::kOffV + st * Gm::kTileBytes + blk * Gm::kBlockBytes,
+                        &p.vmap[s], blk * 64, t * kBN, hk, bb, &bs->v_full[st]);
+          ++nv;
+        }
+      }
+      // Let every copy this thread issued land before the CTA can exit
+      // (immediate unless a consumer aborted).
+      mbar_wait(&bs->q_full, 0, p.err);
+      for (int st = 0; st < 2; ++st) {
+        const int uk = (nk - st + 1) / 2, uv = (nv - st + 1) / 2;   // loads into slot st
+        if (uk > 0) mbar_wait(&bs->k_full[st], (uk - 1) & 1, p.err);
+        if (uv > 0) mbar_wait(&bs->v_full[st], (uv - 1) & 1, p.err);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0 && n_tiles > 0) {
+      constexpr bool kBf16 = Elem<T>::kDtype == HALO_DTYPE_BF16;
+      constexpr uint32_t kIdQK = umma::instr_desc_f16(kBM, kBN, kBf16, false, false);
+      constexpr uint32_t kIdPV = umma::instr_desc_f16(kBM, D, kBf16, false, true);
+      bool ok = wait_bar(&bs->q_full, 0, bs, p.err);
+      auto issue_pv = [&](int j) -> bool {
+        const int st = j & 1;
+        if (!wait_bar(&bs->p_full, j & 1, bs, p.err)) return false;
+        if (!wait_bar(&bs->v_full[st], (j >> 1) & 1, bs, p.err)) return false;
+        umma::fence_after_sync();
+        const uint32_t vbase = sV + st * Gm::kTileBytes;
+#pragma unroll
+        for (int part = 0; part < 2; ++part) {
+          const uint32_t pbase = part ? sPlo : sPhi;
+#pragma unroll
+          for (int kk = 0; kk < kBN / 16; ++kk) {
+            const uint64_t ad = umma::smem_desc_sw128(
+                pbase + (kk >> 2) * Gm::kBlockBytes + (kk & 3) * 32, 16, 1024);
+            const uint64_t bd =
+                umma::smem_desc_sw128(vbase + kk * 16 * 128, Gm::kBlockBytes, 1024);
+            umma::mma_ss(tmem + kColO, ad, bd, kIdPV, (j > 0) || part || kk);
+          }
+        }
+        umma::commit(&bs->pv_done);
+        umma::commit(&bs->v_empty[st]);
+        return true;
+      };
+      for (int i = 0; i < n_tiles && ok; ++i) {
+        const int st = i & 1;
+        if (!(ok = wait_bar(&bs->k_full[st], (i >> 1) & 1, bs, p.err))) break;
+        if (i >= 2 && !(ok = wait_bar(&bs->s_free[st], ((i - 2) >> 1) & 1, bs, p.err))) break;
+        umma::fence_after_sync();
+        const uint32_t kbase = sK + st * Gm::kTileBytes;
+        const uint32_t scol = st ? kColS1 : kColS0;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * Gm::kBlockBytes + (kk & 3) * 32;
+          umma::mma_ss(tmem + scol, umma::smem_desc_sw128(sQ + off, 16, 1024),
+                       umma::smem_desc_sw128(kbase + off, 16, 1024), kIdQK, kk > 0);
+        }
+        umma::commit(&bs->s_full[st]);
+        umma::commit(&bs->k_empty[st]);
+        if (i >= 1) ok = issue_pv(i - 1);
+      }
+      if (ok) issue_pv(n_tiles - 1);
+      umma::commit(&bs->mma_done);
+      mbar_wait(&bs->mma_done, 0, p.err);
+    }
+  } else {
+    // ------------------------------------------------------------ softmax
+    const int sub = warp & 3;                 // TMEM lane quarter of this warp
+    const int r = sub * 32 + lane;            // query row within the tile
+    const uint32_t trow = tmem + ((uint32_t)(sub * 32) << 16);
+    const int64_t qpos = qpos_min + r;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    int i = 0;
+    for (int s = 0; s < p.n_seg && ok; ++s) {
+      const Seg sg = p.seg[s];
+      const int nt = seg_tiles(sg, qpos_max);
+      for (int t = 0; t < nt; ++t, ++i) {
+        const int st = i & 1;
+        ok = __all_sync(0xffffffffu, wait_bar(&bs->s_full[st], (i >> 1) & 1, bs, p.err));
+        if (!ok) break;
+        umma::fence_after_sync();
+        float sv[kBN];
+        const uint32_t scol = st ? kColS1 : kColS0;
+#pragma unroll
+        for (int c = 0; c < kBN / 32; ++c) umma::tmem_ld32(trow + scol + c * 32, sv + c * 32);
+        umma::tmem_wait_ld();
+        umma::fence_before_sync();
+        mbar_arrive(&bs->s_free[st]);
+
+        const int row0 = t * kBN;
+        const int64_t kpos0 = sg.start + row0;
+        const bool full = (row0 + kBN <= sg.len) && (!sg.causal || kpos0 + kBN - 1 <= qpos_min);
+        float mx = -INFINITY;
+        if (full) {
+#pragma unroll
+          for (int c = 0; c < kBN; ++c) {
+            sv[c] *= p.scale_log2;
+            mx = fmaxf(mx, sv[c]);
+          }
+        } else {
+          const int lim_len = sg.len - row0;
+          const int64_t lim_pos = sg.causal ? qpos - kpos0 : (int64_t)kBN;
+#pragma unroll
+          for (int c = 0; c < kBN; ++c) {
+            const bool vis = c < lim_len && (int64_t)c <= lim_pos;
+            sv[c] = vis ? sv[c] * p.scale_log2 : -INFINITY;
+            mx = fmaxf(mx, sv[c]);
+          }
+        }
+
+        // P and O are free once O += P_{i-1} V_{i-1} has completed.
+        if (i > 0) {
+          ok = __all_sync(0xffffffffu, wait_bar(&bs->pv_done, (i - 1) & 1, bs, p.err));
+          if (!ok) break;
+          umma::fence_after_sync();
+        }
+        const bool grow = mx > m + kRescaleLog2 || (m == -INFINITY && mx > -INFINITY);
+        float fac = 1.f;
+        if (grow) {
+          fac = (m == -INFINITY) ? 0.f : ex2(m - mx);
+          l *= fac;
+          m = mx;
+        }
+        if (i > 0 && __any_sync(0xffffffffu, grow)) {
+          // warp-collective rescale of the O rows (factor 1 where the max held)
+#pragma unroll
+          for (int c = 0; c < D / 32; ++c) {
+            float ov[32];
+            umma::tmem_ld32(trow + kColO + c * 32, ov);
+            umma::tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) ov[e] *= fac;
+            umma::tmem_st32(trow + kColO + c * 32, ov);
+          }
+          umma::tmem_wait_st();
+        }
+        const float mu = (m == -INFINITY) ? 0.f : m;
+        float rs = 0.f;
+        const uint32_t prow = (uint32_t)r * 128u;
+#pragma unroll
+        for (int c16 = 0; c16 < kBN / 8; ++c16) {
+          uint32_t hi[4], lo[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float p0 = ex2(sv[c16 * 8 + 2 * e] - mu);
+            const float p1 = ex2(sv[c16 * 8 + 2 * e + 1] - mu);
+            rs += p0 + p1;
+            hi[e] = pack2<T>(p0, p1);
+            float h0, h1;
+            Elem<T>::unpack(hi[e], h0, h1);
+            lo[e] = pack2<T>(p0 - h0, p1 - h1);
+          }
+          const uint32_t off = (uint32_t)(c16 >> 3) * Gm::kBlockBytes + prow +
+                               ((uint32_t)((c16 & 7) ^ (r & 7)) << 4);
+          asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(sPhi + off), "r"(hi[0]),
+                       "r"(hi[1]), "r"(hi[2]), "r"(hi[3]) : "memory");
+          asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(sPlo + off), "r"(lo[0]),
+                       "r"(lo[1]), "r"(lo[2]), "r"(lo[3]) : "memory");
+        }
+        l += rs;
+        fence_proxy_async_smem();      // P is read by the tensor core (async proxy)
+        umma::fence_before_sync();     // orders the O rescale before the MMA thread's reads
+        mbar_arrive(&bs->p_full);
+      }
+    }
+
+    // ---- epilogue: thread r finalises query row qrow0 + r
+    if (ok && n_tiles > 0) {
+      ok = __all_sync(0xffffffffu, wait_bar(&bs->pv_done, (n_tiles - 1) & 1, bs, p.err));
+      if (ok) umma::fence_after_sync();
+    }
+    if (ok) {
+      float ov[D];
+      if (n_tiles > 0) {
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) umma::tmem_ld32(trow + kColO + c * 32, ov + c * 32);
+        umma::tmem_wait_ld();
+      } else {
+#pragma unroll
+        for (int d = 0; d < D; ++d) ov[d] = 0.f;
+      }
+      if (r < q_valid) {
+        const int t = qrow0 + r;
+        const int64_t row = ((int64_t)b * p.H + h) * p.T_q + t;
+        float M = (m == -INFINITY) ? -INFINITY : m * kLn2;   // natural-log score units
+        float L = l;
+        if (p.m != nullptr) {
+          const float mp = p.m[row], lp = p.l[row];
+          const float Mn = fmaxf(M, mp);
+          const float wo = (M == -INFINITY) ? 0.f : expf(M - Mn);
+          const float wp = (mp == -INFINITY) ? 0.f : expf(mp - Mn);
+          const float* op = p.o + row * D;
+          L = L * wo + lp * wp;
+#pragma unroll
+          for (int d = 0; d < D; ++d) ov[d] = ov[d] * wo + op[d] * wp;
+          M = Mn;
+        }
+        if (p.mode == HALO_MERGE_ACCUMULATE) {
+          p.m[row] = M;
+          p.l[row] = L;
+          float4* od = reinterpret_cast<float4*>(p.o + row * D);
+#pragma unroll
+          for (int d = 0; d < D; d += 4) od[d / 4] = make_float4(ov[d], ov[d + 1], ov[d + 2], ov[d + 3]);
+        } else {
+          const float inv = (L > 0.f) ? 1.f / L : 0.f;
+          if (p.lse) p.lse[row] = (L > 0.f) ? M + logf(L) : -INFINITY;
+          const int64_t off = (int64_t)b * p.out_sb + (int64_t)h * p.out_sh + (int64_t)t * p.out_st;
+          if (p.out_dtype == HALO_DTYPE_F32) {
+            float4* od = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + off);
+#pragma unroll
+            for (int d = 0; d < D; d += 4)
+              od[d / 4] = make_float4(ov[d] * inv, ov[d + 1] * inv, ov[d + 2] * inv, ov[d + 3] * inv);
+          } else {
+            uint4* od = reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.out) + off);
+#pragma unroll
+            for (int d = 0; d < D; d += 8)
+              od[d / 8] = make_uint4(pack2<T>(ov[d] * inv, ov[d + 1] * inv),
+                                     pack2<T>(ov[d + 2] * inv, ov[d + 3] * inv),
+                                     pack2<T>(ov[d + 4] * inv, ov[d + 5] * inv),
+                                     pack2<T>(ov[d + 6] * inv, ov[d + 7] * inv));
+          }
+        }
+      }
+    }
+  }
+
+  // ---- teardown: every TMEM access and MMA has completed
+  umma::fence_before_sync();
+  __syncthreads();
+  if (warp == 1) {
+    umma::fence_after_sync();
+    umma::tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+}  // namespace prefill
+
+// ================================================================ host side
+typedef CUresult (*PfEncodeFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                               const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                               const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                               CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static PfEncodeFn pf_encode_fn() {
+  static PfEncodeFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess && q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PfEncodeFn>(ptr);
+  });
+  return fn;
+}
+
+struct PfMapKey {
+  uintptr_t ptr;
+  uint64_t dims[4];
+  uint64_t strides[3];
+  int dtype;
+  bool operator==(const PfMapKey& o) const {
+    return ptr == o.ptr && dtype == o.dtype && std::memcmp(dims, o.dims, sizeof(dims)) == 0 &&
+           std::memcmp(strides, o.strides, sizeof(strides)) == 0;
+  }
+};
+struct PfMapKeyHash {
+  size_t operator()(const PfMapKey& k) const {
+    uint64_t h = 1469598103934665603ull ^ k.ptr;
+    auto mix = [&](uint64_t v) { h = (h ^ v) * 1099511628211ull; };
+    for (int i = 0; i < 4; ++i) mix(k.dims[i]);
+    for (int i = 0; i < 3; ++i) mix(k.strides[i]);
+    mix(static_cast<uint64_t>(k.dtype));
+    return static_cast<size_t>(h);
+  }
+};
+
+// 4-D 16-bit tensor {D, rows, heads, batch} (byte strides of the outer three
+// dims), box {64 elements, 128 rows, 1, 1}, 128-byte swizzle, out-of-bounds
+// rows zero-filled.  Encodings are cached per (pointer, shape, strides).
+static int pf_encode(const void* base, int dtype, const uint64_t dims[4],
+                     const uint64_t strides[3], CUtensorMap* out) {
+  PfMapKey key;
+  key.ptr = reinterpret_cast<uintptr_t>(base);
+  std::memcpy(key.dims, dims, sizeof(key.dims));
+  std::memcpy(key.strides, strides, sizeof(key.strides));
+  key.dtype = dtype;
+  static std::mutex mu;
+  static std::unordered_map<PfMapKey, CUtensorMap, PfMapKeyHash> cache;
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) {
+      *out = it->second;
+      return HALO_OK;
+    }
+  }
+  PfEncodeFn fn = pf_encode_fn();
+  if (!fn) return fail(HALO_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t gdim[4] = {dims[0], dims[1], dims[2], dims[3]};
+  cuuint64_t gstr[3] = {strides[0], strides[1], strides[2]};
+  cuuint32_t box[4] = {64, (cuuint32_t)prefill::kBN, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUtensorMapDataType dt = dtype == HALO_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                          : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUresult r = fn(out, dt, 4, const_cast<void*>(base), gdim, gstr, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(HALO_ERR_INVALID_ARG,
+                "prefill tensor map encode failed (%d): dims {%llu,%llu,%llu,%llu} strides "
+                "{%llu,%llu,%llu} bytes",
+                (int)r, (unsigned long long)dims[0], (unsigned long long)dims[1],
+                (unsigned long long)dims[2], (unsigned long long)dims[3],
+                (unsigned long long)strides[0], (unsigned long long)strides[1],
+                (unsigned long long)strides[2]);
+  std::lock_guard<std::mutex> lk(mu);
+  if (cache.size() > 8192) cache.clear();
+  cache.emplace(key, *out);
+  return HALO_OK;
+}
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+// Chunk c continues segment s in memory and in position (one tensor map).
+static bool pf_continues(const halo_kv_chunk_t& a, int64_t a_len, const halo_kv_chunk_t& c) {
+  return c.causal == a.causal && c.k_stride_b == a.k_stride_b && c.k_stride_h == a.k_stride_h &&
+         c.k_stride_t == a.k_stride_t && c.v_stride_b == a.v_stride_b &&
+         c.v_stride_h == a.v_stride_h && c.v_stride_t == a.v_stride_t &&
+         c.start == a.start + a_len &&
+         static_cast<const char*>(c.k) ==
+             static_cast<const char*>(a.k) + a_len * a.k_stride_t * 2 &&
+         static_cast<const char*>(c.v) ==
+             static_cast<const char*>(a.v) + a_len * a.v_stride_t * 2 &&
+         a_len + c.len <= INT32_MAX;
+}
+
+template <typename T, int D>
+static int launch_kp(const prefill::Params& prm, int grid, cudaStream_t st) {
+  using Gm = prefill::Geom<D>;
+  static std::once_flag once[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  cudaError_t attr_err = cudaSuccess;
+  std::call_once(once[dev & 63], [&] {
+    attr_err = cudaFuncSetAttribute(prefill::kp_kernel<T, D>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, Gm::kSmemBytes);
+  });
+  if (attr_err != cudaSuccess) return cuda_fail(attr_err, "kp_kernel shared-memory attribute");
+  prefill::kp_kernel<T, D><<<grid, prefill::kThreads, Gm::kSmemBytes, st>>>(prm);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "kp_kernel launch");
+  count_launches();
+  return HALO_OK;
+}
+
+}  // namespace halo
+
+using namespace halo;
+
+extern "C" int32_t halo_prefill_attention(const halo_prefill_problem_t* pb,
+                                          const halo_kv_chunk_t* chunks, int32_t n_chunks,
+                                          const halo_prefill_out_t* po, halo_stream_t stream) {
+  if (!pb || !po) return fail(HALO_ERR_INVALID_ARG, "problem/out is NULL");
+  if (pb->B <= 0 || pb->H <= 0 || pb->H_kv <= 0 || pb->T_q < 0 || pb->D <= 0)
+    return fail(HALO_ERR_INVALID_ARG, "non-positive dimension (B=%d H=%d H_kv=%d T_q=%d D=%d)",
+                pb->B, pb->H, pb->H_kv, pb->T_q, pb->D);
+  if (pb->H % pb->H_kv) return fail(HALO_ERR_INVALID_ARG, "H=%d not divisible by H_kv=%d", pb->H, pb->H_kv);
+  if (pb->dtype != HALO_DTYPE_BF16 && pb->dtype != HALO_DTYPE_F16)
+    return fail(HALO_ERR_UNSUPPORTED, "prefill kernel needs bf16 or fp16 (dtype %d)", pb->dtype);
+  if (pb->D != 64 && pb->D != 128)
+    return fail(HALO_ERR_UNSUPPORTED, "prefill kernel head_dim %d (64 or 128)", pb->D);
+  if (n_chunks < 0 || (n_chunks > 0 && !chunks)) return fail(HALO_ERR_INVALID_ARG, "bad chunk list");
+  if (po->mode != HALO_MERGE_FINALIZE && po->mode != HALO_MERGE_ACCUMULATE)
+    return fail(HALO_ERR_INVALID_ARG, "bad mode %d", po->mode);
+  const bool have_state = po->m || po->l || po->o;
+  if (have_state && !(po->m && po->l && po->o))
+    return fail(HALO_ERR_INVALID_ARG, "running state needs all of m, l, o");
+  if (po->mode == HALO_MERGE_ACCUMULATE && !have_state)
+    return fail(HALO_ERR_INVALID_ARG, "accumulate needs m, l, o");
+  if (po->o && !aligned16(po->o)) return fail(HALO_ERR_MISALIGNED, "o must be 16-byte aligned");
+  const int D = pb->D;
+  if (po->mode == HALO_MERGE_FINALIZE) {
+    if (!po->out) return fail(HALO_ERR_INVALID_ARG, "out is NULL");
+    const int oe = po->out_dtype == HALO_DTYPE_F32 ? 4 : 2;
+    if (po->out_dtype != HALO_DTYPE_F32 && po->out_dtype != pb->dtype)
+      return fail(HALO_ERR_UNSUPPORTED, "out dtype must be fp32 or the input dtype");
+    if (!aligned16(po->out) || (po->out_stride_b * oe) % 16 || (po->out_stride_h * oe) % 16 ||
+        (po->out_stride_t * oe) % 16)
+      return fail(HALO_ERR_MISALIGNED, "out rows must be 16-byte aligned");
+  }
+  if (pb->T_q == 0) return HALO_OK;
+  if (!pb->q || !aligned16(pb->q) || (pb->q_stride_t * 2) % 16 || (pb->q_stride_h * 2) % 16 ||
+      (pb->B > 1 && (pb->q_stride_b * 2) % 16) || pb->q_stride_t <= 0 || pb->q_stride_h <= 0)
+    return fail(HALO_ERR_MISALIGNED, "q must be 16-byte aligned with 16-byte row strides");
+
+  // ---- segments: coalesce chunks contiguous in memory and position
+  static thread_local prefill::Params prm;
+  int n_seg = 0;
+  halo_kv_chunk_t cur{};
+  int64_t cur_len = 0;
+  auto flush = [&]() -> int {
+    if (cur_len == 0) return HALO_OK;
+    if (n_seg >= prefill::kMaxSegs)
+      return fail(HALO_ERR_UNSUPPORTED, "more than %d non-contiguous chunks in one call",
+                  prefill::kMaxSegs);
+    const bool bk = cur.k_stride_b == 0, bv = cur.v_stride_b == 0;
+    if (bk != bv) return fail(HALO_ERR_INVALID_ARG, "k and v must both broadcast the batch or neither");
+    const uint64_t dims[4] = {(uint64_t)D, (uint64_t)cur_len, (uint64_t)pb->H_kv,
+                              (uint64_t)(bk ? 1 : pb->B)};
+    const uint64_t ks[3] = {(uint64_t)cur.k_stride_t * 2, (uint64_t)cur.k_stride_h * 2,
+                            (uint64_t)(bk || pb->B == 1 ? cur.k_stride_h * 2 * pb->H_kv
+                                                        : cur.k_stride_b * 2)};
+    const uint64_t vs[3] = {(uint64_t)cur.v_stride_t * 2, (uint64_t)cur.v_stride_h * 2,
+                            (uint64_t)(bv || pb->B == 1 ? cur.v_stride_h * 2 * pb->H_kv
+                                                        : cur.v_stride_b * 2)};
+    int rc = pf_encode(cur.k, pb->dtype, dims, ks, &prm.kmap[n_seg]);
+    if (rc != HALO_OK) return rc;
+    rc = pf_encode(cur.v, pb->dtype, dims, vs, &prm.vmap[n_seg]);
+    if (rc != HALO_OK) return rc;
+    prm.seg[n_seg].start = cur.start;
+    prm.seg[n_seg].len = (int32_t)cur_len;
+    prm.seg[n_seg].causal = cur.causal ? 1 : 0;
+    prm.seg[n_seg].bcast = bk ? 1 : 0;
+    ++n_seg;
+    cur_len = 0;
+    return HALO_OK;
+  };
+  for (int i = 0; i < n_chunks; ++i) {
+    const halo_kv_chunk_t& c = chunks[i];
+    if (c.len < 0) return fail(HALO_ERR_INVALID_ARG, "chunk %d: negative length", i);
+    if (c.len == 0) continue;
+    if (!c.k || !c.v) return fail(HALO_ERR_INVALID_ARG, "chunk %d: NULL k/v", i);
+    if (!aligned16(c.k) || !aligned16(c.v) || (c.k_stride_t * 2) % 16 || (c.v_stride_t * 2) % 16 ||
+        (c.k_stride_h * 2) % 16 || (c.v_stride_h * 2) % 16 || (c.k_stride_b * 2) % 16 ||
+        (c.v_stride_b * 2) % 16 || c.k_stride_t <= 0 || c.v_stride_t <= 0)
+      return fail(HALO_ERR_MISALIGNED, "chunk %d: k/v rows must be 16-byte aligned", i);
+    if (cur_len > 0 && pf_continues(cur, cur_len, c)) {
+      cur_len += c.len;
+      continue;
+    }
+    int rc = flush();
+    if (rc != HALO_OK) return rc;
+    cur = c;
+    cur_len = c.len;
+  }
+  int rc = flush();
+  if (rc != HALO_OK) return rc;
+
+  // ---- Q map {D, T_q, H, B}
+  {
+    const uint64_t dims[4] = {(uint64_t)D, (uint64_t)pb->T_q, (uint64_t)pb->H, (uint64_t)pb->B};
+    const uint64_t qs[3] = {(uint64_t)pb->q_stride_t * 2, (uint64_t)pb->q_stride_h * 2,
+                            (uint64_t)(pb->B > 1 ? pb->q_stride_b * 2
+                                                 : pb->q_stride_h * 2 * pb->H)};
+    rc = pf_encode(pb->q, pb->dtype, dims, qs, &prm.qmap);
+    if (rc != HALO_OK) return rc;
+  }
+  prm.n_seg = n_seg;
+  prm.B = pb->B;
+  prm.H = pb->H;
+  prm.G = pb->H / pb->H_kv;
+  prm.T_q = pb->T_q;
+  prm.n_qtiles = (pb->T_q + prefill::kBM - 1) / prefill::kBM;
+  prm.q_pos0 = pb->q_pos0;
+  prm.scale_log2 = pb->scale * kLog2e;
+  prm.mode = po->mode;
+  prm.out_dtype = po->out_dtype;
+  prm.out = static_cast<char*>(po->out);
+  prm.out_sb = po->out_stride_b;
+  prm.out_sh = po->out_stride_h;
+  prm.out_st = po->out_stride_t;
+  prm.lse = po->lse;
+  prm.m = po->m;
+  prm.l = po->l;
+  prm.o = po->o;
+  prm.err = device_error_ptr();
+  const int64_t grid = (int64_t)prm.n_qtiles * pb->B * pb->H;
+  if (grid > INT32_MAX) return fail(HALO_ERR_UNSUPPORTED, "grid too large");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (pb->event_begin) cudaEventRecord(static_cast<cudaEvent_t>(pb->event_begin), st);
+  if (pb->dtype == HALO_DTYPE_BF16)
+    rc = D == 128 ? launch_kp<__nv_bfloat16, 128>(prm, (int)grid, st)
+                  : launch_kp<__nv_bfloat16, 64>(prm, (int)grid, st);
+  else
+    rc = D == 128 ? launch_kp<__half, 128>(prm, (int)grid, st)
+                  : launch_kp<__half, 64>(prm, (int)grid, st);
+  if (rc == HALO_OK && pb->event_end) cudaEventRecord(static_cast<cudaEvent_t>(pb->event_end), st);
+  return rc;
+}

@@ -194,7 +194,9 @@ extern "C" int32_t halo_page_summary(const void* k, int64_t k_sb, int64_t k_sh, 
   else if (dtype == HALO_DTYPE_F16) page_summary_kernel<__half><<<grid, 128, 0, st>>>(sp);
   else page_summary_kernel<float><<<grid, 128, 0, st>>>(sp);
   cudaError_t e = cudaGetLastError();
-  return e == cudaSuccess ? HALO_OK : cuda_fail(e, "page_summary_kernel launch");
+  if (e != cudaSuccess) return cuda_fail(e, "page_summary_kernel launch");
+  count_launches();
+  return HALO_OK;
 }
 
 extern "C" int32_t halo_page_score_topk(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_st,
@@ -225,6 +227,7 @@ extern "C" int32_t halo_page_score_topk(const void* q, int64_t q_sb, int64_t q_s
   else page_score_kernel<float><<<grid, 128, smem, st>>>(sp);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "page_score_kernel launch");
+  count_launches();
   if (k == 0 && !per_page) return HALO_OK;
   TopkParams tp{scores, exclude, per_page, topk, B * H_kv * T_q, P, k};
   const size_t tsmem = (size_t)n_pow2 * sizeof(unsigned long long);
@@ -236,5 +239,7 @@ extern "C" int32_t halo_page_score_topk(const void* q, int64_t q_sb, int64_t q_s
   });
   page_topk_kernel<<<1, 1024, tsmem, st>>>(tp, n_pow2);
   e = cudaGetLastError();
-  return e == cudaSuccess ? HALO_OK : cuda_fail(e, "page_topk_kernel launch");
+  if (e != cudaSuccess) return cuda_fail(e, "page_topk_kernel launch");
+  count_launches();
+  return HALO_OK;
 }

@@ -217,17 +217,108 @@ def accumulate_decode(q: torch.Tensor, chunks: Sequence[tuple], m: torch.Tensor,
     decode_raw(q3, structs, H_kv, D_v, scale=scale, q_pos=q_pos, merge=mg)
 
 
+PREFILL_MAX_CHUNKS = 48   # chunk descriptors per halo_prefill_attention call
+
+
+def prefill_supported(q: torch.Tensor, chunks: Sequence[tuple]) -> bool:
+    """Whether the tensor-core prefill kernel covers this problem: bf16 or
+    fp16, head dim 64 or 128, value head dim equal to it."""
+    D = q.shape[-1]
+    if q.dtype not in (torch.bfloat16, torch.float16) or D not in (64, 128):
+        return False
+    return all(k.dtype == q.dtype and v.dtype == q.dtype and k.shape[-1] == D and
+               v.shape[-1] == D for (k, v, _s, _c) in chunks)
+
+
+def prefill_attention(q: torch.Tensor, chunks: Sequence[tuple], *, query_pos_offset: int,
+                      scale: Optional[float] = None, out_dtype: Optional[torch.dtype] = None,
+                      out: Optional[torch.Tensor] = None, lse: Optional[torch.Tensor] = None,
+                      state: Optional[tuple] = None, accumulate: bool = False,
+                      events: Optional[tuple] = None):
+    """Chunked-prefill attention on the tcgen05 kernel
+    (``halo_prefill_attention``): ``q (B, H, T_q, D)`` with query row ``i`` at
+    global position ``query_pos_offset + i`` over ``(k, v, start, causal)``
+    chunks (``halo/kv_cache_chunked.py:873-942``).
+
+    ``state = (m, l, o)``: fp32 running state, ``m, l (B, H, T_q)`` and
+    ``o (B, H, T_q, D)`` contiguous.  ``accumulate=True`` folds the chunks
+    into it in place and returns ``None``; otherwise the state (if given) is
+    folded in and ``(out (B, H, T_q, D), lse (B, H, T_q))`` is returned."""
+    _require_cuda(q, "q")
+    B, H, T_q, D = q.shape
+    if q.stride(-1) != 1:
+        q = q.contiguous()
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    H_kv = int(chunks[0][0].shape[1]) if chunks else H
+    groups = [chunks[i:i + PREFILL_MAX_CHUNKS] for i in range(0, len(chunks), PREFILL_MAX_CHUNKS)]
+    if not groups:
+        groups = [[]]
+    if accumulate and state is None:
+        raise L.HaloError("accumulate needs state=(m, l, o)", L.HALO_ERR_INVALID_ARG)
+    if len(groups) > 1 and state is None:
+        state = (torch.full((B, H, T_q), float("-inf"), dtype=torch.float32, device=q.device),
+                 torch.zeros(B, H, T_q, dtype=torch.float32, device=q.device),
+                 torch.zeros(B, H, T_q, D, dtype=torch.float32, device=q.device))
+    if not accumulate:
+        if out is None:
+            out = torch.empty(B, H, T_q, D, dtype=out_dtype or q.dtype, device=q.device)
+        if lse is None:
+            lse = torch.empty(B, H, T_q, dtype=torch.float32, device=q.device)
+    lib = L.lib()
+    for gi, grp in enumerate(groups):
+        last = gi == len(groups) - 1
+        prob = L.PrefillProblem()
+        prob.B, prob.H, prob.H_kv, prob.T_q, prob.D = B, H, H_kv, T_q, D
+        prob.dtype = L.halo_dtype(q.dtype)
+        prob.q = q.data_ptr()
+        prob.q_stride_b, prob.q_stride_h, prob.q_stride_t = q.stride(0), q.stride(1), q.stride(2)
+        prob.q_pos0 = int(query_pos_offset)
+        prob.scale = float(scale)
+        if events is not None and last:
+            prob.event_begin, prob.event_end = events
+        structs, keep = [], []
+        for (k, v, start, causal) in grp:
+            _require_cuda(k, "k")
+            st, t = make_chunk(k, v, start, causal)
+            structs.append(st)
+            keep.append(t)
+        arr = (L.KVChunk * max(len(structs), 1))(*structs)
+        po = L.PrefillOut()
+        if state is not None:
+            m, l, o = state
+            po.m, po.l, po.o = m.data_ptr(), l.data_ptr(), o.data_ptr()
+        if accumulate or not last:
+            po.mode = L.MERGE_ACCUMULATE
+        else:
+            po.mode = L.MERGE_FINALIZE
+            po.out_dtype = L.halo_dtype(out.dtype)
+            po.out = out.data_ptr()
+            po.out_stride_b, po.out_stride_h, po.out_stride_t = out.stride(0), out.stride(1), \
+                out.stride(2)
+            po.lse = lse.data_ptr()
+        with torch.cuda.device(q.device):
+            rc = lib.halo_prefill_attention(ctypes.byref(prob), arr, len(structs), ctypes.byref(po),
+                                            L.stream_handle(q.device))
+        L.check(rc, "halo_prefill_attention")
+    return None if accumulate else (out, lse)
+
+
 def multi_query_attention(q: torch.Tensor, chunks: Sequence[tuple], *, scale: Optional[float] = None,
                           query_pos_offset: int, out_dtype: Optional[torch.dtype] = None):
     """``T_q > 1`` queries (a chunked-prefill slice) over causal chunks: query
     row ``i`` sits at global position ``query_pos_offset + i``
-    (``halo/kv_cache_chunked.py:873-942``).  Each query row is one decode
-    problem whose K/V batch stride is zero, so every row reuses the same
-    chunk memory.  Returns ``(out (B, H, T_q, D_v), lse (B, H, T_q))``."""
+    (``halo/kv_cache_chunked.py:873-942``).  bf16/fp16 with head dim 64 or
+    128 run the tensor-core prefill kernel; other shapes run each query row
+    as one decode problem whose K/V batch stride is zero, so every row reuses
+    the same chunk memory.  Returns ``(out (B, H, T_q, D_v), lse (B, H, T_q))``."""
     _require_cuda(q, "q")
     B, H, T_q, D = q.shape
     if scale is None:
         scale = 1.0 / math.sqrt(D)
+    if chunks and prefill_supported(q, chunks):
+        return prefill_attention(q, chunks, query_pos_offset=query_pos_offset, scale=scale,
+                                 out_dtype=out_dtype)
     D_v = int(chunks[0][1].shape[-1]) if chunks else D
     H_kv = int(chunks[0][0].shape[1]) if chunks else H
     out = torch.empty(B, H, T_q, D_v, dtype=out_dtype or q.dtype, device=q.device)

@@ -229,6 +229,52 @@ int32_t halo_page_score_topk(const void* q, int64_t q_sb, int64_t q_sh, int64_t 
                              const uint8_t* exclude, int32_t k, float* per_page, int64_t* topk,
                              halo_stream_t stream);
 
+/* ---------------------------------------------------------------- prefill */
+/* Multi-query (chunked-prefill) attention on the 5th-generation tensor cores:
+ * T_q query rows per (b, h) at global positions q_pos0 .. q_pos0 + T_q - 1
+ * attend to a list of K/V chunks (a chunk's `causal` flag hides keys after
+ * each query row).  Replaces the T_q > 1 branch of
+ * HALOCacheChunked.compute_attention (halo/kv_cache_chunked.py:873-942) that
+ * halo/chunked_prefill.py:73-135 drives slice by slice.  q is
+ * (B, H, T_q, D) with element strides (q_stride_b, q_stride_h, q_stride_t, 1);
+ * query head h reads KV head h / (H / H_kv).  bf16 or fp16, D = 64 or 128,
+ * value head dim equal to D.  Chunks that continue each other in memory and
+ * position are coalesced; at most 48 remain per call (HALO_ERR_UNSUPPORTED
+ * beyond: split the list and carry the running state). */
+typedef struct halo_prefill_problem {
+  int32_t B, H, H_kv, T_q, D;
+  int32_t dtype;               /* HALO_DTYPE_BF16 or HALO_DTYPE_F16 */
+  const void* q;
+  int64_t q_stride_b, q_stride_h, q_stride_t;
+  int64_t q_pos0;
+  float scale;
+  void* event_begin;           /* optional cudaEvent_t around the kernel */
+  void* event_end;
+} halo_prefill_problem_t;
+
+/* Result of halo_prefill_attention, per (b, h, t) row:
+ * mode HALO_MERGE_FINALIZE: out (B, H, T_q, D) in out_dtype (F32 or the input
+ *   dtype) with element strides (out_stride_b, out_stride_h, out_stride_t, 1);
+ *   lse (B, H, T_q) fp32 contiguous, optional.  Rows with no visible key get
+ *   zeros and -inf.  If m/l/o are non-NULL they are folded in first.
+ * mode HALO_MERGE_ACCUMULATE: the running state m, l (B, H, T_q) and
+ *   o (B, H, T_q, D), fp32 contiguous, with the meaning of halo_merge_args_t,
+ *   is updated in place. */
+typedef struct halo_prefill_out {
+  int32_t mode;
+  int32_t out_dtype;
+  void* out;
+  int64_t out_stride_b, out_stride_h, out_stride_t;
+  float* lse;
+  float* m;
+  float* l;
+  float* o;
+} halo_prefill_out_t;
+
+int32_t halo_prefill_attention(const halo_prefill_problem_t* problem,
+                               const halo_kv_chunk_t* chunks, int32_t n_chunks,
+                               const halo_prefill_out_t* out, halo_stream_t stream);
+
 /* ------------------------------------------------------------------ tiers */
 
 /* Pitched async copy of `height` rows of `width_bytes` between any two of
@@ -246,6 +292,10 @@ const char* halo_last_error_string(void);
 int32_t halo_device_error(int32_t* code_out, int32_t clear);
 /* ABI version: major*10000 + minor*100 + patch. */
 int32_t halo_version(void);
+/* Number of kernels this library has launched in this process (all devices,
+ * all streams).  A counter for benchmarks and tests; no reference
+ * counterpart. */
+uint64_t halo_launch_count(void);
 
 #ifdef __cplusplus
 }
