@@ -12,8 +12,14 @@ Total context is fixed as N grows (strong scaling).  K/V are seeded N(0,1)
 synthetic data resident in HBM; the working set per GPU (4.3 GB / N) is far
 larger than L2, so no flush is needed between steps.
 
-``--seq-len T`` shrinks the cfg5 context (a multiple of 4096 x N) for small
-profiling captures; the line then names the reduced workload.
+``--seq-len T`` shrinks the cfg5 context (a multiple of 4096 x N) or the cfg3
+prompt (a multiple of 4096) for small profiling captures; the line then names
+the reduced workload.
+
+``--workload cfg3`` runs BASELINE config 3 (one GPU): chunked prefill of a
+131072-token prompt in 32 slices of 4096 queries against the accumulated KV,
+causal, 32 q-heads / 8 KV heads, head_dim 128, on the tcgen05 prefill kernel;
+a step is the whole prompt of one layer.
 
 ``--workload cfg4`` runs BASELINE config 4 instead (one GPU): KIVI 2-bit
 decode of B4 / 32 q-heads / 8 KV heads / head_dim 128 over a 65536-token
@@ -45,11 +51,26 @@ if ROOT not in sys.path:
 CFG5 = dict(B=1, H=64, H_kv=8, D=128, T=1 << 20, chunk=4096)
 METRIC = "decode-attn tokens/s & achieved HBM GB/s at 32K-1M ctx, 1/2/4/8 B200"
 
-# DRAM traffic of the split-KV kernel per K/V byte it must read, from one ncu
-# capture (dram__bytes_read.sum + dram__bytes_write.sum over the algorithmic
-# K+V bytes of that launch); the capture and its command are summarised under
-# profiles/.  None until a capture of this workload exists.
-NCU_TRAFFIC_RATIO = None
+# DRAM traffic per algorithmic byte, from one ncu capture of each kernel
+# (dram__bytes_read.sum + dram__bytes_write.sum of the launch over the bytes
+# it must read); the captures and their commands are summarised under
+# profiles/.  kd_kernel: cfg5 reduced to 262144 tokens (1.0738 GB read +
+# 5.3 MB written over 1.0737 GB), scaled to a full launch by the K/V bytes it
+# processes.  kk_kernel: the cfg4 launch itself (201.0 MB + 4.8 MB over
+# 200.9 MB).
+NCU_TRAFFIC_RATIO = 1.0050
+NCU_TRAFFIC_RATIO_KK = 1.0243
+
+
+def _tensor_peak():
+    """Sustained dense bf16 TFLOP/s (a kernel timed inside a long step)."""
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            pk = json.load(f)
+        return float(pk["bf16_tflops_sustained"]), "measured (sustained)"
+    except Exception:
+        return 1400.0, "fallback (sustained)"
 
 
 def _peaks():
@@ -495,7 +516,7 @@ def run_ours_cfg4(args):
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_kind": f"of {peak_kind}",
                          "kernel": "kk_kernel (fused 2-bit dequant-and-attend)",
-                         "bytes_per_launch": nbytes, "traffic": None},
+                         "bytes_per_launch": nbytes, "traffic": nbytes * NCU_TRAFFIC_RATIO_KK},
             "cpu_baseline": cpu and {kk: cpu[kk] for kk in ("value", "unit", "cores", "kind",
                                                            "sample")},
             "e2e": {"value": c["B"] / (e2e_ms / 1e3), "unit": "tokens/s",
@@ -521,22 +542,202 @@ def run_reference_cfg4(args):
     print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------- cfg3 (chunked prefill)
+CFG3 = dict(B=1, H=32, H_kv=8, D=128, T=131072, slice=4096)
+METRIC3 = "chunked-prefill attention: prompt tokens/s & TFLOP/s (causal), 131072 tokens, 1 B200"
+
+
+def _cfg3_flops(T=None):
+    """Algorithmic causal FLOPs of one layer's prefill: 4 H D per visible
+    (query, key) pair, T (T + 1) / 2 pairs."""
+    c = CFG3
+    T = c["T"] if T is None else T
+    return 4 * c["H"] * c["D"] * T * (T + 1) // 2
+
+
+def _cfg3_config():
+    c = CFG3
+    name = ("cfg3: chunked prefill of a 131072-token prompt" if c["T"] == 131072 else
+            f"cfg3 reduced to a {c['T']}-token prompt (profiling case)")
+    return {"workload": f"{name} in {c['T'] // c['slice']} slices of {c['slice']} against the "
+                        "accumulated KV (causal), 32 q-heads / 8 KV heads, head_dim 128, B1, "
+                        "keys with 4 outlier channels x10 per head",
+            "global_batch": c["B"], "seq_len": c["T"], "slice": c["slice"],
+            "parallelism": "single GPU",
+            "l2": "Q/K/V/out %.2f GB per step > L2 (126 MB); no flush" %
+                  ((2 * c["H"] + 2 * c["H_kv"]) * c["T"] * c["D"] * 2 / 1e9)}
+
+
+def _cfg3_inputs(dev, T=None, H=None, H_kv=None):
+    import torch
+    c = CFG3
+    T = c["T"] if T is None else T
+    H = c["H"] if H is None else H
+    H_kv = c["H_kv"] if H_kv is None else H_kv
+    g = torch.Generator(device=dev).manual_seed(3)
+    q = torch.randn(c["B"], H, T, c["D"], device=dev, generator=g, dtype=torch.bfloat16)
+    k = torch.randn(c["B"], H_kv, T, c["D"], device=dev, generator=g)
+    v = torch.randn(c["B"], H_kv, T, c["D"], device=dev, generator=g, dtype=torch.bfloat16)
+    k = _outlier_keys(k, 33).bfloat16()
+    return q, k, v
+
+
+def cpu_baseline_cfg3(budget_s: float = 15.0):
+    """The reference's CPU path for one slice (fp32 attention of the slice's
+    queries over the accumulated keys, causal), through the oracle port, on a
+    sample: one KV head group and the last rows of the last slice, scaled by
+    the causal pair count of the whole prompt."""
+    import torch
+    from oracle import attention as OA
+    torch.set_num_threads(os.cpu_count() or 1)
+    c = CFG3
+    G = c["H"] // c["H_kv"]
+    T = c["T"]
+
+    def run(n_q):
+        q, k, v = _cfg3_inputs(torch.device("cpu"), T=T, H=G, H_kv=1)
+        qs = q[..., T - n_q:, :]
+        t0 = time.perf_counter()
+        OA.chunked_attention(qs, [(k, v, 0, True)], q_pos=T - n_q)
+        return time.perf_counter() - t0, n_q * T - n_q * (n_q - 1) // 2
+
+    t1, p1 = run(16)
+    n_q = int(max(256, min(c["slice"], 16 * budget_s / 3 / max(t1, 1e-3))))
+    t, pairs = run(n_q)
+    s_per_pair_group = t / pairs
+    step_s = s_per_pair_group * (T * (T + 1) // 2) * c["H_kv"]
+    return {"value": T / step_s, "unit": "prompt tokens/s", "cores": torch.get_num_threads(),
+            "kind": "port",
+            "sample": f"last {n_q} queries of the prompt x 1 of {c['H_kv']} KV head groups "
+                      f"against all {T} keys (causal, fp32), time scaled by causal pair count "
+                      f"x{(T * (T + 1) // 2) * c['H_kv'] / pairs:.0f}",
+            "s_per_step": step_s}
+
+
+def run_ours_cfg3(args):
+    import torch
+    from halo_b200 import _lib as L
+    from halo_b200 import ops
+    if args.gpus != 1 or int(os.environ.get("WORLD_SIZE", "1")) != 1:
+        raise SystemExit("cfg3 runs on one GPU")
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    c = CFG3
+    T, S = c["T"], c["slice"]
+    q, k, v = _cfg3_inputs(dev)
+    out = torch.empty_like(q)
+    lse = torch.empty(c["B"], c["H"], T, device=dev)
+
+    def step(qq, kk, vv, oo):
+        for s0 in range(0, T, S):
+            ops.prefill_attention(qq[:, :, s0:s0 + S], [(kk[..., :s0 + S, :], vv[..., :s0 + S, :],
+                                                         0, True)],
+                                  query_pos_offset=s0, out=oo[:, :, s0:s0 + S],
+                                  lse=lse[:, :, s0:s0 + S])
+
+    for _ in range(args.warmup):
+        step(q, k, v, out)
+    torch.cuda.synchronize()
+    K = args.steps
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n0 = L.launch_count()
+    with ClockSampler(0) as clocks:
+        t0.record()
+        for _ in range(K):
+            step(q, k, v, out)
+        t1.record()
+        torch.cuda.synchronize()
+    launches = L.launch_count() - n0
+    ms_step = t0.elapsed_time(t1) / K
+
+    # e2e: the step's Q/K/V come from pinned host memory, the output goes back
+    qh, kh, vh = q.cpu().pin_memory(), k.cpu().pin_memory(), v.cpu().pin_memory()
+    oh = torch.empty_like(qh).pin_memory()
+    qd, kd, vd = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+
+    def e2e_step():
+        qd.copy_(qh, non_blocking=True)
+        kd.copy_(kh, non_blocking=True)
+        vd.copy_(vh, non_blocking=True)
+        step(qd, kd, vd, out)
+        oh.copy_(out, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+
+    e2e_step()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n_e2e = max(1, min(K, 5))
+    e0.record()
+    for _ in range(n_e2e):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / n_e2e
+
+    flops = _cfg3_flops()
+    tflops = flops / (ms_step / 1e3) / 1e12
+    peak, peak_kind = _tensor_peak()
+    cpu = None if args.no_cpu_baseline else cpu_baseline_cfg3()
+    line = {"metric": METRIC3, "value": T / (ms_step / 1e3), "unit": "prompt tokens/s",
+            "n_gpus": 1, "steps": K, "warmup": args.warmup, "ms_per_step": ms_step,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic", "config": _cfg3_config(),
+            "roofline": {"bound": "tensor", "achieved": tflops, "peak": peak, "unit": "TFLOP/s",
+                         "frac": tflops / peak, "peak_kind": f"of {peak_kind}",
+                         "kernel": "kp_kernel (tcgen05 chunked-prefill attention)",
+                         "flops_per_step": flops, "traffic": None,
+                         "note": "algorithmic causal FLOPs; the kernel also runs P_lo V "
+                                 "(1.5x the tensor work) and the masked halves of diagonal tiles"},
+            "cpu_baseline": cpu and {kk: cpu[kk] for kk in ("value", "unit", "cores", "kind",
+                                                           "sample")},
+            "e2e": {"value": T / (e2e_ms / 1e3), "unit": "prompt tokens/s",
+                    "h2d_bytes_per_step": (q.numel() + k.numel() + v.numel()) * 2,
+                    "d2h_bytes_per_step": out.numel() * 2},
+            "clocks": clocks.summary(), "gpu_launches": launches}
+    print(json.dumps(line), flush=True)
+    return line
+
+
+def run_reference_cfg3(args):
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    cpu = cpu_baseline_cfg3(budget_s=max(10.0, 150.0 / max(1, args.steps + args.warmup)))
+    v = cpu["value"]
+    line = {"impl": "reference", "metric": METRIC3, "value": v, "unit": "prompt tokens/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": cpu["s_per_step"] * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": _cfg3_config(),
+            "cpu_baseline": {kk: cpu[kk] for kk in ("value", "unit", "cores", "kind", "sample")},
+            "e2e": {"value": v, "unit": "prompt tokens/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=300)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["cfg5", "cfg4"], default="cfg5")
+    ap.add_argument("--workload", choices=["cfg5", "cfg4", "cfg3"], default="cfg5")
     ap.add_argument("--seq-len", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
     if args.impl == "reference":
-        return run_reference_cfg4(args) if args.workload == "cfg4" else run_reference(args)
+        if args.workload == "cfg4":
+            return run_reference_cfg4(args)
+        if args.workload == "cfg3":
+            return run_reference_cfg3(args)
+        return run_reference(args)
     if args.workload == "cfg4":
         return run_ours_cfg4(args)
+    if args.workload == "cfg3":
+        if args.seq_len:
+            if args.seq_len % CFG3["slice"]:
+                raise SystemExit(f"--seq-len must be a multiple of {CFG3['slice']}")
+            CFG3["T"] = args.seq_len
+        return run_ours_cfg3(args)
     if args.seq_len:
         n = args.gpus * CFG5["chunk"]
         if args.seq_len % n:

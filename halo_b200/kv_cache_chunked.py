@@ -427,15 +427,27 @@ class HALOCacheChunked(HALOCache):
             return sum(1 for c0 in range(0, T_part, cs_) if not (causal and off + c0 > last_visible))
         n_chunks = n_walk(T_cold, 0) + n_walk(T_gpu, T_cold)
 
-        # running state in (B, T_q, H) row order
-        m = torch.full((B, T_q, H), float("-inf"), dtype=torch.float32, device=dev)
-        l = torch.zeros(B, T_q, H, dtype=torch.float32, device=dev)
-        o = torch.zeros(B, T_q, H, D_v, dtype=torch.float32, device=dev)
+        # T_q > 1 in bf16/fp16 with head dim 64/128: tensor-core prefill kernel,
+        # running state (B, H, T_q); otherwise the split-KV kernel, state in
+        # (B, T_q, H) row order.
+        use_pf = causal and ops.prefill_supported(q, [(like, (gpu_v if T_gpu > 0 else tier.v),
+                                                        0, True)])
+        if use_pf:
+            m = torch.full((B, H, T_q), float("-inf"), dtype=torch.float32, device=dev)
+            l = torch.zeros(B, H, T_q, dtype=torch.float32, device=dev)
+            o = torch.zeros(B, H, T_q, D_v, dtype=torch.float32, device=dev)
+        else:
+            m = torch.full((B, T_q, H), float("-inf"), dtype=torch.float32, device=dev)
+            l = torch.zeros(B, T_q, H, dtype=torch.float32, device=dev)
+            o = torch.zeros(B, T_q, H, D_v, dtype=torch.float32, device=dev)
 
         def fold(k, v, start):
             if T_q == 1:
                 ops.accumulate_decode(q, [(k, v, start, False)], m.view(B, H), l.view(B, H),
                                       o.view(B, H, D_v), scale=scale, q_pos=None)
+            elif use_pf:
+                ops.prefill_attention(q, [(k, v, start, True)], query_pos_offset=query_pos_offset,
+                                      scale=scale, state=(m, l, o), accumulate=True)
             else:
                 ops.multi_query_accumulate(q, [(k, v, start, True)], m, l, o, scale=scale,
                                            query_pos_offset=query_pos_offset)
@@ -469,8 +481,13 @@ class HALOCacheChunked(HALOCache):
                 dma += n * row_bytes
                 peak_stage = max(peak_stage, n * row_bytes)
 
-        out = torch.where(l.unsqueeze(-1) > 0, o / l.clamp_min(1e-30).unsqueeze(-1),
-                          torch.zeros_like(o))
+        if use_pf:
+            # no chunks: the kernel only normalises the carried state
+            out, _ = ops.prefill_attention(q, [], query_pos_offset=query_pos_offset, scale=scale,
+                                           state=(m, l, o), out_dtype=q.dtype)
+        else:
+            out = torch.where(l.unsqueeze(-1) > 0, o / l.clamp_min(1e-30).unsqueeze(-1),
+                              torch.zeros_like(o)).permute(0, 2, 1, 3)
         self._stats[layer_idx] = _ChunkedAttentionStats(
             hot_positions=T_gpu, cold_positions=T_cold, n_chunks=n_chunks, chunk_size=cs_,
             peak_staging_bytes=peak_stage, used_lse_merge=n_chunks > 1, dma_bytes=dma)
@@ -484,7 +501,7 @@ class HALOCacheChunked(HALOCache):
             self.refetcher.hits += refetched
         except Exception:
             pass
-        return out.permute(0, 2, 1, 3).to(q.dtype)
+        return out.to(q.dtype)
 
     # ------------------------------------------------------------------ bookkeeping
     def telemetry(self) -> dict:
