@@ -82,6 +82,22 @@ def dequantize_packed(codes, scale, zero, *, bits: int, group_size: int, out=Non
     return out
 
 
+def unpack_codes(codes: torch.Tensor, bits: int) -> torch.Tensor:
+    """Packed codes ``(..., D*bits/8)`` -> uint8 codes ``(..., D)``.  4/8
+    bits: code ``i`` at byte ``i*bits/8``, bit ``(i*bits)%8``.  2 bits: 16
+    codes per 32-bit word, code ``i`` at word ``i/16``, byte ``(i%16)%4``,
+    bits ``2*((i%16)/4)`` (the decoder's interleaved layout)."""
+    lead, nb = codes.shape[:-1], codes.shape[-1]
+    if bits == 2:
+        w = codes.reshape(*lead, nb // 4, 1, 4)
+        sh = (2 * torch.arange(4, device=codes.device, dtype=torch.uint8)).view(4, 1)
+        return ((w >> sh) & 3).reshape(*lead, nb * 4)
+    per = 8 // bits
+    c = codes.unsqueeze(-1).expand(*codes.shape, per)
+    shifts = torch.arange(per, device=codes.device, dtype=torch.uint8) * bits
+    return ((c >> shifts) & ((1 << bits) - 1)).reshape(*lead, nb * per)
+
+
 def _quantize_per_group(x, *, bits: int, group_size: int, axis: int):
     """Reference-shaped quantisation (``baselines/kivi_cache.py:44-69``):
     returns unpacked int8 codes ``(..., D/g, g)`` and scale/zero
@@ -90,10 +106,7 @@ def _quantize_per_group(x, *, bits: int, group_size: int, axis: int):
     shp = x.shape
     x4 = x.reshape(-1, 1, shp[-2] if x.dim() > 1 else 1, shp[-1]) if x.dim() != 4 else x
     codes, scale, zero = quantize_packed(x4, bits=bits, group_size=group_size)
-    per = 8 // bits
-    c = codes.unsqueeze(-1).expand(*codes.shape, per)
-    shifts = torch.arange(per, device=x.device, dtype=torch.uint8) * bits
-    q = ((c >> shifts) & ((1 << bits) - 1)).reshape(*codes.shape[:-1], codes.shape[-1] * per)
+    q = unpack_codes(codes, bits)
     g = shp[-1] // group_size
     return (q.to(torch.int8).reshape(*shp[:-1], g, group_size),
             scale.reshape(*shp[:-1], g, 1), zero.reshape(*shp[:-1], g, 1))
@@ -329,4 +342,4 @@ def wrap_with_kivi(model, *, memory_ratio: int = 4, **kw):
 
 
 __all__ = ["_quantize_per_group", "_dequantize_per_group", "KIVICache", "wrap_with_kivi",
-           "quantize_packed", "dequantize_packed", "kivi_decode"]
+           "quantize_packed", "dequantize_packed", "unpack_codes", "kivi_decode"]

@@ -583,21 +583,10 @@ struct KGeom {
   static_assert(kPackBytes % 16 == 0, "bulk copies need 16-byte multiples");
 };
 
-template <typename T>
-__device__ __forceinline__ uint32_t bits16(float x) {
-  const T h = Elem<T>::from_f32(x);
-  return static_cast<uint32_t>(*reinterpret_cast<const unsigned short*>(&h));
-}
-
-// rnd(fl32(c * s) + z): the reference's dequantisation of one code.
-template <typename T>
-__device__ __forceinline__ uint32_t dq1(uint32_t c, float s, float z) {
-  return bits16<T>(__fadd_rn(__fmul_rn((float)c, s), z));
-}
-
 // Warp w dequantises rows [16w, 16w+16) of one packed K or V tile into the
 // swizzled 64-row 16-bit tile `dq`.  Lane: row 16w + lane/2, half of the
-// row's columns by lane parity; one group (32 columns) at a time.
+// row's columns by lane parity; one group (32 columns) at a time.  All
+// accesses are explicit shared-memory loads and stores.
 template <typename T, int D, int BITS>
 __device__ __forceinline__ void dequant_rows(const char* pack, char* dq) {
   using KG = KGeom<T, D, BITS>;
@@ -607,46 +596,61 @@ __device__ __forceinline__ void dequant_rows(const char* pack, char* dq) {
   const int half = lane & 1;
   constexpr int kCols = D / 2;
   constexpr int kGroups = kCols / 32;
-  const uint8_t* codes = reinterpret_cast<const uint8_t*>(pack) + row * KG::kCB;
-  const T* sc = reinterpret_cast<const T*>(pack + KG::kCodeTile) + row * KG::kGS;
-  const T* ze = reinterpret_cast<const T*>(pack + KG::kCodeTile + KG::kSZTile) + row * KG::kGS;
+  const uint32_t s_codes = smem_addr(pack) + row * KG::kCB;
+  const uint32_t s_sc = smem_addr(pack + KG::kCodeTile) + row * KG::kGS * 2;
+  const uint32_t s_ze = smem_addr(pack + KG::kCodeTile + KG::kSZTile) + row * KG::kGS * 2;
+  const uint32_t s_dq = smem_addr(dq);
 #pragma unroll
   for (int j = 0; j < kGroups; ++j) {
     const int col0 = half * kCols + j * 32;
     const int g = col0 / 32;
-    const float s = Elem<T>::to_f32(sc[g]);
-    const float z = Elem<T>::to_f32(ze[g]);
+    uint16_t sb, zb;
+    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(sb) : "r"(s_sc + 2 * g));
+    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(zb) : "r"(s_ze + 2 * g));
+    const float s = Elem<T>::to_f32(*reinterpret_cast<const T*>(&sb));
+    const float z = Elem<T>::to_f32(*reinterpret_cast<const T*>(&zb));
     uint32_t out[16];
     if constexpr (BITS == 2) {
-      // 4-entry table of this group's values, selected per code with prmt
-      const uint32_t t01 = dq1<T>(0, s, z) | (dq1<T>(1, s, z) << 16);
-      const uint32_t t23 = dq1<T>(2, s, z) | (dq1<T>(3, s, z) << 16);
-      const uint2 cw = *reinterpret_cast<const uint2*>(codes + col0 / 4);
-      const uint32_t words[2] = {cw.x, cw.y};
+      // 4-entry table of this group's values {v0, v1 | v2, v3}; codes are
+      // interleaved so (word >> 2k) & 0x03030303 holds the codes of elements
+      // 4k..4k+3, one per byte, and c * 0x22 + 0x10 is the byte-permute
+      // selector of value c's two bytes.
+      const uint32_t t01 = Elem<T>::pack(__fadd_rn(__fmul_rn(0.f, s), z), __fadd_rn(s, z));
+      const uint32_t t23 =
+          Elem<T>::pack(__fadd_rn(__fmul_rn(2.f, s), z), __fadd_rn(__fmul_rn(3.f, s), z));
+      uint32_t words[2];
+      asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];"
+                   : "=r"(words[0]), "=r"(words[1]) : "r"(s_codes + col0 / 4));
 #pragma unroll
       for (int w = 0; w < 2; ++w)
 #pragma unroll
-        for (int bb = 0; bb < 4; ++bb) {
-          const uint32_t B = (words[w] >> (8 * bb)) & 0xFFu;
-          const uint32_t y = (B & 3u) | ((B & 0xCu) << 6) | ((B & 0x30u) << 12) | ((B & 0xC0u) << 18);
-          out[w * 8 + bb * 2] = __byte_perm(t01, t23, (y & 0xFFFFu) * 0x22u + 0x1010u);
-          out[w * 8 + bb * 2 + 1] = __byte_perm(t01, t23, (y >> 16) * 0x22u + 0x1010u);
+        for (int k = 0; k < 4; ++k) {
+          const uint32_t sel = ((words[w] >> (2 * k)) & 0x03030303u) * 0x22u + 0x10101010u;
+          out[w * 8 + 2 * k] = __byte_perm(t01, t23, sel);
+          out[w * 8 + 2 * k + 1] = __byte_perm(t01, t23, sel >> 16);
         }
     } else {
       constexpr uint32_t kMask = (1u << BITS) - 1u;
       constexpr int kPer = 8 / BITS;
+      uint32_t cw[32 * BITS / 32];
+#pragma unroll
+      for (int i = 0; i < BITS; ++i)
+        asm volatile("ld.shared.u32 %0, [%1];" : "=r"(cw[i]) : "r"(s_codes + col0 * BITS / 8 + 4 * i));
 #pragma unroll
       for (int e = 0; e < 32; e += 2) {
-        const int i0 = col0 + e, i1 = col0 + e + 1;
-        const uint32_t c0 = (codes[i0 / kPer] >> ((i0 % kPer) * BITS)) & kMask;
-        const uint32_t c1 = (codes[i1 / kPer] >> ((i1 % kPer) * BITS)) & kMask;
-        out[e / 2] = dq1<T>(c0, s, z) | (dq1<T>(c1, s, z) << 16);
+        const int i0 = e, i1 = e + 1;
+        const uint32_t c0 = (cw[(i0 / kPer) / 4] >> (8 * ((i0 / kPer) % 4) + (i0 % kPer) * BITS)) & kMask;
+        const uint32_t c1 = (cw[(i1 / kPer) / 4] >> (8 * ((i1 / kPer) % 4) + (i1 % kPer) * BITS)) & kMask;
+        out[e / 2] = Elem<T>::pack(__fadd_rn(__fmul_rn((float)c0, s), z),
+                                   __fadd_rn(__fmul_rn((float)c1, s), z));
       }
     }
 #pragma unroll
     for (int c = 0; c < 4; ++c)
-      *reinterpret_cast<uint4*>(dq + swz<Gm::kInner>(row, col0 / 8 + c)) =
-          make_uint4(out[4 * c], out[4 * c + 1], out[4 * c + 2], out[4 * c + 3]);
+      asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};"
+                   ::"r"(s_dq + swz<Gm::kInner>(row, col0 / 8 + c)), "r"(out[4 * c]),
+                     "r"(out[4 * c + 1]), "r"(out[4 * c + 2]), "r"(out[4 * c + 3])
+                   : "memory");
   }
 }
 

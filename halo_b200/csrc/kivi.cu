@@ -10,9 +10,13 @@
 //   s         = rnd(d / qmax);  z = mn
 //   q         = clamp(rint(rnd(rnd(x - z) / s)), 0, qmax)   (NaN -> 0)
 //   dequant   = rnd(fl32(q * s) + z)                        (no fused multiply-add)
-// Codes are packed 8/bits per byte along head_dim; code i of a row sits in
-// byte i*bits/8 at bit (i*bits) % 8.  Scale and zero are stored per group in
-// the 16-bit type, as the reference stores them.
+// Codes are packed 8/bits per byte along head_dim.  4 and 8 bits: code i of
+// a row sits in byte i*bits/8 at bit (i*bits) % 8.  2 bits: each 32-bit word
+// holds 16 codes interleaved for the decoder -- code i of the row sits in
+// word i/16, byte (i%16)%4, bits 2*((i%16)/4) -- so one shift and mask give
+// the codes of four consecutive elements, one per byte (halo_b200.h
+// documents the layout).  Scale and zero are stored per group in the 16-bit
+// type, as the reference stores them.
 #include <cstdint>
 
 #include "halo_common.cuh"
@@ -70,17 +74,25 @@ __global__ void __launch_bounds__(256) kivi_quantize_kernel(const QuantParams p)
   *ze = Elem<T>::from_f32(mn);
   uint8_t* out = p.codes + b * p.c_sb + h * p.c_sh + (int64_t)t * p.c_st +
                  (int64_t)g * p.group * p.bits / 8;
+  auto code = [&](int i) -> uint32_t {
+    const float tt = rnd<T>(__fsub_rn(Elem<T>::to_f32(x[i]), mn));
+    const float u = rnd<T>(__fdiv_rn(tt, s));
+    const float r = rintf(u);
+    return isnan(r) ? 0u : (uint32_t)fminf(fmaxf(r, 0.f), qmax);
+  };
+  if (p.bits == 2) {
+    // groups are whole 16-code words (group % 16 == 0 is checked)
+    for (int w = 0; w < p.group / 16; ++w) {
+      uint32_t word = 0;
+      for (int e = 0; e < 16; ++e) word |= code(16 * w + e) << (8 * (e & 3) + 2 * (e >> 2));
+      for (int bb = 0; bb < 4; ++bb) out[4 * w + bb] = (uint8_t)(word >> (8 * bb));
+    }
+    return;
+  }
   const int per_byte = 8 / p.bits;
   for (int i0 = 0; i0 < p.group; i0 += per_byte) {
     uint32_t byte = 0;
-    for (int j = 0; j < per_byte; ++j) {
-      const float tt = rnd<T>(__fsub_rn(Elem<T>::to_f32(x[i0 + j]), mn));
-      const float u = rnd<T>(__fdiv_rn(tt, s));
-      const float r = rintf(u);
-      uint32_t c = 0;
-      if (!isnan(r)) c = (uint32_t)fminf(fmaxf(r, 0.f), qmax);
-      byte |= c << (j * p.bits);
-    }
+    for (int j = 0; j < per_byte; ++j) byte |= code(i0 + j) << (j * p.bits);
     out[i0 / per_byte] = (uint8_t)byte;
   }
 }
@@ -108,7 +120,10 @@ __global__ void __launch_bounds__(256) kivi_dequantize_kernel(const QuantParams 
   const int per_byte = 8 / p.bits;
   const uint32_t mask = (1u << p.bits) - 1;
   for (int i = 0; i < p.group; ++i) {
-    const uint32_t c = (in[i / per_byte] >> ((i % per_byte) * p.bits)) & mask;
+    const int e = i & 15;
+    const uint32_t c =
+        p.bits == 2 ? (in[4 * (i >> 4) + (e & 3)] >> (2 * (e >> 2))) & 3u
+                    : (in[i / per_byte] >> ((i % per_byte) * p.bits)) & mask;
     x[i] = Elem<T>::from_f32(__fadd_rn(__fmul_rn((float)c, s), z));
   }
 }
@@ -126,6 +141,8 @@ static int kivi_check(int32_t B, int32_t H, int32_t T, int32_t D, int32_t dtype,
     return fail(HALO_ERR_UNSUPPORTED, "KIVI bits must be 2, 4 or 8 (got %d)", bits);
   if (group <= 0 || D % group || (group * bits) % 8)
     return fail(HALO_ERR_INVALID_ARG, "group %d must divide D=%d and pack to bytes", group, D);
+  if (bits == 2 && group % 16)
+    return fail(HALO_ERR_UNSUPPORTED, "2-bit groups must be multiples of 16 (got %d)", group);
   return HALO_OK;
 }
 

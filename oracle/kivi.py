@@ -82,18 +82,26 @@ def dequantize_per_group(codes: np.ndarray, scale: np.ndarray, zero: np.ndarray,
 
 
 def pack_codes_2bit(codes: np.ndarray) -> np.ndarray:
-    """Pack int8 codes 0..3 four to a byte along the flattened last axis;
-    code ``j`` of a byte sits in bits ``2j..2j+1`` (the device layout)."""
-    c = codes.reshape(*codes.shape[:-2], -1).astype(np.uint8)
-    c = c.reshape(*c.shape[:-1], c.shape[-1] // 4, 4)
-    return (c[..., 0] | (c[..., 1] << 2) | (c[..., 2] << 4) | (c[..., 3] << 6)).astype(np.uint8)
+    """Pack codes 0..3 of each row (flattened last two axes) into the device
+    layout: 16 codes per little-endian 32-bit word, code ``i`` in word
+    ``i // 16``, byte ``(i % 16) % 4``, bits ``2 * ((i % 16) // 4)``."""
+    c = codes.reshape(*codes.shape[:-2], -1).astype(np.uint32)
+    n = c.shape[-1]
+    assert n % 16 == 0
+    c = c.reshape(*c.shape[:-1], n // 16, 4, 4)           # (..., word, k, byte)
+    sh = (2 * np.arange(4, dtype=np.uint32)).reshape(4, 1)
+    byte = np.bitwise_or.reduce(c << sh, axis=-2)        # (..., word, byte)
+    return byte.astype(np.uint8).reshape(*c.shape[:-3], n // 4)
 
 
 def unpack_codes_2bit(packed: np.ndarray, group_size: int) -> np.ndarray:
     """Inverse of :func:`pack_codes_2bit`, back to ``(..., G, group_size)``."""
     p = packed.astype(np.uint8)
-    c = np.stack([(p >> (2 * j)) & 3 for j in range(4)], axis=-1)
-    c = c.reshape(*p.shape[:-1], p.shape[-1] * 4)
+    nb = p.shape[-1]
+    w = p.reshape(*p.shape[:-1], nb // 4, 1, 4)           # (..., word, 1, byte)
+    sh = (2 * np.arange(4, dtype=np.uint8)).reshape(4, 1)
+    c = (w >> sh) & 3                                     # (..., word, k, byte)
+    c = c.reshape(*p.shape[:-1], nb * 4)
     return c.reshape(*c.shape[:-1], c.shape[-1] // group_size, group_size).astype(np.int8)
 
 

@@ -77,10 +77,12 @@ def test_packed_quantize_matches_c_oracle(c_oracle, dtype, bits):
     xb = x.contiguous().view(torch.int16).numpy().view(np.uint16).copy()
     c_oracle.oracle_kivi_quantize(xb.ctypes.data, rows, 128, 32, bits, 0 if dtype == torch.float16 else 1,
                                   ref_c.ctypes.data, ref_s.ctypes.data, ref_z.ctypes.data)
-    per = 8 // bits
-    cb = codes.cpu().numpy().reshape(rows, 128 // per)
-    unpacked = np.stack([(cb >> (bits * j)) & ((1 << bits) - 1) for j in range(per)], -1).reshape(rows, 128)
+    from halo_b200.baselines.kivi_cache import unpack_codes
+    unpacked = unpack_codes(codes, bits).cpu().numpy().reshape(rows, 128)
     np.testing.assert_array_equal(unpacked.astype(np.int8), ref_c.reshape(rows, 128))
+    if bits == 2:   # the device layout is the oracle's packing
+        ref_packed = OK.pack_codes_2bit(ref_c.reshape(rows, 4, 32))
+        np.testing.assert_array_equal(codes.cpu().numpy().reshape(rows, 32), ref_packed)
     np.testing.assert_array_equal(_bits16(scale).reshape(-1), ref_s)
     np.testing.assert_array_equal(_bits16(zero).reshape(-1), ref_z)
 

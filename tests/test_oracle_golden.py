@@ -28,6 +28,17 @@ def _check_digest(d, *ts):
         "seeded inputs changed; regenerate tests/golden with make_golden.py"
 
 
+def test_kivi_2bit_device_layout_known_answers():
+    """16 codes per 32-bit word, code i at byte i % 4, bits 2 * (i // 4)."""
+    row = np.array([e % 4 for e in range(32)], dtype=np.int8).reshape(1, 32)
+    np.testing.assert_array_equal(OK.pack_codes_2bit(row), [0, 85, 170, 255] * 2)
+    row = np.array([(e % 16) // 4 for e in range(32)], dtype=np.int8).reshape(1, 32)
+    np.testing.assert_array_equal(OK.pack_codes_2bit(row), [228] * 8)
+    rng = np.random.default_rng(0)
+    c = rng.integers(0, 4, size=(3, 4, 32)).astype(np.int8)
+    np.testing.assert_array_equal(OK.unpack_codes_2bit(OK.pack_codes_2bit(c), 32), c)
+
+
 @pytest.fixture(scope="module")
 def att():
     return I.load("attention.npz")
