@@ -16,6 +16,14 @@ larger than L2, so no flush is needed between steps.
 prompt (a multiple of 4096) for small profiling captures; the line then names
 the reduced workload.
 
+``--workload cfg2`` runs BASELINE config 2 (one GPU): 32 layers of B8 /
+32 q-heads / 8 KV heads / 32K context in chunks of 1024; hot chunks (first +
+7 most recent) in HBM, 24 cold chunks per layer in pinned host DRAM; per
+layer and step the chunk scorer picks the top-8 cold chunks for a fresh
+query, the ones not already in the layer's GPU slot cache are refetched on a
+copy stream while the hot chunks are attended, then the selected chunks are
+folded in (``halo_b200.tiered.TieredLayer``).
+
 ``--workload cfg3`` runs BASELINE config 3 (one GPU): chunked prefill of a
 131072-token prompt in 32 slices of 4096 queries against the accumulated KV,
 causal, 32 q-heads / 8 KV heads, head_dim 128, on the tcgen05 prefill kernel;
@@ -363,6 +371,189 @@ def run_ours_cfg5(args):
         dist.barrier(device_ids=[local])
         dist.destroy_process_group()
     return line
+
+
+# ---------------------------------------------------------------- cfg2 (tiered decode)
+CFG2 = dict(L=32, B=8, H=32, H_kv=8, D=128, T=32768, chunk=1024, k_sel=8)
+METRIC2 = ("tiered decode tokens/s & achieved HBM GB/s, Llama-3-8B shapes, 32K ctx, "
+           "hot 25% + top-8 cold chunks refetched, 1 B200")
+
+
+def _cfg2_hot(P: int):
+    """hot_ratio 0.25: the first chunk plus the most recent ones."""
+    n_hot = max(1, P // 4)
+    return [0] + list(range(P - (n_hot - 1), P))
+
+
+def _cfg2_config():
+    c = CFG2
+    P = c["T"] // c["chunk"]
+    return {"workload": f"cfg2: tiered decode, {c['L']} layers, B{c['B']}, 32 q-heads / 8 KV "
+                        f"heads, head_dim 128, {c['T']} ctx in {P} chunks of {c['chunk']}; hot = "
+                        f"chunk 0 + {len(_cfg2_hot(P)) - 1} most recent (HBM), {P - len(_cfg2_hot(P))} "
+                        f"cold chunks in pinned host DRAM; per layer and step the chunk scorer picks "
+                        f"the top-{c['k_sel']} cold chunks for a fresh N(0,1) query and the ones not "
+                        f"already in the GPU slot cache are refetched; keys with 4 outlier channels",
+            "global_batch": c["B"], "seq_len": c["T"], "chunk": c["chunk"],
+            "parallelism": "single GPU",
+            "l2": "attended K/V 0.54 GB per layer > L2 (126 MB); no flush"}
+
+
+def cpu_baseline_cfg2(budget_s: float = 15.0):
+    """The reference's CPU decode attention over the same 16 chunks of one
+    layer (torch ops restated in the oracle), scaled by the layer count."""
+    import torch
+    from oracle import attention as OA
+    torch.set_num_threads(os.cpu_count() or 1)
+    c = CFG2
+    g = torch.Generator().manual_seed(2)
+    n_chunks = len(_cfg2_hot(c["T"] // c["chunk"])) + c["k_sel"]
+    q = torch.randn(c["B"], c["H"], 1, c["D"], generator=g).bfloat16()
+
+    def run(n):
+        chunks = []
+        for i in range(n):
+            k = torch.randn(c["B"], c["H_kv"], c["chunk"], c["D"], generator=g).bfloat16()
+            v = torch.randn(c["B"], c["H_kv"], c["chunk"], c["D"], generator=g).bfloat16()
+            chunks.append((k, v, i * c["chunk"], False))
+        t0 = time.perf_counter()
+        OA.chunked_attention(q, chunks)
+        return time.perf_counter() - t0
+
+    t1 = run(1)
+    n = int(max(1, min(n_chunks, budget_s / 2 / max(t1, 1e-3))))
+    t = run(n)
+    step_s = t * (n_chunks / n) * c["L"]
+    return {"value": c["B"] / step_s, "unit": "tokens/s", "cores": torch.get_num_threads(),
+            "kind": "port",
+            "sample": f"{n} of the {n_chunks} attended chunks of one of {c['L']} layers "
+                      f"(fp32 torch ops), scaled x{n_chunks / n * c['L']:.0f}",
+            "s_per_step": step_s}
+
+
+def run_ours_cfg2(args):
+    import torch
+    from halo_b200 import _lib as L
+    from halo_b200.tiered import TieredLayer
+    if args.gpus != 1 or int(os.environ.get("WORLD_SIZE", "1")) != 1:
+        raise SystemExit("cfg2 runs on one GPU")
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    c = CFG2
+    P = c["T"] // c["chunk"]
+    hot = _cfg2_hot(P)
+    copy_stream = torch.cuda.Stream(dev)
+    layers = []
+    g = torch.Generator(device=dev).manual_seed(2)
+    for li in range(c["L"]):
+        k = torch.randn(c["B"], c["H_kv"], c["T"], c["D"], device=dev, generator=g)
+        k = _outlier_keys(k, 200 + li).bfloat16()
+        v = torch.randn(c["B"], c["H_kv"], c["T"], c["D"], device=dev, generator=g,
+                        dtype=torch.bfloat16)
+        layers.append(TieredLayer(k, v, chunk_size=c["chunk"], hot_chunks=hot,
+                                  n_slots=c["k_sel"], copy_stream=copy_stream))
+        del k, v
+    n_q = args.warmup + args.steps + 4
+    qs = torch.randn(n_q, c["L"], c["B"], c["H"], c["D"], device=dev, generator=g,
+                     dtype=torch.bfloat16)
+    out = torch.empty(c["B"], c["H"], c["D"], device=dev, dtype=torch.bfloat16)
+    lse = torch.empty(c["B"], c["H"], device=dev)
+
+    def step(i, evs=None):
+        for li, lay in enumerate(layers):
+            lay.step(qs[i, li], k_sel=c["k_sel"], out=out, lse=lse,
+                     events=evs[li] if evs else None)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    for lay in layers:
+        for kk in lay.stats:
+            lay.stats[kk] = 0
+    K = args.steps
+    mk = lambda: torch.cuda.Event(enable_timing=True)
+    evs = [[[(mk(), mk()), (mk(), mk())] for _ in range(c["L"])] for _ in range(K)]
+    for e in (x for s_ in evs for l_ in s_ for pr in l_ for x in pr):
+        e.record()
+    torch.cuda.synchronize()
+    raw = [[((a.cuda_event, b.cuda_event), (c2.cuda_event, d.cuda_event))
+            for (a, b), (c2, d) in s_] for s_ in evs]
+    t0, t1 = mk(), mk()
+    n0 = L.launch_count()
+    with ClockSampler(0) as clocks:
+        t0.record()
+        for i in range(K):
+            step(args.warmup + i, raw[i])
+        t1.record()
+        torch.cuda.synchronize()
+    launches = L.launch_count() - n0
+    ms_step = t0.elapsed_time(t1) / K
+    kd_ms = sum(a.elapsed_time(b) + c2.elapsed_time(d)
+                for s_ in evs for (a, b), (c2, d) in s_) / K
+    refetched = sum(l_.stats["refetched_chunks"] for l_ in layers) / K
+    refetch_bytes = sum(l_.stats["refetch_bytes"] for l_ in layers) / K
+    att_bytes = (len(hot) + c["k_sel"]) * layers[0].chunk_bytes * c["L"]
+
+    # e2e: the query comes from pinned host memory, the output goes back
+    q_host = qs[:, :, :, :, :].cpu().pin_memory()
+    out_host = torch.empty(c["B"], c["H"], c["D"], dtype=torch.bfloat16).pin_memory()
+    q_dev = torch.empty_like(qs[0])
+
+    def e2e_step(i):
+        q_dev.copy_(q_host[i], non_blocking=True)
+        for li, lay in enumerate(layers):
+            lay.step(q_dev[li], k_sel=c["k_sel"], out=out, lse=lse)
+        out_host.copy_(out, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+
+    e2e_step(0)
+    e0, e1 = mk(), mk()
+    n_e2e = max(1, min(K, 5))
+    e0.record()
+    for i in range(n_e2e):
+        e2e_step(1 + i)
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / n_e2e
+
+    peak, peak_kind = _peaks()
+    achieved = att_bytes / (kd_ms / 1e3) / 1e9
+    cpu = None if args.no_cpu_baseline else cpu_baseline_cfg2()
+    line = {"metric": METRIC2, "value": c["B"] / (ms_step / 1e3), "unit": "tokens/s",
+            "n_gpus": 1, "steps": K, "warmup": args.warmup, "ms_per_step": ms_step,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic", "config": _cfg2_config(),
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "peak_kind": f"of {peak_kind}",
+                         "kernel": "kd_kernel (split-KV decode), hot + selected launches",
+                         "bytes_per_step": att_bytes, "kernel_ms_per_step": kd_ms,
+                         "traffic": att_bytes * NCU_TRAFFIC_RATIO},
+            "refetch": {"chunks_per_step": refetched, "bytes_per_step": refetch_bytes,
+                        "chunks_selected_per_step": c["k_sel"] * c["L"],
+                        "host_link_bound_ms": refetch_bytes / 54e9 * 1e3},
+            "cpu_baseline": cpu and {kk: cpu[kk] for kk in ("value", "unit", "cores", "kind",
+                                                           "sample")},
+            "e2e": {"value": c["B"] / (e2e_ms / 1e3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": qs[0].numel() * 2,
+                    "d2h_bytes_per_step": out.numel() * 2},
+            "clocks": clocks.summary(), "gpu_launches": launches}
+    print(json.dumps(line), flush=True)
+    return line
+
+
+def run_reference_cfg2(args):
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    cpu = cpu_baseline_cfg2(budget_s=max(10.0, 150.0 / max(1, args.steps + args.warmup)))
+    v = cpu["value"]
+    line = {"impl": "reference", "metric": METRIC2, "value": v, "unit": "tokens/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": cpu["s_per_step"] * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": _cfg2_config(),
+            "cpu_baseline": {kk: cpu[kk] for kk in ("value", "unit", "cores", "kind", "sample")},
+            "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
 
 
 # ---------------------------------------------------------------- cfg4 (KIVI)
@@ -718,7 +909,7 @@ def main():
     ap.add_argument("--steps", type=int, default=300)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["cfg5", "cfg4", "cfg3"], default="cfg5")
+    ap.add_argument("--workload", choices=["cfg5", "cfg4", "cfg3", "cfg2"], default="cfg5")
     ap.add_argument("--seq-len", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
@@ -727,11 +918,15 @@ def main():
     if args.impl == "reference":
         if args.workload == "cfg4":
             return run_reference_cfg4(args)
+        if args.workload == "cfg2":
+            return run_reference_cfg2(args)
         if args.workload == "cfg3":
             return run_reference_cfg3(args)
         return run_reference(args)
     if args.workload == "cfg4":
         return run_ours_cfg4(args)
+    if args.workload == "cfg2":
+        return run_ours_cfg2(args)
     if args.workload == "cfg3":
         if args.seq_len:
             if args.seq_len % CFG3["slice"]:
