@@ -149,6 +149,26 @@ SIGNATURES = {
     "halo_prefill_attention": (ctypes.c_int32, [ctypes.POINTER(PrefillProblem),
                                                 ctypes.POINTER(KVChunk), ctypes.c_int32,
                                                 ctypes.POINTER(PrefillOut), ctypes.c_void_p]),
+    "halo_chunked_decode_partials": (ctypes.c_int32, [ctypes.POINTER(DecodeProblem),
+                                                      ctypes.POINTER(KVChunk), ctypes.c_int32,
+                                                      ctypes.c_void_p, ctypes.c_int64,
+                                                      ctypes.POINTER(ctypes.c_int32),
+                                                      ctypes.POINTER(ctypes.c_int64),
+                                                      ctypes.c_void_p]),
+    "halo_exchange_bytes": (ctypes.c_int64, [ctypes.c_int32, ctypes.c_int32, ctypes.c_int32]),
+    "halo_ipc_alloc": (ctypes.c_int32, [ctypes.c_int64, ctypes.POINTER(ctypes.c_void_p),
+                                        ctypes.c_void_p]),
+    "halo_ipc_open": (ctypes.c_int32, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p)]),
+    "halo_ipc_close": (ctypes.c_int32, [ctypes.c_void_p]),
+    "halo_ipc_free": (ctypes.c_int32, [ctypes.c_void_p]),
+    "halo_sharded_merge": (ctypes.c_int32, [ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                                            ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p,
+                                            ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
+                                            ctypes.c_int64, ctypes.c_int64, ctypes.c_int32,
+                                            ctypes.c_int32, ctypes.c_uint32,
+                                            ctypes.POINTER(ctypes.c_void_p), ctypes.c_int32,
+                                            ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
+                                            ctypes.c_void_p, ctypes.c_void_p]),
     "halo_version": (ctypes.c_int32, []),
     "halo_launch_count": (ctypes.c_uint64, []),
 }

@@ -30,6 +30,7 @@
 #include <vector>
 
 #include "halo_common.cuh"
+#include "merge_row.cuh"
 
 namespace halo {
 
@@ -783,11 +784,11 @@ struct MergeParams {
 
 // One CTA of kMergeWarps warps per (b, h) row.  Pass 1: the row max M over
 // every partial (and the prior state).  Pass 2: warp w folds partials
-// s = w, w + kMergeWarps, ... with weights exp(m_s - M), four partials in
+// s = w, w + kMergeWarps, ... with weights exp(m_s - M), eight partials in
 // flight per lane; the warps' sums are then combined through shared memory.
-constexpr int kMergeWarps = 8;
+constexpr int kMergeWarps = 16;
 
-template <int DPL>
+template <int DPL, bool VEC>
 __global__ void __launch_bounds__(kMergeWarps * 32) km_kernel(const MergeParams mp) {
   __shared__ float s_red[kMergeWarps];
   __shared__ float s_l[kMergeWarps];
@@ -800,59 +801,15 @@ __global__ void __launch_bounds__(kMergeWarps * 32) km_kernel(const MergeParams 
   const bool have_prior = mp.m != nullptr;
 
   // ---- pass 1: row max
-  float M = -INFINITY;
-  for (int s = threadIdx.x; s < mp.P; s += blockDim.x) M = fmaxf(M, mr[s * mp.ps]);
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-  if (lane == 0) s_red[warp] = M;
-  __syncthreads();
-  M = have_prior ? mp.m[row] : -INFINITY;
-#pragma unroll
-  for (int w = 0; w < kMergeWarps; ++w) M = fmaxf(M, s_red[w]);
+  float M = row_max<kMergeWarps>(mr, mp.ps, mp.P, s_red);
+  if (have_prior) M = fmaxf(M, mp.m[row]);
 
   // ---- pass 2: weighted sums, this warp's share of the partials
   const int d0 = lane * DPL;
   const bool active = d0 < mp.Dv;
-  float L = 0.f;
+  float L;
   float acc[DPL];
-#pragma unroll
-  for (int e = 0; e < DPL; ++e) acc[e] = 0.f;
-  if (M != -INFINITY) {
-    int s = warp;
-    for (; s + 3 * kMergeWarps < mp.P; s += 4 * kMergeWarps) {
-      float ms[4], ls[4], w[4];
-      float ov[4][DPL];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        ms[j] = mr[(int64_t)(s + j * kMergeWarps) * mp.ps];
-        ls[j] = lr ? lr[(int64_t)(s + j * kMergeWarps) * mp.ps] : 1.f;
-        if (active) {
-          const float* src = orow + (int64_t)(s + j * kMergeWarps) * mp.ops + d0;
-#pragma unroll
-          for (int e = 0; e < DPL; ++e) ov[j][e] = src[e];
-        }
-      }
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        w[j] = (ms[j] == -INFINITY) ? 0.f : expf(ms[j] - M);
-        L = fmaf(ls[j], w[j], L);
-        if (active)
-#pragma unroll
-          for (int e = 0; e < DPL; ++e) acc[e] = fmaf(ov[j][e], w[j], acc[e]);
-      }
-    }
-    for (; s < mp.P; s += kMergeWarps) {
-      const float ms = mr[(int64_t)s * mp.ps];
-      if (ms == -INFINITY) continue;
-      const float w = expf(ms - M);
-      L = fmaf(lr ? lr[(int64_t)s * mp.ps] : 1.f, w, L);
-      if (active) {
-        const float* src = orow + (int64_t)s * mp.ops + d0;
-#pragma unroll
-        for (int e = 0; e < DPL; ++e) acc[e] = fmaf(src[e], w, acc[e]);
-      }
-    }
-  }
+  fold_partials<DPL, kMergeWarps, 8, VEC>(mr, lr, orow, mp.ps, mp.ops, mp.P, mp.Dv, M, L, acc);
   if (lane == 0) s_l[warp] = L;
 #pragma unroll
   for (int e = 0; e < DPL; ++e) s_o[warp][d0 + e] = acc[e];
@@ -1094,10 +1051,13 @@ static int validate_problem(const halo_decode_problem_t* p, const halo_kv_chunk_
 int launch_merge(const MergeParams& mp, cudaStream_t st) {
   if (mp.R == 0) return HALO_OK;
   const int threads = kMergeWarps * 32;
-  if (mp.Dv <= 32) km_kernel<1><<<mp.R, threads, 0, st>>>(mp);
-  else if (mp.Dv <= 64 && mp.Dv % 2 == 0) km_kernel<2><<<mp.R, threads, 0, st>>>(mp);
-  else if (mp.Dv <= 128 && mp.Dv % 4 == 0) km_kernel<4><<<mp.R, threads, 0, st>>>(mp);
-  else if (mp.Dv <= 256 && mp.Dv % 8 == 0) km_kernel<8><<<mp.R, threads, 0, st>>>(mp);
+  const bool vec = (reinterpret_cast<uintptr_t>(mp.o_parts) & 15) == 0 && mp.ops % 4 == 0 &&
+                   mp.ors % 4 == 0;
+  if (mp.Dv <= 32) km_kernel<1, false><<<mp.R, threads, 0, st>>>(mp);
+  else if (mp.Dv <= 64 && mp.Dv % 2 == 0) km_kernel<2, false><<<mp.R, threads, 0, st>>>(mp);
+  else if (mp.Dv <= 128 && mp.Dv % 4 == 0 && vec) km_kernel<4, true><<<mp.R, threads, 0, st>>>(mp);
+  else if (mp.Dv <= 128 && mp.Dv % 4 == 0) km_kernel<4, false><<<mp.R, threads, 0, st>>>(mp);
+  else if (mp.Dv <= 256 && mp.Dv % 8 == 0) km_kernel<8, false><<<mp.R, threads, 0, st>>>(mp);
   else return fail(HALO_ERR_UNSUPPORTED, "Dv %d unsupported by the merge", mp.Dv);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "km_kernel launch");
@@ -1507,16 +1467,14 @@ extern "C" int64_t halo_decode_workspace_bytes(const halo_decode_problem_t* prob
   return workspace_for(problem, plan.S);
 }
 
-extern "C" int32_t halo_chunked_decode(const halo_decode_problem_t* problem,
-                                       const halo_kv_chunk_t* chunks, int32_t n_chunks,
-                                       void* workspace, int64_t workspace_bytes,
-                                       const halo_merge_args_t* merge, halo_stream_t stream) {
-  int rc = validate_problem(problem, chunks, n_chunks);
-  if (rc != HALO_OK) return rc;
-  rc = validate_merge(merge, problem->Dv);
-  if (rc != HALO_OK) return rc;
+// The split-KV launches of a decode: partial (m, l, o) per split in the
+// workspace (m [R][S], l [R][S], o [R][S][Dv], each block 256-byte aligned).
+static int decode_splits(const halo_decode_problem_t* problem, const halo_kv_chunk_t* chunks,
+                         int32_t n_chunks, void* workspace, int64_t workspace_bytes,
+                         cudaStream_t st, int* S_out, float** m_out, float** l_out,
+                         float** o_out) {
   const halo_decode_problem_t& pb = *problem;
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int rc = HALO_OK;
   Plan plan = make_plan(problem, chunks, n_chunks);
   const int64_t need = workspace_for(problem, plan.S);
   if (plan.S > 0 && (!workspace || workspace_bytes < need))
@@ -1590,9 +1548,52 @@ extern "C" int32_t halo_chunked_decode(const halo_decode_problem_t* problem,
       if (e != cudaSuccess) return cuda_fail(e, "cudaEventRecord(event_end)");
     }
   }
-  MergeParams mp = merge_params(merge, pb.B, pb.H, pb.Dv, plan.S, m_part, l_part, o_part, 1,
-                                plan.S, pb.Dv, (int64_t)plan.S * pb.Dv);
+  *S_out = plan.S;
+  *m_out = m_part;
+  *l_out = l_part;
+  *o_out = o_part;
+  return HALO_OK;
+}
+
+extern "C" int32_t halo_chunked_decode(const halo_decode_problem_t* problem,
+                                       const halo_kv_chunk_t* chunks, int32_t n_chunks,
+                                       void* workspace, int64_t workspace_bytes,
+                                       const halo_merge_args_t* merge, halo_stream_t stream) {
+  int rc = validate_problem(problem, chunks, n_chunks);
+  if (rc != HALO_OK) return rc;
+  rc = validate_merge(merge, problem->Dv);
+  if (rc != HALO_OK) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int S = 0;
+  float *m_part = nullptr, *l_part = nullptr, *o_part = nullptr;
+  rc = decode_splits(problem, chunks, n_chunks, workspace, workspace_bytes, st, &S, &m_part,
+                     &l_part, &o_part);
+  if (rc != HALO_OK) return rc;
+  const halo_decode_problem_t& pb = *problem;
+  MergeParams mp = merge_params(merge, pb.B, pb.H, pb.Dv, S, m_part, l_part, o_part, 1, S,
+                                pb.Dv, (int64_t)S * pb.Dv);
   return launch_merge(mp, st);
+}
+
+extern "C" int32_t halo_chunked_decode_partials(const halo_decode_problem_t* problem,
+                                                const halo_kv_chunk_t* chunks, int32_t n_chunks,
+                                                void* workspace, int64_t workspace_bytes,
+                                                int32_t* n_parts, int64_t* offsets,
+                                                halo_stream_t stream) {
+  int rc = validate_problem(problem, chunks, n_chunks);
+  if (rc != HALO_OK) return rc;
+  if (!n_parts || !offsets) return fail(HALO_ERR_INVALID_ARG, "n_parts/offsets NULL");
+  int S = 0;
+  float *m_part = nullptr, *l_part = nullptr, *o_part = nullptr;
+  rc = decode_splits(problem, chunks, n_chunks, workspace, workspace_bytes,
+                     static_cast<cudaStream_t>(stream), &S, &m_part, &l_part, &o_part);
+  if (rc != HALO_OK) return rc;
+  const char* ws = static_cast<const char*>(workspace);
+  *n_parts = S;
+  offsets[0] = reinterpret_cast<const char*>(m_part) - ws;
+  offsets[1] = reinterpret_cast<const char*>(l_part) - ws;
+  offsets[2] = reinterpret_cast<const char*>(o_part) - ws;
+  return HALO_OK;
 }
 
 extern "C" int32_t halo_lse_merge(int32_t B, int32_t H, int32_t Dv, int32_t P,

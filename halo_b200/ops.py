@@ -148,6 +148,33 @@ def _decode_table(q3: torch.Tensor, table: ChunkTable, *, scale: float,
     L.check(rc, "halo_chunked_decode")
 
 
+def decode_partials(q3: torch.Tensor, table: ChunkTable, *, scale: float,
+                    q_pos: Optional[torch.Tensor] = None, events: Optional[tuple] = None):
+    """Split-KV launches only (``halo_chunked_decode_partials``): returns
+    ``(workspace, S, (m_off, l_off, o_off))`` -- the per-split fp32 partial
+    state left in the workspace, ``m``/``l`` ``[B*H][S]``, ``o``
+    ``[B*H][S][D_v]`` at those byte offsets -- for a caller-side merge."""
+    dev = q3.device
+    H_kv = table.H_kv if table.H_kv is not None else q3.shape[1]
+    D_v = table.D_v if table.D_v is not None else q3.shape[2]
+    prob = _problem(q3, H_kv, D_v, q_pos, scale)
+    if events is not None:
+        prob.event_begin, prob.event_end = events
+    lib = L.lib()
+    need = lib.halo_decode_workspace_bytes(ctypes.byref(prob), table.arr, table.n)
+    if need < 0:
+        L.check(int(need), "halo_decode_workspace_bytes")
+    ws = WORKSPACES.get(dev, int(need))
+    n_parts = ctypes.c_int32(0)
+    offs = (ctypes.c_int64 * 3)()
+    with torch.cuda.device(dev):
+        rc = lib.halo_chunked_decode_partials(ctypes.byref(prob), table.arr, table.n,
+                                              ws.data_ptr(), ws.numel(), ctypes.byref(n_parts),
+                                              offs, L.stream_handle(dev))
+    L.check(rc, "halo_chunked_decode_partials")
+    return ws, int(n_parts.value), (int(offs[0]), int(offs[1]), int(offs[2]))
+
+
 def chunked_decode(q: torch.Tensor, chunks, *, scale: Optional[float] = None,
                    q_pos: Optional[torch.Tensor] = None, out_dtype: Optional[torch.dtype] = None,
                    out: Optional[torch.Tensor] = None, lse: Optional[torch.Tensor] = None,

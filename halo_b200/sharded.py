@@ -12,6 +12,7 @@ sharding is new.
 """
 from __future__ import annotations
 
+import ctypes
 import math
 from typing import Optional
 
@@ -27,6 +28,81 @@ def shard_range(n_chunks: int, world: int, rank: int) -> tuple[int, int]:
     return lo, lo + base + (1 if rank < extra else 0)
 
 
+def gather_partials(o_local: torch.Tensor, lse_local: torch.Tensor, group=None,
+                    buffers: Optional[tuple] = None):
+    """All-gather every rank's partial ``(o (B, H, D_v), lse (B, H))``, fp32.
+
+    One collective over a packed ``[o | lse]`` row per rank; returns
+    ``(lse_parts (W, B, H), o_parts (W, B, H, D_v))`` in rank order -- views
+    into the gathered buffer, laid out for ``ops.lse_merge(...,
+    parts_major=True)``.  ``buffers = (local, gathered)`` reuses storage.
+    Works with any ``torch.distributed`` backend (NCCL on GPUs, gloo in
+    the CPU tests)."""
+    import torch.distributed as dist
+    world = dist.get_world_size(group)
+    B, H, D_v = o_local.shape
+    R = B * H
+    n = R * D_v + R
+    if buffers is None:
+        local = torch.empty(n, dtype=torch.float32, device=o_local.device)
+        gathered = torch.empty(world * n, dtype=torch.float32, device=o_local.device)
+    else:
+        local, gathered = buffers
+    if o_local.data_ptr() != local.data_ptr():
+        local[:R * D_v].copy_(o_local.reshape(-1))
+        local[R * D_v:].copy_(lse_local.reshape(-1))
+    dist.all_gather_into_tensor(gathered, local, group=group)   # flat: gloo and NCCL
+    rows = gathered.view(world, n)
+    return rows[:, R * D_v:].view(world, B, H), rows[:, :R * D_v].view(world, B, H, D_v)
+
+
+class P2PExchange:
+    """Every rank's exchange buffer mapped in this process (CUDA IPC over
+    NVLink), for ``halo_sharded_merge``.  Collective: every rank of `group`
+    constructs it at the same point."""
+
+    def __init__(self, rows: int, D_v: int, group=None):
+        import torch.distributed as dist
+        from halo_b200 import _lib as L
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        lib = L.lib()
+        nbytes = lib.halo_exchange_bytes(self.world, rows, D_v)
+        if nbytes < 0:
+            L.check(int(nbytes), "halo_exchange_bytes")
+        own = ctypes.c_void_p()
+        handle = (ctypes.c_char * 64)()
+        L.check(lib.halo_ipc_alloc(nbytes, ctypes.byref(own), handle), "halo_ipc_alloc")
+        self._own = own.value
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        ptrs, self._opened = [], []
+        for j, h in enumerate(handles):
+            if j == self.rank:
+                ptrs.append(self._own)
+                continue
+            p = ctypes.c_void_p()
+            buf = ctypes.create_string_buffer(h, 64)
+            L.check(lib.halo_ipc_open(buf, ctypes.byref(p)), "halo_ipc_open")
+            ptrs.append(p.value)
+            self._opened.append(p.value)
+        self.bufs = (ctypes.c_void_p * self.world)(*ptrs)
+        self.epoch = 0
+        torch.cuda.synchronize()
+        dist.barrier(group)
+
+    def close(self) -> None:
+        from halo_b200 import _lib as L
+        lib = L.lib()
+        torch.cuda.synchronize()
+        for p in self._opened:
+            lib.halo_ipc_close(ctypes.c_void_p(p))
+        self._opened = []
+        if self._own:
+            lib.halo_ipc_free(ctypes.c_void_p(self._own))
+            self._own = None
+
+
 class ShardedDecoder:
     """Decode attention of a query over a sequence-sharded KV cache.
 
@@ -34,13 +110,20 @@ class ShardedDecoder:
     whose first row sits at global position ``start``; they are attended in
     chunks of ``chunk_size`` (the chunk list is described once).  ``group`` is
     a ``torch.distributed`` process group (NCCL) or ``None`` for one GPU.
+    ``exchange``: ``"p2p"`` merges across ranks with one fused kernel over
+    NVLink peer memory (``halo_sharded_merge``), ``"nccl"`` with a local
+    merge, an NCCL all-gather and a merge of the gathered parts.
     """
 
     def __init__(self, k_shard: torch.Tensor, v_shard: torch.Tensor, *, start: int = 0,
-                 chunk_size: int = 4096, group=None):
+                 chunk_size: int = 4096, group=None, exchange: str = "p2p"):
         import torch.distributed as dist
+        if exchange not in ("p2p", "nccl"):
+            raise ValueError(f"exchange must be 'p2p' or 'nccl', not {exchange!r}")
         self.k, self.v = k_shard, v_shard
         self.group = group
+        self.exchange = exchange
+        self._x = None
         self.world = dist.get_world_size(group) if (group is not None or (
             dist.is_available() and dist.is_initialized())) else 1
         T = k_shard.shape[-2]
@@ -55,7 +138,7 @@ class ShardedDecoder:
         if key not in self._bufs:
             R = B * H
             local = torch.empty(R * D_v + R, dtype=torch.float32, device=dev)
-            gathered = torch.empty(self.world, R * D_v + R, dtype=torch.float32, device=dev)
+            gathered = torch.empty(self.world * (R * D_v + R), dtype=torch.float32, device=dev)
             self._bufs[key] = (local, gathered)
         return self._bufs[key]
 
@@ -71,21 +154,52 @@ class ShardedDecoder:
         if self.world == 1:
             return ops.chunked_decode(q3, self.table, scale=scale, out=out, lse=lse,
                                       events=events)
-        import torch.distributed as dist
+        if self.exchange == "p2p":
+            return self._p2p_call(q3, scale, out, lse, events)
         R = B * H
         local, gathered = self._buffers(B, H, D_v, q3.device)
-        ops.chunked_decode(q3, self.table, scale=scale,
-                           out=local[:R * D_v].view(B, H, D_v), lse=local[R * D_v:].view(B, H),
-                           events=events)
-        dist.all_gather_into_tensor(gathered, local, group=self.group)
-        m_parts = gathered[:, R * D_v:].view(self.world, B, H)
-        o_parts = gathered[:, :R * D_v].view(self.world, B, H, D_v)
+        o_loc, l_loc = local[:R * D_v].view(B, H, D_v), local[R * D_v:].view(B, H)
+        ops.chunked_decode(q3, self.table, scale=scale, out=o_loc, lse=l_loc, events=events)
+        m_parts, o_parts = gather_partials(o_loc, l_loc, self.group, buffers=(local, gathered))
         if out is None:
             out = torch.empty(B, H, D_v, dtype=q3.dtype, device=q3.device)
         return ops.lse_merge(m_parts, None, o_parts, out=out, lse=lse, parts_major=True)
 
+    def _p2p_call(self, q3, scale, out, lse, events):
+        from halo_b200 import _lib as L
+        B, H, D = q3.shape
+        D_v = self.table.D_v
+        if self._x is None or self._x_key != (B, H, D_v):
+            if self._x is not None:
+                self._x.close()
+            self._x = P2PExchange(B * H, D_v, self.group)
+            self._x_key = (B, H, D_v)
+        ws, S, (mo, lo, oo) = ops.decode_partials(q3, self.table, scale=scale, events=events)
+        if out is None:
+            out = torch.empty(B, H, D_v, dtype=q3.dtype, device=q3.device)
+        x = self._x
+        x.epoch += 1
+        base = ws.data_ptr()
+        with torch.cuda.device(q3.device):
+            rc = L.lib().halo_sharded_merge(
+                B, H, D_v, S, base + mo, base + lo, base + oo, 1, S, D_v, S * D_v, x.world,
+                x.rank, x.epoch & 0xFFFFFFFF, x.bufs, L.halo_dtype(out.dtype), out.data_ptr(),
+                out.stride(0), out.stride(1), lse.data_ptr() if lse is not None else None,
+                L.stream_handle(q3.device))
+        L.check(rc, "halo_sharded_merge")
+        return out, lse
+
+    def close(self) -> None:
+        """Release the peer mappings (collective-free; call on every rank)."""
+        if self._x is not None:
+            self._x.close()
+            self._x = None
+
     @property
     def launches_per_call(self) -> int:
-        """Kernels of this library per call (split-KV, local merge, and the
-        cross-rank merge when sharded)."""
-        return 2 + (1 if self.world > 1 else 0)
+        """Kernels of this library per call: split-KV + local merge on one
+        GPU; split-KV + fused exchange merge (p2p) or split-KV + local merge +
+        merge of the gathered parts (nccl) when sharded."""
+        if self.world == 1:
+            return 2
+        return 2 if self.exchange == "p2p" else 3

@@ -153,6 +153,52 @@ int32_t halo_chunked_decode_noalloc(const halo_decode_problem_t* problem,
                                     const halo_kv_chunk_t* chunks, int32_t n_chunks,
                                     const halo_merge_args_t* merge, halo_stream_t stream);
 
+/* Only the split-KV launches of halo_chunked_decode: the per-split partial
+ * state stays in `workspace` for the caller to merge (e.g. across GPUs with
+ * halo_sharded_merge).  On return *n_parts = S and offsets[0..2] are the byte
+ * offsets in the workspace of m [B*H][S], l [B*H][S] and o [B*H][S][Dv]
+ * (fp32; m in natural-log score units, l = sum exp(s - m), o unnormalised).
+ * Same inputs and workspace size as halo_chunked_decode. */
+int32_t halo_chunked_decode_partials(const halo_decode_problem_t* problem,
+                                     const halo_kv_chunk_t* chunks, int32_t n_chunks,
+                                     void* workspace, int64_t workspace_bytes,
+                                     int32_t* n_parts, int64_t* offsets, halo_stream_t stream);
+
+/* ------------------------------------------------------- multi-GPU merge */
+
+/* Bytes of one rank's exchange buffer for `world` ranks, `rows` = B*H output
+ * rows of Dv values: data[2][world][rows][Dv + 1] fp32 then
+ * flags[world][rows] uint32. */
+int64_t halo_exchange_bytes(int32_t world, int32_t rows, int32_t Dv);
+
+/* Exchange buffers shared across the processes of one node: halo_ipc_alloc
+ * allocates and zeroes `bytes` of device memory on the current device and
+ * writes its 64-byte CUDA IPC handle to handle_out; halo_ipc_open maps a
+ * peer's handle into this process (peer access over NVLink); close/free
+ * undo them. */
+int32_t halo_ipc_alloc(int64_t bytes, void** dev_ptr, void* handle_out);
+int32_t halo_ipc_open(const void* handle, void** dev_ptr);
+int32_t halo_ipc_close(void* dev_ptr);
+int32_t halo_ipc_free(void* dev_ptr);
+
+/* The cross-GPU step of a sequence-sharded decode in one kernel per rank:
+ * merge this rank's P local partials (layout as halo_lse_merge), write the
+ * normalised (o, lse) row into slot `rank` of every rank's exchange buffer
+ * (bufs[j] = rank j's buffer mapped in this process, bufs[rank] its own)
+ * through NVLink peer stores, publish a per-row flag = epoch, wait for the
+ * rows of all ranks (bounded: HALO_ERR_TIMEOUT in the device error word
+ * after 2 s), and write the merged out (B, H, Dv) in out_dtype and lse
+ * (B, H) (optional).  Every rank calls it with the same epoch, starting at
+ * 1 and increasing by one per call.  Replaces, for the sharded decode, the
+ * local merge + all-gather + merge of (o, lse); the reference
+ * (halo/kv_cache_chunked.py:194-239, single GPU) has no counterpart. */
+int32_t halo_sharded_merge(int32_t B, int32_t H, int32_t Dv, int32_t P, const float* m_parts,
+                           const float* l_parts, const float* o_parts, int64_t part_stride,
+                           int64_t row_stride, int64_t o_part_stride, int64_t o_row_stride,
+                           int32_t world, int32_t rank, uint32_t epoch, void* const* bufs,
+                           int32_t out_dtype, void* out, int64_t out_stride_b,
+                           int64_t out_stride_h, float* lse, halo_stream_t stream);
+
 /* ------------------------------------------------------------------ KIVI */
 
 /* Per-group round-to-nearest quantisation of x (B, H, T, D) (element strides
