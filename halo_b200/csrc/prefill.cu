@@ -38,6 +38,7 @@
 // one P buffer suffices; a commit tracks every earlier MMA of the issuing
 // thread, so s_full(i) also implies pv_done(i-2).
 #include <algorithm>
+#include <cmath>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -464,6 +465,449 @@ __global__ void __launch_bounds__(kThreads, 1) kp_kernel(const __grid_constant__
   }
 }
 
+
+// ======================================================================
+// kp2_kernel: two query tiles per CTA, double-buffered 64-key score tiles.
+//
+// CTA = query tiles A = 2*pair and B = 2*pair + 1 (B may be absent) of one
+// q-head; both walk the same K/V tiles (B's causal range; A joins the tiles
+// it can see).  K/V arrive as 128-key TMA tiles; scores are computed per
+// 64-key sub-tile j (half j%2 of K/V tile j/2).  384 threads:
+//   WG0  warp 0 TMA producer; warp 1 TMEM owner and MMA issuer of tile A
+//        (lane 0); warp 2 MMA issuer of tile B; warp 3 idle.  Registers
+//        lowered to 104 per thread.
+//   WG1  softmax of tile A (thread r = TMEM lane r), 200 registers.
+//   WG2  softmax of tile B, 200 registers.
+// TMEM (512 columns): tile X has two 64-column score buffers S_X[0..1] and a
+// D-column output accumulator O_X: S_A[b] = [64b, 64b+64), S_B[b] =
+// [128+64b, ...), O_A = [256, 256+D), O_B = [256+D, 256+2D).  P of sub-tile
+// j overwrites S_X[j%2] in place as 16-bit pairs (keys 32c..32c+31: hi in
+// columns [32c, 32c+16), lo in [32c+16, 32c+32)) and is the A operand of
+// O_X += P V (tcgen05.mma with A in TMEM).  With two score buffers the MMA
+// issuer computes S_X(j+1) while the softmax of S_X(j) runs; S_X(j+2) waits
+// for O_X += P_X(j) V to finish reading P.  A softmax that must rescale O_X
+// first waits for the previous PV_X.
+// Each tile's issuer runs, per K/V tile, QK(j), QK(j+1), PV(j), PV(j+1) on
+// its own commit chain; the two chains interleave on the tensor pipe.
+// Descriptors are precomputed (one add per MMA) so an issuing thread keeps
+// pace with the pipe.
+// Barriers: q_full; k_full/v_full/k_empty/v_empty [stages]; per tile X and
+// buffer b: s_full (commit after QK), p_full (128 softmax arrivals), pv_done
+// (commit after PV); mma_done per issuer.  K/V empty barriers take one
+// arrival per issuer.  All waits bounded.
+constexpr int kThreads2 = 384;
+constexpr int kSub = 64;                 // keys per score sub-tile
+
+template <int D>
+struct Geom2 {
+  static constexpr int kBlocks = D / 64;
+  static constexpr int kBlockBytes = kBM * 128;
+  static constexpr int kTileBytes = kBlocks * kBlockBytes;
+  static constexpr int kStages = D == 64 ? 4 : 2;
+  static constexpr int kOffQ = 0;                         // Q_A, Q_B
+  static constexpr int kOffK = 2 * kTileBytes;
+  static constexpr int kOffV = kOffK + kStages * kTileBytes;
+  static constexpr int kOffBar = kOffV + kStages * kTileBytes;
+  static constexpr int kSmemBytes = kOffBar + 512 + 1024;
+  static constexpr uint32_t kColO = 256;
+};
+
+struct Bars2 {
+  uint64_t q_full;
+  uint64_t k_full[4], v_full[4], k_empty[4], v_empty[4];
+  uint64_t s_full[2][2], p_full[2][2], pv_done[2][2], mma_done[2];
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+__device__ __forceinline__ bool wait_bar2(uint64_t* bar, uint32_t parity, Bars2* bs,
+                                          unsigned int* err) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+    for (int i = 0; i < 32; ++i)
+      if (mbar_try_wait(bar, parity)) return true;
+    if (*reinterpret_cast<volatile int*>(&bs->abort_flag)) return false;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      set_device_error(err, static_cast<unsigned int>(-HALO_ERR_TIMEOUT));
+      *reinterpret_cast<volatile int*>(&bs->abort_flag) = 1;
+      return false;
+    }
+  }
+}
+
+// Sub-tile walk shared by every role: K/V tile index g (within segment s,
+// tile t of that segment) and which query tiles take part.
+struct Walk {
+  int s, t, g;          // segment, tile in segment, global K/V tile
+  int ntU, ntA;         // tiles of segment s for the union / tile A
+};
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kThreads2, 1) kp2_kernel(const __grid_constant__ Params p) {
+  using Gm = Geom2<D>;
+  constexpr int ST = Gm::kStages;
+  // bf16 keeps P as hi + lo (two MMAs); fp16's 11-bit P alone keeps the
+  // output within the error budget (|err| <~ 2^-12 |v|), so one MMA.
+  constexpr bool kSplitP = Elem<T>::kDtype == HALO_DTYPE_BF16;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  Bars2* bs = reinterpret_cast<Bars2*>(smem + Gm::kOffBar);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  const int BH = p.B * p.H;
+  const int n_pairs = (p.n_qtiles + 1) / 2;
+  const int pair = n_pairs - 1 - (int)(blockIdx.x / BH);   // heavy first
+  const int bh = (int)(blockIdx.x % BH);
+  const int b = bh / p.H, h = bh % p.H, hk = h / p.G;
+  const int qA0 = 2 * pair * kBM;
+  const bool hasB = 2 * pair + 1 < p.n_qtiles;
+  const int validA = min(kBM, p.T_q - qA0);
+  const int validB = hasB ? min(kBM, p.T_q - (qA0 + kBM)) : 0;
+  const int64_t qminA = p.q_pos0 + qA0, qmaxA = qminA + validA - 1;
+  const int64_t qminB = qminA + kBM, qmaxB = qminB + validB - 1;
+  const int64_t qmaxU = hasB ? qmaxB : qmaxA;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bs->q_full, 1);
+    for (int i = 0; i < ST; ++i) {
+      mbar_init(&bs->k_full[i], 1);
+      mbar_init(&bs->v_full[i], 1);
+      mbar_init(&bs->k_empty[i], 2);
+      mbar_init(&bs->v_empty[i], 2);
+    }
+    for (int x = 0; x < 2; ++x) {
+      for (int k = 0; k < 2; ++k) {
+        mbar_init(&bs->s_full[x][k], 1);
+        mbar_init(&bs->p_full[x][k], kBM);
+        mbar_init(&bs->pv_done[x][k], 1);
+      }
+      mbar_init(&bs->mma_done[x], 1);
+    }
+    bs->abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    umma::tmem_alloc(&bs->tmem_base, kTmemCols);
+    umma::tmem_relinquish();
+  }
+  umma::fence_before_sync();
+  __syncthreads();
+  umma::fence_after_sync();
+  const uint32_t tmem = bs->tmem_base;
+
+  // K/V tiles of the union walk and tile A's share of them
+  int nU = 0, nA = 0;
+  for (int s = 0; s < p.n_seg; ++s) {
+    nU += seg_tiles(p.seg[s], qmaxU);
+    nA += seg_tiles(p.seg[s], qmaxA);
+  }
+
+  const uint32_t sQ = smem_addr(smem + Gm::kOffQ);
+  const uint32_t sK = smem_addr(smem + Gm::kOffK);
+  const uint32_t sV = smem_addr(smem + Gm::kOffV);
+
+  // Register split (128 x 104 + 256 x 200 = 384 x 168, the launch budget),
+  // made inside each role's branch so the compiler sizes each role's code
+  // for its own budget.
+  if (warp < 4) {
+    umma::regs_dec<104>();
+    if (warp == 0) {
+      // ---------------------------------------------------------- producer
+      if (lane == 0 && nU > 0) {
+        mbar_arrive_expect_tx(&bs->q_full, (hasB ? 2 : 1) * Gm::kTileBytes);
+        for (int x = 0; x < (hasB ? 2 : 1); ++x)
+          for (int blk = 0; blk < Gm::kBlocks; ++blk)
+            tma_load_4d(smem + Gm::kOffQ + x * Gm::kTileBytes + blk * Gm::kBlockBytes, &p.qmap,
+                        blk * 64, qA0 + x * kBM, h, b, &bs->q_full);
+        int nk = 0, nv = 0;
+        bool ok = true;
+        for (int s = 0; s < p.n_seg && ok; ++s) {
+          const int nt = seg_tiles(p.seg[s], qmaxU);
+          const int bb = p.seg[s].bcast ? 0 : b;
+          for (int t = 0; t < nt; ++t) {
+            const int st = nk % ST, use = nk / ST;
+            if (use > 0 && !(ok = wait_bar2(&bs->k_empty[st], (use - 1) & 1, bs, p.err))) break;
+            mbar_arrive_expect_tx(&bs->k_full[st], Gm::kTileBytes);
+            for (int blk = 0; blk < Gm::kBlocks; ++blk)
+              tma_load_4d(smem + Gm::kOffK + st * Gm::kTileBytes + blk * Gm::kBlockBytes,
+                          &p.kmap[s], blk * 64, t * kBN, hk, bb, &bs->k_full[st]);
+            ++nk;
+            if (use > 0 && !(ok = wait_bar2(&bs->v_empty[st], (use - 1) & 1, bs, p.err))) break;
+            mbar_arrive_expect_tx(&bs->v_full[st], Gm::kTileBytes);
+            for (int blk = 0; blk < Gm::kBlocks; ++blk)
+              tma_load_4d(smem + Gm::kOffV + st * Gm::kTileBytes + blk * Gm::kBlockBytes,
+                          &p.vmap[s], blk * 64, t * kBN, hk, bb, &bs->v_full[st]);
+            ++nv;
+          }
+        }
+        // let every issued copy land before the CTA can exit
+        mbar_wait(&bs->q_full, 0, p.err);
+        for (int st = 0; st < ST; ++st) {
+          const int uk = (nk - st + ST - 1) / ST, uv = (nv - st + ST - 1) / ST;
+          if (uk > 0) mbar_wait(&bs->k_full[st], (uk - 1) & 1, p.err);
+          if (uv > 0) mbar_wait(&bs->v_full[st], (uv - 1) & 1, p.err);
+        }
+      }
+    } else if ((warp == 1 || warp == 2) && lane == 0 && nU > 0) {
+      // ---------------------------------------------------------- MMA issuers
+      // warp 1 issues tile A's MMAs, warp 2 tile B's: two independent
+      // commit chains, so one tile's waits never idle the other's work.
+      // Both walk every K/V tile and arrive on its empty barriers (count 2):
+      // a commit when they read it, a plain arrive when they sit it out.
+      const int x = warp - 1;
+      constexpr bool kBf16 = Elem<T>::kDtype == HALO_DTYPE_BF16;
+      constexpr uint32_t kIdQK = umma::instr_desc_f16(kBM, kSub, kBf16, false, false);
+      constexpr uint32_t kIdPV = umma::instr_desc_f16(kBM, D, kBf16, false, true);
+      const uint64_t qdesc = umma::smem_desc_sw128(sQ + x * Gm::kTileBytes, 16, 1024);
+      const uint64_t kdesc0 = umma::smem_desc_sw128(sK, 16, 1024);
+      const uint64_t vdesc0 = umma::smem_desc_sw128(sV, Gm::kBlockBytes, 1024);
+      const uint32_t scol0 = tmem + x * 128;
+      const uint32_t ocol = tmem + Gm::kColO + x * D;
+      bool ok = true;
+      if (x == 0 || hasB) ok = wait_bar2(&bs->q_full, 0, bs, p.err);
+      int g = 0, jx = 0;
+      for (int s = 0; s < p.n_seg && ok; ++s) {
+        const int ntU = seg_tiles(p.seg[s], qmaxU);
+        const int ntA = seg_tiles(p.seg[s], qmaxA);
+        for (int t = 0; t < ntU && ok; ++t, ++g) {
+          const bool in = x ? hasB : (t < ntA);
+          const int st = g % ST, use = g / ST;
+          if (!(ok = wait_bar2(&bs->k_full[st], use & 1, bs, p.err))) break;
+          if (in) {
+            const uint64_t kdesc = kdesc0 + (uint64_t)((st * Gm::kTileBytes) >> 4);
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+              const int j = jx + hh, bf = j & 1;
+              if (j >= 2 && !(ok = wait_bar2(&bs->pv_done[x][bf], ((j - 2) >> 1) & 1, bs, p.err)))
+                break;
+              umma::fence_after_sync();
+              const uint64_t kd = kdesc + (uint64_t)((hh * kSub * 128) >> 4);
+#pragma unroll
+              for (int kk = 0; kk < D / 16; ++kk) {
+                const uint32_t off = ((kk >> 2) * Gm::kBlockBytes + (kk & 3) * 32) >> 4;
+                umma::mma_ss(scol0 + bf * kSub, qdesc + off, kd + off, kIdQK, kk > 0);
+              }
+              umma::commit(&bs->s_full[x][bf]);
+            }
+            if (!ok) break;
+            umma::commit(&bs->k_empty[st]);
+          } else {
+            mbar_arrive(&bs->k_empty[st]);
+          }
+          if (!(ok = wait_bar2(&bs->v_full[st], use & 1, bs, p.err))) break;
+          if (in) {
+            const uint64_t vdesc = vdesc0 + (uint64_t)((st * Gm::kTileBytes) >> 4);
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+              const int j = jx + hh, bf = j & 1;
+              if (!(ok = wait_bar2(&bs->p_full[x][bf], (j >> 1) & 1, bs, p.err))) break;
+              umma::fence_after_sync();
+              const uint32_t pcol = scol0 + bf * kSub;
+              const uint64_t vd = vdesc + (uint64_t)((hh * kSub * 128) >> 4);
+#pragma unroll
+              for (int part = 0; part < (kSplitP ? 2 : 1); ++part)
+#pragma unroll
+                for (int kk = 0; kk < kSub / 16; ++kk)
+                  umma::mma_ts(ocol, pcol + (kk >> 1) * 32 + part * 16 + (kk & 1) * 8,
+                               vd + (uint64_t)((kk * 16 * 128) >> 4), kIdPV, (j > 0) || part || kk);
+              umma::commit(&bs->pv_done[x][bf]);
+            }
+            if (!ok) break;
+            umma::commit(&bs->v_empty[st]);
+            jx += 2;
+          } else {
+            mbar_arrive(&bs->v_empty[st]);
+          }
+        }
+      }
+      // this thread's MMAs complete before the CTA can free TMEM
+      umma::commit(&bs->mma_done[x]);
+      mbar_wait(&bs->mma_done[x], 0, p.err);
+    }
+  } else {
+    umma::regs_inc<200>();
+    // ------------------------------------------------------------ softmax X
+    const int x = (warp - 4) >> 2;              // 0: tile A, 1: tile B
+    const int sub = warp & 3;
+    const int r = sub * 32 + lane;
+    const uint32_t trow = tmem + ((uint32_t)(sub * 32) << 16);
+    const uint32_t ocol = Gm::kColO + x * D;
+    const bool active = x == 0 || hasB;
+    const int64_t qmin = x ? qminB : qminA;
+    const int64_t qmaxX = x ? qmaxB : qmaxA;
+    const int64_t qpos = qmin + r;
+    int nX = 0;                                  // sub-tiles of tile X
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    int j = 0;
+    for (int s = 0; s < p.n_seg && ok && active; ++s) {
+      const Seg sg = p.seg[s];
+      const int nt = seg_tiles(sg, qmaxX);
+      for (int t = 0; t < nt * 2; ++t, ++j) {
+        const int bf = j & 1;
+        const uint32_t scol = x * 128 + bf * kSub;
+        ok = __all_sync(0xffffffffu, wait_bar2(&bs->s_full[x][bf], (j >> 1) & 1, bs, p.err));
+        if (!ok) break;
+        umma::fence_after_sync();
+        const int row0 = (t >> 1) * kBN + (t & 1) * kSub;
+        const int64_t kpos0 = sg.start + row0;
+        const bool full = (row0 + kSub <= sg.len) && (!sg.causal || kpos0 + kSub - 1 <= qmin);
+        const int lim_len = sg.len - row0;
+        const int64_t lim_pos = sg.causal ? qpos - kpos0 : (int64_t)kSub;
+        // the sub-tile's 64 scores: two loads, one wait
+        float sv[kSub];
+        umma::tmem_ld32(trow + scol, sv);
+        umma::tmem_ld32(trow + scol + 32, sv + 32);
+        umma::tmem_wait_ld();
+        if (!full) {
+#pragma unroll
+          for (int c = 0; c < kSub; ++c)
+            if (!(c < lim_len && (int64_t)c <= lim_pos)) sv[c] = -INFINITY;
+        }
+        float mx8[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) mx8[e] = sv[e];
+#pragma unroll
+        for (int c = 8; c < kSub; ++c) mx8[c & 7] = fmaxf(mx8[c & 7], sv[c]);
+        const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                               fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]))) *
+                         p.scale_log2;
+        const bool grow = mx > m + kRescaleLog2 || (m == -INFINITY && mx > -INFINITY);
+        float fac = 1.f;
+        if (grow) {
+          fac = (m == -INFINITY) ? 0.f : ex2(m - mx);
+          l *= fac;
+          m = mx;
+        }
+        if (j > 0 && __any_sync(0xffffffffu, grow)) {
+          // O_X must be quiescent: wait for O_X += P_X(j-1) V
+          ok = __all_sync(0xffffffffu, wait_bar2(&bs->pv_done[x][bf ^ 1], ((j - 1) >> 1) & 1,
+                                                  bs, p.err));
+          if (!ok) break;
+          umma::fence_after_sync();
+#pragma unroll
+          for (int c = 0; c < D / 32; ++c) {
+            float ov[32];
+            umma::tmem_ld32(trow + ocol + c * 32, ov);
+            umma::tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) ov[e] *= fac;
+            umma::tmem_st32(trow + ocol + c * 32, ov);
+          }
+        }
+        // P = exp2(s * scale_log2 - m) as 16-bit pairs into S's columns
+        const float nmu = (m == -INFINITY) ? 0.f : -m;
+        const float sl2 = p.scale_log2;
+        float rs4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int c = 0; c < kSub / 32; ++c) {
+          uint32_t hi[16], lo[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const float p0 = ex2(fmaf(sv[c * 32 + 2 * e], sl2, nmu));
+            const float p1 = ex2(fmaf(sv[c * 32 + 2 * e + 1], sl2, nmu));
+            rs4[e & 3] += p0 + p1;
+            if constexpr (kSplitP) {
+              // hi = p truncated to bf16 (upper halves, one byte permute
+              // per pair), lo = rnd(p - hi): ~16 significant bits in all
+              const uint32_t b0 = __float_as_uint(p0), b1 = __float_as_uint(p1);
+              hi[e] = __byte_perm(b0, b1, 0x7632);
+              lo[e] = pack2<T>(p0 - __uint_as_float(b0 & 0xFFFF0000u),
+                               p1 - __uint_as_float(b1 & 0xFFFF0000u));
+            } else {
+              hi[e] = pack2<T>(p0, p1);
+            }
+          }
+          umma::tmem_st16u(trow + scol + c * 32, hi);
+          if constexpr (kSplitP) umma::tmem_st16u(trow + scol + c * 32 + 16, lo);
+        }
+        l += (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
+        umma::tmem_wait_st();
+        umma::fence_before_sync();
+        mbar_arrive(&bs->p_full[x][bf]);
+      }
+    }
+    nX = j;
+
+    // ---- epilogue of tile X: thread r finalises query row q0 + r
+    if (active && ok && nX > 0) {
+      ok = __all_sync(0xffffffffu, wait_bar2(&bs->pv_done[x][(nX - 1) & 1], ((nX - 1) >> 1) & 1,
+                                              bs, p.err));
+      if (ok) umma::fence_after_sync();
+    }
+    const int validX = x ? validB : validA;
+    if (active && ok) {
+      const int t = qA0 + x * kBM + r;
+      const bool live = r < validX;
+      const int64_t row = ((int64_t)b * p.H + h) * p.T_q + t;
+      float M = (m == -INFINITY) ? -INFINITY : m * kLn2;
+      float L = l, wo = 1.f, wp = 0.f;
+      const float* op = nullptr;
+      if (live && p.m != nullptr) {
+        const float mp = p.m[row], lp = p.l[row];
+        const float Mn = fmaxf(M, mp);
+        wo = (M == -INFINITY) ? 0.f : expf(M - Mn);
+        wp = (mp == -INFINITY) ? 0.f : expf(mp - Mn);
+        op = p.o + row * D;
+        L = L * wo + lp * wp;
+        M = Mn;
+      }
+      const float inv = (L > 0.f) ? 1.f / L : 0.f;
+      if (live && p.mode != HALO_MERGE_ACCUMULATE && p.lse)
+        p.lse[row] = (L > 0.f) ? M + logf(L) : -INFINITY;
+      if (live && p.mode == HALO_MERGE_ACCUMULATE) {
+        p.m[row] = M;
+        p.l[row] = L;
+      }
+      const int64_t off = (int64_t)b * p.out_sb + (int64_t)h * p.out_sh + (int64_t)t * p.out_st;
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        float ov[32];
+        if (nX > 0) {
+          umma::tmem_ld32(trow + ocol + c * 32, ov);   // warp-collective: every lane
+          umma::tmem_wait_ld();
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) ov[e] = 0.f;
+        }
+        if (!live) continue;
+        if (op) {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) ov[e] = ov[e] * wo + op[c * 32 + e] * wp;
+        }
+        if (p.mode == HALO_MERGE_ACCUMULATE) {
+          float4* od = reinterpret_cast<float4*>(p.o + row * D + c * 32);
+#pragma unroll
+          for (int e = 0; e < 32; e += 4) od[e / 4] = make_float4(ov[e], ov[e + 1], ov[e + 2], ov[e + 3]);
+        } else if (p.out_dtype == HALO_DTYPE_F32) {
+          float4* od = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + off + c * 32);
+#pragma unroll
+          for (int e = 0; e < 32; e += 4)
+            od[e / 4] = make_float4(ov[e] * inv, ov[e + 1] * inv, ov[e + 2] * inv, ov[e + 3] * inv);
+        } else {
+          uint4* od = reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.out) + off + c * 32);
+#pragma unroll
+          for (int e = 0; e < 32; e += 8)
+            od[e / 8] = make_uint4(pack2<T>(ov[e] * inv, ov[e + 1] * inv),
+                                   pack2<T>(ov[e + 2] * inv, ov[e + 3] * inv),
+                                   pack2<T>(ov[e + 4] * inv, ov[e + 5] * inv),
+                                   pack2<T>(ov[e + 6] * inv, ov[e + 7] * inv));
+        }
+      }
+    }
+  }
+
+  // ---- teardown: every TMEM access and MMA has completed
+  umma::fence_before_sync();
+  __syncthreads();
+  if (warp == 1) {
+    umma::fence_after_sync();
+    umma::tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
 }  // namespace prefill
 
 // ================================================================ host side
@@ -585,6 +1029,25 @@ static int launch_kp(const prefill::Params& prm, int grid, cudaStream_t st) {
   return HALO_OK;
 }
 
+template <typename T, int D>
+static int launch_kp2(const prefill::Params& prm, int grid, cudaStream_t st) {
+  using Gm = prefill::Geom2<D>;
+  static std::once_flag once[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  cudaError_t attr_err = cudaSuccess;
+  std::call_once(once[dev & 63], [&] {
+    attr_err = cudaFuncSetAttribute(prefill::kp2_kernel<T, D>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, Gm::kSmemBytes);
+  });
+  if (attr_err != cudaSuccess) return cuda_fail(attr_err, "kp2_kernel shared-memory attribute");
+  prefill::kp2_kernel<T, D><<<grid, prefill::kThreads2, Gm::kSmemBytes, st>>>(prm);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "kp2_kernel launch");
+  count_launches();
+  return HALO_OK;
+}
+
 }  // namespace halo
 
 using namespace halo;
@@ -601,6 +1064,8 @@ extern "C" int32_t halo_prefill_attention(const halo_prefill_problem_t* pb,
     return fail(HALO_ERR_UNSUPPORTED, "prefill kernel needs bf16 or fp16 (dtype %d)", pb->dtype);
   if (pb->D != 64 && pb->D != 128)
     return fail(HALO_ERR_UNSUPPORTED, "prefill kernel head_dim %d (64 or 128)", pb->D);
+  if (!(pb->scale > 0.f) || !std::isfinite(pb->scale))
+    return fail(HALO_ERR_UNSUPPORTED, "prefill kernel needs a positive finite scale");
   if (n_chunks < 0 || (n_chunks > 0 && !chunks)) return fail(HALO_ERR_INVALID_ARG, "bad chunk list");
   if (po->mode != HALO_MERGE_FINALIZE && po->mode != HALO_MERGE_ACCUMULATE)
     return fail(HALO_ERR_INVALID_ARG, "bad mode %d", po->mode);
@@ -706,16 +1171,16 @@ extern "C" int32_t halo_prefill_attention(const halo_prefill_problem_t* pb,
   prm.l = po->l;
   prm.o = po->o;
   prm.err = device_error_ptr();
-  const int64_t grid = (int64_t)prm.n_qtiles * pb->B * pb->H;
+  const int64_t grid = (int64_t)((prm.n_qtiles + 1) / 2) * pb->B * pb->H;
   if (grid > INT32_MAX) return fail(HALO_ERR_UNSUPPORTED, "grid too large");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (pb->event_begin) cudaEventRecord(static_cast<cudaEvent_t>(pb->event_begin), st);
   if (pb->dtype == HALO_DTYPE_BF16)
-    rc = D == 128 ? launch_kp<__nv_bfloat16, 128>(prm, (int)grid, st)
-                  : launch_kp<__nv_bfloat16, 64>(prm, (int)grid, st);
+    rc = D == 128 ? launch_kp2<__nv_bfloat16, 128>(prm, (int)grid, st)
+                  : launch_kp2<__nv_bfloat16, 64>(prm, (int)grid, st);
   else
-    rc = D == 128 ? launch_kp<__half, 128>(prm, (int)grid, st)
-                  : launch_kp<__half, 64>(prm, (int)grid, st);
+    rc = D == 128 ? launch_kp2<__half, 128>(prm, (int)grid, st)
+                  : launch_kp2<__half, 64>(prm, (int)grid, st);
   if (rc == HALO_OK && pb->event_end) cudaEventRecord(static_cast<cudaEvent_t>(pb->event_end), st);
   return rc;
 }

@@ -431,7 +431,7 @@ class HALOCacheChunked(HALOCache):
         # running state (B, H, T_q); otherwise the split-KV kernel, state in
         # (B, T_q, H) row order.
         use_pf = causal and ops.prefill_supported(q, [(like, (gpu_v if T_gpu > 0 else tier.v),
-                                                        0, True)])
+                                                        0, True)], scale)
         if use_pf:
             m = torch.full((B, H, T_q), float("-inf"), dtype=torch.float32, device=dev)
             l = torch.zeros(B, H, T_q, dtype=torch.float32, device=dev)

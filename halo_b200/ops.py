@@ -247,11 +247,13 @@ def accumulate_decode(q: torch.Tensor, chunks: Sequence[tuple], m: torch.Tensor,
 PREFILL_MAX_CHUNKS = 48   # chunk descriptors per halo_prefill_attention call
 
 
-def prefill_supported(q: torch.Tensor, chunks: Sequence[tuple]) -> bool:
+def prefill_supported(q: torch.Tensor, chunks: Sequence[tuple], scale: Optional[float] = None) -> bool:
     """Whether the tensor-core prefill kernel covers this problem: bf16 or
-    fp16, head dim 64 or 128, value head dim equal to it."""
+    fp16, head dim 64 or 128, value head dim equal to it, positive scale."""
     D = q.shape[-1]
     if q.dtype not in (torch.bfloat16, torch.float16) or D not in (64, 128):
+        return False
+    if scale is not None and not (math.isfinite(scale) and scale > 0):
         return False
     return all(k.dtype == q.dtype and v.dtype == q.dtype and k.shape[-1] == D and
                v.shape[-1] == D for (k, v, _s, _c) in chunks)
@@ -343,7 +345,7 @@ def multi_query_attention(q: torch.Tensor, chunks: Sequence[tuple], *, scale: Op
     B, H, T_q, D = q.shape
     if scale is None:
         scale = 1.0 / math.sqrt(D)
-    if chunks and prefill_supported(q, chunks):
+    if chunks and prefill_supported(q, chunks, scale):
         return prefill_attention(q, chunks, query_pos_offset=query_pos_offset, scale=scale,
                                  out_dtype=out_dtype)
     D_v = int(chunks[0][1].shape[-1]) if chunks else D
