@@ -2,41 +2,18 @@
 //
 // T_q > 1 query rows of one (batch, head) slice attend to a list of K/V
 // chunks (the accumulated cache of halo/kv_cache_chunked.py:873-942 and the
-// slices of halo/chunked_prefill.py:73-135 in lzbaclz/HALO).  One CTA owns a
-// tile of 128 query rows of one q-head and walks every visible 128-row K/V
-// tile of every chunk with an online softmax; there is no split over keys,
-// so the result leaves the CTA already merged.
+// slices of halo/chunked_prefill.py:73-135 in lzbaclz/HALO) with an online
+// softmax; there is no split over keys, so results leave a CTA merged.  The
+// kernel (kp2_kernel below) gives each CTA two 128-row query tiles of one
+// q-head; its layout, warp roles and synchronisation are described at the
+// kernel.
 //
-// Warp roles (192 threads, one CTA per SM):
-//   warp 0      TMA producer: the Q tile once, then K and V tiles through
-//               two-slot rings (128B-swizzled boxes of 128 rows x 64 elements).
-//   warp 1      TMEM owner (allocates 512 columns) and, on lane 0, the MMA
-//               issuer: S_i = Q K_i^T into one of two TMEM score buffers, and
-//               O += P_i V_i into the TMEM output accumulator.
-//   warps 2-5   softmax: thread r owns query row r = TMEM lane r.  It loads
-//               its S row from TMEM, masks, keeps the running max m and sum l
-//               (log2 domain), writes P = exp2(s - m) to shared memory as a
-//               16-bit pair hi + lo (hi = rnd(p), lo = rnd(p - hi)) and
-//               rescales its O row in TMEM when the max grows by more than
-//               2^8 (the rescale is otherwise deferred: P stays <= 256).
-// O accumulates P_hi V + P_lo V, so P carries ~16 significant bits into the
-// fp32 accumulator; a single 16-bit P would put errors of up to 2^-9 |v| on
-// the output, above the 2e-3 budget for peaked rows.
-//
-// TMEM columns: S0 [0,128), S1 [128,256), O [256, 256+D).
-// Shared memory (D = 128): Q 32 KB | K x2 64 KB | V x2 64 KB | P_hi, P_lo 64 KB.
-//
-// Synchronisation (mbarriers; every wait bounded, see mbar_wait):
-//   q_full, k_full[2], v_full[2]   TMA transaction counts
-//   k_empty[2], v_empty[2]         tcgen05.commit after the MMAs reading them
-//   s_full[2]                      tcgen05.commit after S_i = Q K_i^T
-//   s_free[2]                      128 softmax threads after reading S_i
-//   p_full                         128 softmax threads after writing P_i
-//   pv_done                        tcgen05.commit after O += P_i V_i
-//   mma_done                       the MMA thread's final commit
-// The softmax of tile i waits for pv_done(i-1) before it touches P or O, so
-// one P buffer suffices; a commit tracks every earlier MMA of the issuing
-// thread, so s_full(i) also implies pv_done(i-2).
+// Numerics: scores and outputs accumulate in fp32 (TMEM).  P = exp2(s*c - m)
+// with a running max m that is only moved when it grows by more than 2^8
+// (O is then rescaled in TMEM), so P <= 256.  bf16 inputs feed P to the
+// tensor core as hi + lo 16-bit parts (two MMAs; ~16 significant bits): a
+// single bf16 P puts errors up to ~2^-9 |v| on peaked rows, above the 2e-3
+// budget.  fp16 inputs use one fp16 P (11 bits, |err| <~ 2^-12 |v|).
 #include <algorithm>
 #include <cmath>
 #include <cstdarg>
@@ -58,10 +35,8 @@ namespace prefill {
 
 constexpr int kBM = 128;            // query rows per CTA (TMEM lanes)
 constexpr int kBN = 128;            // keys per tile
-constexpr int kThreads = 192;
 constexpr int kMaxSegs = 48;
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColS0 = 0, kColS1 = 128, kColO = 256;
 constexpr float kRescaleLog2 = 8.f;
 
 struct Seg {
@@ -91,53 +66,14 @@ struct alignas(64) Params {
   unsigned int* err;
 };
 
-template <int D>
-struct Geom {
-  static constexpr int kBlocks = D / 64;                 // 64-element swizzle blocks per row
-  static constexpr int kBlockBytes = kBM * 128;          // 128 rows x 128 B
-  static constexpr int kTileBytes = kBlocks * kBlockBytes;
-  static constexpr int kPBytes = 2 * kBlockBytes;        // 128 keys = 2 blocks
-  static constexpr int kOffQ = 0;
-  static constexpr int kOffK = kOffQ + kTileBytes;
-  static constexpr int kOffV = kOffK + 2 * kTileBytes;
-  static constexpr int kOffPhi = kOffV + 2 * kTileBytes;
-  static constexpr int kOffPlo = kOffPhi + kPBytes;
-  static constexpr int kOffBar = kOffPlo + kPBytes;
-  static constexpr int kBarBytes = 256;
-  static constexpr int kSmemBytes = kOffBar + kBarBytes + 1024;  // + base alignment slack
-};
-
-struct Bars {
-  uint64_t q_full, k_full[2], v_full[2], k_empty[2], v_empty[2];
-  uint64_t s_full[2], s_free[2], p_full, pv_done, mma_done;
-  uint32_t tmem_base;
-  int abort_flag;
-};
-
-// Bounded wait that also gives up once another role has aborted.
-__device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, Bars* bs,
-                                         unsigned int* err) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = globaltimer_ns();
-  while (true) {
-    for (int i = 0; i < 32; ++i)
-      if (mbar_try_wait(bar, parity)) return true;
-    if (*reinterpret_cast<volatile int*>(&bs->abort_flag)) return false;
-    if (globaltimer_ns() - t0 > kWaitLimitNs) {
-      set_device_error(err, static_cast<unsigned int>(-HALO_ERR_TIMEOUT));
-      *reinterpret_cast<volatile int*>(&bs->abort_flag) = 1;
-      return false;
-    }
-  }
-}
-
+// exp2 on the special-function unit (relative error ~2^-22).
 __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
 
-// Tiles of segment `s` visible to query positions <= qmax.
+// K/V tiles of segment `sg` visible to query positions <= qmax.
 __device__ __forceinline__ int seg_tiles(const Seg& sg, int64_t qmax) {
   int n = (sg.len + kBN - 1) / kBN;
   if (sg.causal) {
@@ -153,318 +89,6 @@ template <typename T>
 __device__ __forceinline__ uint32_t pack2(float a, float b) {
   return Elem<T>::pack(a, b);
 }
-
-template <typename T, int D>
-__global__ void __launch_bounds__(kThreads, 1) kp_kernel(const __grid_constant__ Params p) {
-  using Gm = Geom<D>;
-  extern __shared__ __align__(1024) unsigned char smem_raw[];
-  unsigned char* smem = reinterpret_cast<unsigned char*>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  Bars* bs = reinterpret_cast<Bars*>(smem + Gm::kOffBar);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-
-  // heavy-first order: the last query tiles see the most keys
-  const int BH = p.B * p.H;
-  const int qt = p.n_qtiles - 1 - (int)(blockIdx.x / BH);
-  const int bh = (int)(blockIdx.x % BH);
-  const int b = bh / p.H, h = bh % p.H, hk = h / p.G;
-  const int qrow0 = qt * kBM;
-  const int q_valid = min(kBM, p.T_q - qrow0);
-  const int64_t qpos_min = p.q_pos0 + qrow0;
-  const int64_t qpos_max = qpos_min + q_valid - 1;
-
-  if (threadIdx.x == 0) {
-    mbar_init(&bs->q_full, 1);
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&bs->k_full[i], 1);
-      mbar_init(&bs->v_full[i], 1);
-      mbar_init(&bs->k_empty[i], 1);
-      mbar_init(&bs->v_empty[i], 1);
-      mbar_init(&bs->s_full[i], 1);
-      mbar_init(&bs->s_free[i], kBM);
-    }
-    mbar_init(&bs->p_full, kBM);
-    mbar_init(&bs->pv_done, 1);
-    mbar_init(&bs->mma_done, 1);
-    bs->abort_flag = 0;
-    fence_mbar_init();
-  }
-  if (warp == 1) {
-    umma::tmem_alloc(&bs->tmem_base, kTmemCols);
-    umma::tmem_relinquish();
-  }
-  umma::fence_before_sync();
-  __syncthreads();
-  umma::fence_after_sync();
-  const uint32_t tmem = bs->tmem_base;
-
-  int n_tiles = 0;
-  for (int s = 0; s < p.n_seg; ++s) n_tiles += seg_tiles(p.seg[s], qpos_max);
-
-  const uint32_t sQ = smem_addr(smem + Gm::kOffQ);
-  const uint32_t sK = smem_addr(smem + Gm::kOffK);
-  const uint32_t sV = smem_addr(smem + Gm::kOffV);
-  const uint32_t sPhi = smem_addr(smem + Gm::kOffPhi);
-  const uint32_t sPlo = smem_addr(smem + Gm::kOffPlo);
-
-  if (warp == 0) {
-    // ------------------------------------------------------------ producer
-    if (lane == 0 && n_tiles > 0) {
-      mbar_arrive_expect_tx(&bs->q_full, Gm::kTileBytes);
-      for (int blk = 0; blk < Gm::kBlocks; ++blk)
-        tma_load_4d(smem + Gm::kOffQ + blk * Gm::kBlockBytes, &p.qmap, blk * 64, qrow0, h, b,
-                    &bs->q_full);
-      int nk = 0, nv = 0;   // K and V tiles issued
-      bool ok = true;
-      for (int s = 0; s < p.n_seg && ok; ++s) {
-        const int nt = seg_tiles(p.seg[s], qpos_max);
-        const int bb = p.seg[s].bcast ? 0 : b;
-        for (int t = 0; t < nt; ++t) {
-          const int st = nk & 1, use = nk >> 1;
-          if (use > 0 && !(ok = wait_bar(&bs->k_empty[st], (use - 1) & 1, bs, p.err))) break;
-          mbar_arrive_expect_tx(&bs->k_full[st], Gm::kTileBytes);
-          for (int blk = 0; blk < Gm::kBlocks; ++blk)
-            tma_load_4d(smem + Gm::kOffK + st * Gm::kTileBytes + blk * Gm::kBlockBytes,
-                        &p.kmap[s], blk * 64, t * kBN, hk, bb, &bs->k_full[st]);
-          ++nk;
-          if (use > 0 && !(ok = wait_bar(&bs->v_empty[st], (use - 1) & 1, bs, p.err))) break;
-          mbar_arrive_expect_tx(&bs->v_full[st], Gm::kTileBytes);
-          for (int blk = 0; blk < Gm::kBlocks; ++blk)
-            tma_load_4d(smem + Gm::kOffV + st * Gm::kTileBytes + blk * Gm::kBlockBytes,
-                        &p.vmap[s], blk * 64, t * kBN, hk, bb, &bs->v_full[st]);
-          ++nv;
-        }
-      }
-      // Let every copy this thread issued land before the CTA can exit
-      // (immediate unless a consumer aborted).
-      mbar_wait(&bs->q_full, 0, p.err);
-      for (int st = 0; st < 2; ++st) {
-        const int uk = (nk - st + 1) / 2, uv = (nv - st + 1) / 2;   // loads into slot st
-        if (uk > 0) mbar_wait(&bs->k_full[st], (uk - 1) & 1, p.err);
-        if (uv > 0) mbar_wait(&bs->v_full[st], (uv - 1) & 1, p.err);
-      }
-    }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
-    if (lane == 0 && n_tiles > 0) {
-      constexpr bool kBf16 = Elem<T>::kDtype == HALO_DTYPE_BF16;
-      constexpr uint32_t kIdQK = umma::instr_desc_f16(kBM, kBN, kBf16, false, false);
-      constexpr uint32_t kIdPV = umma::instr_desc_f16(kBM, D, kBf16, false, true);
-      bool ok = wait_bar(&bs->q_full, 0, bs, p.err);
-      auto issue_pv = [&](int j) -> bool {
-        const int st = j & 1;
-        if (!wait_bar(&bs->p_full, j & 1, bs, p.err)) return false;
-        if (!wait_bar(&bs->v_full[st], (j >> 1) & 1, bs, p.err)) return false;
-        umma::fence_after_sync();
-        const uint32_t vbase = sV + st * Gm::kTileBytes;
-#pragma unroll
-        for (int part = 0; part < 2; ++part) {
-          const uint32_t pbase = part ? sPlo : sPhi;
-#pragma unroll
-          for (int kk = 0; kk < kBN / 16; ++kk) {
-            const uint64_t ad = umma::smem_desc_sw128(
-                pbase + (kk >> 2) * Gm::kBlockBytes + (kk & 3) * 32, 16, 1024);
-            const uint64_t bd =
-                umma::smem_desc_sw128(vbase + kk * 16 * 128, Gm::kBlockBytes, 1024);
-            umma::mma_ss(tmem + kColO, ad, bd, kIdPV, (j > 0) || part || kk);
-          }
-        }
-        umma::commit(&bs->pv_done);
-        umma::commit(&bs->v_empty[st]);
-        return true;
-      };
-      for (int i = 0; i < n_tiles && ok; ++i) {
-        const int st = i & 1;
-        if (!(ok = wait_bar(&bs->k_full[st], (i >> 1) & 1, bs, p.err))) break;
-        if (i >= 2 && !(ok = wait_bar(&bs->s_free[st], ((i - 2) >> 1) & 1, bs, p.err))) break;
-        umma::fence_after_sync();
-        const uint32_t kbase = sK + st * Gm::kTileBytes;
-        const uint32_t scol = st ? kColS1 : kColS0;
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * Gm::kBlockBytes + (kk & 3) * 32;
-          umma::mma_ss(tmem + scol, umma::smem_desc_sw128(sQ + off, 16, 1024),
-                       umma::smem_desc_sw128(kbase + off, 16, 1024), kIdQK, kk > 0);
-        }
-        umma::commit(&bs->s_full[st]);
-        umma::commit(&bs->k_empty[st]);
-        if (i >= 1) ok = issue_pv(i - 1);
-      }
-      if (ok) issue_pv(n_tiles - 1);
-      umma::commit(&bs->mma_done);
-      mbar_wait(&bs->mma_done, 0, p.err);
-    }
-  } else {
-    // ------------------------------------------------------------ softmax
-    const int sub = warp & 3;                 // TMEM lane quarter of this warp
-    const int r = sub * 32 + lane;            // query row within the tile
-    const uint32_t trow = tmem + ((uint32_t)(sub * 32) << 16);
-    const int64_t qpos = qpos_min + r;
-    float m = -INFINITY, l = 0.f;
-    bool ok = true;
-    int i = 0;
-    for (int s = 0; s < p.n_seg && ok; ++s) {
-      const Seg sg = p.seg[s];
-      const int nt = seg_tiles(sg, qpos_max);
-      for (int t = 0; t < nt; ++t, ++i) {
-        const int st = i & 1;
-        ok = __all_sync(0xffffffffu, wait_bar(&bs->s_full[st], (i >> 1) & 1, bs, p.err));
-        if (!ok) break;
-        umma::fence_after_sync();
-        float sv[kBN];
-        const uint32_t scol = st ? kColS1 : kColS0;
-#pragma unroll
-        for (int c = 0; c < kBN / 32; ++c) umma::tmem_ld32(trow + scol + c * 32, sv + c * 32);
-        umma::tmem_wait_ld();
-        umma::fence_before_sync();
-        mbar_arrive(&bs->s_free[st]);
-
-        const int row0 = t * kBN;
-        const int64_t kpos0 = sg.start + row0;
-        const bool full = (row0 + kBN <= sg.len) && (!sg.causal || kpos0 + kBN - 1 <= qpos_min);
-        float mx = -INFINITY;
-        if (full) {
-#pragma unroll
-          for (int c = 0; c < kBN; ++c) {
-            sv[c] *= p.scale_log2;
-            mx = fmaxf(mx, sv[c]);
-          }
-        } else {
-          const int lim_len = sg.len - row0;
-          const int64_t lim_pos = sg.causal ? qpos - kpos0 : (int64_t)kBN;
-#pragma unroll
-          for (int c = 0; c < kBN; ++c) {
-            const bool vis = c < lim_len && (int64_t)c <= lim_pos;
-            sv[c] = vis ? sv[c] * p.scale_log2 : -INFINITY;
-            mx = fmaxf(mx, sv[c]);
-          }
-        }
-
-        // P and O are free once O += P_{i-1} V_{i-1} has completed.
-        if (i > 0) {
-          ok = __all_sync(0xffffffffu, wait_bar(&bs->pv_done, (i - 1) & 1, bs, p.err));
-          if (!ok) break;
-          umma::fence_after_sync();
-        }
-        const bool grow = mx > m + kRescaleLog2 || (m == -INFINITY && mx > -INFINITY);
-        float fac = 1.f;
-        if (grow) {
-          fac = (m == -INFINITY) ? 0.f : ex2(m - mx);
-          l *= fac;
-          m = mx;
-        }
-        if (i > 0 && __any_sync(0xffffffffu, grow)) {
-          // warp-collective rescale of the O rows (factor 1 where the max held)
-#pragma unroll
-          for (int c = 0; c < D / 32; ++c) {
-            float ov[32];
-            umma::tmem_ld32(trow + kColO + c * 32, ov);
-            umma::tmem_wait_ld();
-#pragma unroll
-            for (int e = 0; e < 32; ++e) ov[e] *= fac;
-            umma::tmem_st32(trow + kColO + c * 32, ov);
-          }
-          umma::tmem_wait_st();
-        }
-        const float mu = (m == -INFINITY) ? 0.f : m;
-        float rs = 0.f;
-        const uint32_t prow = (uint32_t)r * 128u;
-#pragma unroll
-        for (int c16 = 0; c16 < kBN / 8; ++c16) {
-          uint32_t hi[4], lo[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float p0 = ex2(sv[c16 * 8 + 2 * e] - mu);
-            const float p1 = ex2(sv[c16 * 8 + 2 * e + 1] - mu);
-            rs += p0 + p1;
-            hi[e] = pack2<T>(p0, p1);
-            float h0, h1;
-            Elem<T>::unpack(hi[e], h0, h1);
-            lo[e] = pack2<T>(p0 - h0, p1 - h1);
-          }
-          const uint32_t off = (uint32_t)(c16 >> 3) * Gm::kBlockBytes + prow +
-                               ((uint32_t)((c16 & 7) ^ (r & 7)) << 4);
-          asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(sPhi + off), "r"(hi[0]),
-                       "r"(hi[1]), "r"(hi[2]), "r"(hi[3]) : "memory");
-          asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(sPlo + off), "r"(lo[0]),
-                       "r"(lo[1]), "r"(lo[2]), "r"(lo[3]) : "memory");
-        }
-        l += rs;
-        fence_proxy_async_smem();      // P is read by the tensor core (async proxy)
-        umma::fence_before_sync();     // orders the O rescale before the MMA thread's reads
-        mbar_arrive(&bs->p_full);
-      }
-    }
-
-    // ---- epilogue: thread r finalises query row qrow0 + r
-    if (ok && n_tiles > 0) {
-      ok = __all_sync(0xffffffffu, wait_bar(&bs->pv_done, (n_tiles - 1) & 1, bs, p.err));
-      if (ok) umma::fence_after_sync();
-    }
-    if (ok) {
-      float ov[D];
-      if (n_tiles > 0) {
-#pragma unroll
-        for (int c = 0; c < D / 32; ++c) umma::tmem_ld32(trow + kColO + c * 32, ov + c * 32);
-        umma::tmem_wait_ld();
-      } else {
-#pragma unroll
-        for (int d = 0; d < D; ++d) ov[d] = 0.f;
-      }
-      if (r < q_valid) {
-        const int t = qrow0 + r;
-        const int64_t row = ((int64_t)b * p.H + h) * p.T_q + t;
-        float M = (m == -INFINITY) ? -INFINITY : m * kLn2;   // natural-log score units
-        float L = l;
-        if (p.m != nullptr) {
-          const float mp = p.m[row], lp = p.l[row];
-          const float Mn = fmaxf(M, mp);
-          const float wo = (M == -INFINITY) ? 0.f : expf(M - Mn);
-          const float wp = (mp == -INFINITY) ? 0.f : expf(mp - Mn);
-          const float* op = p.o + row * D;
-          L = L * wo + lp * wp;
-#pragma unroll
-          for (int d = 0; d < D; ++d) ov[d] = ov[d] * wo + op[d] * wp;
-          M = Mn;
-        }
-        if (p.mode == HALO_MERGE_ACCUMULATE) {
-          p.m[row] = M;
-          p.l[row] = L;
-          float4* od = reinterpret_cast<float4*>(p.o + row * D);
-#pragma unroll
-          for (int d = 0; d < D; d += 4) od[d / 4] = make_float4(ov[d], ov[d + 1], ov[d + 2], ov[d + 3]);
-        } else {
-          const float inv = (L > 0.f) ? 1.f / L : 0.f;
-          if (p.lse) p.lse[row] = (L > 0.f) ? M + logf(L) : -INFINITY;
-          const int64_t off = (int64_t)b * p.out_sb + (int64_t)h * p.out_sh + (int64_t)t * p.out_st;
-          if (p.out_dtype == HALO_DTYPE_F32) {
-            float4* od = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + off);
-#pragma unroll
-            for (int d = 0; d < D; d += 4)
-              od[d / 4] = make_float4(ov[d] * inv, ov[d + 1] * inv, ov[d + 2] * inv, ov[d + 3] * inv);
-          } else {
-            uint4* od = reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.out) + off);
-#pragma unroll
-            for (int d = 0; d < D; d += 8)
-              od[d / 8] = make_uint4(pack2<T>(ov[d] * inv, ov[d + 1] * inv),
-                                     pack2<T>(ov[d + 2] * inv, ov[d + 3] * inv),
-                                     pack2<T>(ov[d + 4] * inv, ov[d + 5] * inv),
-                                     pack2<T>(ov[d + 6] * inv, ov[d + 7] * inv));
-          }
-        }
-      }
-    }
-  }
-
-  // ---- teardown: every TMEM access and MMA has completed
-  umma::fence_before_sync();
-  __syncthreads();
-  if (warp == 1) {
-    umma::fence_after_sync();
-    umma::tmem_dealloc(tmem, kTmemCols);
-  }
-}
-
 
 // ======================================================================
 // kp2_kernel: two query tiles per CTA, double-buffered 64-key score tiles.
@@ -487,14 +111,15 @@ __global__ void __launch_bounds__(kThreads, 1) kp_kernel(const __grid_constant__
 // issuer computes S_X(j+1) while the softmax of S_X(j) runs; S_X(j+2) waits
 // for O_X += P_X(j) V to finish reading P.  A softmax that must rescale O_X
 // first waits for the previous PV_X.
-// Each tile's issuer runs, per K/V tile, QK(j), QK(j+1), PV(j), PV(j+1) on
-// its own commit chain; the two chains interleave on the tensor pipe.
+// Each tile's issuer runs PV(j), QK(j+2), PV(j+1), QK(j+3), ... on its own
+// commit chain; the two chains interleave on the tensor pipe.
 // Descriptors are precomputed (one add per MMA) so an issuing thread keeps
 // pace with the pipe.
 // Barriers: q_full; k_full/v_full/k_empty/v_empty [stages]; per tile X and
 // buffer b: s_full (commit after QK), p_full (128 softmax arrivals), pv_done
 // (commit after PV); mma_done per issuer.  K/V empty barriers take one
-// arrival per issuer.  All waits bounded.
+// arrival per issuer (the producer stands in for an issuer whose tile sits
+// that K/V tile out).  All waits bounded.
 constexpr int kThreads2 = 384;
 constexpr int kSub = 64;                 // keys per score sub-tile
 
@@ -625,20 +250,26 @@ __global__ void __launch_bounds__(kThreads2, 1) kp2_kernel(const __grid_constant
         bool ok = true;
         for (int s = 0; s < p.n_seg && ok; ++s) {
           const int nt = seg_tiles(p.seg[s], qmaxU);
+          const int ntA = seg_tiles(p.seg[s], qmaxA);
           const int bb = p.seg[s].bcast ? 0 : b;
           for (int t = 0; t < nt; ++t) {
+            // the empty barriers take one arrival per issuer; the issuer of a
+            // tile that sits this K/V tile out is arrived for here
+            const uint32_t absent = (t < ntA ? 0u : 1u) + (hasB ? 0u : 1u);
             const int st = nk % ST, use = nk / ST;
             if (use > 0 && !(ok = wait_bar2(&bs->k_empty[st], (use - 1) & 1, bs, p.err))) break;
             mbar_arrive_expect_tx(&bs->k_full[st], Gm::kTileBytes);
             for (int blk = 0; blk < Gm::kBlocks; ++blk)
               tma_load_4d(smem + Gm::kOffK + st * Gm::kTileBytes + blk * Gm::kBlockBytes,
                           &p.kmap[s], blk * 64, t * kBN, hk, bb, &bs->k_full[st]);
+            if (absent) mbar_arrive_n(&bs->k_empty[st], absent);
             ++nk;
             if (use > 0 && !(ok = wait_bar2(&bs->v_empty[st], (use - 1) & 1, bs, p.err))) break;
             mbar_arrive_expect_tx(&bs->v_full[st], Gm::kTileBytes);
             for (int blk = 0; blk < Gm::kBlocks; ++blk)
               tma_load_4d(smem + Gm::kOffV + st * Gm::kTileBytes + blk * Gm::kBlockBytes,
                           &p.vmap[s], blk * 64, t * kBN, hk, bb, &bs->v_full[st]);
+            if (absent) mbar_arrive_n(&bs->v_empty[st], absent);
             ++nv;
           }
         }
@@ -650,12 +281,13 @@ __global__ void __launch_bounds__(kThreads2, 1) kp2_kernel(const __grid_constant
           if (uv > 0) mbar_wait(&bs->v_full[st], (uv - 1) & 1, p.err);
         }
       }
-    } else if ((warp == 1 || warp == 2) && lane == 0 && nU > 0) {
+    } else if ((warp == 1 || (warp == 2 && hasB)) && lane == 0 && nU > 0) {
       // ---------------------------------------------------------- MMA issuers
       // warp 1 issues tile A's MMAs, warp 2 tile B's: two independent
       // commit chains, so one tile's waits never idle the other's work.
-      // Both walk every K/V tile and arrive on its empty barriers (count 2):
-      // a commit when they read it, a plain arrive when they sit it out.
+      // Both walk every K/V tile: they wait on its full barriers (keeping
+      // the phase parity in step) and commit to its empty barriers when
+      // they read it; the producer arrives for an issuer that sits it out.
       const int x = warp - 1;
       constexpr bool kBf16 = Elem<T>::kDtype == HALO_DTYPE_BF16;
       constexpr uint32_t kIdQK = umma::instr_desc_f16(kBM, kSub, kBf16, false, false);
@@ -665,61 +297,111 @@ __global__ void __launch_bounds__(kThreads2, 1) kp2_kernel(const __grid_constant
       const uint64_t vdesc0 = umma::smem_desc_sw128(sV, Gm::kBlockBytes, 1024);
       const uint32_t scol0 = tmem + x * 128;
       const uint32_t ocol = tmem + Gm::kColO + x * D;
-      bool ok = true;
-      if (x == 0 || hasB) ok = wait_bar2(&bs->q_full, 0, bs, p.err);
-      int g = 0, jx = 0;
-      for (int s = 0; s < p.n_seg && ok; ++s) {
-        const int ntU = seg_tiles(p.seg[s], qmaxU);
-        const int ntA = seg_tiles(p.seg[s], qmaxA);
-        for (int t = 0; t < ntU && ok; ++t, ++g) {
-          const bool in = x ? hasB : (t < ntA);
-          const int st = g % ST, use = g / ST;
-          if (!(ok = wait_bar2(&bs->k_full[st], use & 1, bs, p.err))) break;
-          if (in) {
-            const uint64_t kdesc = kdesc0 + (uint64_t)((st * Gm::kTileBytes) >> 4);
+      bool ok = wait_bar2(&bs->q_full, 0, bs, p.err);
+      // Two cursors walk the K/V tiles: QK runs two sub-tiles ahead of PV
+      // (QK(j+2) is issued right after PV(j), whose completion frees the
+      // score buffer it reuses), so the softmax of S(j+1) overlaps PV(j)
+      // and QK(j+2).  Tiles this tile sits out are only waited on.
+      struct Cursor {
+        int s, t, g, ntU, ntA;
+      };
+      auto load = [&](Cursor& c) {
+        while (c.s < p.n_seg) {
+          c.ntU = seg_tiles(p.seg[c.s], qmaxU);
+          c.ntA = seg_tiles(p.seg[c.s], qmaxA);
+          if (c.t < c.ntU) return;
+          ++c.s;
+          c.t = 0;
+        }
+      };
+      auto next = [&](Cursor& c) {
+        ++c.t;
+        ++c.g;
+        if (c.t >= c.ntU) {
+          ++c.s;
+          c.t = 0;
+          load(c);
+        }
+      };
+      auto takes_part = [&](const Cursor& c) { return x ? hasB : (c.t < c.ntA); };
+      Cursor cq{0, 0, 0, 0, 0}, cp{0, 0, 0, 0, 0};
+      load(cq);
+      load(cp);
+      int jq = 0, jp = 0, hq = 0, hp = 0;
+      // K side: skip tiles this tile sits out, then QK of the next sub-tile
+      auto qk_step = [&]() -> int {   // 1 issued, 0 walk finished, -1 error
+        while (cq.s < p.n_seg && !takes_part(cq)) {
+          const int st = cq.g % ST;
+          if (!wait_bar2(&bs->k_full[st], (cq.g / ST) & 1, bs, p.err)) return -1;
+          next(cq);
+        }
+        if (cq.s >= p.n_seg) return 0;
+        const int st = cq.g % ST;
+        if (hq == 0 && !wait_bar2(&bs->k_full[st], (cq.g / ST) & 1, bs, p.err)) return -1;
+        const int j = jq, bf = j & 1;
+        if (j >= 2 && !wait_bar2(&bs->pv_done[x][bf], ((j - 2) >> 1) & 1, bs, p.err)) return -1;
+        umma::fence_after_sync();
+        const uint64_t kd = kdesc0 + (uint64_t)((st * Gm::kTileBytes + hq * kSub * 128) >> 4);
 #pragma unroll
-            for (int hh = 0; hh < 2; ++hh) {
-              const int j = jx + hh, bf = j & 1;
-              if (j >= 2 && !(ok = wait_bar2(&bs->pv_done[x][bf], ((j - 2) >> 1) & 1, bs, p.err)))
-                break;
-              umma::fence_after_sync();
-              const uint64_t kd = kdesc + (uint64_t)((hh * kSub * 128) >> 4);
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = ((kk >> 2) * Gm::kBlockBytes + (kk & 3) * 32) >> 4;
+          umma::mma_ss(scol0 + bf * kSub, qdesc + off, kd + off, kIdQK, kk > 0);
+        }
+        umma::commit(&bs->s_full[x][bf]);
+        ++jq;
+        if (hq == 1) {
+          umma::commit(&bs->k_empty[st]);
+          next(cq);
+          hq = 0;
+        } else {
+          hq = 1;
+        }
+        return 1;
+      };
+      // V side: skip tiles this tile sits out, then PV of the next sub-tile
+      auto pv_step = [&]() -> bool {
+        while (!takes_part(cp)) {
+          const int st = cp.g % ST;
+          if (!wait_bar2(&bs->v_full[st], (cp.g / ST) & 1, bs, p.err)) return false;
+          next(cp);
+        }
+        const int st = cp.g % ST;
+        if (hp == 0 && !wait_bar2(&bs->v_full[st], (cp.g / ST) & 1, bs, p.err)) return false;
+        const int j = jp, bf = j & 1;
+        if (!wait_bar2(&bs->p_full[x][bf], (j >> 1) & 1, bs, p.err)) return false;
+        umma::fence_after_sync();
+        const uint32_t pcol = scol0 + bf * kSub;
+        const uint64_t vd = vdesc0 + (uint64_t)((st * Gm::kTileBytes + hp * kSub * 128) >> 4);
 #pragma unroll
-              for (int kk = 0; kk < D / 16; ++kk) {
-                const uint32_t off = ((kk >> 2) * Gm::kBlockBytes + (kk & 3) * 32) >> 4;
-                umma::mma_ss(scol0 + bf * kSub, qdesc + off, kd + off, kIdQK, kk > 0);
-              }
-              umma::commit(&bs->s_full[x][bf]);
-            }
-            if (!ok) break;
-            umma::commit(&bs->k_empty[st]);
-          } else {
-            mbar_arrive(&bs->k_empty[st]);
-          }
-          if (!(ok = wait_bar2(&bs->v_full[st], use & 1, bs, p.err))) break;
-          if (in) {
-            const uint64_t vdesc = vdesc0 + (uint64_t)((st * Gm::kTileBytes) >> 4);
+        for (int part = 0; part < (kSplitP ? 2 : 1); ++part)
 #pragma unroll
-            for (int hh = 0; hh < 2; ++hh) {
-              const int j = jx + hh, bf = j & 1;
-              if (!(ok = wait_bar2(&bs->p_full[x][bf], (j >> 1) & 1, bs, p.err))) break;
-              umma::fence_after_sync();
-              const uint32_t pcol = scol0 + bf * kSub;
-              const uint64_t vd = vdesc + (uint64_t)((hh * kSub * 128) >> 4);
-#pragma unroll
-              for (int part = 0; part < (kSplitP ? 2 : 1); ++part)
-#pragma unroll
-                for (int kk = 0; kk < kSub / 16; ++kk)
-                  umma::mma_ts(ocol, pcol + (kk >> 1) * 32 + part * 16 + (kk & 1) * 8,
-                               vd + (uint64_t)((kk * 16 * 128) >> 4), kIdPV, (j > 0) || part || kk);
-              umma::commit(&bs->pv_done[x][bf]);
-            }
-            if (!ok) break;
-            umma::commit(&bs->v_empty[st]);
-            jx += 2;
-          } else {
-            mbar_arrive(&bs->v_empty[st]);
-          }
+          for (int kk = 0; kk < kSub / 16; ++kk)
+            umma::mma_ts(ocol, pcol + (kk >> 1) * 32 + part * 16 + (kk & 1) * 8,
+                         vd + (uint64_t)((kk * 16 * 128) >> 4), kIdPV, (j > 0) || part || kk);
+        umma::commit(&bs->pv_done[x][bf]);
+        ++jp;
+        if (hp == 1) {
+          umma::commit(&bs->v_empty[st]);
+          next(cp);
+          hp = 0;
+        } else {
+          hp = 1;
+        }
+        return true;
+      };
+      // Offset tile B by one softmax: its chain starts once tile A's first P
+      // is out, so the two softmax warpgroups alternate with the MMAs
+      // instead of competing at the same moments.
+      if (x == 1 && ok && p.seg[0].len > 0 && seg_tiles(p.seg[0], qmaxA) > 0)
+        ok = wait_bar2(&bs->p_full[0][0], 0, bs, p.err);
+      int rq = ok ? qk_step() : -1;
+      if (rq > 0) rq = qk_step();
+      ok = rq >= 0;
+      while (ok && jp < jq) {
+        if (!(ok = pv_step())) break;
+        if (rq > 0) {
+          rq = qk_step();
+          ok = rq >= 0;
         }
       }
       // this thread's MMAs complete before the CTA can free TMEM
@@ -1008,25 +690,6 @@ static bool pf_continues(const halo_kv_chunk_t& a, int64_t a_len, const halo_kv_
          static_cast<const char*>(c.v) ==
              static_cast<const char*>(a.v) + a_len * a.v_stride_t * 2 &&
          a_len + c.len <= INT32_MAX;
-}
-
-template <typename T, int D>
-static int launch_kp(const prefill::Params& prm, int grid, cudaStream_t st) {
-  using Gm = prefill::Geom<D>;
-  static std::once_flag once[64];
-  int dev = 0;
-  cudaGetDevice(&dev);
-  cudaError_t attr_err = cudaSuccess;
-  std::call_once(once[dev & 63], [&] {
-    attr_err = cudaFuncSetAttribute(prefill::kp_kernel<T, D>,
-                                    cudaFuncAttributeMaxDynamicSharedMemorySize, Gm::kSmemBytes);
-  });
-  if (attr_err != cudaSuccess) return cuda_fail(attr_err, "kp_kernel shared-memory attribute");
-  prefill::kp_kernel<T, D><<<grid, prefill::kThreads, Gm::kSmemBytes, st>>>(prm);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, "kp_kernel launch");
-  count_launches();
-  return HALO_OK;
 }
 
 template <typename T, int D>

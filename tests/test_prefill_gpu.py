@@ -166,12 +166,13 @@ def test_prefill_more_chunks_than_one_call_takes():
     _check(out, lse, ro, rl)
 
 
-def test_prefill_large_slice_outlier_keys():
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_prefill_large_slice_outlier_keys(dtype):
     """A 1024-query slice after 7K rows of history, outlier keys: peaked
-    softmax rows stress the split-P accumulation."""
+    softmax rows stress the P precision (bf16 hi + lo, fp16 single)."""
     ops = _ops()
     B, H, H_kv, D, T_q, T = 1, 8, 2, 128, 1024, 8192
-    q, k, v = _qkv(B, H, H_kv, T, T_q, D, torch.bfloat16, seed=77)
+    q, k, v = _qkv(B, H, H_kv, T, T_q, D, dtype, seed=77)
     kd, vd = k.to(DEV), v.to(DEV)
     chunks = [(kd[..., a:a + 4096, :], vd[..., a:a + 4096, :], a, True) for a in range(0, T, 4096)]
     out, lse = ops.prefill_attention(q.to(DEV), chunks, query_pos_offset=T - T_q,
