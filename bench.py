@@ -878,7 +878,7 @@ def run_ours_cfg3(args):
             "data": "synthetic", "config": _cfg3_config(),
             "roofline": {"bound": "tensor", "achieved": tflops, "peak": peak, "unit": "TFLOP/s",
                          "frac": tflops / peak, "peak_kind": f"of {peak_kind}",
-                         "kernel": "kp_kernel (tcgen05 chunked-prefill attention)",
+                         "kernel": "kp2_kernel (tcgen05 chunked-prefill attention)",
                          "flops_per_step": flops, "traffic": None,
                          "note": "algorithmic causal FLOPs; the kernel also runs P_lo V "
                                  "(1.5x the tensor work) and the masked halves of diagonal tiles"},
