@@ -165,7 +165,7 @@ SIGNATURES = {
                                             ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p,
                                             ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
                                             ctypes.c_int64, ctypes.c_int64, ctypes.c_int32,
-                                            ctypes.c_int32, ctypes.c_uint32,
+                                            ctypes.c_int32,
                                             ctypes.POINTER(ctypes.c_void_p), ctypes.c_int32,
                                             ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
                                             ctypes.c_void_p, ctypes.c_void_p]),

@@ -60,6 +60,12 @@ constexpr int kConsumerWarps = 4;    // each owns 16 rows of every stage
 constexpr int kThreads = (kConsumerWarps + 1) * 32;
 constexpr int kMaxSegs = 48;         // tensor-map pairs per launch
 constexpr int kMaxItems = 512;       // work items per launch
+// Control block at the start of every decode workspace: the dynamic
+// schedule's per-pair piece counters and its exit counter.  It must be zero
+// before a workspace's first use; every call leaves it zero.
+constexpr int64_t kCtrlBytes = 4096;
+constexpr int kMaxDynPairs = (int)(kCtrlBytes / 4) - 1;
+constexpr int kPieceTiles = 2;       // 64-row tiles per piece of the dynamic schedule
 
 // A work item: `rows` consecutive rows of one segment (a K/V view with its
 // own pair of tensor maps), starting at segment row `row0`, whose first row
@@ -83,11 +89,37 @@ struct alignas(64) DecodeParams {
   float* l_part;
   float* o_part;
   unsigned int* err;  // device error word
+  unsigned int* ctrl; // dynamic schedule: counters[n_pairs], exit counter
   int32_t B, H, H_kv, G, gblocks;
   int32_t S;          // partial slots per (b, h) row
   int32_t n_items, n_units;
+  int32_t n_pairs, n_pieces;  // dynamic schedule: pairs, pieces per pair
   float scale_log2;   // softmax scale * log2(e)
 };
+static_assert(sizeof(DecodeParams) <= 32764, "kernel parameter block limit");
+
+// Parameter block of the dynamically scheduled decode for launches of at
+// most kDynSegs segments: DecodeParams' fields with short tables, ~1.6 KB
+// instead of ~29 KB.  A launch's parameter block travels through the GPU's
+// command path; on B200 28 KB more of it costs ~2 us per launch.
+constexpr int kDynSegs = 4;
+struct alignas(64) DynParams {
+  CUtensorMap maps[2 * kDynSegs];
+  CUtensorMap qmap;
+  Item items[kDynSegs];
+  const int64_t* q_pos;
+  float* m_part;
+  float* l_part;
+  float* o_part;
+  unsigned int* err;
+  unsigned int* ctrl;
+  int32_t B, H, H_kv, G, gblocks;
+  int32_t S;
+  int32_t n_items, n_units;
+  int32_t n_pairs, n_pieces;
+  float scale_log2;
+};
+
 
 template <typename T, int D, int STAGES>
 struct Geom {
@@ -165,132 +197,129 @@ struct RingTiles {
   }
 };
 
-template <typename T, int D, int STAGES, class P, class Tiles>
-__device__ __forceinline__ bool consume_mma(const P& p, const Unit& un, const Item& it,
-                                            Tiles& tiles, const char* qslot,
-                                            uint64_t* qempty, int n_tiles,
-                                            int& gt, int64_t qpos) {
+// Q fragments (A operand) of all k-steps from a swizzled q tile.
+template <typename T, int D, int STAGES>
+__device__ __forceinline__ void load_q_frags(const char* qslot, uint32_t (&qf)[D / 16][4]) {
   using Gm = Geom<T, D, STAGES>;
   const int lane = threadIdx.x & 31;
-  const int warp = threadIdx.x >> 5;
+  const uint32_t qb = smem_addr(qslot);
+#pragma unroll
+  for (int kk = 0; kk < D / 16; ++kk) {
+    const int row = lane & 15;
+    const int c16 = kk * 2 + (lane >> 4);
+    ldsm_x4(qb + swz<Gm::kInner, Gm::kGpb>(row, c16), qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3]);
+  }
+}
 
-  // Q fragments (A operand) for all k-steps, loaded once per unit.
-  uint32_t qf[D / 16][4];
+// One 64-row K/V tile on the tensor cores for this warp's 16 rows of it:
+// S = Q K^T (16 q-heads x 16 keys), scale + mask, online softmax (rows
+// g0 = lane/4 and g1 = lane/4 + 8 of the q-head block), O += P V with
+// P = hi + lo (two 16-bit MMAs).  Row r of the tile (0..63) is a key if
+// r < valid and, for a causal tile, pos0 + r <= qpos.
+template <typename T, int D, int STAGES>
+__device__ __forceinline__ void mma_tile(float scale_log2, uint32_t kbase, uint32_t vbase,
+                                         const uint32_t (&qf)[D / 16][4], float (&o)[D / 8][4],
+                                         float& m0, float& m1, float& l0, float& l1, int valid,
+                                         int64_t pos0, bool causal, int64_t qpos) {
+  using Gm = Geom<T, D, STAGES>;
+  const int lane = threadIdx.x & 31;
+  const int wrow = (threadIdx.x >> 5) * 16;
+  const int c = lane & 3;
+
+  // ---- S = Q K^T
+  float sacc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
   {
-    const uint32_t qb = smem_addr(qslot);
+    const int key = wrow + (lane & 7) + ((lane >> 4) << 3);
 #pragma unroll
     for (int kk = 0; kk < D / 16; ++kk) {
-      const int row = lane & 15;
-      const int c16 = kk * 2 + (lane >> 4);
-      ldsm_x4(qb + swz<Gm::kInner, Gm::kGpb>(row, c16), qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3]);
+      const int c16 = kk * 2 + ((lane >> 3) & 1);
+      uint32_t b00, b01, b10, b11;
+      ldsm_x4(kbase + swz<Gm::kInner>(key, c16), b00, b01, b10, b11);
+      mma_16816(sacc[0], qf[kk], b00, b01, (T*)nullptr);
+      mma_16816(sacc[1], qf[kk], b10, b11, (T*)nullptr);
     }
   }
-  __syncwarp();
-  if (lane == 0) mbar_arrive(qempty);
 
-  float o[D / 8][4];
+  // ---- scale + mask (rows beyond the valid range, or causally hidden)
 #pragma unroll
-  for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+  for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int r = wrow + nt * 8 + 2 * c + e;
+      const bool ok = r < valid && (!causal || pos0 + r <= qpos);
+      sacc[nt][e] = ok ? sacc[nt][e] * scale_log2 : -INFINITY;
+      sacc[nt][e + 2] = ok ? sacc[nt][e + 2] * scale_log2 : -INFINITY;
+    }
+
+  // ---- online softmax
+  float r0 = fmaxf(fmaxf(sacc[0][0], sacc[0][1]), fmaxf(sacc[1][0], sacc[1][1]));
+  float r1 = fmaxf(fmaxf(sacc[0][2], sacc[0][3]), fmaxf(sacc[1][2], sacc[1][3]));
+  r0 = fmaxf(r0, __shfl_xor_sync(0xffffffffu, r0, 1));
+  r0 = fmaxf(r0, __shfl_xor_sync(0xffffffffu, r0, 2));
+  r1 = fmaxf(r1, __shfl_xor_sync(0xffffffffu, r1, 1));
+  r1 = fmaxf(r1, __shfl_xor_sync(0xffffffffu, r1, 2));
+  const float mn0 = fmaxf(m0, r0), mn1 = fmaxf(m1, r1);
+  const float mu0 = (mn0 == -INFINITY) ? 0.f : mn0;
+  const float mu1 = (mn1 == -INFINITY) ? 0.f : mn1;
+  const float a0 = exp2f(m0 - mu0), a1 = exp2f(m1 - mu1);
+  m0 = mn0;
+  m1 = mn1;
+  float pr[2][4];
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt) {
+    pr[nt][0] = exp2f(sacc[nt][0] - mu0);
+    pr[nt][1] = exp2f(sacc[nt][1] - mu0);
+    pr[nt][2] = exp2f(sacc[nt][2] - mu1);
+    pr[nt][3] = exp2f(sacc[nt][3] - mu1);
+  }
+  l0 = l0 * a0 + (pr[0][0] + pr[0][1] + pr[1][0] + pr[1][1]);
+  l1 = l1 * a1 + (pr[0][2] + pr[0][3] + pr[1][2] + pr[1][3]);
+  if (__any_sync(0xffffffffu, a0 != 1.f || a1 != 1.f)) {
+#pragma unroll
+    for (int i = 0; i < D / 8; ++i) {
+      o[i][0] *= a0;
+      o[i][1] *= a0;
+      o[i][2] *= a1;
+      o[i][3] *= a1;
+    }
+  }
+
+  // ---- O += P V with P = hi + lo (two 16-bit MMAs)
+  uint32_t ph[4], pl[4];
+  {
+    const float v[4][2] = {{pr[0][0], pr[0][1]}, {pr[0][2], pr[0][3]},
+                           {pr[1][0], pr[1][1]}, {pr[1][2], pr[1][3]}};
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      ph[r] = Elem<T>::pack(v[r][0], v[r][1]);
+      float h0, h1;
+      Elem<T>::unpack(ph[r], h0, h1);
+      pl[r] = Elem<T>::pack(v[r][0] - h0, v[r][1] - h1);
+    }
+  }
+  {
+    const int key = wrow + (lane & 7) + (((lane >> 3) & 1) << 3);
+#pragma unroll
+    for (int j = 0; j < D / 16; ++j) {
+      const int c16 = j * 2 + (lane >> 4);
+      uint32_t v0, v1, v2, v3;
+      ldsm_x4_t(vbase + swz<Gm::kInner>(key, c16), v0, v1, v2, v3);
+      mma_16816(o[2 * j], ph, v0, v1, (T*)nullptr);
+      mma_16816(o[2 * j], pl, v0, v1, (T*)nullptr);
+      mma_16816(o[2 * j + 1], ph, v2, v3, (T*)nullptr);
+      mma_16816(o[2 * j + 1], pl, v2, v3, (T*)nullptr);
+    }
+  }
+}
+
+// This warp's partial state (m, l, o) of the unit's q-heads -> partial slot
+// `slot` of each (b, h) row (rows < gcount only).
+template <int D, class P>
+__device__ __forceinline__ void store_partial_mma(const P& p, const Unit& un, int slot,
+                                                  const float (&o)[D / 8][4], float m0, float m1,
+                                                  float l0, float l1) {
+  const int lane = threadIdx.x & 31;
   const int c = lane & 3;
-  const int item_end = it.row0 + it.rows;
-  const int wrow = warp * 16;
-  bool ok = true;
-
-  for (int t = 0; t < n_tiles; ++t, ++gt) {
-    uint32_t kbase, vbase;
-    if (!tiles.acquire(t, gt, kbase, vbase)) { ok = false; ++gt; break; }
-
-    // ---- S = Q K^T (16 q-heads x 16 keys)
-    float sacc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-    {
-      const int key = wrow + (lane & 7) + ((lane >> 4) << 3);
-#pragma unroll
-      for (int kk = 0; kk < D / 16; ++kk) {
-        const int c16 = kk * 2 + ((lane >> 3) & 1);
-        uint32_t b00, b01, b10, b11;
-        ldsm_x4(kbase + swz<Gm::kInner>(key, c16), b00, b01, b10, b11);
-        mma_16816(sacc[0], qf[kk], b00, b01, (T*)nullptr);
-        mma_16816(sacc[1], qf[kk], b10, b11, (T*)nullptr);
-      }
-    }
-
-    // ---- scale + mask (rows beyond the item, or causally hidden)
-    const int row_base = it.row0 + t * kBlockN + wrow;
-#pragma unroll
-    for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int row = row_base + nt * 8 + 2 * c + e;
-        const bool valid =
-            row < item_end && (!it.causal || it.start + (row - it.row0) <= qpos);
-        sacc[nt][e] = valid ? sacc[nt][e] * p.scale_log2 : -INFINITY;
-        sacc[nt][e + 2] = valid ? sacc[nt][e + 2] * p.scale_log2 : -INFINITY;
-      }
-
-    // ---- online softmax (rows g0 = lane/4, g1 = lane/4 + 8)
-    float r0 = fmaxf(fmaxf(sacc[0][0], sacc[0][1]), fmaxf(sacc[1][0], sacc[1][1]));
-    float r1 = fmaxf(fmaxf(sacc[0][2], sacc[0][3]), fmaxf(sacc[1][2], sacc[1][3]));
-    r0 = fmaxf(r0, __shfl_xor_sync(0xffffffffu, r0, 1));
-    r0 = fmaxf(r0, __shfl_xor_sync(0xffffffffu, r0, 2));
-    r1 = fmaxf(r1, __shfl_xor_sync(0xffffffffu, r1, 1));
-    r1 = fmaxf(r1, __shfl_xor_sync(0xffffffffu, r1, 2));
-    const float mn0 = fmaxf(m0, r0), mn1 = fmaxf(m1, r1);
-    const float mu0 = (mn0 == -INFINITY) ? 0.f : mn0;
-    const float mu1 = (mn1 == -INFINITY) ? 0.f : mn1;
-    const float a0 = exp2f(m0 - mu0), a1 = exp2f(m1 - mu1);
-    m0 = mn0;
-    m1 = mn1;
-    float pr[2][4];
-#pragma unroll
-    for (int nt = 0; nt < 2; ++nt) {
-      pr[nt][0] = exp2f(sacc[nt][0] - mu0);
-      pr[nt][1] = exp2f(sacc[nt][1] - mu0);
-      pr[nt][2] = exp2f(sacc[nt][2] - mu1);
-      pr[nt][3] = exp2f(sacc[nt][3] - mu1);
-    }
-    l0 = l0 * a0 + (pr[0][0] + pr[0][1] + pr[1][0] + pr[1][1]);
-    l1 = l1 * a1 + (pr[0][2] + pr[0][3] + pr[1][2] + pr[1][3]);
-    if (__any_sync(0xffffffffu, a0 != 1.f || a1 != 1.f)) {
-#pragma unroll
-      for (int i = 0; i < D / 8; ++i) {
-        o[i][0] *= a0;
-        o[i][1] *= a0;
-        o[i][2] *= a1;
-        o[i][3] *= a1;
-      }
-    }
-
-    // ---- O += P V with P = hi + lo (two 16-bit MMAs)
-    uint32_t ph[4], pl[4];
-    {
-      const float v[4][2] = {{pr[0][0], pr[0][1]}, {pr[0][2], pr[0][3]},
-                             {pr[1][0], pr[1][1]}, {pr[1][2], pr[1][3]}};
-#pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        ph[r] = Elem<T>::pack(v[r][0], v[r][1]);
-        float h0, h1;
-        Elem<T>::unpack(ph[r], h0, h1);
-        pl[r] = Elem<T>::pack(v[r][0] - h0, v[r][1] - h1);
-      }
-    }
-    {
-      const int key = wrow + (lane & 7) + (((lane >> 3) & 1) << 3);
-#pragma unroll
-      for (int j = 0; j < D / 16; ++j) {
-        const int c16 = j * 2 + (lane >> 4);
-        uint32_t v0, v1, v2, v3;
-        ldsm_x4_t(vbase + swz<Gm::kInner>(key, c16), v0, v1, v2, v3);
-        mma_16816(o[2 * j], ph, v0, v1, (T*)nullptr);
-        mma_16816(o[2 * j], pl, v0, v1, (T*)nullptr);
-        mma_16816(o[2 * j + 1], ph, v2, v3, (T*)nullptr);
-        mma_16816(o[2 * j + 1], pl, v2, v3, (T*)nullptr);
-      }
-    }
-    tiles.release(gt);
-  }
-
-  // ---- this warp's partial state -> global (rows < gcount only)
   l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
   l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
   l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
@@ -300,15 +329,48 @@ __device__ __forceinline__ bool consume_mma(const P& p, const Unit& un, const It
   for (int half = 0; half < 2; ++half) {
     const int g = g0 + 8 * half;
     if (g < un.gcount) {
-      if (c == 0) write_partial_meta(p, un, it, warp, g, half ? m1 : m0, half ? l1 : l0);
       const int h = un.h_kv * p.G + un.gbase + g;
-      float* op = p.o_part + (((int64_t)un.b * p.H + h) * p.S + it.slot + warp) * D;
+      const int64_t row = ((int64_t)un.b * p.H + h) * p.S + slot;
+      if (c == 0) {
+        const float m = half ? m1 : m0;
+        p.m_part[row] = (m == -INFINITY) ? -INFINITY : m * kLn2;
+        p.l_part[row] = half ? l1 : l0;
+      }
+      float* op = p.o_part + row * D;
 #pragma unroll
       for (int i = 0; i < D / 8; ++i)
         *reinterpret_cast<float2*>(op + i * 8 + 2 * c) =
             make_float2(o[i][2 * half], o[i][2 * half + 1]);
     }
   }
+}
+
+template <typename T, int D, int STAGES, class P, class Tiles>
+__device__ __forceinline__ bool consume_mma(const P& p, const Unit& un, const Item& it,
+                                            Tiles& tiles, const char* qslot,
+                                            uint64_t* qempty, int n_tiles,
+                                            int& gt, int64_t qpos) {
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  uint32_t qf[D / 16][4];
+  load_q_frags<T, D, STAGES>(qslot, qf);
+  __syncwarp();
+  if (lane == 0) mbar_arrive(qempty);
+
+  float o[D / 8][4];
+#pragma unroll
+  for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+  bool ok = true;
+  for (int t = 0; t < n_tiles; ++t, ++gt) {
+    uint32_t kbase, vbase;
+    if (!tiles.acquire(t, gt, kbase, vbase)) { ok = false; ++gt; break; }
+    mma_tile<T, D, STAGES>(p.scale_log2, kbase, vbase, qf, o, m0, m1, l0, l1,
+                           it.rows - t * kBlockN, it.start + (int64_t)t * kBlockN,
+                           it.causal != 0, qpos);
+    tiles.release(gt);
+  }
+  store_partial_mma<D>(p, un, it.slot + warp, o, m0, m1, l0, l1);
   return ok;
 }
 
@@ -463,6 +525,9 @@ __global__ void __launch_bounds__(kThreads, MINB) kd_kernel(const __grid_constan
   uint64_t* qfull = empty + STAGES;
   uint64_t* qempty = qfull + 2;
 
+  // the merge launched after this kernel may be scheduled from now on; it
+  // waits for this grid to finish before reading the partials
+  grid_dep_trigger();
   const int tid = threadIdx.x;
   if (tid == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -534,6 +599,223 @@ __global__ void __launch_bounds__(kThreads, MINB) kd_kernel(const __grid_constan
     }
     if (!ok) return;  // the error word is set; remaining units are abandoned
   }
+}
+
+// ---------------------------------------------------------------- kd, dynamic schedule
+// Same tile math as kd_kernel, but the rows are handed out at run time.
+// Each (batch, kv-head, q-head block) pair gets a group of CTAs: CTA c
+// serves pair c % n_pairs and is member c / n_pairs of its group.  The
+// pair's rows (every segment of the launch, in order) are cut into pieces of
+// kPieceTiles 64-row tiles, and the group's producer lanes take pieces from
+// the pair's counter in the workspace control block, so CTAs on SMs that
+// stream faster take more pieces and the group finishes within about one
+// piece of each other (a static split leaves the CTAs of slower SMs
+// finishing ~15 % after the median).  Each consumer warp folds every piece
+// its CTA takes into one running state; at the end the four warps' states
+// are combined through shared memory into the CTA's partial, slot `member`
+// (so a row has one partial per CTA of its group).  The
+// producer tells the consumers what each stage holds through a per-stage
+// descriptor written before the stage's barrier arrival; a descriptor with
+// no rows ends the work.  Every CTA's producer lane counts itself out on the
+// control block's exit counter after its last take and once its consumers
+// are done; the last one zeroes the counters for the next call.
+struct TileDesc {
+  int64_t pos0;    // global position of the tile's first row
+  int32_t valid;   // rows of the tile inside its segment; 0 = no more work
+  int32_t causal;
+};
+
+template <typename T, int D, int STAGES>
+struct DynGeom {
+  using Gm = Geom<T, D, STAGES>;
+  static constexpr int kDescOff = Gm::kSmemBytes - 1024;   // after the barrier block
+  static constexpr int kSmemBytes = Gm::kSmemBytes + 128;
+  static_assert(STAGES * (int)sizeof(TileDesc) + 8 <= 128, "descriptor area");
+};
+
+template <typename T, int D, int STAGES, int MINB, class P>
+__global__ void __launch_bounds__(kThreads, MINB)
+    kd_dyn_kernel(const __grid_constant__ P p) {
+  using Gm = Geom<T, D, STAGES>;
+  using DG = DynGeom<T, D, STAGES>;
+  extern __shared__ char smem_raw[];
+  char* base = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                       ~uintptr_t(1023));
+  char* ring = base;
+  char* qslot = ring + STAGES * Gm::kStageBytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(qslot + 2 * Gm::kQSlotBytes + Gm::kPBytes);
+  uint64_t* empty = full + STAGES;
+  uint64_t* qfull = empty + STAGES;
+  TileDesc* desc = reinterpret_cast<TileDesc*>(base + DG::kDescOff);
+  uint64_t* cons_done = reinterpret_cast<uint64_t*>(desc + STAGES);
+
+  grid_dep_trigger();
+  const int tid = threadIdx.x;
+  if (tid == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kConsumerWarps);
+    }
+    mbar_init(qfull, 1);
+    mbar_init(cons_done, kConsumerWarps);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  const int warp = tid >> 5, lane = tid & 31;
+  const int pair = (int)(blockIdx.x % (unsigned)p.n_pairs);
+  const int member = (int)(blockIdx.x / (unsigned)p.n_pairs);
+  Unit un;
+  un.item = 0;
+  un.gbase = (pair % p.gblocks) * Gm::kGpb;
+  un.gcount = min(Gm::kGpb, p.G - un.gbase);
+  un.h_kv = (pair / p.gblocks) % p.H_kv;
+  un.b = pair / p.gblocks / p.H_kv;
+
+  if (warp == kConsumerWarps) {
+    if (lane == 0) {
+      mbar_arrive_expect_tx(qfull, Gm::kNBox * Gm::kGpb * Gm::kInner);
+#pragma unroll
+      for (int bx = 0; bx < Gm::kNBox; ++bx)
+        tma_load_3d(qslot + bx * Gm::kGpb * Gm::kInner, &p.qmap, bx * Gm::kBoxElems,
+                    un.h_kv * p.G + un.gbase, un.b, qfull);
+      // member m's first piece is piece m; later pieces come from the
+      // pair's counter (offset by the group size)
+      unsigned int* ctr = p.ctrl + pair;
+      const unsigned int cpg = gridDim.x / (unsigned)p.n_pairs;
+      int gt = 0;
+      bool ok = true;
+      unsigned int next = (unsigned)member;
+      while (ok && next < (unsigned int)p.n_pieces) {
+        const int piece = (int)next;
+        next = cpg + atomicAdd(ctr, 1u);   // the next take is in flight while this piece loads
+        int si = 0;                  // items[i].slot = first piece of segment i
+        while (si + 1 < p.n_items && p.items[si + 1].slot <= piece) ++si;
+        const Item& it = p.items[si];
+        const int t0 = (piece - it.slot) * kPieceTiles;
+        const int t1 = min(t0 + kPieceTiles, (it.rows + kBlockN - 1) / kBlockN);
+        const CUtensorMap* kmap = &p.maps[2 * si];
+        const CUtensorMap* vmap = &p.maps[2 * si + 1];
+        const int bc = it.b_bcast ? 0 : un.b;
+        for (int t = t0; t < t1; ++t, ++gt) {
+          const int s = gt % STAGES;
+          if (gt >= STAGES && !(ok = mbar_wait(&empty[s], ((gt / STAGES) & 1) ^ 1, p.err))) break;
+          const int r0 = t * kBlockN;
+          desc[s].pos0 = it.start + r0;
+          desc[s].valid = min(kBlockN, it.rows - r0);
+          desc[s].causal = it.causal;
+          char* kd = ring + s * Gm::kStageBytes;
+          char* vd = kd + Gm::kTileBytes;
+          mbar_arrive_expect_tx(&full[s], 2u * Gm::kTileBytes);
+#pragma unroll
+          for (int bx = 0; bx < Gm::kNBox; ++bx) {
+            tma_load_4d(kd + bx * Gm::kBoxBytes, kmap, bx * Gm::kBoxElems, it.row0 + r0, un.h_kv,
+                        bc, &full[s]);
+            tma_load_4d(vd + bx * Gm::kBoxBytes, vmap, bx * Gm::kBoxElems, it.row0 + r0, un.h_kv,
+                        bc, &full[s]);
+          }
+        }
+      }
+      if (ok) {   // end of work: a stage descriptor with no rows
+        const int s = gt % STAGES;
+        if (gt < STAGES || (ok = mbar_wait(&empty[s], ((gt / STAGES) & 1) ^ 1, p.err))) {
+          desc[s].valid = 0;
+          mbar_arrive(&full[s]);
+        }
+      }
+      // the consumers are done with every stage (bounded), then count out
+      mbar_wait(cons_done, 0, p.err);
+      __threadfence();
+      if (atomicAdd(p.ctrl + p.n_pairs, 1u) == gridDim.x - 1) {
+        for (int i = 0; i < p.n_pairs; ++i) p.ctrl[i] = 0;
+        p.ctrl[p.n_pairs] = 0;
+      }
+    }
+    return;
+  }
+
+  // ---------------- consumer warps
+  float o[D / 8][4];
+#pragma unroll
+  for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+  if (mbar_wait(qfull, 0, p.err)) {
+    uint32_t qf[D / 16][4];
+    load_q_frags<T, D, STAGES>(qslot, qf);
+    const int64_t qpos = (p.q_pos != nullptr) ? p.q_pos[un.b] : INT64_MAX;
+    for (int gt = 0;; ++gt) {
+      const int s = gt % STAGES;
+      if (!mbar_wait(&full[s], (gt / STAGES) & 1, p.err)) break;
+      const TileDesc d = desc[s];
+      if (d.valid == 0) break;
+      const uint32_t kbase = smem_addr(ring + s * Gm::kStageBytes);
+      mma_tile<T, D, STAGES>(p.scale_log2, kbase, kbase + Gm::kTileBytes, qf, o, m0, m1, l0, l1,
+                             d.valid, d.pos0, d.causal != 0, qpos);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+    }
+  }
+  // ---- combine the four warps' states into the CTA's partial (slot
+  // `member`): every warp is past its last tile, so the ring is free scratch
+  named_bar_sync(1, kConsumerWarps * 32);
+  constexpr int kStride = D + 8;
+  static_assert(kConsumerWarps * 16 * (kStride + 2) * 4 <= STAGES * Gm::kStageBytes,
+                "combine scratch must fit in the ring");
+  float* sc = reinterpret_cast<float*>(ring);
+  float* sm = sc + kConsumerWarps * 16 * kStride;
+  float* sl = sm + kConsumerWarps * 16;
+  {
+    const int c = lane & 3, g0 = lane >> 2;
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+    float* r0 = sc + (warp * 16 + g0) * kStride;
+    float* r1 = r0 + 8 * kStride;
+#pragma unroll
+    for (int i = 0; i < D / 8; ++i) {
+      *reinterpret_cast<float2*>(r0 + i * 8 + 2 * c) = make_float2(o[i][0], o[i][1]);
+      *reinterpret_cast<float2*>(r1 + i * 8 + 2 * c) = make_float2(o[i][2], o[i][3]);
+    }
+    if (c == 0) {
+      sm[warp * 16 + g0] = m0;
+      sm[warp * 16 + g0 + 8] = m1;
+      sl[warp * 16 + g0] = l0;
+      sl[warp * 16 + g0 + 8] = l1;
+    }
+  }
+  named_bar_sync(1, kConsumerWarps * 32);
+  {
+    constexpr int kCols = D / 8;          // columns per thread: 8 threads per row
+    const int r = tid >> 3, c0 = (tid & 7) * kCols;
+    if (r < un.gcount) {
+      float M = -INFINITY;
+#pragma unroll
+      for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, sm[w * 16 + r]);
+      float wt[kConsumerWarps], L = 0.f;
+#pragma unroll
+      for (int w = 0; w < kConsumerWarps; ++w) {
+        const float mw = sm[w * 16 + r];
+        wt[w] = (mw == -INFINITY) ? 0.f : exp2f(mw - M);
+        L = fmaf(sl[w * 16 + r], wt[w], L);
+      }
+      const int h = un.h_kv * p.G + un.gbase + r;
+      const int64_t prow = ((int64_t)un.b * p.H + h) * p.S + member;
+      float* op = p.o_part + prow * D + c0;
+#pragma unroll
+      for (int j = 0; j < kCols; ++j) {
+        float acc = 0.f;
+#pragma unroll
+        for (int w = 0; w < kConsumerWarps; ++w) acc = fmaf(sc[(w * 16 + r) * kStride + c0 + j], wt[w], acc);
+        op[j] = acc;
+      }
+      if ((tid & 7) == 0) {
+        p.m_part[prow] = (M == -INFINITY) ? -INFINITY : M * kLn2;
+        p.l_part[prow] = L;
+      }
+    }
+  }
+  __syncwarp();
+  if (lane == 0) mbar_arrive(cons_done);
 }
 
 // ---------------------------------------------------------------- KIVI decode
@@ -697,6 +979,9 @@ __global__ void __launch_bounds__(kThreads, 2) kk_kernel(const __grid_constant__
   uint64_t* qfull = empty + STAGES;
   uint64_t* qempty = qfull + 2;
 
+  // the merge launched after this kernel may be scheduled from now on; it
+  // waits for this grid to finish before reading the partials
+  grid_dep_trigger();
   const int tid = threadIdx.x;
   if (tid == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -795,6 +1080,7 @@ __global__ void __launch_bounds__(kMergeWarps * 32) km_kernel(const MergeParams 
   __shared__ __align__(16) float s_o[kMergeWarps][DPL * 32];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = blockIdx.x;
+  grid_dep_wait();   // the partials' writer has finished (dependent launch)
   const float* mr = mp.m_parts + (int64_t)row * mp.rs;
   const float* lr = mp.l_parts ? mp.l_parts + (int64_t)row * mp.rs : nullptr;
   const float* orow = mp.o_parts + (int64_t)row * mp.ors;
@@ -1053,13 +1339,20 @@ int launch_merge(const MergeParams& mp, cudaStream_t st) {
   const int threads = kMergeWarps * 32;
   const bool vec = (reinterpret_cast<uintptr_t>(mp.o_parts) & 15) == 0 && mp.ops % 4 == 0 &&
                    mp.ors % 4 == 0;
-  if (mp.Dv <= 32) km_kernel<1, false><<<mp.R, threads, 0, st>>>(mp);
-  else if (mp.Dv <= 64 && mp.Dv % 2 == 0) km_kernel<2, false><<<mp.R, threads, 0, st>>>(mp);
-  else if (mp.Dv <= 128 && mp.Dv % 4 == 0 && vec) km_kernel<4, true><<<mp.R, threads, 0, st>>>(mp);
-  else if (mp.Dv <= 128 && mp.Dv % 4 == 0) km_kernel<4, false><<<mp.R, threads, 0, st>>>(mp);
-  else if (mp.Dv <= 256 && mp.Dv % 8 == 0) km_kernel<8, false><<<mp.R, threads, 0, st>>>(mp);
+  // launched as a dependent of the kernel that wrote the partials, so its
+  // launch overlaps that kernel's last CTAs (km_kernel waits for it first)
+  cudaError_t e;
+  if (mp.Dv <= 32) e = launch_dependent(km_kernel<1, false>, mp.R, threads, 0, st, mp);
+  else if (mp.Dv <= 64 && mp.Dv % 2 == 0)
+    e = launch_dependent(km_kernel<2, false>, mp.R, threads, 0, st, mp);
+  else if (mp.Dv <= 128 && mp.Dv % 4 == 0 && vec)
+    e = launch_dependent(km_kernel<4, true>, mp.R, threads, 0, st, mp);
+  else if (mp.Dv <= 128 && mp.Dv % 4 == 0)
+    e = launch_dependent(km_kernel<4, false>, mp.R, threads, 0, st, mp);
+  else if (mp.Dv <= 256 && mp.Dv % 8 == 0)
+    e = launch_dependent(km_kernel<8, false>, mp.R, threads, 0, st, mp);
   else return fail(HALO_ERR_UNSUPPORTED, "Dv %d unsupported by the merge", mp.Dv);
-  cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "km_kernel launch");
   count_launches();
   return HALO_OK;
@@ -1119,10 +1412,16 @@ struct Seg {
 
 struct Plan {
   std::vector<Seg> segs;
-  std::vector<Item> items;  // items[i].slot = i * kConsumerWarps
+  std::vector<Item> items;  // static: items[i].slot = i * kConsumerWarps
   int32_t split_tiles = 0;
   int32_t S = 0;            // partial slots per (b, h) row
+  // dynamic schedule (kd_dyn_kernel): one item per segment whose slot is
+  // its first piece; `grid` CTAs = n_pairs groups of S / kConsumerWarps
+  bool dyn = false;
+  int32_t n_pairs = 0, n_pieces = 0, grid = 0;
 };
+
+static int dyn_ctas_per_sm(int dtype, int D);
 
 static int gpb_for(int dtype) { return dtype == HALO_DTYPE_F32 ? 8 : 16; }
 
@@ -1165,6 +1464,39 @@ static Plan make_plan(const halo_decode_problem_t* p, const halo_kv_chunk_t* chu
   for (const Seg& sg : plan.segs) {
     seg_tiles.push_back(ceil_div64(sg.view.len, kBlockN));
     total_tiles += seg_tiles.back();
+  }
+
+  // Dynamic schedule: 16-bit inputs, one launch's worth of segments, and
+  // enough pieces for every CTA of a pair's group to take several; the
+  // groups must fill at least 90 % of the resident CTA slots.
+  if (p->dtype != HALO_DTYPE_F32 && p->max_split_rows <= 0 &&
+      (int64_t)plan.segs.size() <= kMaxSegs && pairs <= kMaxDynPairs) {
+    const int64_t cap = (int64_t)device_sms() * dyn_ctas_per_sm(p->dtype, p->D);
+    const int64_t cpg = cap / pairs;
+    int64_t pieces = 0;
+    for (int64_t t : seg_tiles) pieces += ceil_div64(t, kPieceTiles);
+    if (cpg >= 1 && pairs * cpg * 10 >= cap * 9 && pieces >= 4 * cpg) {
+      plan.dyn = true;
+      plan.n_pairs = (int32_t)pairs;
+      plan.n_pieces = (int32_t)pieces;
+      plan.grid = (int32_t)(pairs * cpg);
+      plan.S = (int32_t)cpg;     // one combined partial per CTA of a group
+      int32_t first = 0;
+      for (size_t si = 0; si < plan.segs.size(); ++si) {
+        const Seg& sg = plan.segs[si];
+        Item it;
+        it.seg = (int32_t)si;
+        it.row0 = 0;
+        it.rows = (int32_t)sg.view.len;
+        it.start = sg.view.start;
+        it.causal = sg.view.causal;
+        it.b_bcast = (sg.view.k_stride_b == 0 || sg.view.v_stride_b == 0) ? 1 : 0;
+        it.slot = first;
+        first += (int32_t)ceil_div64(seg_tiles[si], kPieceTiles);
+        plan.items.push_back(it);
+      }
+      return plan;
+    }
   }
   int64_t split = 0;
   // Memoise the choice per layout signature: decode steps repeat layouts.
@@ -1239,7 +1571,7 @@ static Plan make_plan(const halo_decode_problem_t* p, const halo_kv_chunk_t* chu
 
 static int64_t workspace_for(const halo_decode_problem_t* p, int S) {
   const int64_t R = (int64_t)p->B * p->H;
-  return align256(R * S * 4) * 2 + align256(R * S * (int64_t)p->Dv * 4);
+  return kCtrlBytes + align256(R * S * 4) * 2 + align256(R * S * (int64_t)p->Dv * 4);
 }
 
 template <typename T, int D>
@@ -1308,6 +1640,120 @@ static int launch_kd(const DecodeParams& prm, cudaStream_t st) {
   if (e != cudaSuccess) return cuda_fail(e, "kd_kernel launch");
   count_launches();
   return HALO_OK;
+}
+
+// Shared-memory attribute of one dynamic-schedule instantiation, set once
+// per device.
+template <typename T, int D, class P>
+static void kd_dyn_prepare() {
+  using C = KdConfig<T, D>;
+  using DG = DynGeom<T, D, C::kStages>;
+  static std::once_flag once[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::call_once(once[dev & 63], [] {
+    cudaFuncSetAttribute(kd_dyn_kernel<T, D, C::kStages, C::kMinBlocks, P>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, DG::kSmemBytes);
+  });
+}
+
+template <typename T, int D>
+static int kd_dyn_ctas_per_sm() {
+  using C = KdConfig<T, D>;
+  using DG = DynGeom<T, D, C::kStages>;
+  static std::once_flag once[64];
+  static int cache[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::call_once(once[dev & 63], [&] {
+    kd_dyn_prepare<T, D, DynParams>();
+    kd_dyn_prepare<T, D, DecodeParams>();
+    int n = 0, n2 = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+            &n, kd_dyn_kernel<T, D, C::kStages, C::kMinBlocks, DynParams>, kThreads,
+            DG::kSmemBytes) != cudaSuccess || n <= 0)
+      n = 1;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+            &n2, kd_dyn_kernel<T, D, C::kStages, C::kMinBlocks, DecodeParams>, kThreads,
+            DG::kSmemBytes) != cudaSuccess || n2 <= 0)
+      n2 = 1;
+    cache[dev & 63] = std::min(n, n2);
+  });
+  return cache[dev & 63];
+}
+
+template <typename T>
+static int dyn_ctas_for(int D) {
+  if (D == 16) return kd_dyn_ctas_per_sm<T, 16>();
+  if (D == 32) return kd_dyn_ctas_per_sm<T, 32>();
+  if (D == 64) return kd_dyn_ctas_per_sm<T, 64>();
+  if (D == 80) return kd_dyn_ctas_per_sm<T, 80>();
+  if (D == 96) return kd_dyn_ctas_per_sm<T, 96>();
+  if (D == 128) return kd_dyn_ctas_per_sm<T, 128>();
+  return 1;
+}
+
+static int dyn_ctas_per_sm(int dtype, int D) {
+  if (dtype == HALO_DTYPE_BF16) return dyn_ctas_for<__nv_bfloat16>(D);
+  if (dtype == HALO_DTYPE_F16) return dyn_ctas_for<__half>(D);
+  return 1;
+}
+
+template <typename T, int D, class P>
+static int launch_kd_dyn(const P& prm, int grid, cudaStream_t st) {
+  using C = KdConfig<T, D>;
+  using DG = DynGeom<T, D, C::kStages>;
+  kd_dyn_ctas_per_sm<T, D>();   // sets the shared-memory attributes once
+  kd_dyn_kernel<T, D, C::kStages, C::kMinBlocks, P><<<grid, kThreads, DG::kSmemBytes, st>>>(prm);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "kd_dyn_kernel launch");
+  count_launches();
+  return HALO_OK;
+}
+
+template <typename T, class P>
+static int dispatch_kd_dyn_t(int D, const P& prm, int grid, cudaStream_t st) {
+  if (D == 16) return launch_kd_dyn<T, 16>(prm, grid, st);
+  if (D == 32) return launch_kd_dyn<T, 32>(prm, grid, st);
+  if (D == 64) return launch_kd_dyn<T, 64>(prm, grid, st);
+  if (D == 80) return launch_kd_dyn<T, 80>(prm, grid, st);
+  if (D == 96) return launch_kd_dyn<T, 96>(prm, grid, st);
+  if (D == 128) return launch_kd_dyn<T, 128>(prm, grid, st);
+  return fail(HALO_ERR_UNSUPPORTED, "head_dim %d unsupported", D);
+}
+
+// Launch the dynamic schedule from a filled DecodeParams: through the
+// compact parameter block when the segments fit in it.
+static int dispatch_kd_dyn(int dtype, int D, const DecodeParams& prm, int grid, cudaStream_t st) {
+  if (dtype != HALO_DTYPE_BF16 && dtype != HALO_DTYPE_F16)
+    return fail(HALO_ERR_UNSUPPORTED, "dynamic schedule needs 16-bit inputs");
+  if (prm.n_items <= kDynSegs) {
+    DynParams dp;
+    for (int i = 0; i < 2 * prm.n_items; ++i) dp.maps[i] = prm.maps[i];
+    dp.qmap = prm.qmap;
+    for (int i = 0; i < prm.n_items; ++i) dp.items[i] = prm.items[i];
+    dp.q_pos = prm.q_pos;
+    dp.m_part = prm.m_part;
+    dp.l_part = prm.l_part;
+    dp.o_part = prm.o_part;
+    dp.err = prm.err;
+    dp.ctrl = prm.ctrl;
+    dp.B = prm.B;
+    dp.H = prm.H;
+    dp.H_kv = prm.H_kv;
+    dp.G = prm.G;
+    dp.gblocks = prm.gblocks;
+    dp.S = prm.S;
+    dp.n_items = prm.n_items;
+    dp.n_units = prm.n_units;
+    dp.n_pairs = prm.n_pairs;
+    dp.n_pieces = prm.n_pieces;
+    dp.scale_log2 = prm.scale_log2;
+    if (dtype == HALO_DTYPE_BF16) return dispatch_kd_dyn_t<__nv_bfloat16>(D, dp, grid, st);
+    return dispatch_kd_dyn_t<__half>(D, dp, grid, st);
+  }
+  if (dtype == HALO_DTYPE_BF16) return dispatch_kd_dyn_t<__nv_bfloat16>(D, prm, grid, st);
+  return dispatch_kd_dyn_t<__half>(D, prm, grid, st);
 }
 
 static int dispatch_kd(int dtype, int D, const DecodeParams& prm, cudaStream_t st) {
@@ -1485,9 +1931,9 @@ static int decode_splits(const halo_decode_problem_t* problem, const halo_kv_chu
 
   const int64_t R = (int64_t)pb.B * pb.H;
   char* ws = static_cast<char*>(workspace);
-  float* m_part = reinterpret_cast<float*>(ws);
-  float* l_part = reinterpret_cast<float*>(ws + align256(R * plan.S * 4));
-  float* o_part = reinterpret_cast<float*>(ws + 2 * align256(R * plan.S * 4));
+  float* m_part = reinterpret_cast<float*>(ws + kCtrlBytes);
+  float* l_part = reinterpret_cast<float*>(ws + kCtrlBytes + align256(R * plan.S * 4));
+  float* o_part = reinterpret_cast<float*>(ws + kCtrlBytes + 2 * align256(R * plan.S * 4));
 
   if (plan.S > 0) {
     const int G = pb.H / pb.H_kv;
@@ -1512,8 +1958,29 @@ static int decode_splits(const halo_decode_problem_t* problem, const halo_kv_chu
       cudaError_t e = cudaEventRecord(static_cast<cudaEvent_t>(pb.event_begin), st);
       if (e != cudaSuccess) return cuda_fail(e, "cudaEventRecord(event_begin)");
     }
+    if (plan.dyn) {
+      prm.ctrl = reinterpret_cast<unsigned int*>(ws);
+      prm.n_pairs = plan.n_pairs;
+      prm.n_pieces = plan.n_pieces;
+      prm.n_items = (int32_t)plan.items.size();
+      prm.n_units = plan.grid;
+      for (size_t si = 0; si < plan.segs.size(); ++si) {
+        const Seg& sg = plan.segs[si];
+        rc = encode_view(sg.view.k, sg.view.len, pb.H_kv, pb.B, pb.D, pb.dtype,
+                         sg.view.k_stride_b, sg.view.k_stride_h, sg.view.k_stride_t,
+                         &prm.maps[2 * si]);
+        if (rc == HALO_OK)
+          rc = encode_view(sg.view.v, sg.view.len, pb.H_kv, pb.B, pb.Dv, pb.dtype,
+                           sg.view.v_stride_b, sg.view.v_stride_h, sg.view.v_stride_t,
+                           &prm.maps[2 * si + 1]);
+        if (rc != HALO_OK) return rc;
+        prm.items[si] = plan.items[si];
+      }
+      rc = dispatch_kd_dyn(pb.dtype, pb.D, prm, plan.grid, st);
+      if (rc != HALO_OK) return rc;
+    }
     // One launch unless the segment or item tables overflow the parameter block.
-    size_t i = 0;
+    size_t i = plan.dyn ? plan.items.size() : 0;
     while (i < plan.items.size()) {
       int n_items = 0, n_seg = 0, last_seg = -1;
       while (i + n_items < plan.items.size() && n_items < kMaxItems) {
@@ -1666,9 +2133,9 @@ extern "C" int32_t halo_kivi_decode(const halo_decode_problem_t* problem,
     return fail(HALO_ERR_MISALIGNED, "workspace must be 256-byte aligned");
   const int64_t R = (int64_t)pb.B * pb.H;
   char* ws = static_cast<char*>(workspace);
-  float* m_part = reinterpret_cast<float*>(ws);
-  float* l_part = reinterpret_cast<float*>(ws + align256(R * S * 4));
-  float* o_part = reinterpret_cast<float*>(ws + 2 * align256(R * S * 4));
+  float* m_part = reinterpret_cast<float*>(ws + kCtrlBytes);
+  float* l_part = reinterpret_cast<float*>(ws + kCtrlBytes + align256(R * S * 4));
+  float* o_part = reinterpret_cast<float*>(ws + kCtrlBytes + 2 * align256(R * S * 4));
   if (S > 0) {
     static thread_local KiviParams prm;
     rc = encode_q_map(pb, &prm.qmap);

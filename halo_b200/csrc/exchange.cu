@@ -5,21 +5,30 @@
 // all-gather of (o, lse) -> merge of the gathered parts" (three launches and
 // a collective) with one kernel per rank: CTA r merges row r's local
 // partials, stores the row's normalised (o, lse) straight into slot
-// [rank][r] of every rank's exchange buffer (plain stores through peer
-// pointers, i.e. NVLink P2P writes), publishes a per-row flag on each rank
-// with a system-scope release, waits (bounded) for the flags of all ranks
-// for row r in its own buffer, and folds the `world` parts into the output.
-// The merge is the identity of halo/kv_cache_chunked.py:194-239 (lzbaclz/HALO)
-// generalised to P parts; the reference is single-GPU, this exchange is new.
+// [rank][r] of every peer's exchange buffer (plain stores through peer
+// pointers, i.e. NVLink P2P writes), waits (bounded) until the rows of all
+// ranks for row r are in its own buffer, and folds the `world` parts into
+// the output.  The merge is the identity of halo/kv_cache_chunked.py:194-239
+// (lzbaclz/HALO) generalised to P parts; the reference is single-GPU, this
+// exchange is new.
+//
+// Every value travels as one 64-bit word: the call's epoch in the high half,
+// the fp32 bits in the low half.  An aligned 64-bit store is single-copy
+// atomic, so a reader that sees the current epoch in a word also sees that
+// word's value: no flags, no system-scope fences, one NVLink trip.
 //
 // Exchange buffer (one per rank, allocated with halo_ipc_alloc, mapped on
-// every peer with halo_ipc_open), fp32 data then uint32 flags:
-//   data[2][world][R][Dv + 1]   parity = epoch & 1; o then lse per row
-//   flag[world][R]              last epoch whose row arrived from that rank
-// Epochs increase by one per call.  A rank can only run one call ahead of
-// any peer (it needs that peer's row of the current call first), so the
-// parity slot it writes was last read two calls earlier, and readers wait
-// for flag >= epoch.  No TMA, no multicast: plain loads and stores.
+// every peer with halo_ipc_open), then control words only the owner touches:
+//   word[2][world][R][Dv + 1]   parity = epoch & 1; o then lse per row
+//   ctrl[4]                     [0] epoch of the last completed call,
+//                               [1] CTAs of the running call that finished
+// The epoch lives on the device: each CTA reads ctrl[0] + 1 when it starts,
+// and the last CTA to finish stores it back, so every rank advances by one
+// per call without the host passing a counter, and a captured CUDA graph
+// replays correctly.  A rank can only run one call ahead of any peer (it
+// needs that peer's row of the current call first), so the parity slot it
+// writes was last read two calls earlier.  No TMA, no multicast: plain
+// loads and stores.
 #include <cstdint>
 #include <cstring>
 
@@ -44,7 +53,6 @@ struct Params {
   int64_t ps, rs, ops, ors;
   int32_t R, H, P, Dv;
   int32_t world, rank;
-  uint32_t epoch;
   char* bufs[kMaxWorld];    // every rank's exchange buffer, mapped here
   int32_t out_dtype;
   char* out;
@@ -53,14 +61,14 @@ struct Params {
   unsigned int* err;
 };
 
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+__device__ __forceinline__ uint64_t ld_relaxed_sys(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
 
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void st_relaxed_sys(uint64_t* p, uint64_t v) {
+  asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
 // One CTA (kWarps warps) per (b, h) row; lane l owns the DPL consecutive
@@ -71,15 +79,27 @@ __global__ void __launch_bounds__(kWarps * 32) kx_kernel(const __grid_constant__
   __shared__ float s_l[kWarps];
   __shared__ __align__(16) float s_o[kWarps][DPL * 32];
   __shared__ float s_row[257];
+  __shared__ float s_x[kMaxWorld][257];
+  __shared__ float s_w[kMaxWorld];
   __shared__ int s_ok;
+  __shared__ uint32_t s_epoch;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = blockIdx.x;
   const int Dv = p.Dv;
-  const size_t row_floats = (size_t)Dv + 1;
-  const size_t par_floats = (size_t)p.world * p.R * row_floats;
-  float* const data_own = reinterpret_cast<float*>(p.bufs[p.rank]);
-  uint32_t* const flags_own = reinterpret_cast<uint32_t*>(data_own + 2 * par_floats);
-  const int par = p.epoch & 1u;
+  const size_t row_words = (size_t)Dv + 1;
+  const size_t rank_words = (size_t)p.R * row_words;
+  const size_t par_words = (size_t)p.world * rank_words;
+  uint64_t* const data_own = reinterpret_cast<uint64_t*>(p.bufs[p.rank]);
+  uint32_t* const ctrl = reinterpret_cast<uint32_t*>(data_own + 2 * par_words);
+  grid_dep_wait();   // the partials' writer has finished (dependent launch)
+  if (threadIdx.x == 0) {
+    s_epoch = *reinterpret_cast<volatile uint32_t*>(ctrl) + 1u;
+    s_ok = 1;
+  }
+  __syncthreads();
+  const uint32_t epoch = s_epoch;
+  const int par = epoch & 1u;
+  const uint64_t tag = (uint64_t)epoch << 32;
 
   // ---- 1. local merge of this rank's P partials
   const float* mr = p.m_parts + (int64_t)row * p.rs;
@@ -111,72 +131,80 @@ __global__ void __launch_bounds__(kWarps * 32) kx_kernel(const __grid_constant__
   }
   __syncthreads();
 
-  // ---- 2. push the row into slot [rank][row] of every rank's buffer
+  // ---- 2. push the row into slot [rank][row] of every peer's buffer
   for (int j = 0; j < p.world; ++j) {
-    float* dst = reinterpret_cast<float*>(p.bufs[j]) + par * par_floats +
-                 ((size_t)p.rank * p.R + row) * row_floats;
-    for (int d = threadIdx.x; d <= Dv; d += blockDim.x) dst[d] = s_row[d];
-  }
-  __syncthreads();
-  if (threadIdx.x < p.world) {
-    __threadfence_system();
-    uint32_t* f = reinterpret_cast<uint32_t*>(reinterpret_cast<float*>(p.bufs[threadIdx.x]) +
-                                              2 * par_floats) +
-                  (size_t)p.rank * p.R + row;
-    st_release_sys(f, p.epoch);
+    if (j == p.rank) continue;
+    uint64_t* dst = reinterpret_cast<uint64_t*>(p.bufs[j]) + par * par_words +
+                    (size_t)p.rank * rank_words + (size_t)row * row_words;
+    for (int d = threadIdx.x; d <= Dv; d += blockDim.x)
+      st_relaxed_sys(dst + d, tag | __float_as_uint(s_row[d]));
   }
 
-  // ---- 3. wait (bounded) for every rank's row
-  if (threadIdx.x == 0) s_ok = 1;
-  __syncthreads();
-  if (threadIdx.x < p.world) {
-    const uint32_t* f = flags_own + (size_t)threadIdx.x * p.R + row;
-    bool ok = (int32_t)(ld_acquire_sys(f) - p.epoch) >= 0;
-    if (!ok) {
+  // ---- 3. collect every rank's row (bounded wait on the epoch tags)
+  const uint64_t* src = data_own + par * par_words + (size_t)row * row_words;
+  for (int i = threadIdx.x; i < p.world * (int)row_words; i += blockDim.x) {
+    const int j = i / (int)row_words, d = i - j * (int)row_words;
+    if (j == p.rank) {
+      s_x[j][d] = s_row[d];
+      continue;
+    }
+    const uint64_t* w = src + (size_t)j * rank_words + d;
+    uint64_t v = ld_relaxed_sys(w);
+    if ((uint32_t)(v >> 32) != epoch) {
       const uint64_t t0 = globaltimer_ns();
-      while (true) {
-        for (int i = 0; i < 64 && !ok; ++i) ok = (int32_t)(ld_acquire_sys(f) - p.epoch) >= 0;
-        if (ok) break;
-        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      bool ok = false;
+      while (!ok) {
+        for (int k = 0; k < 64 && !ok; ++k) {
+          v = ld_relaxed_sys(w);
+          ok = (uint32_t)(v >> 32) == epoch;
+        }
+        if (!ok && globaltimer_ns() - t0 > kWaitLimitNs) {
           set_device_error(p.err, static_cast<unsigned int>(-HALO_ERR_TIMEOUT));
           s_ok = 0;
           break;
         }
       }
+      if (!ok) break;
     }
+    s_x[j][d] = __uint_as_float((uint32_t)v);
   }
   __syncthreads();
-  if (!s_ok) return;
 
   // ---- 4. fold the world parts (lse-weighted) and write the output
-  const float* base = data_own + par * par_floats + (size_t)row * row_floats;
-  const size_t rank_stride = (size_t)p.R * row_floats;
-  float Mx = -INFINITY;
-  for (int j = 0; j < p.world; ++j) Mx = fmaxf(Mx, __ldcg(base + j * rank_stride + Dv));
-  float W = 0.f;
-  for (int j = 0; j < p.world; ++j) {
-    const float lj = __ldcg(base + j * rank_stride + Dv);
-    W += (lj == -INFINITY) ? 0.f : expf(lj - Mx);
-  }
-  const int b = row / p.H, h = row % p.H;
-  if (threadIdx.x == 0 && p.lse)
-    p.lse[row] = (W > 0.f) ? Mx + logf(W) : -INFINITY;
-  const float invW = (W > 0.f) ? 1.f / W : 0.f;
-  for (int d = threadIdx.x; d < Dv; d += blockDim.x) {
-    float v = 0.f;
-    for (int j = 0; j < p.world; ++j) {
-      const float lj = __ldcg(base + j * rank_stride + Dv);
-      if (lj == -INFINITY) continue;
-      v = fmaf(__ldcg(base + j * rank_stride + d), expf(lj - Mx), v);
+  if (s_ok) {
+    float Mx = -INFINITY;
+    for (int j = 0; j < p.world; ++j) Mx = fmaxf(Mx, s_x[j][Dv]);
+    if (threadIdx.x < p.world) {
+      const float lj = s_x[threadIdx.x][Dv];
+      s_w[threadIdx.x] = (lj == -INFINITY) ? 0.f : expf(lj - Mx);
     }
-    v *= invW;
-    const int64_t off = (int64_t)b * p.out_sb + (int64_t)h * p.out_sh + d;
-    if (p.out_dtype == HALO_DTYPE_F32)
-      reinterpret_cast<float*>(p.out)[off] = v;
-    else if (p.out_dtype == HALO_DTYPE_BF16)
-      reinterpret_cast<__nv_bfloat16*>(p.out)[off] = __float2bfloat16_rn(v);
-    else
-      reinterpret_cast<__half*>(p.out)[off] = __float2half_rn(v);
+    __syncthreads();
+    float W = 0.f;
+    for (int j = 0; j < p.world; ++j) W += s_w[j];
+    const int b = row / p.H, h = row % p.H;
+    if (threadIdx.x == 0 && p.lse) p.lse[row] = (W > 0.f) ? Mx + logf(W) : -INFINITY;
+    const float invW = (W > 0.f) ? 1.f / W : 0.f;
+    for (int d = threadIdx.x; d < Dv; d += blockDim.x) {
+      float v = 0.f;
+      for (int j = 0; j < p.world; ++j)
+        if (s_w[j] != 0.f) v = fmaf(s_x[j][d], s_w[j], v);
+      v *= invW;
+      const int64_t off = (int64_t)b * p.out_sb + (int64_t)h * p.out_sh + d;
+      if (p.out_dtype == HALO_DTYPE_F32)
+        reinterpret_cast<float*>(p.out)[off] = v;
+      else if (p.out_dtype == HALO_DTYPE_BF16)
+        reinterpret_cast<__nv_bfloat16*>(p.out)[off] = __float2bfloat16_rn(v);
+      else
+        reinterpret_cast<__half*>(p.out)[off] = __float2half_rn(v);
+    }
+  }
+  // the last CTA of the call publishes its epoch for the next call
+  if (threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(ctrl + 1, 1u) == (uint32_t)p.R - 1) {
+      ctrl[1] = 0;
+      *reinterpret_cast<volatile uint32_t*>(ctrl) = epoch;
+    }
   }
 }
 
@@ -189,8 +217,7 @@ extern "C" int64_t halo_exchange_bytes(int32_t world, int32_t rows, int32_t Dv) 
   if (world <= 0 || world > exchange::kMaxWorld || rows <= 0 || Dv <= 0 || Dv > 256)
     return fail(HALO_ERR_INVALID_ARG, "bad exchange shape (world %d, rows %d, Dv %d)", world,
                 rows, Dv);
-  const int64_t data = 2LL * world * rows * (Dv + 1) * 4;
-  return data + (int64_t)world * rows * 4;
+  return 2LL * world * rows * (Dv + 1) * 8 + 16;   // tagged words + control words
 }
 
 extern "C" int32_t halo_ipc_alloc(int64_t bytes, void** dev_ptr, void* handle_out) {
@@ -237,7 +264,7 @@ extern "C" int32_t halo_sharded_merge(int32_t B, int32_t H, int32_t Dv, int32_t 
                                       const float* o_parts, int64_t part_stride,
                                       int64_t row_stride, int64_t o_part_stride,
                                       int64_t o_row_stride, int32_t world, int32_t rank,
-                                      uint32_t epoch, void* const* bufs, int32_t out_dtype,
+                                      void* const* bufs, int32_t out_dtype,
                                       void* out, int64_t out_stride_b, int64_t out_stride_h,
                                       float* lse, halo_stream_t stream) {
   if (B <= 0 || H <= 0 || P < 0 || Dv <= 0 || Dv > 256)
@@ -262,7 +289,6 @@ extern "C" int32_t halo_sharded_merge(int32_t B, int32_t H, int32_t Dv, int32_t 
   prm.Dv = Dv;
   prm.world = world;
   prm.rank = rank;
-  prm.epoch = epoch;
   for (int j = 0; j < world; ++j) {
     if (!bufs[j]) return fail(HALO_ERR_INVALID_ARG, "exchange buffer %d is NULL", j);
     prm.bufs[j] = static_cast<char*>(bufs[j]);
@@ -277,12 +303,15 @@ extern "C" int32_t halo_sharded_merge(int32_t B, int32_t H, int32_t Dv, int32_t 
   const dim3 grid(prm.R), block(exchange::kWarps * 32);
   const bool vec = (reinterpret_cast<uintptr_t>(o_parts) & 15) == 0 && o_part_stride % 4 == 0 &&
                    o_row_stride % 4 == 0;
-  if (Dv <= 32) exchange::kx_kernel<1, false><<<grid, block, 0, st>>>(prm);
-  else if (Dv <= 64) exchange::kx_kernel<2, false><<<grid, block, 0, st>>>(prm);
-  else if (Dv <= 128 && Dv % 4 == 0 && vec) exchange::kx_kernel<4, true><<<grid, block, 0, st>>>(prm);
-  else if (Dv <= 128) exchange::kx_kernel<4, false><<<grid, block, 0, st>>>(prm);
-  else exchange::kx_kernel<8, false><<<grid, block, 0, st>>>(prm);
-  cudaError_t e = cudaGetLastError();
+  // a dependent launch: scheduled while the split-KV kernel's last CTAs run
+  cudaError_t e;
+  if (Dv <= 32) e = launch_dependent(exchange::kx_kernel<1, false>, grid, block, 0, st, prm);
+  else if (Dv <= 64) e = launch_dependent(exchange::kx_kernel<2, false>, grid, block, 0, st, prm);
+  else if (Dv <= 128 && Dv % 4 == 0 && vec)
+    e = launch_dependent(exchange::kx_kernel<4, true>, grid, block, 0, st, prm);
+  else if (Dv <= 128) e = launch_dependent(exchange::kx_kernel<4, false>, grid, block, 0, st, prm);
+  else e = launch_dependent(exchange::kx_kernel<8, false>, grid, block, 0, st, prm);
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "kx_kernel launch");
   count_launches(1);
   return HALO_OK;

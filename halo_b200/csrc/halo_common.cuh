@@ -40,6 +40,41 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 // Wall-clock limit of every bounded wait (nanoseconds).
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
 
+// Named CTA barrier `id` (1..15) over `threads` threads (a multiple of 32).
+__device__ __forceinline__ void named_bar_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// ---------------------------------------------------------------- programmatic dependent launch
+// A kernel launched with launch_dependent() may be scheduled before the
+// kernel ahead of it in the stream has finished (once every CTA of that
+// kernel has called grid_dep_trigger() or exited); it must call
+// grid_dep_wait() before touching anything the earlier kernel writes, which
+// returns once that kernel has completed and its memory is visible.  For a
+// kernel launched normally grid_dep_wait() returns at once.
+__device__ __forceinline__ void grid_dep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void grid_dep_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_dependent(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                                    cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<Args&&>(args)...);
+}
+
 // ---------------------------------------------------------------- mbarrier
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));

@@ -17,7 +17,9 @@ from halo_b200 import _lib as L
 
 
 class _Workspaces:
-    """Grow-only device scratch per (device, stream); stream-ordered reuse."""
+    """Grow-only device scratch per (device, stream); stream-ordered reuse.
+    Allocated zeroed: the decode workspaces start with a control block that
+    must be zero before first use (the kernels leave it zero)."""
 
     def __init__(self):
         self._bufs: dict = {}
@@ -26,7 +28,7 @@ class _Workspaces:
         key = (device.index, torch.cuda.current_stream(device).cuda_stream)
         buf = self._bufs.get(key)
         if buf is None or buf.numel() < nbytes:
-            buf = torch.empty(max(nbytes, 1 << 16), dtype=torch.uint8, device=device)
+            buf = torch.zeros(max(nbytes, 1 << 16), dtype=torch.uint8, device=device)
             self._bufs[key] = buf
         return buf
 

@@ -87,7 +87,6 @@ class P2PExchange:
             ptrs.append(p.value)
             self._opened.append(p.value)
         self.bufs = (ctypes.c_void_p * self.world)(*ptrs)
-        self.epoch = 0
         torch.cuda.synchronize()
         dist.barrier(group)
 
@@ -178,16 +177,39 @@ class ShardedDecoder:
         if out is None:
             out = torch.empty(B, H, D_v, dtype=q3.dtype, device=q3.device)
         x = self._x
-        x.epoch += 1
         base = ws.data_ptr()
         with torch.cuda.device(q3.device):
             rc = L.lib().halo_sharded_merge(
                 B, H, D_v, S, base + mo, base + lo, base + oo, 1, S, D_v, S * D_v, x.world,
-                x.rank, x.epoch & 0xFFFFFFFF, x.bufs, L.halo_dtype(out.dtype), out.data_ptr(),
+                x.rank, x.bufs, L.halo_dtype(out.dtype), out.data_ptr(),
                 out.stride(0), out.stride(1), lse.data_ptr() if lse is not None else None,
                 L.stream_handle(q3.device))
         L.check(rc, "halo_sharded_merge")
         return out, lse
+
+    def capture(self, q: torch.Tensor, *, out: torch.Tensor, lse: Optional[torch.Tensor] = None,
+                scale: Optional[float] = None) -> "torch.cuda.CUDAGraph":
+        """Capture one call on the fixed buffers ``q``/``out``/``lse`` in a
+        CUDA graph; ``graph.replay()`` reruns the decode on whatever ``q``
+        holds, with no host work per step beyond the graph launch.  Makes
+        one eager call first (plans, workspace, exchange buffers), so every
+        rank must capture at the same point of its call sequence.  The
+        cross-GPU exchange counts its epochs on the device, so replays stay
+        in step across ranks.  ``exchange="nccl"`` is not captured (its
+        collective runs through ``torch.distributed``)."""
+        if self.world > 1 and self.exchange != "p2p":
+            raise ValueError("capture() needs exchange='p2p' when sharded")
+        # the eager call runs on the capture stream so the stream's workspace
+        # exists (zeroed) before capture
+        side = torch.cuda.Stream(q.device)
+        side.wait_stream(torch.cuda.current_stream(q.device))
+        with torch.cuda.stream(side):
+            self(q, out=out, lse=lse, scale=scale)
+        torch.cuda.synchronize(q.device)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=side):
+            self(q, out=out, lse=lse, scale=scale)
+        return graph
 
     def close(self) -> None:
         """Release the peer mappings (collective-free; call on every rank)."""

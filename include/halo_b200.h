@@ -10,7 +10,11 @@
  *    ELEMENTS; the innermost (head_dim) dimension is always contiguous.
  *  - All work is enqueued on the given stream; nothing synchronises the host.
  *  - The library allocates no device memory: callers pass workspaces sized by
- *    the matching *_workspace_bytes() query.
+ *    the matching *_workspace_bytes() query.  A decode workspace starts with
+ *    a 4096-byte control block (the dynamic schedule's counters) that must
+ *    be zero before the workspace's first use; every call leaves it zero, so
+ *    zero a workspace once when allocating it and reuse it freely (one call
+ *    in flight per workspace).
  *  - Kernels never wait without a limit: a wait that exceeds ~2 s records
  *    HALO_ERR_TIMEOUT in the per-device error word (halo_device_error) and
  *    the kernel returns.
@@ -108,7 +112,8 @@ typedef struct halo_merge_args {
 /* ------------------------------------------------------------------ decode */
 
 /* Bytes of device workspace halo_chunked_decode needs for this problem and
- * chunk list (partial (m, l, o) per split).  Returns < 0 on invalid input. */
+ * chunk list: the zeroed control block, then the partial (m, l, o) per
+ * split.  Returns < 0 on invalid input. */
 int64_t halo_decode_workspace_bytes(const halo_decode_problem_t* problem,
                                     const halo_kv_chunk_t* chunks, int32_t n_chunks);
 
@@ -167,8 +172,10 @@ int32_t halo_chunked_decode_partials(const halo_decode_problem_t* problem,
 /* ------------------------------------------------------- multi-GPU merge */
 
 /* Bytes of one rank's exchange buffer for `world` ranks, `rows` = B*H output
- * rows of Dv values: data[2][world][rows][Dv + 1] fp32 then
- * flags[world][rows] uint32. */
+ * rows of Dv values: data[2][world][rows][Dv + 1] fp32, flags[world][rows]
+ * uint32, then 16 bytes of control words (the buffer's call epoch).  The
+ * buffer must start zeroed (halo_ipc_alloc does) and serves one sequence
+ * of calls with one (world, rows, Dv). */
 int64_t halo_exchange_bytes(int32_t world, int32_t rows, int32_t Dv);
 
 /* Exchange buffers shared across the processes of one node: halo_ipc_alloc
@@ -185,17 +192,18 @@ int32_t halo_ipc_free(void* dev_ptr);
  * merge this rank's P local partials (layout as halo_lse_merge), write the
  * normalised (o, lse) row into slot `rank` of every rank's exchange buffer
  * (bufs[j] = rank j's buffer mapped in this process, bufs[rank] its own)
- * through NVLink peer stores, publish a per-row flag = epoch, wait for the
- * rows of all ranks (bounded: HALO_ERR_TIMEOUT in the device error word
- * after 2 s), and write the merged out (B, H, Dv) in out_dtype and lse
- * (B, H) (optional).  Every rank calls it with the same epoch, starting at
- * 1 and increasing by one per call.  Replaces, for the sharded decode, the
- * local merge + all-gather + merge of (o, lse); the reference
+ * through NVLink peer stores, publish a per-row flag = the call's epoch,
+ * wait for the rows of all ranks (bounded: HALO_ERR_TIMEOUT in the device
+ * error word after 2 s), and write the merged out (B, H, Dv) in out_dtype
+ * and lse (B, H) (optional).  Every rank makes the same sequence of calls;
+ * the epoch is counted on the device in the rank's own buffer, so the call
+ * can be captured in a CUDA graph and replayed.  Replaces, for the sharded
+ * decode, the local merge + all-gather + merge of (o, lse); the reference
  * (halo/kv_cache_chunked.py:194-239, single GPU) has no counterpart. */
 int32_t halo_sharded_merge(int32_t B, int32_t H, int32_t Dv, int32_t P, const float* m_parts,
                            const float* l_parts, const float* o_parts, int64_t part_stride,
                            int64_t row_stride, int64_t o_part_stride, int64_t o_row_stride,
-                           int32_t world, int32_t rank, uint32_t epoch, void* const* bufs,
+                           int32_t world, int32_t rank, void* const* bufs,
                            int32_t out_dtype, void* out, int64_t out_stride_b,
                            int64_t out_stride_h, float* lse, halo_stream_t stream);
 

@@ -245,11 +245,65 @@ def test_large_context_properties(cuda_device):
     v2 = (v.float() * 2).bfloat16()     # exact doubling
     ch2 = [(k[..., a:b, :], v2[..., a:b, :], a, False) for a, b in _bounds(T, chunk)]
     o3, l3 = ops.chunked_decode(q, ch2, out_dtype=torch.float32)
-    assert (o3 - 2 * o1).abs().max().item() <= 1e-5 and torch.equal(l3, l1)
+    # the default (dynamic) schedule may fold the keys in a different order
+    # from call to call: equal up to fp32 rounding
+    assert (o3 - 2 * o1).abs().max().item() <= 1e-5 and (l3 - l1).abs().max().item() <= 1e-6
+    # the static split (max_split_rows > 0) is deterministic: bit-identical
+    s1 = ops.chunked_decode(q, ch, out_dtype=torch.float32, max_split_rows=4096)
+    s3 = ops.chunked_decode(q, ch2, out_dtype=torch.float32, max_split_rows=4096)
+    assert torch.equal(s3[1], s1[1]) and torch.equal(s3[0], 2 * s1[0])
+    assert (s1[0] - o1).abs().max().item() <= 1e-5
     # spot-check one kv-head group against the fp64 oracle
     ro, rl = OA.full_attention_f64(q[:, :8].cpu(), k[:, :1].cpu(), v[:, :1].cpu())
     assert (o1[:, :8].cpu().double() - ro[:, :, 0]).abs().max().item() <= OUT_TOL_16
     assert (l1[:, :8].cpu().double() - rl[:, :, 0]).abs().max().item() <= LSE_TOL
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("layout", ["contiguous", "causal", "scattered"])
+def test_decode_dynamic_schedule(cuda_device, dtype, layout):
+    """Contexts long enough for the dynamic schedule (pieces taken at run
+    time by groups of CTAs per kv-head): parity with the oracle and with the
+    static split, per-batch causal positions, chunks from separate buffers
+    (one segment each), repeated calls (the counters are reset by the
+    kernel), and the workspace control block left zero."""
+    ops = _ops()
+    from halo_b200 import _lib as L
+    g = torch.Generator().manual_seed(77)
+    B, H, H_kv, D, T, chunk = 2, 64, 8, 128, 32768, 4096
+    q = torch.randn(B, H, 1, D, generator=g).to(dtype)
+    k = torch.randn(B, H_kv, T, D, generator=g)
+    k[..., torch.randperm(D, generator=g)[:4]] *= 10
+    k, v = k.to(dtype), torch.randn(B, H_kv, T, D, generator=g).to(dtype)
+    dev = cuda_device
+    causal = layout != "contiguous"
+    if layout == "scattered":   # every chunk its own allocation
+        ch = [(k[..., a:b, :].to(dev).contiguous(), v[..., a:b, :].to(dev).contiguous(), a, True)
+              for a, b in _bounds(T, chunk)]
+    else:
+        ch = _gpu_chunks(k, v, _bounds(T, chunk), causal=causal, dev=dev)
+    q_pos = torch.tensor([T - 1, 20000], device=dev) if causal else None
+    qd = q.to(dev)
+    outs = [ops.chunked_decode(qd, ch, q_pos=q_pos, out_dtype=torch.float32) for _ in range(3)]
+    st = ops.chunked_decode(qd, ch, q_pos=q_pos, out_dtype=torch.float32, max_split_rows=2048)
+    G = H // H_kv
+    for b in range(B):
+        qp = (T - 1 if b == 0 else 20000) if causal else None
+        for hk in range(H_kv):      # one kv-head group at a time (oracle memory)
+            hs = slice(hk * G, (hk + 1) * G)
+            ro, rl = OA.full_attention_f64(q[b:b + 1, hs], k[b:b + 1, hk:hk + 1],
+                                           v[b:b + 1, hk:hk + 1], q_pos=qp)
+            for out, lse in outs + [st]:
+                assert (out[b:b + 1, hs].cpu().double() - ro[:, :, 0]).abs().max().item() \
+                    <= OUT_TOL_16
+                assert (lse[b:b + 1, hs].cpu().double() - rl[:, :, 0]).abs().max().item() \
+                    <= LSE_TOL
+    for out, lse in outs:
+        assert (out - st[0]).abs().max().item() <= 1e-5
+    ws = ops.WORKSPACES.get(torch.device(dev), 4096)
+    torch.cuda.synchronize()
+    assert torch.count_nonzero(ws[:4096]).item() == 0
+    assert L.device_error() == 0
 
 
 def test_device_error_word_clear(cuda_device):

@@ -66,7 +66,7 @@ def test_noalloc_matches_workspace_entry_point_twice(cuda_device):
         prob = _problem(L, q, H_kv, q_pos, 1.0 / math.sqrt(D))
         need = lib.halo_decode_workspace_bytes(ctypes.byref(prob), arr, n)
         assert need > 0
-        ws = torch.empty(need, dtype=torch.uint8, device=dev)
+        ws = torch.zeros(need, dtype=torch.uint8, device=dev)   # control block zeroed
         out_ref = torch.empty(B, H, D, dtype=torch.float32, device=dev)
         lse_ref = torch.empty(B, H, dtype=torch.float32, device=dev)
         L.check(lib.halo_chunked_decode(ctypes.byref(prob), arr, n, ws.data_ptr(), need,
