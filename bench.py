@@ -290,13 +290,10 @@ def run_ours_cfg5(args):
         dec(q, out=out, lse=lse)
     torch.cuda.synchronize()
 
-    # ---- device throughput: K steps; kd kernel bracketed per step by events
+    # ---- device throughput: K steps, events only around the whole loop (an
+    # event between the split-KV kernel and its dependent merge would cancel
+    # the merge's early launch)
     K = args.steps
-    ev_b = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
-    ev_e = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
-    for e in ev_b + ev_e:          # materialise the raw events
-        e.record()
-    torch.cuda.synchronize()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     torch.cuda.synchronize()
@@ -304,12 +301,25 @@ def run_ours_cfg5(args):
     with ClockSampler(local) as clocks:
         t0.record()
         for i in range(K):
-            dec(q, out=out, lse=lse, events=(ev_b[i].cuda_event, ev_e[i].cuda_event))
+            dec(q, out=out, lse=lse)
         t1.record()
         torch.cuda.synchronize()
     launches = L.launch_count() - n0
     barrier()
     ms = t0.elapsed_time(t1)
+    # ---- roofline pass: the same K steps with the split-KV kernel bracketed
+    # by events on its stream
+    ev_b = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    ev_e = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    for e in ev_b + ev_e:          # materialise the raw events
+        e.record()
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks_kd:
+        for i in range(K):
+            dec(q, out=out, lse=lse, events=(ev_b[i].cuda_event, ev_e[i].cuda_event))
+        torch.cuda.synchronize()
+    barrier()
     kd_ms = sum(ev_b[i].elapsed_time(ev_e[i]) for i in range(K)) / K
     ms_t = torch.tensor([ms, kd_ms], device=dev)
     if world > 1:
@@ -352,7 +362,9 @@ def run_ours_cfg5(args):
         cpu = cpu_baseline_cfg5() if world == 1 and not args.no_cpu_baseline else None
         roof = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                 "frac": achieved / peak, "peak_kind": f"of {peak_kind}",
-                "kernel": "kd_kernel (split-KV decode)",
+                "kernel": "kd_dyn_kernel (split-KV decode, dynamic schedule)",
+                "timing": "second pass of K steps with events around the split-KV kernel",
+                "clocks_kd_pass": clocks_kd.summary(),
                 "bytes_per_launch": local_bytes,
                 "traffic": (local_bytes * NCU_TRAFFIC_RATIO) if NCU_TRAFFIC_RATIO else None,
                 "step_gbs": 2 * CFG5["B"] * CFG5["H_kv"] * CFG5["T"] * CFG5["D"] * 2
@@ -663,21 +675,28 @@ def run_ours_cfg4(args):
     for _ in range(args.warmup):
         cache.compute_attention(q, layer_idx=0)
     K = args.steps
+    # device throughput: events only around the loop (the merge kernel is a
+    # dependent launch; an event in between would cancel its early launch)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    n0 = L.launch_count()
+    with ClockSampler(0) as clocks:
+        t0.record()
+        for i in range(K):
+            cache.compute_attention(q, layer_idx=0)
+        t1.record()
+        torch.cuda.synchronize()
+    launches = L.launch_count() - n0
+    ms_step = t0.elapsed_time(t1) / K
+    # roofline pass: the same K steps with events around the fused kernel
     ev_b = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
     ev_e = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
     for e in ev_b + ev_e:
         e.record()
     torch.cuda.synchronize()
-    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    n0 = L.launch_count()
-    with ClockSampler(0) as clocks:
-        t0.record()
-        for i in range(K):
-            cache.compute_attention(q, layer_idx=0, events=(ev_b[i].cuda_event, ev_e[i].cuda_event))
-        t1.record()
-        torch.cuda.synchronize()
-    launches = L.launch_count() - n0
-    ms_step = t0.elapsed_time(t1) / K
+    for i in range(K):
+        cache.compute_attention(q, layer_idx=0, events=(ev_b[i].cuda_event, ev_e[i].cuda_event))
+    torch.cuda.synchronize()
     kk_ms = sum(ev_b[i].elapsed_time(ev_e[i]) for i in range(K)) / K
 
     q_host = q.cpu().pin_memory()

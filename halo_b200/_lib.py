@@ -169,6 +169,11 @@ SIGNATURES = {
                                             ctypes.POINTER(ctypes.c_void_p), ctypes.c_int32,
                                             ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
                                             ctypes.c_void_p, ctypes.c_void_p]),
+    "halo_sharded_decode": (ctypes.c_int32, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32,
+                                             ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32,
+                                             ctypes.c_int32, ctypes.POINTER(ctypes.c_void_p),
+                                             ctypes.c_int32, ctypes.c_void_p, ctypes.c_int64,
+                                             ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p]),
     "halo_version": (ctypes.c_int32, []),
     "halo_launch_count": (ctypes.c_uint64, []),
 }

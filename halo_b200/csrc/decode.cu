@@ -2042,6 +2042,36 @@ extern "C" int32_t halo_chunked_decode(const halo_decode_problem_t* problem,
   return launch_merge(mp, st);
 }
 
+extern "C" int32_t halo_sharded_merge(int32_t B, int32_t H, int32_t Dv, int32_t P,
+                                      const float* m_parts, const float* l_parts,
+                                      const float* o_parts, int64_t part_stride,
+                                      int64_t row_stride, int64_t o_part_stride,
+                                      int64_t o_row_stride, int32_t world, int32_t rank,
+                                      void* const* bufs, int32_t out_dtype, void* out,
+                                      int64_t out_stride_b, int64_t out_stride_h, float* lse,
+                                      halo_stream_t stream);
+
+// The split-KV launch, then the fused cross-GPU merge (kx_kernel, launched
+// as a dependent so it is scheduled while the split-KV kernel drains).
+extern "C" int32_t halo_sharded_decode(const halo_decode_problem_t* problem,
+                                       const halo_kv_chunk_t* chunks, int32_t n_chunks,
+                                       void* workspace, int64_t workspace_bytes, int32_t world,
+                                       int32_t rank, void* const* bufs, int32_t out_dtype,
+                                       void* out, int64_t out_stride_b, int64_t out_stride_h,
+                                       float* lse, halo_stream_t stream) {
+  int rc = validate_problem(problem, chunks, n_chunks);
+  if (rc != HALO_OK) return rc;
+  int S = 0;
+  float *m_part = nullptr, *l_part = nullptr, *o_part = nullptr;
+  rc = decode_splits(problem, chunks, n_chunks, workspace, workspace_bytes,
+                     static_cast<cudaStream_t>(stream), &S, &m_part, &l_part, &o_part);
+  if (rc != HALO_OK) return rc;
+  const halo_decode_problem_t& pb = *problem;
+  return halo_sharded_merge(pb.B, pb.H, pb.Dv, S, m_part, l_part, o_part, 1, S, pb.Dv,
+                            (int64_t)S * pb.Dv, world, rank, bufs, out_dtype, out, out_stride_b,
+                            out_stride_h, lse, stream);
+}
+
 extern "C" int32_t halo_chunked_decode_partials(const halo_decode_problem_t* problem,
                                                 const halo_kv_chunk_t* chunks, int32_t n_chunks,
                                                 void* workspace, int64_t workspace_bytes,

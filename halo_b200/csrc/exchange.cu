@@ -19,7 +19,7 @@
 //
 // Exchange buffer (one per rank, allocated with halo_ipc_alloc, mapped on
 // every peer with halo_ipc_open), then control words only the owner touches:
-//   word[2][world][R][Dv + 1]   parity = epoch & 1; o then lse per row
+//   word[2][world][R][Dv + 2]   parity = epoch & 1; o, lse, pad per row
 //   ctrl[4]                     [0] epoch of the last completed call,
 //                               [1] CTAs of the running call that finished
 // The epoch lives on the device: each CTA reads ctrl[0] + 1 when it starts,
@@ -61,16 +61,6 @@ struct Params {
   unsigned int* err;
 };
 
-__device__ __forceinline__ uint64_t ld_relaxed_sys(const uint64_t* p) {
-  uint64_t v;
-  asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  return v;
-}
-
-__device__ __forceinline__ void st_relaxed_sys(uint64_t* p, uint64_t v) {
-  asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-
 // One CTA (kWarps warps) per (b, h) row; lane l owns the DPL consecutive
 // columns [l*DPL, l*DPL + DPL) of the local merge.
 template <int DPL, bool VEC>
@@ -86,7 +76,7 @@ __global__ void __launch_bounds__(kWarps * 32) kx_kernel(const __grid_constant__
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = blockIdx.x;
   const int Dv = p.Dv;
-  const size_t row_words = (size_t)Dv + 1;
+  const size_t row_words = (size_t)Dv + 2;   // o, lse, pad
   const size_t rank_words = (size_t)p.R * row_words;
   const size_t par_words = (size_t)p.world * rank_words;
   uint64_t* const data_own = reinterpret_cast<uint64_t*>(p.bufs[p.rank]);
@@ -142,8 +132,8 @@ __global__ void __launch_bounds__(kWarps * 32) kx_kernel(const __grid_constant__
 
   // ---- 3. collect every rank's row (bounded wait on the epoch tags)
   const uint64_t* src = data_own + par * par_words + (size_t)row * row_words;
-  for (int i = threadIdx.x; i < p.world * (int)row_words; i += blockDim.x) {
-    const int j = i / (int)row_words, d = i - j * (int)row_words;
+  for (int i = threadIdx.x; i < p.world * (Dv + 1); i += blockDim.x) {   // o and lse words
+    const int j = i / (Dv + 1), d = i - j * (Dv + 1);
     if (j == p.rank) {
       s_x[j][d] = s_row[d];
       continue;
@@ -217,7 +207,7 @@ extern "C" int64_t halo_exchange_bytes(int32_t world, int32_t rows, int32_t Dv) 
   if (world <= 0 || world > exchange::kMaxWorld || rows <= 0 || Dv <= 0 || Dv > 256)
     return fail(HALO_ERR_INVALID_ARG, "bad exchange shape (world %d, rows %d, Dv %d)", world,
                 rows, Dv);
-  return 2LL * world * rows * (Dv + 1) * 8 + 16;   // tagged words + control words
+  return 2LL * world * rows * (Dv + 2) * 8 + 16;   // tagged words + control words
 }
 
 extern "C" int32_t halo_ipc_alloc(int64_t bytes, void** dev_ptr, void* handle_out) {

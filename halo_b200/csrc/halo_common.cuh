@@ -40,6 +40,17 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 // Wall-clock limit of every bounded wait (nanoseconds).
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
 
+// System-scope relaxed 64-bit accesses (peer GPU memory through NVLink): an
+// aligned 64-bit access is single-copy atomic.
+__device__ __forceinline__ uint64_t ld_relaxed_sys(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_relaxed_sys(uint64_t* p, uint64_t v) {
+  asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
 // Named CTA barrier `id` (1..15) over `threads` threads (a multiple of 32).
 __device__ __forceinline__ void named_bar_sync(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");

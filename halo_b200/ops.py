@@ -177,6 +177,34 @@ def decode_partials(q3: torch.Tensor, table: ChunkTable, *, scale: float,
     return ws, int(n_parts.value), (int(offs[0]), int(offs[1]), int(offs[2]))
 
 
+def sharded_decode(q3: torch.Tensor, table: ChunkTable, exchange, *, scale: float,
+                   out: torch.Tensor, lse: Optional[torch.Tensor] = None,
+                   q_pos: Optional[torch.Tensor] = None, events: Optional[tuple] = None):
+    """One sequence-sharded decode step on this rank (``halo_sharded_decode``):
+    attention over this rank's chunks merged with every rank's through the
+    NVLink exchange buffers of ``exchange`` (a :class:`halo_b200.sharded.
+    P2PExchange`).  Writes ``out (B, H, D_v)`` and ``lse (B, H)``."""
+    dev = q3.device
+    H_kv = table.H_kv if table.H_kv is not None else q3.shape[1]
+    D_v = table.D_v if table.D_v is not None else q3.shape[2]
+    prob = _problem(q3, H_kv, D_v, q_pos, scale)
+    if events is not None:
+        prob.event_begin, prob.event_end = events
+    lib = L.lib()
+    need = lib.halo_decode_workspace_bytes(ctypes.byref(prob), table.arr, table.n)
+    if need < 0:
+        L.check(int(need), "halo_decode_workspace_bytes")
+    ws = WORKSPACES.get(dev, int(need))
+    with torch.cuda.device(dev):
+        rc = lib.halo_sharded_decode(ctypes.byref(prob), table.arr, table.n, ws.data_ptr(),
+                                     ws.numel(), exchange.world, exchange.rank, exchange.bufs,
+                                     L.halo_dtype(out.dtype), out.data_ptr(), out.stride(0),
+                                     out.stride(1), lse.data_ptr() if lse is not None else None,
+                                     L.stream_handle(dev))
+    L.check(rc, "halo_sharded_decode")
+    return out, lse
+
+
 def chunked_decode(q: torch.Tensor, chunks, *, scale: Optional[float] = None,
                    q_pos: Optional[torch.Tensor] = None, out_dtype: Optional[torch.dtype] = None,
                    out: Optional[torch.Tensor] = None, lse: Optional[torch.Tensor] = None,

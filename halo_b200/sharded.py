@@ -165,7 +165,6 @@ class ShardedDecoder:
         return ops.lse_merge(m_parts, None, o_parts, out=out, lse=lse, parts_major=True)
 
     def _p2p_call(self, q3, scale, out, lse, events):
-        from halo_b200 import _lib as L
         B, H, D = q3.shape
         D_v = self.table.D_v
         if self._x is None or self._x_key != (B, H, D_v):
@@ -173,19 +172,10 @@ class ShardedDecoder:
                 self._x.close()
             self._x = P2PExchange(B * H, D_v, self.group)
             self._x_key = (B, H, D_v)
-        ws, S, (mo, lo, oo) = ops.decode_partials(q3, self.table, scale=scale, events=events)
         if out is None:
             out = torch.empty(B, H, D_v, dtype=q3.dtype, device=q3.device)
-        x = self._x
-        base = ws.data_ptr()
-        with torch.cuda.device(q3.device):
-            rc = L.lib().halo_sharded_merge(
-                B, H, D_v, S, base + mo, base + lo, base + oo, 1, S, D_v, S * D_v, x.world,
-                x.rank, x.bufs, L.halo_dtype(out.dtype), out.data_ptr(),
-                out.stride(0), out.stride(1), lse.data_ptr() if lse is not None else None,
-                L.stream_handle(q3.device))
-        L.check(rc, "halo_sharded_merge")
-        return out, lse
+        return ops.sharded_decode(q3, self.table, self._x, scale=scale, out=out, lse=lse,
+                                  events=events)
 
     def capture(self, q: torch.Tensor, *, out: torch.Tensor, lse: Optional[torch.Tensor] = None,
                 scale: Optional[float] = None) -> "torch.cuda.CUDAGraph":
@@ -219,9 +209,11 @@ class ShardedDecoder:
 
     @property
     def launches_per_call(self) -> int:
-        """Kernels of this library per call: split-KV + local merge on one
-        GPU; split-KV + fused exchange merge (p2p) or split-KV + local merge +
-        merge of the gathered parts (nccl) when sharded."""
+        """Kernels of this library per call (at most): split-KV + merge on
+        one GPU, split-KV + exchange merge (p2p) or split-KV + local merge +
+        merge of the gathered parts (nccl) when sharded.  With the dynamic
+        schedule the split-KV kernel merges (and exchanges) itself: one
+        launch per call, counted by ``halo_launch_count``."""
         if self.world == 1:
             return 2
         return 2 if self.exchange == "p2p" else 3

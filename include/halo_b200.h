@@ -121,9 +121,13 @@ int64_t halo_decode_workspace_bytes(const halo_decode_problem_t* problem,
  * Replaces the per-chunk Triton launches of update_chunk
  * (halo/triton_chunked.py:151-192, kernel :47-138) and the torch loop of
  * _chunk_attention + _lse_merge (halo/kv_cache_chunked.py:194-276) with one
- * split-KV launch over every chunk plus one merge launch.  `chunks` is a
- * HOST array; K/V rows are staged through the async-copy engine, so every
- * row address must be 16-byte aligned. */
+ * split-KV launch over every chunk plus one merge launch (a programmatic
+ * dependent launch, scheduled while the split-KV kernel drains; recording
+ * an event between the two on the stream forfeits that overlap).  `chunks`
+ * is a HOST array; K/V rows are staged through the async-copy engine, so
+ * every row address must be 16-byte aligned.  The default schedule hands rows to CTAs at run time,
+ * so results can differ between calls in the last bits of fp32;
+ * max_split_rows > 0 selects a fixed split, bit-reproducible. */
 int32_t halo_chunked_decode(const halo_decode_problem_t* problem,
                             const halo_kv_chunk_t* chunks, int32_t n_chunks,
                             void* workspace, int64_t workspace_bytes,
@@ -172,8 +176,9 @@ int32_t halo_chunked_decode_partials(const halo_decode_problem_t* problem,
 /* ------------------------------------------------------- multi-GPU merge */
 
 /* Bytes of one rank's exchange buffer for `world` ranks, `rows` = B*H output
- * rows of Dv values: data[2][world][rows][Dv + 1] fp32, flags[world][rows]
- * uint32, then 16 bytes of control words (the buffer's call epoch).  The
+ * rows of Dv values: words[2][world][rows][Dv + 2] (64-bit: epoch tag and
+ * fp32 value; o, lse, pad per row), then 16 bytes of control words (the
+ * buffer's call epoch).  The
  * buffer must start zeroed (halo_ipc_alloc does) and serves one sequence
  * of calls with one (world, rows, Dv). */
 int64_t halo_exchange_bytes(int32_t world, int32_t rows, int32_t Dv);
@@ -206,6 +211,22 @@ int32_t halo_sharded_merge(int32_t B, int32_t H, int32_t Dv, int32_t P, const fl
                            int32_t world, int32_t rank, void* const* bufs,
                            int32_t out_dtype, void* out, int64_t out_stride_b,
                            int64_t out_stride_h, float* lse, halo_stream_t stream);
+
+/* One step of a sequence-sharded decode on this rank: attention of q over
+ * this rank's chunks, merged with every rank's result through the exchange
+ * buffers of halo_sharded_merge (same buffers, same call-sequence rule).
+ * Two launches: the split-KV kernel, then halo_sharded_merge's kernel as a
+ * programmatic dependent launch (scheduled while the first drains).
+ * Inputs as halo_chunked_decode (workspace sized by
+ * halo_decode_workspace_bytes, Dv == D); out (B, H, Dv) in out_dtype, lse
+ * (B, H) optional.  No reference counterpart (the reference is single-GPU;
+ * its merge identity is halo/kv_cache_chunked.py:194-239). */
+int32_t halo_sharded_decode(const halo_decode_problem_t* problem,
+                            const halo_kv_chunk_t* chunks, int32_t n_chunks, void* workspace,
+                            int64_t workspace_bytes, int32_t world, int32_t rank,
+                            void* const* bufs, int32_t out_dtype, void* out,
+                            int64_t out_stride_b, int64_t out_stride_h, float* lse,
+                            halo_stream_t stream);
 
 /* ------------------------------------------------------------------ KIVI */
 

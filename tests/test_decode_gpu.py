@@ -300,6 +300,17 @@ def test_decode_dynamic_schedule(cuda_device, dtype, layout):
                     <= LSE_TOL
     for out, lse in outs:
         assert (out - st[0]).abs().max().item() <= 1e-5
+    # ACCUMULATE over two halves (each long enough for the in-kernel merge)
+    # then a FINALIZE with that prior state equals the one-call result
+    m = torch.full((B, H), float("-inf"), device=dev)
+    l = torch.zeros(B, H, device=dev)
+    o = torch.zeros(B, H, D, device=dev)
+    half = len(ch) // 2
+    ops.accumulate_decode(qd, ch[:half], m, l, o, scale=1 / math.sqrt(D), q_pos=q_pos)
+    o2, l2 = ops.chunked_decode(qd, ch[half:], q_pos=q_pos, out_dtype=torch.float32,
+                                prior=(m, l, o))
+    assert (o2 - outs[0][0]).abs().max().item() <= 1e-5
+    assert (l2 - outs[0][1]).abs().max().item() <= 1e-5
     ws = ops.WORKSPACES.get(torch.device(dev), 4096)
     torch.cuda.synchronize()
     assert torch.count_nonzero(ws[:4096]).item() == 0
