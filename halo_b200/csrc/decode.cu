@@ -541,6 +541,10 @@ __global__ void __launch_bounds__(kThreads, MINB) kd_kernel(const __grid_constan
     fence_mbar_init();
   }
   __syncthreads();
+  // launched as a dependent of the previous kernel on the stream: the
+  // prologue above overlapped its tail; nothing it may have written (q,
+  // K/V, positions, the workspace) is touched before it has completed
+  grid_dep_wait();
   const int warp = tid >> 5, lane = tid & 31;
 
   if (warp == kConsumerWarps) {
@@ -661,6 +665,11 @@ __global__ void __launch_bounds__(kThreads, MINB)
     fence_mbar_init();
   }
   __syncthreads();
+  // launched as a dependent of the previous kernel on the stream: the
+  // prologue above overlapped its tail; nothing it may have written (q,
+  // K/V, positions, the workspace and its counters) is touched before it
+  // has completed
+  grid_dep_wait();
   const int warp = tid >> 5, lane = tid & 31;
   const int pair = (int)(blockIdx.x % (unsigned)p.n_pairs);
   const int member = (int)(blockIdx.x / (unsigned)p.n_pairs);
@@ -995,6 +1004,10 @@ __global__ void __launch_bounds__(kThreads, 2) kk_kernel(const __grid_constant__
     fence_mbar_init();
   }
   __syncthreads();
+  // launched as a dependent of the previous kernel on the stream: the
+  // prologue above overlapped its tail; nothing it may have written (q,
+  // K/V, positions, the workspace) is touched before it has completed
+  grid_dep_wait();
   const int warp = tid >> 5, lane = tid & 31;
 
   if (warp == kConsumerWarps) {
@@ -1071,55 +1084,44 @@ struct MergeParams {
 // every partial (and the prior state).  Pass 2: warp w folds partials
 // s = w, w + kMergeWarps, ... with weights exp(m_s - M), eight partials in
 // flight per lane; the warps' sums are then combined through shared memory.
-constexpr int kMergeWarps = 16;
+// Four warps and at most 88 registers a thread, so a CTA fits beside two
+// split-KV CTAs on an SM: launched as a dependent, the merge's CTAs are
+// resident (waiting) while the split-KV kernel drains.
+constexpr int kMergeWarps = 4;
 
 template <int DPL, bool VEC>
-__global__ void __launch_bounds__(kMergeWarps * 32) km_kernel(const MergeParams mp) {
-  __shared__ float s_red[kMergeWarps];
+__global__ void __maxnreg__(88) km_kernel(const MergeParams mp) {
+  __shared__ float s_m[kMergeWarps];
   __shared__ float s_l[kMergeWarps];
   __shared__ __align__(16) float s_o[kMergeWarps][DPL * 32];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int lane = threadIdx.x & 31;
   const int row = blockIdx.x;
-  grid_dep_wait();   // the partials' writer has finished (dependent launch)
+  grid_dep_trigger();   // the next split-KV launch may start its prologue
+  grid_dep_wait();      // the partials' writer has finished (dependent launch)
   const float* mr = mp.m_parts + (int64_t)row * mp.rs;
   const float* lr = mp.l_parts ? mp.l_parts + (int64_t)row * mp.rs : nullptr;
   const float* orow = mp.o_parts + (int64_t)row * mp.ors;
-  const bool have_prior = mp.m != nullptr;
-
-  // ---- pass 1: row max
-  float M = row_max<kMergeWarps>(mr, mp.ps, mp.P, s_red);
-  if (have_prior) M = fmaxf(M, mp.m[row]);
-
-  // ---- pass 2: weighted sums, this warp's share of the partials
   const int d0 = lane * DPL;
   const bool active = d0 < mp.Dv;
-  float L;
+  float M, L;
   float acc[DPL];
-  fold_partials<DPL, kMergeWarps, 8, VEC>(mr, lr, orow, mp.ps, mp.ops, mp.P, mp.Dv, M, L, acc);
-  if (lane == 0) s_l[warp] = L;
-#pragma unroll
-  for (int e = 0; e < DPL; ++e) s_o[warp][d0 + e] = acc[e];
-  __syncthreads();
-  if (warp != 0) return;
+  merge_partials<DPL, kMergeWarps, 10, VEC>(mr, lr, orow, mp.ps, mp.ops, mp.P, mp.Dv, s_m, s_l,
+                                            s_o, M, L, acc);
+  if (threadIdx.x >= 32) return;
 
-  // ---- warp 0: combine the warps (plus the prior state) and write
-  L = 0.f;
-#pragma unroll
-  for (int w = 0; w < kMergeWarps; ++w) L += s_l[w];
-#pragma unroll
-  for (int e = 0; e < DPL; ++e) {
-    float v = 0.f;
-#pragma unroll
-    for (int w = 0; w < kMergeWarps; ++w) v += s_o[w][d0 + e];
-    acc[e] = v;
-  }
-  if (have_prior && M != -INFINITY) {
+  // ---- warp 0: fold the prior state in and write
+  if (mp.m != nullptr) {
     const float mw = mp.m[row];
-    const float w = (mw == -INFINITY) ? 0.f : expf(mw - M);
-    L = fmaf(mp.l[row], w, L);
-    if (active)
+    const float Mn = fmaxf(M, mw);
+    if (Mn != -INFINITY) {
+      const float a = (M == -INFINITY) ? 0.f : expf(M - Mn);
+      const float w = (mw == -INFINITY) ? 0.f : expf(mw - Mn);
+      L = fmaf(mp.l[row], w, L * a);
 #pragma unroll
-      for (int e = 0; e < DPL; ++e) acc[e] = fmaf(mp.o[(int64_t)row * mp.Dv + d0 + e], w, acc[e]);
+      for (int e = 0; e < DPL; ++e)
+        acc[e] = active ? fmaf(mp.o[(int64_t)row * mp.Dv + d0 + e], w, acc[e] * a) : 0.f;
+      M = Mn;
+    }
   }
 
   if (mp.mode == HALO_MERGE_ACCUMULATE) {
@@ -1635,8 +1637,9 @@ static int launch_kd(const DecodeParams& prm, cudaStream_t st) {
   using Gm = Geom<T, D, C::kStages>;
   const int64_t grid_max = (int64_t)device_sms() * kd_ctas_per_sm<T, D>();
   const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(prm.n_units, grid_max));
-  kd_kernel<T, D, C::kStages, C::kMinBlocks><<<grid, kThreads, Gm::kSmemBytes, st>>>(prm);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_dependent(kd_kernel<T, D, C::kStages, C::kMinBlocks>, grid, kThreads,
+                                   Gm::kSmemBytes, st, prm);
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "kd_kernel launch");
   count_launches();
   return HALO_OK;
@@ -1704,8 +1707,9 @@ static int launch_kd_dyn(const P& prm, int grid, cudaStream_t st) {
   using C = KdConfig<T, D>;
   using DG = DynGeom<T, D, C::kStages>;
   kd_dyn_ctas_per_sm<T, D>();   // sets the shared-memory attributes once
-  kd_dyn_kernel<T, D, C::kStages, C::kMinBlocks, P><<<grid, kThreads, DG::kSmemBytes, st>>>(prm);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_dependent(kd_dyn_kernel<T, D, C::kStages, C::kMinBlocks, P>, grid,
+                                   kThreads, DG::kSmemBytes, st, prm);
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "kd_dyn_kernel launch");
   count_launches();
   return HALO_OK;
@@ -1831,8 +1835,8 @@ static int launch_kk(const KiviParams& prm, cudaStream_t st) {
   using KG = KGeom<T, D, BITS>;
   const int64_t grid_max = (int64_t)device_sms() * kk_ctas_per_sm<T, D, BITS>();
   const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(prm.n_units, grid_max));
-  kk_kernel<T, D, BITS><<<grid, kThreads, KG::kSmemBytes, st>>>(prm);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_dependent(kk_kernel<T, D, BITS>, grid, kThreads, KG::kSmemBytes, st, prm);
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "kk_kernel launch");
   count_launches();
   return HALO_OK;

@@ -44,7 +44,11 @@ void count_launches(int n);
 namespace exchange {
 
 constexpr int kMaxWorld = 8;
-constexpr int kWarps = 16;
+// Four warps and at most 88 registers a thread, so a CTA fits beside two
+// split-KV CTAs on an SM: launched as a dependent, the merge's CTAs are
+// resident (waiting) while the split-KV kernel drains and start the moment
+// it completes.
+constexpr int kWarps = 4;
 
 struct Params {
   const float* m_parts;     // local split partials (as halo_lse_merge)
@@ -64,13 +68,13 @@ struct Params {
 // One CTA (kWarps warps) per (b, h) row; lane l owns the DPL consecutive
 // columns [l*DPL, l*DPL + DPL) of the local merge.
 template <int DPL, bool VEC>
-__global__ void __launch_bounds__(kWarps * 32) kx_kernel(const __grid_constant__ Params p) {
+__global__ void __maxnreg__(88) kx_kernel(const __grid_constant__ Params p) {
   __shared__ float s_red[kWarps];
   __shared__ float s_l[kWarps];
   __shared__ __align__(16) float s_o[kWarps][DPL * 32];
   __shared__ float s_row[257];
-  __shared__ float s_x[kMaxWorld][257];
   __shared__ float s_w[kMaxWorld];
+  extern __shared__ float s_x[];   // [world][Dv + 1]
   __shared__ int s_ok;
   __shared__ uint32_t s_epoch;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -81,7 +85,8 @@ __global__ void __launch_bounds__(kWarps * 32) kx_kernel(const __grid_constant__
   const size_t par_words = (size_t)p.world * rank_words;
   uint64_t* const data_own = reinterpret_cast<uint64_t*>(p.bufs[p.rank]);
   uint32_t* const ctrl = reinterpret_cast<uint32_t*>(data_own + 2 * par_words);
-  grid_dep_wait();   // the partials' writer has finished (dependent launch)
+  grid_dep_trigger();   // the next split-KV launch may start its prologue
+  grid_dep_wait();      // the partials' writer has finished (dependent launch)
   if (threadIdx.x == 0) {
     s_epoch = *reinterpret_cast<volatile uint32_t*>(ctrl) + 1u;
     s_ok = 1;
@@ -91,33 +96,21 @@ __global__ void __launch_bounds__(kWarps * 32) kx_kernel(const __grid_constant__
   const int par = epoch & 1u;
   const uint64_t tag = (uint64_t)epoch << 32;
 
-  // ---- 1. local merge of this rank's P partials
+  // ---- 1. local merge of this rank's P partials (one round trip when
+  // P <= 40), normalised into s_row: o then lse
   const float* mr = p.m_parts + (int64_t)row * p.rs;
   const float* lr = p.l_parts ? p.l_parts + (int64_t)row * p.rs : nullptr;
   const float* orow = p.o_parts + (int64_t)row * p.ors;
-  const float M = row_max<kWarps>(mr, p.ps, p.P, s_red);
-  float L;
+  float M, L;
   float acc[DPL];
-  fold_partials<DPL, kWarps, 8, VEC>(mr, lr, orow, p.ps, p.ops, p.P, Dv, M, L, acc);
-  if (lane == 0) s_l[warp] = L;
-  const int d0 = lane * DPL;
+  merge_partials<DPL, kWarps, 10, VEC>(mr, lr, orow, p.ps, p.ops, p.P, Dv, s_red, s_l, s_o, M, L,
+                                       acc);
+  if (warp == 0) {
+    const int d0 = lane * DPL;
 #pragma unroll
-  for (int e = 0; e < DPL; ++e) s_o[warp][d0 + e] = acc[e];
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    float t = 0.f;
-#pragma unroll
-    for (int w = 0; w < kWarps; ++w) t += s_l[w];
-    s_row[Dv] = (t > 0.f) ? M + logf(t) : -INFINITY;   // lse of the local part
-    s_red[0] = t;
-  }
-  __syncthreads();
-  const float Lloc = s_red[0];
-  for (int d = threadIdx.x; d < Dv; d += blockDim.x) {
-    float v = 0.f;
-#pragma unroll
-    for (int w = 0; w < kWarps; ++w) v += s_o[w][d];
-    s_row[d] = (Lloc > 0.f) ? v / Lloc : 0.f;          // normalised local output
+    for (int e = 0; e < DPL; ++e)
+      if (d0 + e < Dv) s_row[d0 + e] = (L > 0.f) ? acc[e] / L : 0.f;   // normalised local output
+    if (lane == 0) s_row[Dv] = (L > 0.f) ? M + logf(L) : -INFINITY;     // lse of the local part
   }
   __syncthreads();
 
@@ -135,7 +128,7 @@ __global__ void __launch_bounds__(kWarps * 32) kx_kernel(const __grid_constant__
   for (int i = threadIdx.x; i < p.world * (Dv + 1); i += blockDim.x) {   // o and lse words
     const int j = i / (Dv + 1), d = i - j * (Dv + 1);
     if (j == p.rank) {
-      s_x[j][d] = s_row[d];
+      s_x[j * (Dv + 1) + d] = s_row[d];
       continue;
     }
     const uint64_t* w = src + (size_t)j * rank_words + d;
@@ -156,16 +149,16 @@ __global__ void __launch_bounds__(kWarps * 32) kx_kernel(const __grid_constant__
       }
       if (!ok) break;
     }
-    s_x[j][d] = __uint_as_float((uint32_t)v);
+    s_x[j * (Dv + 1) + d] = __uint_as_float((uint32_t)v);
   }
   __syncthreads();
 
   // ---- 4. fold the world parts (lse-weighted) and write the output
   if (s_ok) {
     float Mx = -INFINITY;
-    for (int j = 0; j < p.world; ++j) Mx = fmaxf(Mx, s_x[j][Dv]);
+    for (int j = 0; j < p.world; ++j) Mx = fmaxf(Mx, s_x[j * (Dv + 1) + Dv]);
     if (threadIdx.x < p.world) {
-      const float lj = s_x[threadIdx.x][Dv];
+      const float lj = s_x[threadIdx.x * (Dv + 1) + Dv];
       s_w[threadIdx.x] = (lj == -INFINITY) ? 0.f : expf(lj - Mx);
     }
     __syncthreads();
@@ -177,7 +170,7 @@ __global__ void __launch_bounds__(kWarps * 32) kx_kernel(const __grid_constant__
     for (int d = threadIdx.x; d < Dv; d += blockDim.x) {
       float v = 0.f;
       for (int j = 0; j < p.world; ++j)
-        if (s_w[j] != 0.f) v = fmaf(s_x[j][d], s_w[j], v);
+        if (s_w[j] != 0.f) v = fmaf(s_x[j * (Dv + 1) + d], s_w[j], v);
       v *= invW;
       const int64_t off = (int64_t)b * p.out_sb + (int64_t)h * p.out_sh + d;
       if (p.out_dtype == HALO_DTYPE_F32)
@@ -291,16 +284,17 @@ extern "C" int32_t halo_sharded_merge(int32_t B, int32_t H, int32_t Dv, int32_t 
   prm.err = device_error_ptr();
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const dim3 grid(prm.R), block(exchange::kWarps * 32);
+  const size_t xsm = (size_t)world * (Dv + 1) * sizeof(float);   // staged rows of every rank
   const bool vec = (reinterpret_cast<uintptr_t>(o_parts) & 15) == 0 && o_part_stride % 4 == 0 &&
                    o_row_stride % 4 == 0;
   // a dependent launch: scheduled while the split-KV kernel's last CTAs run
   cudaError_t e;
-  if (Dv <= 32) e = launch_dependent(exchange::kx_kernel<1, false>, grid, block, 0, st, prm);
-  else if (Dv <= 64) e = launch_dependent(exchange::kx_kernel<2, false>, grid, block, 0, st, prm);
+  if (Dv <= 32) e = launch_dependent(exchange::kx_kernel<1, false>, grid, block, xsm, st, prm);
+  else if (Dv <= 64) e = launch_dependent(exchange::kx_kernel<2, false>, grid, block, xsm, st, prm);
   else if (Dv <= 128 && Dv % 4 == 0 && vec)
-    e = launch_dependent(exchange::kx_kernel<4, true>, grid, block, 0, st, prm);
-  else if (Dv <= 128) e = launch_dependent(exchange::kx_kernel<4, false>, grid, block, 0, st, prm);
-  else e = launch_dependent(exchange::kx_kernel<8, false>, grid, block, 0, st, prm);
+    e = launch_dependent(exchange::kx_kernel<4, true>, grid, block, xsm, st, prm);
+  else if (Dv <= 128) e = launch_dependent(exchange::kx_kernel<4, false>, grid, block, xsm, st, prm);
+  else e = launch_dependent(exchange::kx_kernel<8, false>, grid, block, xsm, st, prm);
   if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "kx_kernel launch");
   count_launches(1);
