@@ -374,6 +374,175 @@ __device__ __forceinline__ bool consume_mma(const P& p, const Unit& un, const It
   return ok;
 }
 
+// ---- transposed tile math for GQA groups of at most 8 q-heads
+// S^T = K Q^T with the 16 keys of the warp as the MMA's M rows and the
+// q-heads as its 8 columns, and O^T = V^T P^T: half the MMAs of the
+// q-heads-as-rows form (whose 16 rows are mostly empty for G <= 8) and half
+// the accumulator registers (O^T is D x 8), so more CTAs fit on an SM.
+// Thread t holds heads 2(t%4), 2(t%4)+1 and keys t/4, t/4 + 8 of the warp's
+// 16; the per-head max over keys is a reduction across the eight lanes that
+// share t%4.  P^T goes from the S^T accumulator layout to the B operand of
+// the P V product with one movmatrix transpose per 8x8 block.
+
+// Q^T fragments (B operand) of all k-steps: q-heads as columns.
+template <typename T, int D, int STAGES>
+__device__ __forceinline__ void load_qT_frags(const char* qslot, uint32_t (&qb)[D / 16][2]) {
+  using Gm = Geom<T, D, STAGES>;
+  static_assert(D % 32 == 0, "two k-steps per ldmatrix.x4");
+  const int lane = threadIdx.x & 31;
+  const uint32_t base = smem_addr(qslot);
+#pragma unroll
+  for (int kk = 0; kk < D / 16; kk += 2)
+    ldsm_x4(base + swz<Gm::kInner, Gm::kGpb>(lane & 7, kk * 2 + (lane >> 3)), qb[kk][0],
+            qb[kk][1], qb[kk + 1][0], qb[kk + 1][1]);
+}
+
+template <typename T, int D, int STAGES>
+__device__ __forceinline__ void mma_tile_t(float scale_log2, uint32_t kbase, uint32_t vbase,
+                                           const uint32_t (&qb)[D / 16][2],
+                                           float (&o)[D / 16][4], float& m0, float& m1, float& l0,
+                                           float& l1, int valid, int64_t pos0, bool causal,
+                                           int64_t qpos) {
+  using Gm = Geom<T, D, STAGES>;
+  const int lane = threadIdx.x & 31;
+  const int wrow = (threadIdx.x >> 5) * 16;
+  const int g = lane >> 2;
+
+  // ---- S^T = K Q^T (16 keys x 8 heads)
+  float s[4] = {0.f, 0.f, 0.f, 0.f};
+  {
+    const int key = wrow + (lane & 15);
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk) {
+      uint32_t a[4];
+      ldsm_x4(kbase + swz<Gm::kInner>(key, kk * 2 + (lane >> 4)), a[0], a[1], a[2], a[3]);
+      mma_16816(s, a, qb[kk][0], qb[kk][1], (T*)nullptr);
+    }
+  }
+
+  // ---- scale + mask: s[0], s[1] are key g, s[2], s[3] key g + 8
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const int r = wrow + g + ((e >> 1) << 3);
+    const bool ok = r < valid && (!causal || pos0 + r <= qpos);
+    s[e] = ok ? s[e] * scale_log2 : -INFINITY;
+  }
+
+  // ---- online softmax per head (columns 2c, 2c+1): max over the 16 keys
+  float t0 = fmaxf(s[0], s[2]), t1 = fmaxf(s[1], s[3]);
+#pragma unroll
+  for (int off = 4; off < 32; off <<= 1) {
+    t0 = fmaxf(t0, __shfl_xor_sync(0xffffffffu, t0, off));
+    t1 = fmaxf(t1, __shfl_xor_sync(0xffffffffu, t1, off));
+  }
+  const float mn0 = fmaxf(m0, t0), mn1 = fmaxf(m1, t1);
+  const float mu0 = (mn0 == -INFINITY) ? 0.f : mn0;
+  const float mu1 = (mn1 == -INFINITY) ? 0.f : mn1;
+  const float a0 = exp2f(m0 - mu0), a1 = exp2f(m1 - mu1);
+  m0 = mn0;
+  m1 = mn1;
+  const float p0 = exp2f(s[0] - mu0), p1 = exp2f(s[1] - mu1);
+  const float p2 = exp2f(s[2] - mu0), p3 = exp2f(s[3] - mu1);
+  l0 = l0 * a0 + (p0 + p2);      // this thread's keys; reduced over lanes at the end
+  l1 = l1 * a1 + (p1 + p3);
+  if (__any_sync(0xffffffffu, a0 != 1.f || a1 != 1.f)) {
+#pragma unroll
+    for (int i = 0; i < D / 16; ++i) {
+      o[i][0] *= a0;
+      o[i][1] *= a1;
+      o[i][2] *= a0;
+      o[i][3] *= a1;
+    }
+  }
+
+  // ---- P^T = hi + lo, transposed into the B operand (keys x heads)
+  uint32_t bh[2], bl[2];
+  {
+    const uint32_t h0 = Elem<T>::pack(p0, p1), h1 = Elem<T>::pack(p2, p3);
+    float x0, x1, x2, x3;
+    Elem<T>::unpack(h0, x0, x1);
+    Elem<T>::unpack(h1, x2, x3);
+    const uint32_t r0 = Elem<T>::pack(p0 - x0, p1 - x1), r1 = Elem<T>::pack(p2 - x2, p3 - x3);
+    bh[0] = movmatrix_t(h0);
+    bh[1] = movmatrix_t(h1);
+    bl[0] = movmatrix_t(r0);
+    bl[1] = movmatrix_t(r1);
+  }
+
+  // ---- O^T += V^T P^T, 16 rows of d at a time
+  {
+    const int key = wrow + (lane & 7) + ((lane >> 4) << 3);
+#pragma unroll
+    for (int i = 0; i < D / 16; ++i) {
+      uint32_t a[4];
+      ldsm_x4_t(vbase + swz<Gm::kInner>(key, i * 2 + ((lane >> 3) & 1)), a[0], a[1], a[2], a[3]);
+      mma_16816(o[i], a, bh[0], bh[1], (T*)nullptr);
+      mma_16816(o[i], a, bl[0], bl[1], (T*)nullptr);
+    }
+  }
+}
+
+// This warp's transposed partial state -> partial slot `slot` of its heads.
+template <int D, class P>
+__device__ __forceinline__ void store_partial_t(const P& p, const Unit& un, int slot,
+                                                const float (&o)[D / 16][4], float m0, float m1,
+                                                float l0, float l1) {
+  const int lane = threadIdx.x & 31;
+  const int g = lane >> 2, c = lane & 3;
+#pragma unroll
+  for (int off = 4; off < 32; off <<= 1) {
+    l0 += __shfl_xor_sync(0xffffffffu, l0, off);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, off);
+  }
+#pragma unroll
+  for (int e = 0; e < 2; ++e) {
+    const int hl = 2 * c + e;
+    if (hl < un.gcount) {
+      const int h = un.h_kv * p.G + un.gbase + hl;
+      const int64_t row = ((int64_t)un.b * p.H + h) * p.S + slot;
+      if (g == 0) {
+        const float m = e ? m1 : m0;
+        p.m_part[row] = (m == -INFINITY) ? -INFINITY : m * kLn2;
+        p.l_part[row] = e ? l1 : l0;
+      }
+      float* op = p.o_part + row * D;
+#pragma unroll
+      for (int i = 0; i < D / 16; ++i) {
+        op[i * 16 + g] = o[i][e];
+        op[i * 16 + g + 8] = o[i][e + 2];
+      }
+    }
+  }
+}
+
+template <typename T, int D, int STAGES, class P, class Tiles>
+__device__ __forceinline__ bool consume_mma_t(const P& p, const Unit& un, const Item& it,
+                                              Tiles& tiles, const char* qslot, uint64_t* qempty,
+                                              int n_tiles, int& gt, int64_t qpos) {
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  uint32_t qb[D / 16][2];
+  load_qT_frags<T, D, STAGES>(qslot, qb);
+  __syncwarp();
+  if (lane == 0) mbar_arrive(qempty);
+
+  float o[D / 16][4];
+#pragma unroll
+  for (int i = 0; i < D / 16; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+  bool ok = true;
+  for (int t = 0; t < n_tiles; ++t, ++gt) {
+    uint32_t kbase, vbase;
+    if (!tiles.acquire(t, gt, kbase, vbase)) { ok = false; ++gt; break; }
+    mma_tile_t<T, D, STAGES>(p.scale_log2, kbase, vbase, qb, o, m0, m1, l0, l1,
+                             it.rows - t * kBlockN, it.start + (int64_t)t * kBlockN,
+                             it.causal != 0, qpos);
+    tiles.release(gt);
+  }
+  store_partial_t<D>(p, un, it.slot + warp, o, m0, m1, l0, l1);
+  return ok;
+}
+
 // fp32 inputs: CUDA-core FMA path, up to 8 q-heads per unit.  For S, lane
 // pair (2k, 2k+1) owns key k of the warp's 16 rows, each lane one half of
 // the row's 16-byte chunks; for P V lane l owns output columns l, l+32, ...
@@ -972,8 +1141,9 @@ struct DequantTiles {
   __device__ __forceinline__ void release(int) { __syncwarp(); }
 };
 
-template <typename T, int D, int BITS>
-__global__ void __launch_bounds__(kThreads, 2) kk_kernel(const __grid_constant__ KiviParams p) {
+// TR: transposed tile math (GQA groups of at most 8 q-heads), 3 CTAs per SM.
+template <typename T, int D, int BITS, bool TR>
+__global__ void __launch_bounds__(kThreads, TR ? 3 : 2) kk_kernel(const __grid_constant__ KiviParams p) {
   using KG = KGeom<T, D, BITS>;
   using Gm = typename KG::Gm;
   constexpr int STAGES = KG::kStages;
@@ -1057,9 +1227,14 @@ __global__ void __launch_bounds__(kThreads, 2) kk_kernel(const __grid_constant__
     const int64_t qpos = (it.causal && p.q_pos != nullptr) ? p.q_pos[un.b] : INT64_MAX;
     const int n_tiles = (it.rows + kBlockN - 1) / kBlockN;
     DequantTiles<T, D, BITS> tiles{stages, kdq, vdq, full, empty, p.err};
-    if (!consume_mma<T, D, STAGES>(p, un, it, tiles, qring + qs * Gm::kQSlotBytes, &qempty[qs],
-                                   n_tiles, gt, qpos))
-      return;
+    bool ok;
+    if constexpr (TR)
+      ok = consume_mma_t<T, D, STAGES>(p, un, it, tiles, qring + qs * Gm::kQSlotBytes, &qempty[qs],
+                                       n_tiles, gt, qpos);
+    else
+      ok = consume_mma<T, D, STAGES>(p, un, it, tiles, qring + qs * Gm::kQSlotBytes, &qempty[qs],
+                                     n_tiles, gt, qpos);
+    if (!ok) return;
   }
 }
 
@@ -1811,7 +1986,7 @@ static int encode_q_map(const halo_decode_problem_t& pb, CUtensorMap* out) {
 }
 
 // ---------------------------------------------------------------- KIVI host side
-template <typename T, int D, int BITS>
+template <typename T, int D, int BITS, bool TR>
 static int kk_ctas_per_sm() {
   using KG = KGeom<T, D, BITS>;
   static std::once_flag once[64];
@@ -1819,10 +1994,10 @@ static int kk_ctas_per_sm() {
   int dev = 0;
   cudaGetDevice(&dev);
   std::call_once(once[dev & 63], [&] {
-    cudaFuncSetAttribute(kk_kernel<T, D, BITS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaFuncSetAttribute(kk_kernel<T, D, BITS, TR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          KG::kSmemBytes);
     int n = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kk_kernel<T, D, BITS>, kThreads,
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kk_kernel<T, D, BITS, TR>, kThreads,
                                                       KG::kSmemBytes) != cudaSuccess || n <= 0)
       n = 1;
     cache[dev & 63] = n;
@@ -1830,38 +2005,65 @@ static int kk_ctas_per_sm() {
   return cache[dev & 63];
 }
 
+// The transposed tile math serves GQA groups of at most 8 q-heads.
+static bool kk_transposed(int G) { return G <= 8; }
+
 template <typename T, int D, int BITS>
+static int kk_occupancy(int G) {
+  return kk_transposed(G) ? kk_ctas_per_sm<T, D, BITS, true>() : kk_ctas_per_sm<T, D, BITS, false>();
+}
+
+static int kk_occupancy_for(int dtype, int D, int bits, int G) {
+  const bool bf = dtype == HALO_DTYPE_BF16;
+#define HALO_KK_OCC(DD, BB)                                                            \
+  if (D == DD && bits == BB)                                                           \
+    return bf ? kk_occupancy<__nv_bfloat16, DD, BB>(G) : kk_occupancy<__half, DD, BB>(G);
+  HALO_KK_OCC(128, 2) HALO_KK_OCC(128, 4) HALO_KK_OCC(128, 8)
+  HALO_KK_OCC(64, 2) HALO_KK_OCC(64, 4) HALO_KK_OCC(64, 8)
+#undef HALO_KK_OCC
+  return 2;
+}
+
+template <typename T, int D, int BITS, bool TR>
 static int launch_kk(const KiviParams& prm, cudaStream_t st) {
   using KG = KGeom<T, D, BITS>;
-  const int64_t grid_max = (int64_t)device_sms() * kk_ctas_per_sm<T, D, BITS>();
+  const int64_t grid_max = (int64_t)device_sms() * kk_ctas_per_sm<T, D, BITS, TR>();
   const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(prm.n_units, grid_max));
-  cudaError_t e = launch_dependent(kk_kernel<T, D, BITS>, grid, kThreads, KG::kSmemBytes, st, prm);
+  cudaError_t e =
+      launch_dependent(kk_kernel<T, D, BITS, TR>, grid, kThreads, KG::kSmemBytes, st, prm);
   if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "kk_kernel launch");
   count_launches();
   return HALO_OK;
 }
 
+template <typename T, int D, int BITS>
+static int launch_kk_g(const KiviParams& prm, cudaStream_t st) {
+  return kk_transposed(prm.G) ? launch_kk<T, D, BITS, true>(prm, st)
+                              : launch_kk<T, D, BITS, false>(prm, st);
+}
+
 template <typename T>
 static int dispatch_kk_t(int D, int bits, const KiviParams& prm, cudaStream_t st) {
   if (D == 128) {
-    if (bits == 2) return launch_kk<T, 128, 2>(prm, st);
-    if (bits == 4) return launch_kk<T, 128, 4>(prm, st);
-    if (bits == 8) return launch_kk<T, 128, 8>(prm, st);
+    if (bits == 2) return launch_kk_g<T, 128, 2>(prm, st);
+    if (bits == 4) return launch_kk_g<T, 128, 4>(prm, st);
+    if (bits == 8) return launch_kk_g<T, 128, 8>(prm, st);
   } else if (D == 64) {
-    if (bits == 2) return launch_kk<T, 64, 2>(prm, st);
-    if (bits == 4) return launch_kk<T, 64, 4>(prm, st);
-    if (bits == 8) return launch_kk<T, 64, 8>(prm, st);
+    if (bits == 2) return launch_kk_g<T, 64, 2>(prm, st);
+    if (bits == 4) return launch_kk_g<T, 64, 4>(prm, st);
+    if (bits == 8) return launch_kk_g<T, 64, 8>(prm, st);
   }
   return fail(HALO_ERR_UNSUPPORTED, "KIVI decode: D %d bits %d", D, bits);
 }
 
 // Rows per work item for the KIVI decode: the same cost model as the plain
 // decode planner (persistent makespan + merge traffic), one segment.
-static int64_t kivi_split_tiles(const halo_decode_problem_t* p, int64_t rows) {
+static int64_t kivi_split_tiles(const halo_decode_problem_t* p, int64_t rows, int bits) {
   const int G = p->H / p->H_kv;
   const int64_t pairs = (int64_t)p->B * p->H_kv * ((G + 15) / 16);
-  const int64_t grid = (int64_t)device_sms() * 2;
+  const int64_t grid =
+      (int64_t)device_sms() * kk_occupancy_for(p->dtype, p->D, bits, G);
   const int64_t tiles = ceil_div64(rows, kBlockN);
   if (p->max_split_rows > 0) return std::max<int64_t>(1, p->max_split_rows / kBlockN);
   double best = 1e300;
@@ -2137,8 +2339,13 @@ extern "C" uint64_t halo_launch_count(void) {
 extern "C" int64_t halo_kivi_decode_workspace_bytes(const halo_decode_problem_t* problem,
                                                     int32_t rows) {
   if (!problem || rows < 0) return fail(HALO_ERR_INVALID_ARG, "bad arguments");
-  const int64_t split = kivi_split_tiles(problem, rows);
-  const int64_t items = rows > 0 ? ceil_div64(ceil_div64(rows, kBlockN), split) : 0;
+  // the split depends on the kernel variant's occupancy: size for the
+  // largest over the code widths
+  int64_t items = 0;
+  for (int bits : {2, 4, 8}) {
+    const int64_t split = kivi_split_tiles(problem, rows, bits);
+    if (rows > 0) items = std::max(items, ceil_div64(ceil_div64(rows, kBlockN), split));
+  }
   return workspace_for(problem, (int)(items * kConsumerWarps));
 }
 
@@ -2154,7 +2361,7 @@ extern "C" int32_t halo_kivi_decode(const halo_decode_problem_t* problem,
   if (causal && !problem->q_pos) return fail(HALO_ERR_INVALID_ARG, "causal needs q_pos");
   const halo_decode_problem_t& pb = *problem;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const int64_t split = kivi_split_tiles(problem, rows);
+  const int64_t split = kivi_split_tiles(problem, rows, bits);
   const int64_t tiles = ceil_div64(rows, kBlockN);
   const int n_items = rows > 0 ? (int)ceil_div64(tiles, split) : 0;
   if (n_items > kMaxItems) return fail(HALO_ERR_UNSUPPORTED, "too many KIVI work items");

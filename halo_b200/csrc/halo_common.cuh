@@ -213,6 +213,14 @@ __device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t&
                : "r"(addr));
 }
 
+// Transpose of an 8x8 matrix of 16-bit values held one row pair per thread
+// (thread t: row t/4, columns 2(t%4), 2(t%4)+1) across the warp.
+__device__ __forceinline__ uint32_t movmatrix_t(uint32_t x) {
+  uint32_t y;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
+}
+
 template <typename T>
 struct Elem;
 

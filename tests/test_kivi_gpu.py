@@ -116,6 +116,31 @@ def test_fused_kivi_decode_matches_oracle(dtype, bits, D):
     assert (lse.cpu().double() - rl[:, :, 0]).abs().max().item() <= 1e-4
 
 
+@pytest.mark.parametrize("G", [1, 8, 16])
+def test_fused_kivi_decode_gqa_groups(G):
+    """Both tile layouts of the fused kernel: groups of at most 8 q-heads use
+    the transposed (keys-as-rows) MMA form, larger groups the q-heads-as-rows
+    form."""
+    from halo_b200.baselines.kivi_cache import _Packed, kivi_decode
+    dtype, bits, D = torch.float16, 2, 128
+    g = torch.Generator().manual_seed(200 + G)
+    B, H_kv, T = 2, 2, 1500
+    H = H_kv * G
+    k = torch.randn(B, H_kv, T, D, generator=g)
+    k[..., 5] *= 10
+    v = torch.randn(B, H_kv, T, D, generator=g)
+    q = torch.randn(B, H, D, generator=g).to(dtype)
+    kq = _Packed(B, H_kv, D, dtype, torch.device(DEV), bits, 32)
+    vq = _Packed(B, H_kv, D, dtype, torch.device(DEV), bits, 32)
+    kq.append(k.to(dtype).to(DEV))
+    vq.append(v.to(dtype).to(DEV))
+    out, lse = kivi_decode(q.to(DEV), kq, vq, T, bits, scale=1 / math.sqrt(D),
+                           out=torch.empty(B, H, D, device=DEV))
+    ro, rl = OA.full_attention_f64(q.unsqueeze(2), kq.dequantized().cpu(), vq.dequantized().cpu())
+    assert (out.cpu().double() - ro[:, :, 0]).abs().max().item() <= 2e-3
+    assert (lse.cpu().double() - rl[:, :, 0]).abs().max().item() <= 1e-4
+
+
 def test_kivi_cache_reference_behaviour():
     """Reference tests/test_kivi_cache.py:37-107 on the GPU cache."""
     from halo_b200.baselines.kivi_cache import KIVICache
