@@ -115,6 +115,8 @@ __global__ void __maxnreg__(88) kx_kernel(const __grid_constant__ Params p) {
   __syncthreads();
 
   // ---- 2. push the row into slot [rank][row] of every peer's buffer
+  // (NVLink stores; pulling instead, with peer loads, measured slower: every
+  // poll of a word not yet written is a remote round trip)
   for (int j = 0; j < p.world; ++j) {
     if (j == p.rank) continue;
     uint64_t* dst = reinterpret_cast<uint64_t*>(p.bufs[j]) + par * par_words +
@@ -123,33 +125,49 @@ __global__ void __maxnreg__(88) kx_kernel(const __grid_constant__ Params p) {
       st_relaxed_sys(dst + d, tag | __float_as_uint(s_row[d]));
   }
 
-  // ---- 3. collect every rank's row (bounded wait on the epoch tags)
+  // ---- 3. collect every rank's row from this rank's buffer (bounded wait
+  // on the epoch tags): a thread issues the loads of kBatch of its words
+  // before checking any, so an 8-rank row costs one or two round trips
+  // rather than eight
+  constexpr int kBatch = 8;
   const uint64_t* src = data_own + par * par_words + (size_t)row * row_words;
-  for (int i = threadIdx.x; i < p.world * (Dv + 1); i += blockDim.x) {   // o and lse words
-    const int j = i / (Dv + 1), d = i - j * (Dv + 1);
-    if (j == p.rank) {
-      s_x[j * (Dv + 1) + d] = s_row[d];
-      continue;
+  auto word = [&](int j, int d) -> const uint64_t* { return src + (size_t)j * rank_words + d; };
+  const int n_words = p.world * (Dv + 1);   // o and lse words of every rank
+  bool all_ok = true;
+  for (int base = threadIdx.x; base < n_words && all_ok; base += kBatch * blockDim.x) {
+    uint64_t v[kBatch];
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      const int i = base + u * blockDim.x;
+      const int j = i / (Dv + 1), d = i - j * (Dv + 1);
+      v[u] = (i < n_words && j != p.rank) ? ld_relaxed_sys(word(j, d)) : 0;
     }
-    const uint64_t* w = src + (size_t)j * rank_words + d;
-    uint64_t v = ld_relaxed_sys(w);
-    if ((uint32_t)(v >> 32) != epoch) {
-      const uint64_t t0 = globaltimer_ns();
-      bool ok = false;
-      while (!ok) {
-        for (int k = 0; k < 64 && !ok; ++k) {
-          v = ld_relaxed_sys(w);
-          ok = (uint32_t)(v >> 32) == epoch;
-        }
-        if (!ok && globaltimer_ns() - t0 > kWaitLimitNs) {
-          set_device_error(p.err, static_cast<unsigned int>(-HALO_ERR_TIMEOUT));
-          s_ok = 0;
-          break;
-        }
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      const int i = base + u * blockDim.x;
+      if (i >= n_words || !all_ok) continue;
+      const int j = i / (Dv + 1), d = i - j * (Dv + 1);
+      if (j == p.rank) {
+        s_x[i] = s_row[d];
+        continue;
       }
-      if (!ok) break;
+      uint64_t w = v[u];
+      if ((uint32_t)(w >> 32) != epoch) {
+        const uint64_t* a = word(j, d);
+        const uint64_t t0 = globaltimer_ns();
+        while ((uint32_t)(w >> 32) != epoch) {
+          for (int k = 0; k < 64 && (uint32_t)(w >> 32) != epoch; ++k) w = ld_relaxed_sys(a);
+          if ((uint32_t)(w >> 32) != epoch && globaltimer_ns() - t0 > kWaitLimitNs) {
+            set_device_error(p.err, static_cast<unsigned int>(-HALO_ERR_TIMEOUT));
+            s_ok = 0;
+            all_ok = false;
+            break;
+          }
+        }
+        if (!all_ok) continue;
+      }
+      s_x[i] = __uint_as_float((uint32_t)w);   // i = j * (Dv + 1) + d
     }
-    s_x[j * (Dv + 1) + d] = __uint_as_float((uint32_t)v);
   }
   __syncthreads();
 
@@ -181,9 +199,9 @@ __global__ void __maxnreg__(88) kx_kernel(const __grid_constant__ Params p) {
         reinterpret_cast<__half*>(p.out)[off] = __float2half_rn(v);
     }
   }
-  // the last CTA of the call publishes its epoch for the next call
+  // the last CTA of the call publishes its epoch for the next call (the
+  // kernel boundary makes it visible to the next launch)
   if (threadIdx.x == 0) {
-    __threadfence();
     if (atomicAdd(ctrl + 1, 1u) == (uint32_t)p.R - 1) {
       ctrl[1] = 0;
       *reinterpret_cast<volatile uint32_t*>(ctrl) = epoch;

@@ -195,11 +195,11 @@ int32_t halo_ipc_free(void* dev_ptr);
 
 /* The cross-GPU step of a sequence-sharded decode in one kernel per rank:
  * merge this rank's P local partials (layout as halo_lse_merge), write the
- * normalised (o, lse) row into slot `rank` of every rank's exchange buffer
- * (bufs[j] = rank j's buffer mapped in this process, bufs[rank] its own)
- * through NVLink peer stores, publish a per-row flag = the call's epoch,
- * wait for the rows of all ranks (bounded: HALO_ERR_TIMEOUT in the device
- * error word after 2 s), and write the merged out (B, H, Dv) in out_dtype
+ * normalised (o, lse) row, tagged with the call's epoch, into slot `rank`
+ * of every rank's exchange buffer (bufs[j] = rank j's buffer mapped in this
+ * process, bufs[rank] its own) through NVLink peer stores, wait for the
+ * rows of all ranks (bounded: HALO_ERR_TIMEOUT in the device error word
+ * after 2 s), and write the merged out (B, H, Dv) in out_dtype
  * and lse (B, H) (optional).  Every rank makes the same sequence of calls;
  * the epoch is counted on the device in the rank's own buffer, so the call
  * can be captured in a CUDA graph and replayed.  Replaces, for the sharded
