@@ -3,21 +3,29 @@
 // Replaces the reference's per-chunk Triton kernel (halo/triton_chunked.py:47-138,
 // one program per (b, q-head), one launch per chunk, K/V re-read by every
 // q-head of a GQA group) with:
-//   * kd: one CTA per (work item, kv-head, batch row).  A work item is a
-//     contiguous row range of one chunk.  A producer warp streams 64-row K/V
-//     tiles into a 3-stage shared-memory ring with per-row async bulk copies
-//     (cp.async.bulk + mbarrier transaction counts); four consumer warps
-//     each own 16 rows of every tile and attend ALL q-heads of the GQA group
-//     at once, so every K/V byte is read from HBM exactly once.
+//   * kd: a producer lane streams 64-row K/V tiles into a 3-stage
+//     shared-memory ring with tensor TMA (cp.async.bulk.tensor + mbarrier
+//     transaction counts); four consumer warps each own 16 rows of every
+//     tile and attend ALL q-heads of the GQA group at once, so every K/V
+//     byte is read from HBM exactly once.
 //       - bf16/fp16: S = Q K^T and O += P V on tensor cores (mma.m16n8k16,
 //         fp32 accumulate).  P is split into a 16-bit high part and a 16-bit
 //         residual, so P V keeps ~16 mantissa bits (the reference's P is fp32).
 //       - fp32: CUDA-core FMA (exact fp32 products and sums).
 //     Online softmax in the exp2 domain with warp-shuffle row reductions.
-//     Each CTA writes one partial state (m, l, o) per q-head.
-//   * km: one warp per (b, q-head) folds all partial states (and optionally a
-//     prior running state) into the final output + LSE, or into the running
-//     (m, l, o) accumulators of update_chunk.
+//     kd_dyn_kernel (16-bit inputs, long contexts) hands the rows out at run
+//     time from per-pair counters and writes one combined partial per CTA;
+//     kd_kernel splits them statically (fp32, short contexts, or a fixed
+//     max_split_rows, which is bit-reproducible).
+//   * kk: the same pipeline over KIVI-packed K/V, dequantised per tile in
+//     shared memory; GQA groups of at most 8 q-heads use transposed tile
+//     math (keys as the MMA rows).
+//   * km: one CTA per (b, q-head) row folds all partial states (and
+//     optionally a prior running state) into the final output + LSE, or
+//     into the running (m, l, o) accumulators of update_chunk.
+// Every split-KV kernel is a programmatic dependent launch of its
+// predecessor, and the merge one of the split-KV kernel, so consecutive
+// kernels overlap launch and prologue with the previous kernel's tail.
 #include <algorithm>
 #include <atomic>
 #include <cmath>
