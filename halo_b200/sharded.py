@@ -2,9 +2,12 @@
 
 One process per GPU.  Rank ``r`` of ``N`` holds a contiguous range of the
 context's chunks (its KV shard) and computes a partial ``(o, lse)`` over them
-with the split-KV kernel; the ``N`` partials (fp32, ``B*H*(D_v+1)`` floats per
-rank) are all-gathered over NCCL and folded by the LSE-merge kernel on every
-rank.  The merge is associative and commutative (the identity behind
+with the split-KV kernel.  The ``N`` partials (fp32, ``B*H*(D_v+1)`` values
+per rank) are exchanged and folded on every rank: by default in one kernel
+that stores each row into every peer's exchange buffer over NVLink (CUDA IPC
+mappings, ``halo_sharded_decode``), or with an NCCL all-gather and the
+LSE-merge kernel (``exchange="nccl"``).  The merge is associative and
+commutative (the identity behind
 ``halo/kv_cache_chunked.py:194-239``; reference path relative to the
 lzbaclz/HALO root), so the result equals single-GPU attention over the whole
 context up to fp32 reduction order.  The reference runs on one GPU only; this
@@ -186,7 +189,9 @@ class ShardedDecoder:
         rank must capture at the same point of its call sequence.  The
         cross-GPU exchange counts its epochs on the device, so replays stay
         in step across ranks.  ``exchange="nccl"`` is not captured (its
-        collective runs through ``torch.distributed``)."""
+        collective runs through ``torch.distributed``).  The graph refers
+        to this decoder's workspace and exchange buffers: release it before
+        :meth:`close`."""
         if self.world > 1 and self.exchange != "p2p":
             raise ValueError("capture() needs exchange='p2p' when sharded")
         # the eager call runs on the capture stream so the stream's workspace
