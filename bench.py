@@ -938,6 +938,11 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
+    if args.seq_len and args.workload == "cfg5":
+        n = args.gpus * CFG5["chunk"]
+        if args.seq_len % n:
+            raise SystemExit(f"--seq-len must be a multiple of {n}")
+        CFG5["T"] = args.seq_len
     if args.impl == "reference":
         if args.workload == "cfg4":
             return run_reference_cfg4(args)
@@ -956,11 +961,6 @@ def main():
                 raise SystemExit(f"--seq-len must be a multiple of {CFG3['slice']}")
             CFG3["T"] = args.seq_len
         return run_ours_cfg3(args)
-    if args.seq_len:
-        n = args.gpus * CFG5["chunk"]
-        if args.seq_len % n:
-            raise SystemExit(f"--seq-len must be a multiple of {n}")
-        CFG5["T"] = args.seq_len
     return run_ours_cfg5(args)
 
 
