@@ -317,6 +317,34 @@ def test_decode_dynamic_schedule(cuda_device, dtype, layout):
     assert L.device_error() == 0
 
 
+@pytest.mark.parametrize("D,H,H_kv", [(64, 64, 8), (96, 32, 2)])
+def test_decode_dynamic_schedule_shapes(cuda_device, D, H, H_kv):
+    """The dynamic schedule at other head dims and group counts (G = 8 and
+    16, i.e. one q-head block per pair), with every batch row reading one
+    shared K/V buffer (batch stride 0)."""
+    ops = _ops()
+    from halo_b200 import _lib as L
+    g = torch.Generator().manual_seed(D + H)
+    B, T, chunk = 2, 32768, 4096
+    q = torch.randn(B, H, 1, D, generator=g).bfloat16()
+    k1 = torch.randn(1, H_kv, T, D, generator=g).bfloat16()
+    v1 = torch.randn(1, H_kv, T, D, generator=g).bfloat16()
+    dev = cuda_device
+    kd, vd = k1.to(dev).expand(B, -1, -1, -1), v1.to(dev).expand(B, -1, -1, -1)
+    ch = [(kd[..., a:b, :], vd[..., a:b, :], a, False) for a, b in _bounds(T, chunk)]
+    out, lse = ops.chunked_decode(q.to(dev), ch, out_dtype=torch.float32)
+    st, sl = ops.chunked_decode(q.to(dev), ch, out_dtype=torch.float32, max_split_rows=2048)
+    assert (out - st).abs().max().item() <= 1e-5 and (lse - sl).abs().max().item() <= 1e-5
+    G = H // H_kv
+    for hk in range(H_kv):
+        hs = slice(hk * G, (hk + 1) * G)
+        ro, rl = OA.full_attention_f64(q[:, hs], k1[:, hk:hk + 1].expand(B, -1, -1, -1),
+                                       v1[:, hk:hk + 1].expand(B, -1, -1, -1))
+        assert (out[:, hs].cpu().double() - ro[:, :, 0]).abs().max().item() <= OUT_TOL_16
+        assert (lse[:, hs].cpu().double() - rl[:, :, 0]).abs().max().item() <= LSE_TOL
+    assert L.device_error() == 0
+
+
 def test_device_error_word_clear(cuda_device):
     from halo_b200 import _lib as L
     assert L.device_error(clear=True) == 0
