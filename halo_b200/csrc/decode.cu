@@ -101,7 +101,7 @@ struct alignas(64) DecodeParams {
   int32_t B, H, H_kv, G, gblocks;
   int32_t S;          // partial slots per (b, h) row
   int32_t n_items, n_units;
-  int32_t n_pairs, n_pieces;  // dynamic schedule: pairs, pieces per pair
+  int32_t n_pairs, n_dyn_tiles;  // dynamic schedule: pairs, 64-row tiles per pair
   float scale_log2;   // softmax scale * log2(e)
 };
 static_assert(sizeof(DecodeParams) <= 32764, "kernel parameter block limit");
@@ -124,7 +124,7 @@ struct alignas(64) DynParams {
   int32_t B, H, H_kv, G, gblocks;
   int32_t S;
   int32_t n_items, n_units;
-  int32_t n_pairs, n_pieces;
+  int32_t n_pairs, n_dyn_tiles;
   float scale_log2;
 };
 
@@ -786,13 +786,14 @@ __global__ void __launch_bounds__(kThreads, MINB) kd_kernel(const __grid_constan
 // Same tile math as kd_kernel, but the rows are handed out at run time.
 // Each (batch, kv-head, q-head block) pair gets a group of CTAs: CTA c
 // serves pair c % n_pairs and is member c / n_pairs of its group.  The
-// pair's rows (every segment of the launch, in order) are cut into pieces of
-// kPieceTiles 64-row tiles, and the group's producer lanes take pieces from
-// the pair's counter in the workspace control block, so CTAs on SMs that
-// stream faster take more pieces and the group finishes within about one
-// piece of each other (a static split leaves the CTAs of slower SMs
-// finishing ~15 % after the median).  Each consumer warp folds every piece
-// its CTA takes into one running state; at the end the four warps' states
+// pair's rows (every segment of the launch, in order) are numbered in 64-row
+// tiles, and the group's producer lanes take them from the pair's counter
+// in the workspace control block, kPieceTiles at a time and one at a time
+// near the end.  CTAs on SMs that stream faster take more tiles and the
+// group finishes within about one tile of each other (a static split leaves
+// the CTAs of slower SMs finishing ~15 % after the median).  Each consumer
+// warp folds every tile its CTA takes into one running state; at the end
+// the four warps' states
 // are combined through shared memory into the CTA's partial, slot `member`
 // (so a row has one partial per CTA of its group).  The
 // producer tells the consumers what each stage holds through a per-stage
@@ -864,25 +865,35 @@ __global__ void __launch_bounds__(kThreads, MINB)
       for (int bx = 0; bx < Gm::kNBox; ++bx)
         tma_load_3d(qslot + bx * Gm::kGpb * Gm::kInner, &p.qmap, bx * Gm::kBoxElems,
                     un.h_kv * p.G + un.gbase, un.b, qfull);
-      // member m's first piece is piece m; later pieces come from the
-      // pair's counter (offset by the group size)
+      // Takes are ranges of the pair's tiles (numbered across its
+      // segments): member m's first take is tiles [2m, 2m + 2); later
+      // takes come from the pair's counter (offset by the 2 * cpg
+      // pre-assigned tiles), two tiles at a time, then one at a time over
+      // the last ~4 tiles per CTA so the group finishes closer together.
+      // The next take is in flight while the current one loads.
       unsigned int* ctr = p.ctrl + pair;
       const unsigned int cpg = gridDim.x / (unsigned)p.n_pairs;
+      const unsigned int n_tiles = (unsigned)p.n_dyn_tiles;
+      const unsigned int single = n_tiles > 4u * cpg ? n_tiles - 4u * cpg : 0u;
       int gt = 0;
       bool ok = true;
-      unsigned int next = (unsigned)member;
-      while (ok && next < (unsigned int)p.n_pieces) {
-        const int piece = (int)next;
-        next = cpg + atomicAdd(ctr, 1u);   // the next take is in flight while this piece loads
-        int si = 0;                  // items[i].slot = first piece of segment i
-        while (si + 1 < p.n_items && p.items[si + 1].slot <= piece) ++si;
-        const Item& it = p.items[si];
-        const int t0 = (piece - it.slot) * kPieceTiles;
-        const int t1 = min(t0 + kPieceTiles, (it.rows + kBlockN - 1) / kBlockN);
-        const CUtensorMap* kmap = &p.maps[2 * si];
-        const CUtensorMap* vmap = &p.maps[2 * si + 1];
-        const int bc = it.b_bcast ? 0 : un.b;
-        for (int t = t0; t < t1; ++t, ++gt) {
+      unsigned int cur = 2u * member, len = kPieceTiles;
+      unsigned int nxt = 0, nlen = 0;
+      auto take = [&]() {
+        nlen = (cur + len >= single) ? 1u : (unsigned)kPieceTiles;
+        nxt = 2u * cpg + atomicAdd(ctr, nlen);
+      };
+      if (cur < n_tiles) take();
+      while (ok && cur < n_tiles) {
+        const unsigned int end = min(cur + len, n_tiles);
+        for (unsigned int tt = cur; tt < end && ok; ++tt, ++gt) {
+          int si = 0;                  // items[i].slot = first tile of segment i
+          while (si + 1 < p.n_items && p.items[si + 1].slot <= (int)tt) ++si;
+          const Item& it = p.items[si];
+          const int t = (int)tt - it.slot;
+          const CUtensorMap* kmap = &p.maps[2 * si];
+          const CUtensorMap* vmap = &p.maps[2 * si + 1];
+          const int bc = it.b_bcast ? 0 : un.b;
           const int s = gt % STAGES;
           if (gt >= STAGES && !(ok = mbar_wait(&empty[s], ((gt / STAGES) & 1) ^ 1, p.err))) break;
           const int r0 = t * kBlockN;
@@ -900,6 +911,9 @@ __global__ void __launch_bounds__(kThreads, MINB)
                         bc, &full[s]);
           }
         }
+        cur = nxt;
+        len = nlen;
+        if (ok && cur < n_tiles) take();
       }
       if (ok) {   // end of work: a stage descriptor with no rows
         const int s = gt % STAGES;
@@ -1601,9 +1615,10 @@ struct Plan {
   int32_t split_tiles = 0;
   int32_t S = 0;            // partial slots per (b, h) row
   // dynamic schedule (kd_dyn_kernel): one item per segment whose slot is
-  // its first piece; `grid` CTAs = n_pairs groups of S / kConsumerWarps
+  // its first tile (tiles numbered across the segments); `grid` CTAs =
+  // n_pairs groups of S CTAs
   bool dyn = false;
-  int32_t n_pairs = 0, n_pieces = 0, grid = 0;
+  int32_t n_pairs = 0, n_tiles = 0, grid = 0;
 };
 
 static int dyn_ctas_per_sm(int dtype, int D);
@@ -1658,12 +1673,12 @@ static Plan make_plan(const halo_decode_problem_t* p, const halo_kv_chunk_t* chu
       (int64_t)plan.segs.size() <= kMaxSegs && pairs <= kMaxDynPairs) {
     const int64_t cap = (int64_t)device_sms() * dyn_ctas_per_sm(p->dtype, p->D);
     const int64_t cpg = cap / pairs;
-    int64_t pieces = 0;
-    for (int64_t t : seg_tiles) pieces += ceil_div64(t, kPieceTiles);
-    if (cpg >= 1 && pairs * cpg * 10 >= cap * 9 && pieces >= 4 * cpg) {
+    int64_t pieces = 0;   // in tiles: the kernel takes them two or one at a time
+    for (int64_t t : seg_tiles) pieces += t;
+    if (cpg >= 1 && pairs * cpg * 10 >= cap * 9 && pieces >= 8 * cpg) {
       plan.dyn = true;
       plan.n_pairs = (int32_t)pairs;
-      plan.n_pieces = (int32_t)pieces;
+      plan.n_tiles = (int32_t)pieces;
       plan.grid = (int32_t)(pairs * cpg);
       plan.S = (int32_t)cpg;     // one combined partial per CTA of a group
       int32_t first = 0;
@@ -1677,7 +1692,7 @@ static Plan make_plan(const halo_decode_problem_t* p, const halo_kv_chunk_t* chu
         it.causal = sg.view.causal;
         it.b_bcast = (sg.view.k_stride_b == 0 || sg.view.v_stride_b == 0) ? 1 : 0;
         it.slot = first;
-        first += (int32_t)ceil_div64(seg_tiles[si], kPieceTiles);
+        first += (int32_t)seg_tiles[si];
         plan.items.push_back(it);
       }
       return plan;
@@ -1934,7 +1949,7 @@ static int dispatch_kd_dyn(int dtype, int D, const DecodeParams& prm, int grid, 
     dp.n_items = prm.n_items;
     dp.n_units = prm.n_units;
     dp.n_pairs = prm.n_pairs;
-    dp.n_pieces = prm.n_pieces;
+    dp.n_dyn_tiles = prm.n_dyn_tiles;
     dp.scale_log2 = prm.scale_log2;
     if (dtype == HALO_DTYPE_BF16) return dispatch_kd_dyn_t<__nv_bfloat16>(D, dp, grid, st);
     return dispatch_kd_dyn_t<__half>(D, dp, grid, st);
@@ -2175,7 +2190,7 @@ static int decode_splits(const halo_decode_problem_t* problem, const halo_kv_chu
     if (plan.dyn) {
       prm.ctrl = reinterpret_cast<unsigned int*>(ws);
       prm.n_pairs = plan.n_pairs;
-      prm.n_pieces = plan.n_pieces;
+      prm.n_dyn_tiles = plan.n_tiles;
       prm.n_items = (int32_t)plan.items.size();
       prm.n_units = plan.grid;
       for (size_t si = 0; si < plan.segs.size(); ++si) {
