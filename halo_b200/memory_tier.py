@@ -3,8 +3,14 @@
 buffers ``(L, max_blocks, H_kv, block, D)``.  The DRAM tier is pinned host
 memory, so a block moves to or from HBM with one DMA.
 
-The NVMe tier of the reference is outside this package's scope (it is not on
-the HBM attention path); asking for it raises ``ValueError``.
+The NVMe tier (``halo/memory_tier.py:61-103, 228-258``) keeps each block as
+raw bytes in two files (``keys.bin``, ``values.bin``, one slot per (layer,
+block), like the reference's ``numpy.memmap`` layout, so any dtype including
+bf16 round-trips bit-exactly).  The reference copies a block out of the
+memory map into a new tensor; here a block is read with one positioned read
+(``os.preadv``) straight into a pinned host bounce buffer.  A block bound for
+HBM then crosses PCIe with a single DMA, and a block leaving HBM lands in
+the bounce buffer before one positioned write.
 """
 from __future__ import annotations
 
@@ -24,6 +30,73 @@ class MemoryTier(str, Enum):
         return name if isinstance(name, cls) else cls(str(name).lower())
 
 
+class _FileTier:
+    """NVMe tier: keys and values of block (layer, b) at byte offset
+    ``(layer * max_blocks + b) * block_bytes`` of ``keys.bin`` / ``values.bin``
+    (files sized for every slot when created).  Reads and writes go through
+    a pinned host bounce buffer with one positioned syscall per tensor."""
+
+    def __init__(self, shape, dtype, path: str, pin: bool) -> None:
+        import os
+        import torch
+        self.shape = tuple(shape)
+        self.dtype = dtype
+        self.block_shape = self.shape[2:]
+        itemsize = torch.tensor([], dtype=dtype).element_size()
+        self.block_elems = 1
+        for n in self.block_shape:
+            self.block_elems *= int(n)
+        self.block_bytes = self.block_elems * itemsize
+        total = self.shape[0] * self.shape[1] * self.block_bytes
+        os.makedirs(path, exist_ok=True)
+        self.paths = (os.path.join(path, "keys.bin"), os.path.join(path, "values.bin"))
+        self.fds = []
+        for fp in self.paths:
+            fd = os.open(fp, os.O_RDWR | os.O_CREAT, 0o644)
+            os.ftruncate(fd, total)
+            self.fds.append(fd)
+        self.bounce = torch.empty(2, self.block_elems, dtype=dtype, pin_memory=pin)
+
+    def _offset(self, layer: int, block: int) -> int:
+        if not (0 <= layer < self.shape[0] and 0 <= block < self.shape[1]):
+            raise IndexError(f"block ({layer}, {block}) outside the NVMe tier")
+        return (layer * self.shape[1] + block) * self.block_bytes
+
+    def read(self, layer: int, block: int, device=None):
+        """Block ``(keys, values)`` as new tensors on ``device`` (host if None)."""
+        import os
+        import torch
+        off = self._offset(layer, block)
+        out = []
+        for i, fd in enumerate(self.fds):
+            view = memoryview(self.bounce[i].view(torch.uint8).numpy())
+            n = os.preadv(fd, [view], off)
+            if n != self.block_bytes:
+                raise IOError(f"short read from {self.paths[i]} ({n} of {self.block_bytes} bytes)")
+            t = self.bounce[i].view(self.block_shape)
+            out.append(t.to(device, copy=True) if device is not None else t.clone())
+        return out[0], out[1]
+
+    def write(self, layer: int, block: int, keys, values) -> None:
+        import os
+        import torch
+        off = self._offset(layer, block)
+        for i, (fd, src) in enumerate(zip(self.fds, (keys, values))):
+            self.bounce[i].view(self.block_shape).copy_(src)      # D2H or host copy
+            if src.is_cuda:
+                torch.cuda.current_stream(src.device).synchronize()
+            view = memoryview(self.bounce[i].view(torch.uint8).numpy())
+            n = os.pwritev(fd, [view], off)
+            if n != self.block_bytes:
+                raise IOError(f"short write to {self.paths[i]} ({n} of {self.block_bytes} bytes)")
+
+    def close(self) -> None:
+        import os
+        for fd in self.fds:
+            os.close(fd)
+        self.fds = []
+
+
 class TieredStorage:
     """One block buffer per tier plus a (layer, block) -> tier directory."""
 
@@ -31,8 +104,7 @@ class TieredStorage:
                  block_size: int, dtype, device, nvme_path: Optional[str] = None,
                  max_blocks: int = 4096) -> None:
         self.tiers = [MemoryTier.from_name(t) for t in tiers]
-        if MemoryTier.NVME in self.tiers:
-            raise ValueError("the NVMe tier is not part of halo_b200 (gpu and dram only)")
+        self._nvme_path = nvme_path
         self.num_layers = num_layers
         self.num_kv_heads = num_kv_heads
         self.head_dim = head_dim
@@ -65,12 +137,23 @@ class TieredStorage:
         return self._block(layer, block, self._directory.get((layer, block), MemoryTier.GPU))
 
     # ------------------------------------------------------------------ internals
+    def _pin(self) -> bool:
+        import torch
+        return torch.cuda.is_available() and getattr(self.gpu_device, "type", "cpu") == "cuda"
+
     def _ensure(self, tier: MemoryTier):
         if tier in self._buffers:
             return self._buffers[tier]
         if tier not in self.tiers:
             raise ValueError(f"Tier {tier} not requested at construction time.")
         import torch
+        if tier is MemoryTier.NVME:
+            import os
+            import tempfile
+            path = (self._nvme_path or os.environ.get("HALO_NVME_PATH")
+                    or os.path.join(tempfile.gettempdir(), "halo_nvme"))
+            self._buffers[tier] = _FileTier(self._shape, self.dtype, path, self._pin())
+            return self._buffers[tier]
         if tier is MemoryTier.GPU:
             kw = dict(device=self.gpu_device)
         else:
@@ -82,13 +165,38 @@ class TieredStorage:
         return bufs
 
     def _block(self, layer, block, tier):
-        k, v = self._ensure(tier)
+        buf = self._ensure(tier)
+        if isinstance(buf, _FileTier):
+            return buf.read(layer, block)
+        k, v = buf
         return k[layer, block], v[layer, block]
 
     def _store(self, layer, block, keys, values, tier) -> None:
-        k, v = self._ensure(tier)
+        buf = self._ensure(tier)
+        if isinstance(buf, _FileTier):
+            buf.write(layer, block, keys, values)
+            return
+        k, v = buf
         k[layer, block].copy_(keys, non_blocking=True)
         v[layer, block].copy_(values, non_blocking=True)
+
+    def refetch_block(self, *, layer: int, block: int, device):
+        """The block's ``(keys, values)`` on ``device`` wherever it lives: an
+        NVMe block is read into the pinned bounce buffer and crosses PCIe in
+        one DMA per tensor."""
+        tier = self._directory.get((layer, block), MemoryTier.GPU)
+        buf = self._ensure(tier)
+        if isinstance(buf, _FileTier):
+            return buf.read(layer, block, device=device)
+        k, v = self._block(layer, block, tier)
+        return k.to(device, non_blocking=True), v.to(device, non_blocking=True)
+
+    def close(self) -> None:
+        """Close the NVMe tier's files (the data stays on disk)."""
+        buf = self._buffers.get(MemoryTier.NVME)
+        if isinstance(buf, _FileTier):
+            buf.close()
+            del self._buffers[MemoryTier.NVME]
 
     def __repr__(self) -> str:  # pragma: no cover
         return f"TieredStorage(tiers=[{','.join(t.value for t in self.tiers)}], blocks={self.max_blocks})"

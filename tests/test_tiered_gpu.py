@@ -82,3 +82,21 @@ def test_tiered_step_reuses_resident_chunks():
     o2, l2, c2 = lay.step(q, k_sel=4)
     assert c1 == c2 and lay.stats["refetched_chunks"] == n1 == 4
     assert torch.equal(o1, o2) and torch.equal(l1, l2)
+
+
+def test_nvme_tier_round_trip_through_hbm(tmp_path):
+    """A block written in HBM goes to the NVMe tier through the pinned bounce
+    buffer and comes back to HBM with one positioned read and one DMA."""
+    from halo_b200.memory_tier import TieredStorage
+    st = TieredStorage(tiers=["gpu", "dram", "nvme"], num_layers=2, num_kv_heads=4,
+                       head_dim=128, block_size=64, dtype=torch.bfloat16,
+                       device=torch.device(DEV), max_blocks=8, nvme_path=str(tmp_path / "nvme"))
+    g = torch.Generator().manual_seed(5)
+    k = torch.randn(4, 64, 128, generator=g).bfloat16().to(DEV)
+    v = torch.randn(4, 64, 128, generator=g).bfloat16().to(DEV)
+    st.write_new_block(layer=1, block=5, keys=k, values=v, tier="gpu")
+    st.move_block(layer=1, block=5, src="gpu", dst="nvme")
+    rk, rv = st.refetch_block(layer=1, block=5, device=torch.device(DEV))
+    torch.cuda.synchronize()
+    assert rk.is_cuda and torch.equal(rk, k) and torch.equal(rv, v)
+    st.close()
