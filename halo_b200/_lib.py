@@ -141,6 +141,21 @@ SIGNATURES = {
                                               ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p,
                                               ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p,
                                               ctypes.c_void_p]),
+    "halo_page_mean": (ctypes.c_int32, [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
+                                        ctypes.c_int64, ctypes.c_int32, ctypes.c_int32,
+                                        ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                                        ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p,
+                                        ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                        ctypes.c_void_p]),
+    "halo_page_press_topk": (ctypes.c_int32, [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
+                                              ctypes.c_int64, ctypes.c_int32, ctypes.c_int32,
+                                              ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                                              ctypes.c_int32, ctypes.c_void_p, ctypes.c_int64,
+                                              ctypes.c_int64, ctypes.c_int64, ctypes.c_int32,
+                                              ctypes.c_float, ctypes.c_float, ctypes.c_float,
+                                              ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p,
+                                              ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p,
+                                              ctypes.c_void_p]),
     "halo_copy2d_async": (ctypes.c_int32, [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p,
                                            ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
                                            ctypes.c_void_p]),

@@ -83,14 +83,15 @@ class _QuestScorerAdapter:
         self._num_full_pages[layer_idx] = n_full
         self.observe_calls += 1
 
-    def _run(self, layer_idx: int, query, k: int, exclude=None):
+    def _run(self, layer_idx: int, query, k: int, exclude=None, per_page_only: bool = False):
         kmin, kmax = self._k_min[layer_idx], self._k_max[layer_idx]
         B, H_kv, P, D = kmin.shape
         q = query if query.stride(-1) == 1 else query.contiguous()
         Bq, H, T_q, _ = q.shape
         scores = torch.empty(B, H_kv, T_q, P, dtype=torch.float32, device=q.device)
         topk = torch.empty(max(k, 1), dtype=torch.int64, device=q.device)
-        per_page = torch.empty(P, dtype=torch.float32, device=q.device) if k > 0 else None
+        per_page = (torch.empty(P, dtype=torch.float32, device=q.device)
+                    if (k > 0 or per_page_only) else None)
         ex = None
         if exclude is not None:
             ex = torch.zeros(P, dtype=torch.uint8, device=q.device)

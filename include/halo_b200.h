@@ -306,6 +306,32 @@ int32_t halo_page_score_topk(const void* q, int64_t q_sb, int64_t q_sh, int64_t 
                              const uint8_t* exclude, int32_t k, float* per_page, int64_t* topk,
                              halo_stream_t stream);
 
+/* Per-page mean key of the HALOPress ablation scorer (observe_keys of
+ * baselines/scorer_ablations.py:208-218): for pages page_begin ..
+ * page_begin + n_pages - 1 of K (B, H_kv, T, D), kmean[b][h][p][d] = fp32 sum
+ * over the page's rows in row order, divided by page_size, rounded once to
+ * the key dtype.  Strides as halo_page_summary. */
+int32_t halo_page_mean(const void* k, int64_t k_sb, int64_t k_sh, int64_t k_st, int32_t B,
+                       int32_t H_kv, int32_t D, int32_t dtype, int32_t page_size,
+                       int32_t page_begin, int32_t n_pages, void* kmean, int64_t o_sb,
+                       int64_t o_sh, int64_t o_sp, halo_stream_t stream);
+
+/* HALOPress page selection (select_hot_pages of
+ * baselines/scorer_ablations.py:220-268): scores[b][h_kv][t][p] = q_g . kmean
+ * (fp32; q_g the GQA mean rounded to q's dtype, as halo_page_score_topk);
+ * attn = max over (b, h_kv, t), minus its min, divided by its max when
+ * positive; rec = exp(-(P-1-p)/refresh_window) over its sum (+1e-12) over
+ * its max (+1e-12); sink = 1 for the first n_sink_pages pages; score =
+ * alpha*attn + beta*rec + gamma*sink (one rounding per operation) into
+ * per_page (optional); topk ((k,) int64) gets the k best pages, largest
+ * first, ties to the lower index.  P <= 8192. */
+int32_t halo_page_press_topk(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_st, int32_t B,
+                             int32_t H, int32_t T_q, int32_t H_kv, int32_t D, int32_t dtype,
+                             const void* kmean, int64_t o_sb, int64_t o_sh, int64_t o_sp,
+                             int32_t P, float alpha, float beta, float gamma,
+                             int32_t refresh_window, int32_t n_sink_pages, float* scores,
+                             int32_t k, float* per_page, int64_t* topk, halo_stream_t stream);
+
 /* ---------------------------------------------------------------- prefill */
 /* Multi-query (chunked-prefill) attention on the 5th-generation tensor cores:
  * T_q query rows per (b, h) at global positions q_pos0 .. q_pos0 + T_q - 1

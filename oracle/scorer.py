@@ -98,5 +98,68 @@ def num_hot_pages(P: int, memory_ratio: float, min_pages: int) -> int:
     return min(K, P)
 
 
+def round_to(x: np.ndarray, dtype: str) -> np.ndarray:
+    """float32 values rounded once to ``dtype`` ("bf16", "f16" or "f32")."""
+    x = np.asarray(x, dtype=np.float32)
+    if dtype == "bf16":
+        return bf16_bits_to_f32(f32_to_bf16_bits(x))
+    if dtype == "f16":
+        return x.astype(np.float16).astype(np.float32)
+    return x
+
+
+def page_means(K: np.ndarray, page_size: int, *, dtype: str) -> np.ndarray:
+    """Per-page mean key of the HALOPress scorer
+    (``baselines/scorer_ablations.py:208-218``, ``new_k.mean(dim=-2)``): an
+    fp32 sum over the page's rows taken in row order, one division by the
+    page size, one rounding to the key dtype.  (torch sums in its own order;
+    results agree with the reference to one unit in the last place.)
+    ``K``: (B, H_kv, T, D) float32 values; only full pages count."""
+    B, H_kv, T, D = K.shape
+    n = T // page_size
+    pages = np.asarray(K, dtype=np.float32)[:, :, : n * page_size].reshape(B, H_kv, n, page_size, D)
+    s = pages[:, :, :, 0].copy()
+    for r in range(1, page_size):
+        s = (s + pages[:, :, :, r]).astype(np.float32)
+    return round_to(s / np.float32(page_size), dtype)
+
+
+def press_scores(q_g: np.ndarray, k_mean: np.ndarray, *, alpha: float, beta: float,
+                 gamma: float, sink_tokens: int, refresh_window: int,
+                 page_size: int) -> np.ndarray:
+    """The HALOPress closed-form page score
+    (``baselines/scorer_ablations.py:220-262``): the attention proxy
+    ``q . K_mean`` (fp32, channel sum in float64 then rounded: the
+    reference's order is unspecified), max over (batch, kv-head, query),
+    min-max normalised; a recency term ``exp(-(P-1-p)/window)`` normalised by
+    its sum and then its max; sink pages (the first ``sink // page + 1``)
+    at 1; ``alpha*attn + beta*rec + gamma*sink`` with one fp32 rounding per
+    operation.  ``q_g``: (B, H_kv, T_q, D), ``k_mean``: (B, H_kv, P, D),
+    float32 values."""
+    f32 = np.float32
+    qe = q_g[:, :, :, None, :].astype(np.float32)
+    attn = (qe * k_mean[:, :, None].astype(np.float32)).astype(np.float64).sum(axis=-1)
+    attn = attn.astype(np.float32).max(axis=(0, 1, 2))
+    attn = (attn - attn.min()).astype(np.float32)
+    if float(attn.max()) > 0.0:
+        attn = (attn / attn.max()).astype(np.float32)
+    P = attn.shape[0]
+    pos = np.arange(P, dtype=np.float32)
+    rec = np.exp(-(f32(P - 1) - pos) / f32(max(refresh_window, 1))).astype(np.float32)
+    rec = (rec / (rec.astype(np.float64).sum().astype(np.float32) + f32(1e-12))).astype(np.float32)
+    rec = (rec / (rec.max() + f32(1e-12))).astype(np.float32)
+    sink = np.zeros(P, dtype=np.float32)
+    sink[: min(sink_tokens // max(page_size, 1) + 1, P)] = 1.0
+    return ((f32(alpha) * attn + f32(beta) * rec).astype(np.float32) + f32(gamma) * sink).astype(np.float32)
+
+
+def topk_sorted(score: np.ndarray, k: int) -> np.ndarray:
+    """The ``k`` largest pages (ties to the lower index), returned sorted
+    ascending as the reference's ``topk(...).indices.sort()`` does."""
+    order = np.lexsort((np.arange(score.shape[0]), -score.astype(np.float64)))
+    return np.sort(order[:k]).astype(np.int64)
+
+
 __all__ = ["bf16_bits_to_f32", "f32_to_bf16_bits", "page_summaries",
-           "gqa_mean_query", "score_pages", "select_topk", "num_hot_pages"]
+           "gqa_mean_query", "score_pages", "select_topk", "num_hot_pages", "round_to",
+           "page_means", "press_scores", "topk_sorted"]

@@ -114,6 +114,31 @@ def scorer_inputs(name):
     return K, q, page, mr, mp
 
 
+# HALOPress ablation scorer (baselines/scorer_ablations.py:184-268):
+# name -> (B, H, H_kv, T, D, page, dtype, seed, memory_ratio, min_pages,
+#          alpha, beta, gamma, sink_tokens, refresh_window)
+PRESS_CASES = {
+    "press_f32_gqa4": (2, 8, 2, 130, 32, 16, torch.float32, 51, 4.0, 2, 1.0, 0.5, 2.0, 4, 64),
+    "press_bf16_gqa4": (2, 16, 4, 512, 128, 32, torch.bfloat16, 52, 4.0, 4, 1.0, 0.5, 2.0, 4, 8),
+    "press_bf16_gqa3_tq2": (1, 6, 2, 256, 64, 16, torch.bfloat16, 53, 2.0, 1, 0.7, 1.5, 0.0, 40, 3),
+}
+
+
+def press_inputs(name):
+    B, H, H_kv, T, D, page, dtype, seed, mr, mp, a, b, c, sink, win = PRESS_CASES[name]
+    g = torch.Generator().manual_seed(seed)
+    K = torch.randn(B, H_kv, T, D, generator=g)
+    idx = torch.randperm(D, generator=g)[:4]
+    K[..., idx] *= 10.0
+    K = K.to(dtype)
+    T_q = 2 if name.endswith("tq2") else 1
+    q = torch.randn(B, H, T_q, D, generator=g).to(dtype)
+    cfg = dict(page_size=page, memory_ratio=mr, min_pages_selected=mp, halopress_alpha=a,
+               halopress_beta=b, halopress_gamma=c, halopress_sink_tokens=sink,
+               halopress_refresh_window=win)
+    return K, q, cfg
+
+
 def load(name: str) -> dict:
     """Load ``tests/golden/<name>.npz`` as ``{case: {key: array}}``."""
     out: dict = {}

@@ -160,6 +160,31 @@ def gen_scorer(Q) -> dict:
     return out
 
 
+def gen_press(A) -> dict:
+    """The reference's HALOPress ablation scorer (page-mean keys, closed-form
+    attention + recency + sink score, top-k), plus its uniform-random and FIFO
+    selections for the same inputs."""
+    out = {}
+    for name in I.PRESS_CASES:
+        K, q, cfg = I.press_inputs(name)
+        c = A.AblationScorerConfig(**cfg)
+        ad = A.HALOPressScorerAdapter(c)
+        ad.observe_keys(0, K)
+        top = ad.select_hot_pages(0, q)
+        kmean = ad._k_mean[0]
+        d = {"digest": np.bytes_(I.digest(K, q)), "topk": top.numpy().astype(np.int64)}
+        if K.dtype == torch.bfloat16:
+            d["kmean_bits"] = bits16(kmean)
+        else:
+            d["kmean"] = kmean.numpy()
+        for cls, key in ((A.UniformRandomScorerAdapter, "uniform"), (A.FIFOScorerAdapter, "fifo")):
+            other = cls(c)
+            other.observe_keys(0, K)
+            d[key] = other.select_hot_pages(0, q).numpy().astype(np.int64)
+        out[name] = d
+    return out
+
+
 def save(name: str, groups: dict) -> None:
     flat = {f"{case}/{key}": val for case, arrays in groups.items() for key, val in arrays.items()}
     path = os.path.join(I.HERE, name)
@@ -170,6 +195,7 @@ def save(name: str, groups: dict) -> None:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="path to the lzbaclz/HALO checkout")
+    ap.add_argument("--only", default="", help="regenerate one file (e.g. press)")
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
     warnings.filterwarnings("ignore")
@@ -183,6 +209,11 @@ def main() -> None:
     from halo.scorer import HALOScorer
     import baselines.kivi_cache as K
     import baselines.quest_path_d as Q
+    import baselines.scorer_ablations as A
+
+    if args.only == "press":
+        save("press.npz", gen_press(A))
+        return
 
     def make_cache(chunk, H_kv, D, dtype):
         cfg = HALOConfig(hot_ratio=0.25, tiers=("gpu", "dram"))

@@ -197,3 +197,40 @@ def test_oracle_scorer(name):
         # only exact-score ties may flip: compare the selected score multisets
         ref_pp = g["scores"].max(axis=(0, 1, 2))
         np.testing.assert_allclose(np.sort(per_page[top]), np.sort(ref_pp[ref_top]), rtol=1e-6)
+
+
+@pytest.mark.parametrize("name", list(I.PRESS_CASES))
+def test_oracle_press_scorer(name):
+    """HALOPress ablation scorer: page means bit-exact (bf16 / fp32), the
+    closed-form score's top-k equal to the reference's selection."""
+    g = I.load("press.npz")[name]
+    K, q, cfg = I.press_inputs(name)
+    assert g["digest"].item().decode() == I.digest(K, q)
+    dt = "bf16" if K.dtype == torch.bfloat16 else "f32"
+    km = OS.page_means(K.float().numpy(), cfg["page_size"], dtype=dt)
+    ref = OS.bf16_bits_to_f32(g["kmean_bits"]) if dt == "bf16" else g["kmean"]
+    np.testing.assert_array_equal(km, ref)
+    qg = OS.gqa_mean_query(q.float().numpy(), K.shape[1], dtype=dt)
+    sc = OS.press_scores(qg, km, alpha=cfg["halopress_alpha"], beta=cfg["halopress_beta"],
+                         gamma=cfg["halopress_gamma"], sink_tokens=cfg["halopress_sink_tokens"],
+                         refresh_window=cfg["halopress_refresh_window"],
+                         page_size=cfg["page_size"])
+    k = OS.num_hot_pages(sc.shape[0], cfg["memory_ratio"], cfg["min_pages_selected"])
+    np.testing.assert_array_equal(OS.topk_sorted(sc, k), g["topk"])
+
+
+@pytest.mark.parametrize("name", list(I.PRESS_CASES))
+def test_host_ablation_scorers_match_reference(name):
+    """The uniform-random and FIFO scorers are host index rules: identical
+    selections to the reference's for the same seed and page count."""
+    from halo_b200.baselines.scorer_ablations import (AblationScorerConfig, FIFOScorerAdapter,
+                                                      UniformRandomScorerAdapter)
+    g = I.load("press.npz")[name]
+    K, q, cfg = I.press_inputs(name)
+    c = AblationScorerConfig(**cfg)
+    for cls, key in ((UniformRandomScorerAdapter, "uniform"), (FIFOScorerAdapter, "fifo")):
+        ad = cls(c)
+        ad.observe_keys(0, K)
+        top = ad.select_hot_pages(0, q)
+        np.testing.assert_array_equal(top.numpy(), g[key])
+        assert ad.score_calls == 1 and ad.cumulative_hot_pages == len(g[key])

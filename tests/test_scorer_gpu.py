@@ -123,3 +123,43 @@ def test_topk_exclusion_and_large_page_count():
     masked = ref.copy()
     masked[excl] = -np.inf
     _assert_same_selection(top.numpy(), masked, len(top))
+
+
+@pytest.mark.parametrize("name", list(I.PRESS_CASES))
+def test_press_scorer_matches_oracle_and_reference(name):
+    """HALOPress ablation scorer on the GPU: page means bit-exact against the
+    oracle (same summation order) and the reference; the selection equal to
+    the reference's; pages summarised in two observe calls give the same
+    means as one."""
+    from halo_b200.baselines.scorer_ablations import AblationScorerConfig, HALOPressScorerAdapter
+    g = I.load("press.npz")[name]
+    K, q, cfg = I.press_inputs(name)
+    dt = "bf16" if K.dtype == torch.bfloat16 else "f32"
+    ad = HALOPressScorerAdapter(AblationScorerConfig(**cfg))
+    Kd = K.to("cuda")
+    half = (K.shape[-2] // cfg["page_size"] // 2) * cfg["page_size"]
+    ad.observe_keys(0, Kd[..., :half, :])           # first pages, then the rest
+    ad.observe_keys(0, Kd)
+    km = ad._k_mean[0].float().cpu().numpy()
+    ref = OS.page_means(K.float().numpy(), cfg["page_size"], dtype=dt)
+    np.testing.assert_array_equal(km, ref)
+    top = ad.select_hot_pages(0, q.to("cuda"))
+    assert top.device.type == "cpu" and top.dtype == torch.int64
+    np.testing.assert_array_equal(top.numpy(), g["topk"])
+    assert ad.score_calls == 1 and ad.cumulative_hot_pages == len(g["topk"])
+
+
+def test_magicpig_sampled_scorer_is_seeded_and_valid():
+    from halo_b200.baselines.scorer_ablations import (AblationScorerConfig,
+                                                      MagicPIGSampledScorerAdapter)
+    K, q, cfg = I.press_inputs("press_bf16_gqa4")
+    picks = []
+    for _ in range(2):
+        ad = MagicPIGSampledScorerAdapter(AblationScorerConfig(page_size=cfg["page_size"], seed=3))
+        ad.observe_keys(0, K.to("cuda"))
+        picks.append(ad.select_hot_pages(0, q.to("cuda")))
+    P = K.shape[-2] // cfg["page_size"]
+    top = picks[0]
+    assert torch.equal(picks[0], picks[1])
+    assert len(top) == ad._num_hot_pages(P) and len(set(top.tolist())) == len(top)
+    assert torch.equal(top, top.sort().values) and int(top.min()) >= 0 and int(top.max()) < P
