@@ -46,7 +46,6 @@ from __future__ import annotations
 
 import argparse
 import json
-import math
 import os
 import statistics
 import sys
@@ -623,7 +622,6 @@ def cpu_baseline_cfg4(budget_s: float = 15.0):
     """The reference's CPU decode step for cfg4 -- dequantise the whole
     prefix (its update() does so on every call) and attend in fp32 -- through
     the oracle port, on a sample of rows of one batch element, scaled."""
-    import numpy as np
     import torch
     from oracle import attention as OA
     from oracle import kivi as OK

@@ -8,7 +8,6 @@ import glob
 import os
 import re
 
-import pytest
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 

@@ -7,7 +7,6 @@ import math
 import os
 import random
 
-import numpy as np
 import pytest
 import torch
 

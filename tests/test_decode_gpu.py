@@ -10,7 +10,6 @@ from __future__ import annotations
 import math
 import random
 
-import numpy as np
 import pytest
 import torch
 

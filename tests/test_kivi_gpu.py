@@ -90,7 +90,7 @@ def test_packed_quantize_matches_c_oracle(c_oracle, dtype, bits):
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
 @pytest.mark.parametrize("bits,D", [(2, 128), (2, 64), (4, 128), (8, 64)])
 def test_fused_kivi_decode_matches_oracle(dtype, bits, D):
-    from halo_b200.baselines.kivi_cache import _Packed, dequantize_packed, kivi_decode
+    from halo_b200.baselines.kivi_cache import _Packed, kivi_decode
     g = torch.Generator().manual_seed(100 + bits + D)
     B, H, H_kv, T = 2, 16, 4, 1000
     k = torch.randn(B, H_kv, T, D, generator=g)

@@ -4,7 +4,6 @@ fp32 output within 2e-3 max-abs, LSE within 1e-4 (natural log), rows with no
 visible key give zeros and -inf, running-state folds equal one call."""
 from __future__ import annotations
 
-import math
 
 import pytest
 import torch

@@ -4,7 +4,6 @@ bit-exact, scores within fp32 summation-order noise, selected indices
 identical apart from exact score ties (relative gap < 1e-6)."""
 from __future__ import annotations
 
-import math
 
 import numpy as np
 import pytest

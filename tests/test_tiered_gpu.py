@@ -4,7 +4,6 @@ the output equals the oracle's attention over hot + selected chunks, and the
 delta refetch copies exactly the chunks that were not resident."""
 from __future__ import annotations
 
-import numpy as np
 import pytest
 import torch
 
