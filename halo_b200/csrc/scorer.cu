@@ -97,11 +97,11 @@ __global__ void __launch_bounds__(128) page_mean_kernel(const SummaryParams p) {
   const int page = p.page_begin + pg;
   const T* base = reinterpret_cast<const T*>(p.k) + b * p.sb + h * p.sh + (int64_t)page * p.page * p.st;
   T* out = reinterpret_cast<T*>(p.kmin) + b * p.ob + h * p.oh + (int64_t)page * p.op;
-  const float inv_n = (float)p.page;
+  const float n_rows = (float)p.page;
   for (int d = lane; d < p.D; d += 32) {
     float s = 0.f;
     for (int r = 0; r < p.page; ++r) s = __fadd_rn(s, ld_f32(base + (int64_t)r * p.st + d));
-    out[d] = st_elem<T>(__fdiv_rn(s, inv_n));
+    out[d] = st_elem<T>(__fdiv_rn(s, n_rows));
   }
 }
 
