@@ -139,6 +139,37 @@ def press_inputs(name):
     return K, q, cfg
 
 
+# ``HALO_OVERRIDES`` strings for ``parse_overrides`` (halo/policy.py:163-212):
+# plain literals, strings that are not literals, nested brackets, quoted
+# commas, escaped quotes, empty and key-less pairs, '=' inside a value.
+OVERRIDE_CASES = [
+    "",
+    "   ",
+    "hot_ratio=0.05",
+    "tiers=[gpu, dram]",
+    "tiers=['gpu','dram','nvme'],block_size=16",
+    " chunked=True , chunk_size=1024 ,recent_window=128 ",
+    "name='a,b',x=(1,2),y={'k': [1, 2]}",
+    "bad, z=3",
+    "path=/tmp/x=y",
+    "q=\"it's\"",
+    "a=1,,b=2",
+    "esc='a\\',b',c=4",
+    "nested=[[1,2],[3,(4,5)]],t=None,f=-1e-3",
+    "unknown_knob=7,hot_ratio=0.5",
+]
+
+# ``HALOConfig().with_overrides(d)`` inputs (halo/policy.py:139-155): known
+# fields are replaced, the rest lands in ``extra``.
+WITH_OVERRIDES_CASES = [
+    {},
+    {"hot_ratio": 0.25, "chunked": True},
+    {"tiers": ("gpu", "dram", "nvme"), "nvme_path": "/tmp/halo"},
+    {"mystery": 1, "another": "x"},
+    {"chunk_size": 2048, "mystery": [1, 2]},
+]
+
+
 def load(name: str) -> dict:
     """Load ``tests/golden/<name>.npz`` as ``{case: {key: array}}``."""
     out: dict = {}

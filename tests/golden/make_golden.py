@@ -7,9 +7,12 @@ Run in the build container, where a reference checkout is importable:
 It imports ``halo.kv_cache_chunked.HALOCacheChunked`` (``_chunk_attention``,
 ``_lse_merge``, ``compute_attention``), ``baselines.kivi_cache``
 (``_quantize_per_group`` / ``_dequantize_per_group``) and
-``baselines.quest_path_d._QuestScorerAdapter`` from the reference, runs them
-on the seeded inputs of ``tests/golden/inputs.py`` and stores their outputs
-plus an input digest in ``tests/golden/*.npz``.  The GPU box has no reference
+``baselines.quest_path_d._QuestScorerAdapter``, the ablation scorers of
+``baselines.scorer_ablations`` and ``halo.policy`` (``HALOConfig``,
+``parse_overrides``) from the reference, runs them on the seeded inputs of
+``tests/golden/inputs.py`` and stores their outputs plus an input digest in
+``tests/golden/*.npz`` (the policy results, as ``repr`` strings, in
+``tests/golden/policy.json``).  The GPU box has no reference
 checkout; tests only read the committed fixtures.
 """
 from __future__ import annotations
@@ -185,6 +188,29 @@ def gen_press(A) -> dict:
     return out
 
 
+def gen_policy(P) -> dict:
+    """The reference's ``HALOConfig`` defaults, ``parse_overrides`` and
+    ``with_overrides`` results, as ``repr`` strings (exact, JSON-safe)."""
+    import dataclasses
+    cfg = P.HALOConfig()
+    return {
+        "defaults": {f.name: repr(getattr(cfg, f.name)) for f in dataclasses.fields(cfg)},
+        "parse_overrides": [repr(P.parse_overrides(s)) for s in I.OVERRIDE_CASES],
+        "with_overrides": [
+            {f.name: repr(getattr(cfg.with_overrides(d), f.name)) for f in dataclasses.fields(cfg)}
+            for d in I.WITH_OVERRIDES_CASES],
+    }
+
+
+def save_json(name: str, obj: dict) -> None:
+    import json
+    path = os.path.join(I.HERE, name)
+    with open(path, "w") as f:
+        json.dump(obj, f, indent=1, sort_keys=True)
+        f.write("\n")
+    print(f"wrote {path}: {os.path.getsize(path) / 1024:.1f} KiB")
+
+
 def save(name: str, groups: dict) -> None:
     flat = {f"{case}/{key}": val for case, arrays in groups.items() for key, val in arrays.items()}
     path = os.path.join(I.HERE, name)
@@ -211,8 +237,13 @@ def main() -> None:
     import baselines.quest_path_d as Q
     import baselines.scorer_ablations as A
 
+    import halo.policy as P
+
     if args.only == "press":
         save("press.npz", gen_press(A))
+        return
+    if args.only == "policy":
+        save_json("policy.json", gen_policy(P))
         return
 
     def make_cache(chunk, H_kv, D, dtype):
@@ -232,6 +263,8 @@ def main() -> None:
     save("config1.npz", gen_config1(C))
     save("kivi.npz", gen_kivi(K))
     save("scorer.npz", gen_scorer(Q))
+    save("press.npz", gen_press(A))
+    save_json("policy.json", gen_policy(P))
 
 
 if __name__ == "__main__":
