@@ -1277,13 +1277,13 @@ struct MergeParams {
   float* o;
 };
 
-// One CTA of kMergeWarps warps per (b, h) row.  Pass 1: the row max M over
-// every partial (and the prior state).  Pass 2: warp w folds partials
-// s = w, w + kMergeWarps, ... with weights exp(m_s - M), eight partials in
-// flight per lane; the warps' sums are then combined through shared memory.
-// Four warps and at most 88 registers a thread, so a CTA fits beside two
-// split-KV CTAs on an SM: launched as a dependent, the merge's CTAs are
-// resident (waiting) while the split-KV kernel drains.
+// One CTA of kMergeWarps warps per (b, h) row: merge_partials folds the
+// row's partials (warp w takes s = w, w + kMergeWarps, ...; up to 40 of them,
+// 16 for rows wider than 128, in one memory round trip) with a running max,
+// and the warps' states are combined through shared memory; the prior state
+// is folded in last.  Four warps and at most 88 registers a thread, so a CTA
+// fits beside two split-KV CTAs on an SM: launched as a dependent, the
+// merge's CTAs are resident (waiting) while the split-KV kernel drains.
 constexpr int kMergeWarps = 4;
 
 template <int DPL, bool VEC>
@@ -1302,8 +1302,8 @@ __global__ void __maxnreg__(88) km_kernel(const MergeParams mp) {
   const bool active = d0 < mp.Dv;
   float M, L;
   float acc[DPL];
-  merge_partials<DPL, kMergeWarps, 10, VEC>(mr, lr, orow, mp.ps, mp.ops, mp.P, mp.Dv, s_m, s_l,
-                                            s_o, M, L, acc);
+  merge_partials<DPL, kMergeWarps, kMergeRound<DPL>, VEC>(mr, lr, orow, mp.ps, mp.ops, mp.P,
+                                                          mp.Dv, s_m, s_l, s_o, M, L, acc);
   if (threadIdx.x >= 32) return;
 
   // ---- warp 0: fold the prior state in and write
@@ -2280,8 +2280,15 @@ extern "C" int32_t halo_sharded_merge(int32_t B, int32_t H, int32_t Dv, int32_t 
                                       int64_t out_stride_b, int64_t out_stride_h, float* lse,
                                       halo_stream_t stream);
 
+namespace halo {
+int validate_exchange(int32_t B, int32_t H, int32_t Dv, int32_t P, const float* m_parts,
+                      const float* o_parts, int32_t world, int32_t rank, void* const* bufs,
+                      int32_t out_dtype, const void* out);
+}
+
 // The split-KV launch, then the fused cross-GPU merge (kx_kernel, launched
-// as a dependent so it is scheduled while the split-KV kernel drains).
+// as a dependent so it is scheduled while the split-KV kernel drains).  The
+// exchange arguments are checked before anything is launched.
 extern "C" int32_t halo_sharded_decode(const halo_decode_problem_t* problem,
                                        const halo_kv_chunk_t* chunks, int32_t n_chunks,
                                        void* workspace, int64_t workspace_bytes, int32_t world,
@@ -2290,12 +2297,16 @@ extern "C" int32_t halo_sharded_decode(const halo_decode_problem_t* problem,
                                        float* lse, halo_stream_t stream) {
   int rc = validate_problem(problem, chunks, n_chunks);
   if (rc != HALO_OK) return rc;
+  const halo_decode_problem_t& pb = *problem;
+  // P = 0 here: the partial arrays are the workspace's, placed below
+  rc = validate_exchange(pb.B, pb.H, pb.Dv, 0, nullptr, nullptr, world, rank, bufs, out_dtype,
+                         out);
+  if (rc != HALO_OK) return rc;
   int S = 0;
   float *m_part = nullptr, *l_part = nullptr, *o_part = nullptr;
   rc = decode_splits(problem, chunks, n_chunks, workspace, workspace_bytes,
                      static_cast<cudaStream_t>(stream), &S, &m_part, &l_part, &o_part);
   if (rc != HALO_OK) return rc;
-  const halo_decode_problem_t& pb = *problem;
   return halo_sharded_merge(pb.B, pb.H, pb.Dv, S, m_part, l_part, o_part, 1, S, pb.Dv,
                             (int64_t)S * pb.Dv, world, rank, bufs, out_dtype, out, out_stride_b,
                             out_stride_h, lse, stream);

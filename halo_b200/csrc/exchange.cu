@@ -97,14 +97,14 @@ __global__ void __maxnreg__(88) kx_kernel(const __grid_constant__ Params p) {
   const uint64_t tag = (uint64_t)epoch << 32;
 
   // ---- 1. local merge of this rank's P partials (one round trip when
-  // P <= 40), normalised into s_row: o then lse
+  // P <= 40, or 16 for rows wider than 128), normalised into s_row: o then lse
   const float* mr = p.m_parts + (int64_t)row * p.rs;
   const float* lr = p.l_parts ? p.l_parts + (int64_t)row * p.rs : nullptr;
   const float* orow = p.o_parts + (int64_t)row * p.ors;
   float M, L;
   float acc[DPL];
-  merge_partials<DPL, kWarps, 10, VEC>(mr, lr, orow, p.ps, p.ops, p.P, Dv, s_red, s_l, s_o, M, L,
-                                       acc);
+  merge_partials<DPL, kWarps, kMergeRound<DPL>, VEC>(mr, lr, orow, p.ps, p.ops, p.P, Dv, s_red,
+                                                     s_l, s_o, M, L, acc);
   if (warp == 0) {
     const int d0 = lane * DPL;
 #pragma unroll
@@ -210,6 +210,26 @@ __global__ void __maxnreg__(88) kx_kernel(const __grid_constant__ Params p) {
 }
 
 }  // namespace exchange
+
+// Host-side checks of a sharded merge's arguments, shared by
+// halo_sharded_merge and halo_sharded_decode (which runs them before it
+// launches the split-KV kernel).
+int validate_exchange(int32_t B, int32_t H, int32_t Dv, int32_t P, const float* m_parts,
+                      const float* o_parts, int32_t world, int32_t rank, void* const* bufs,
+                      int32_t out_dtype, const void* out) {
+  if (B <= 0 || H <= 0 || P < 0 || Dv <= 0 || Dv > 256)
+    return fail(HALO_ERR_INVALID_ARG, "bad merge shape");
+  if (world <= 0 || world > exchange::kMaxWorld || rank < 0 || rank >= world)
+    return fail(HALO_ERR_INVALID_ARG, "bad world %d / rank %d", world, rank);
+  if ((P > 0 && (!m_parts || !o_parts)) || !bufs || !out)
+    return fail(HALO_ERR_INVALID_ARG, "NULL pointer");
+  if (out_dtype != HALO_DTYPE_F32 && out_dtype != HALO_DTYPE_BF16 && out_dtype != HALO_DTYPE_F16)
+    return fail(HALO_ERR_INVALID_ARG, "bad out dtype %d", out_dtype);
+  for (int j = 0; j < world; ++j)
+    if (!bufs[j]) return fail(HALO_ERR_INVALID_ARG, "exchange buffer %d is NULL", j);
+  return HALO_OK;
+}
+
 }  // namespace halo
 
 using namespace halo;
@@ -268,14 +288,9 @@ extern "C" int32_t halo_sharded_merge(int32_t B, int32_t H, int32_t Dv, int32_t 
                                       void* const* bufs, int32_t out_dtype,
                                       void* out, int64_t out_stride_b, int64_t out_stride_h,
                                       float* lse, halo_stream_t stream) {
-  if (B <= 0 || H <= 0 || P < 0 || Dv <= 0 || Dv > 256)
-    return fail(HALO_ERR_INVALID_ARG, "bad merge shape");
-  if (world <= 0 || world > exchange::kMaxWorld || rank < 0 || rank >= world)
-    return fail(HALO_ERR_INVALID_ARG, "bad world %d / rank %d", world, rank);
-  if ((P > 0 && (!m_parts || !o_parts)) || !bufs || !out)
-    return fail(HALO_ERR_INVALID_ARG, "NULL pointer");
-  if (out_dtype != HALO_DTYPE_F32 && out_dtype != HALO_DTYPE_BF16 && out_dtype != HALO_DTYPE_F16)
-    return fail(HALO_ERR_INVALID_ARG, "bad out dtype %d", out_dtype);
+  const int rc = validate_exchange(B, H, Dv, P, m_parts, o_parts, world, rank, bufs, out_dtype,
+                                   out);
+  if (rc != HALO_OK) return rc;
   exchange::Params prm{};
   prm.m_parts = m_parts;
   prm.l_parts = l_parts;
@@ -290,10 +305,7 @@ extern "C" int32_t halo_sharded_merge(int32_t B, int32_t H, int32_t Dv, int32_t 
   prm.Dv = Dv;
   prm.world = world;
   prm.rank = rank;
-  for (int j = 0; j < world; ++j) {
-    if (!bufs[j]) return fail(HALO_ERR_INVALID_ARG, "exchange buffer %d is NULL", j);
-    prm.bufs[j] = static_cast<char*>(bufs[j]);
-  }
+  for (int j = 0; j < world; ++j) prm.bufs[j] = static_cast<char*>(bufs[j]);
   prm.out_dtype = out_dtype;
   prm.out = static_cast<char*>(out);
   prm.out_sb = out_stride_b;

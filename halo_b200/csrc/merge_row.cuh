@@ -18,7 +18,12 @@ namespace halo {
 // s_o [WARPS][DPL * 32]).  Every thread returns the row's M (natural log,
 // -inf if no partial has a key), L = sum_s l_s e^{m_s - M} and, for its
 // lane's columns d0 = lane * DPL ..., acc = sum_s e^{m_s - M} o_s.
-// With P <= WARPS * ROUND the whole row takes one round trip.
+// With P <= WARPS * ROUND the whole row takes one round trip.  A round
+// holds ROUND * (DPL + 2) loaded values per thread: kMergeRound<DPL> keeps
+// that within the merge kernels' 88-register budget for every row width.
+template <int DPL>
+constexpr int kMergeRound = DPL >= 8 ? 4 : 10;
+
 template <int DPL, int WARPS, int ROUND, bool VEC>
 __device__ __forceinline__ void merge_partials(const float* mr, const float* lr, const float* orow,
                                                int64_t ps, int64_t ops, int P, int Dv,

@@ -62,3 +62,77 @@ def test_invalid_arguments_are_reported_without_gpu():
     c.k_stride_b = c.v_stride_b = 128 * 8 * 4
     arr = (L.KVChunk * 1)(c)
     assert lib.halo_decode_workspace_bytes(ctypes.byref(prob), arr, 1) > 0
+
+
+def _valid_problem(L):
+    prob = L.DecodeProblem()
+    prob.B, prob.H, prob.H_kv, prob.D, prob.Dv, prob.dtype = 1, 8, 2, 128, 128, L.DTYPE_BF16
+    prob.q = 0x2000
+    prob.scale = 0.088
+    c = L.KVChunk()
+    c.k = c.v = 0x100000
+    c.k_stride_t = c.v_stride_t = 128
+    c.k_stride_h = c.v_stride_h = 128 * 64
+    c.k_stride_b = c.v_stride_b = 128 * 64 * 2
+    c.len = 64
+    return prob, (L.KVChunk * 1)(c)
+
+
+def test_exchange_arguments_are_checked_before_any_launch():
+    """halo_sharded_decode rejects a bad world / rank / buffer table before
+    it launches the split-KV kernel; on a host without a GPU any launch
+    would report HALO_ERR_CUDA instead."""
+    from halo_b200 import _lib as L
+    lib = L.lib()
+    assert lib.halo_exchange_bytes(2, 64, 128) == 2 * 2 * 64 * 130 * 8 + 16
+    for world, rows, dv in ((0, 64, 128), (9, 64, 128), (2, 0, 128), (2, 64, 257)):
+        assert lib.halo_exchange_bytes(world, rows, dv) == L.HALO_ERR_INVALID_ARG
+    prob, arr = _valid_problem(L)
+    bufs2 = (ctypes.c_void_p * 2)(0x4000, 0x8000)
+    null2 = (ctypes.c_void_p * 2)(0x4000, None)
+    out = 0x10000
+    cases = [
+        (0, 0, bufs2, L.DTYPE_F32, out),      # world 0
+        (2, 2, bufs2, L.DTYPE_F32, out),      # rank outside the world
+        (9, 0, bufs2, L.DTYPE_F32, out),      # more ranks than the exchange holds
+        (2, 1, null2, L.DTYPE_F32, out),      # a peer buffer missing
+        (2, 0, bufs2, 7, out),                # unknown output dtype
+        (2, 0, bufs2, L.DTYPE_F32, None),     # no output
+    ]
+    for world, rank, bufs, odt, o in cases:
+        rc = lib.halo_sharded_decode(ctypes.byref(prob), arr, 1, 0x30000, 1 << 20, world, rank,
+                                     bufs, odt, o, 1024, 128, None, None)
+        assert rc == L.HALO_ERR_INVALID_ARG, (world, rank, odt)
+        rc = lib.halo_sharded_merge(1, 8, 128, 4, 0x100, None, 0x200, 1, 4, 128, 512, world,
+                                    rank, bufs, odt, o, 1024, 128, None, None)
+        assert rc == L.HALO_ERR_INVALID_ARG, (world, rank, odt)
+    rc = lib.halo_sharded_merge(1, 8, 300, 4, 0x100, None, 0x200, 1, 4, 300, 1200, 2, 0, bufs2,
+                                L.DTYPE_F32, out, 2400, 300, None, None)
+    assert rc == L.HALO_ERR_INVALID_ARG
+
+
+def test_scorer_arguments_are_checked_before_any_launch():
+    from halo_b200 import _lib as L
+    lib = L.lib()
+    # page mean: bad page size, negative first page, unknown dtype
+    for page, begin, dt in ((0, 0, L.DTYPE_BF16), (16, -1, L.DTYPE_BF16), (16, 0, 9)):
+        rc = lib.halo_page_mean(0x1000, 0, 0, 0, 1, 2, 64, dt, page, begin, 4, 0x2000, 0, 0, 0,
+                                None)
+        assert rc == L.HALO_ERR_INVALID_ARG
+    # no pages: nothing to do, no launch
+    assert lib.halo_page_mean(0x1000, 0, 0, 0, 1, 2, 64, L.DTYPE_BF16, 16, 0, 0, 0x2000, 0, 0,
+                              0, None) == L.HALO_OK
+
+    def press(H, H_kv, P, k, n_sink=1, topk=0x5000):
+        return lib.halo_page_press_topk(0x1000, 0, 0, 0, 1, H, 1, H_kv, 64, L.DTYPE_BF16, 0x2000,
+                                        0, 0, 0, P, 1.0, 0.5, 2.0, 64, n_sink, 0x3000, k, None,
+                                        topk, None)
+    assert press(6, 4, 10, 2) == L.HALO_ERR_INVALID_ARG          # H not a multiple of H_kv
+    assert press(8, 2, 10, 11) == L.HALO_ERR_INVALID_ARG         # k > P
+    assert press(8, 2, 10, 2, n_sink=-1) == L.HALO_ERR_INVALID_ARG
+    assert press(8, 2, 10, 2, topk=None) == L.HALO_ERR_INVALID_ARG
+    assert press(8, 2, 8193, 2) == L.HALO_ERR_UNSUPPORTED        # top-k holds 8192 pages
+    assert press(8, 2, 0, 0) == L.HALO_OK
+    rc = lib.halo_page_score_topk(0x1000, 0, 0, 0, 1, 8, 1, 2, 64, L.DTYPE_BF16, 0x2000, 0x3000,
+                                  0, 0, 0, 16385, 0x4000, None, 4, None, 0x5000, None)
+    assert rc == L.HALO_ERR_UNSUPPORTED                          # top-k holds 16384 pages

@@ -227,6 +227,72 @@ def test_lse_merge_parts(cuda_device):
     assert (lse.cpu().double() - rl[:, :, 0]).abs().max().item() <= 1e-5
 
 
+def _random_parts(B, H, P, Dv, seed):
+    """Synthetic partial states (natural-log max m, weight l, unnormalised
+    output o), a few parts fully masked (m = -inf, l = 0, o = 0)."""
+    g = torch.Generator().manual_seed(seed)
+    m = torch.randn(B, H, P, generator=g) * 3
+    l = torch.rand(B, H, P, generator=g) * 50 + 0.5
+    o = torch.randn(B, H, P, Dv, generator=g) * l.unsqueeze(-1)
+    dead = torch.rand(B, H, P, generator=g) < 0.2
+    dead[..., 0] = False                      # every row keeps one live part
+    m[dead], l[dead] = float("-inf"), 0.0
+    o[dead] = 0.0
+    return m, l, o
+
+
+def _merge_f64(m, l, o):
+    md, ld, od = m.double(), l.double(), o.double()
+    M = md.amax(-1, keepdim=True)
+    w = torch.where(torch.isneginf(md), torch.zeros_like(md), torch.exp(md - M))
+    L = (w * ld).sum(-1)
+    return (w.unsqueeze(-1) * od).sum(-2) / L.unsqueeze(-1), M.squeeze(-1) + torch.log(L)
+
+
+@pytest.mark.parametrize("Dv", [192, 256])
+@pytest.mark.parametrize("P", [3, 37])
+def test_lse_merge_wide_rows(cuda_device, Dv, P):
+    """Rows wider than 128 columns (eight a lane, partials folded 16 per
+    memory round trip): the P-way merge equals a float64 merge."""
+    ops = _ops()
+    B, H = 2, 8
+    m, l, o = _random_parts(B, H, P, Dv, seed=Dv + P)
+    out, lse = ops.lse_merge(m.to(cuda_device), l.to(cuda_device), o.to(cuda_device))
+    ro, rl = _merge_f64(m, l, o)
+    assert (out.cpu().double() - ro).abs().max().item() <= 1e-5
+    assert (lse.cpu().double() - rl).abs().max().item() <= 1e-5
+
+
+@pytest.mark.parametrize("Dv", [128, 256])
+def test_sharded_merge_single_rank(cuda_device, Dv):
+    """halo_sharded_merge with a world of one (no peer traffic): the local
+    merge, the exchange through this rank's own buffer and the fold give
+    the plain merge; two calls cover both epoch parities of the buffer."""
+    import ctypes
+    from halo_b200 import _lib as L
+    lib = L.lib()
+    B, H, P = 1, 8, 21
+    m, l, o = _random_parts(B, H, P, Dv, seed=3 * Dv)
+    md, ld, od = (t.contiguous().to(cuda_device) for t in (m, l, o))
+    nbytes = lib.halo_exchange_bytes(1, B * H, Dv)
+    assert nbytes > 0
+    buf = torch.zeros(nbytes, dtype=torch.uint8, device=cuda_device)
+    bufs = (ctypes.c_void_p * 1)(buf.data_ptr())
+    ro, rl = _merge_f64(m, l, o)
+    for _ in range(2):
+        out = torch.full((B, H, Dv), float("nan"), device=cuda_device)
+        lse = torch.full((B, H), float("nan"), device=cuda_device)
+        rc = lib.halo_sharded_merge(B, H, Dv, P, md.data_ptr(), ld.data_ptr(), od.data_ptr(), 1, P,
+                                    Dv, P * Dv, 1, 0, bufs, L.DTYPE_F32, out.data_ptr(),
+                                    out.stride(0), out.stride(1), lse.data_ptr(),
+                                    L.stream_handle(cuda_device))
+        L.check(rc, "halo_sharded_merge")
+        torch.cuda.synchronize()
+        assert L.device_error() == 0
+        assert (out.cpu().double() - ro).abs().max().item() <= 1e-5
+        assert (lse.cpu().double() - rl).abs().max().item() <= 1e-5
+
+
 def test_large_context_properties(cuda_device):
     """Config-5-like context at reduced heads: chunk-order invariance and
     linearity in V (attention is linear in V for fixed q, k)."""
