@@ -1050,7 +1050,10 @@ struct alignas(64) KiviParams {
   float scale_log2;
 };
 
-template <typename T, int D, int BITS>
+// Packed-tile geometry of kk_kernel.  TR (the transposed tile math) runs
+// 4 CTAs per SM, whose shared memory leaves room for a 2-stage packed ring;
+// the other variant runs 2 CTAs per SM with 4 stages.
+template <typename T, int D, int BITS, bool TR = false>
 struct KGeom {
   using Gm = Geom<T, D, 1>;
   static constexpr int kCB = D * BITS / 8;        // code bytes per row
@@ -1058,7 +1061,7 @@ struct KGeom {
   static constexpr int kCodeTile = 64 * kCB;
   static constexpr int kSZTile = 64 * kGS * 2;
   static constexpr int kPackBytes = kCodeTile + 2 * kSZTile;
-  static constexpr int kStages = 4;
+  static constexpr int kStages = TR ? 2 : 4;
   static constexpr int kStageBytes = 2 * kPackBytes;
   static constexpr int kDqBytes = 2 * Gm::kTileBytes;
   static constexpr int kSmemBytes =
@@ -1139,9 +1142,9 @@ __device__ __forceinline__ void dequant_rows(const char* pack, char* dq) {
 
 // Tile provider: wait for a packed stage, dequantise this warp's rows of K
 // and V into the 16-bit tiles, free the packed stage at once.
-template <typename T, int D, int BITS>
+template <typename T, int D, int BITS, bool TR>
 struct DequantTiles {
-  using KG = KGeom<T, D, BITS>;
+  using KG = KGeom<T, D, BITS, TR>;
   char* stages;
   char* kdq;
   char* vdq;
@@ -1163,10 +1166,10 @@ struct DequantTiles {
   __device__ __forceinline__ void release(int) { __syncwarp(); }
 };
 
-// TR: transposed tile math (GQA groups of at most 8 q-heads), 3 CTAs per SM.
+// TR: transposed tile math (GQA groups of at most 8 q-heads), 4 CTAs per SM.
 template <typename T, int D, int BITS, bool TR>
-__global__ void __launch_bounds__(kThreads, TR ? 3 : 2) kk_kernel(const __grid_constant__ KiviParams p) {
-  using KG = KGeom<T, D, BITS>;
+__global__ void __launch_bounds__(kThreads, TR ? 4 : 2) kk_kernel(const __grid_constant__ KiviParams p) {
+  using KG = KGeom<T, D, BITS, TR>;
   using Gm = typename KG::Gm;
   constexpr int STAGES = KG::kStages;
   extern __shared__ char smem_raw[];
@@ -1248,7 +1251,7 @@ __global__ void __launch_bounds__(kThreads, TR ? 3 : 2) kk_kernel(const __grid_c
     if (!mbar_wait(&qfull[qs], (ut >> 1) & 1, p.err)) return;
     const int64_t qpos = (it.causal && p.q_pos != nullptr) ? p.q_pos[un.b] : INT64_MAX;
     const int n_tiles = (it.rows + kBlockN - 1) / kBlockN;
-    DequantTiles<T, D, BITS> tiles{stages, kdq, vdq, full, empty, p.err};
+    DequantTiles<T, D, BITS, TR> tiles{stages, kdq, vdq, full, empty, p.err};
     bool ok;
     if constexpr (TR)
       ok = consume_mma_t<T, D, STAGES>(p, un, it, tiles, qring + qs * Gm::kQSlotBytes, &qempty[qs],
@@ -2011,7 +2014,7 @@ static int encode_q_map(const halo_decode_problem_t& pb, CUtensorMap* out) {
 // ---------------------------------------------------------------- KIVI host side
 template <typename T, int D, int BITS, bool TR>
 static int kk_ctas_per_sm() {
-  using KG = KGeom<T, D, BITS>;
+  using KG = KGeom<T, D, BITS, TR>;
   static std::once_flag once[64];
   static int cache[64] = {0};
   int dev = 0;
@@ -2049,7 +2052,7 @@ static int kk_occupancy_for(int dtype, int D, int bits, int G) {
 
 template <typename T, int D, int BITS, bool TR>
 static int launch_kk(const KiviParams& prm, cudaStream_t st) {
-  using KG = KGeom<T, D, BITS>;
+  using KG = KGeom<T, D, BITS, TR>;
   const int64_t grid_max = (int64_t)device_sms() * kk_ctas_per_sm<T, D, BITS, TR>();
   const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(prm.n_units, grid_max));
   cudaError_t e =
