@@ -34,6 +34,7 @@
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <type_traits>
 #include <unordered_map>
 #include <vector>
 
@@ -463,18 +464,23 @@ __device__ __forceinline__ void mma_tile_t(float scale_log2, uint32_t kbase, uin
     }
   }
 
-  // ---- P^T = hi + lo, transposed into the B operand (keys x heads)
-  uint32_t bh[2], bl[2];
+  // ---- P^T transposed into the B operand (keys x heads).  fp16 keeps 11
+  // significant bits of P (relative error <= 2^-11) in one MMA; bf16 keeps
+  // 8, so its P is split into hi + lo (two MMAs, ~16 bits).
+  constexpr bool kSplitP = !std::is_same<T, __half>::value;
+  uint32_t bh[2], bl[2] = {0u, 0u};
   {
     const uint32_t h0 = Elem<T>::pack(p0, p1), h1 = Elem<T>::pack(p2, p3);
-    float x0, x1, x2, x3;
-    Elem<T>::unpack(h0, x0, x1);
-    Elem<T>::unpack(h1, x2, x3);
-    const uint32_t r0 = Elem<T>::pack(p0 - x0, p1 - x1), r1 = Elem<T>::pack(p2 - x2, p3 - x3);
     bh[0] = movmatrix_t(h0);
     bh[1] = movmatrix_t(h1);
-    bl[0] = movmatrix_t(r0);
-    bl[1] = movmatrix_t(r1);
+    if constexpr (kSplitP) {
+      float x0, x1, x2, x3;
+      Elem<T>::unpack(h0, x0, x1);
+      Elem<T>::unpack(h1, x2, x3);
+      const uint32_t r0 = Elem<T>::pack(p0 - x0, p1 - x1), r1 = Elem<T>::pack(p2 - x2, p3 - x3);
+      bl[0] = movmatrix_t(r0);
+      bl[1] = movmatrix_t(r1);
+    }
   }
 
   // ---- O^T += V^T P^T, 16 rows of d at a time
@@ -485,7 +491,7 @@ __device__ __forceinline__ void mma_tile_t(float scale_log2, uint32_t kbase, uin
       uint32_t a[4];
       ldsm_x4_t(vbase + swz<Gm::kInner>(key, i * 2 + ((lane >> 3) & 1)), a[0], a[1], a[2], a[3]);
       mma_16816(o[i], a, bh[0], bh[1], (T*)nullptr);
-      mma_16816(o[i], a, bl[0], bl[1], (T*)nullptr);
+      if constexpr (kSplitP) mma_16816(o[i], a, bl[0], bl[1], (T*)nullptr);
     }
   }
 }
