@@ -406,8 +406,93 @@ __device__ __forceinline__ void load_qT_frags(const char* qslot, uint32_t (&qb)[
             qb[kk][1], qb[kk + 1][0], qb[kk + 1][1]);
 }
 
+// ---- K-direct (2-bit codes, transposed tile math).  Thread (g, c) of a
+// warp (g = lane / 4, c = lane % 4) owns the K elements of its rows g and
+// g + 8 in head-dim columns [c*D/4, (c+1)*D/4): one quantisation group
+// (half of one for D = 64), so one 4-entry value table per row.  The S^T
+// MMAs take K in a permuted k order: logical column 2c + e + 8h of k-step kk
+// is head-dim column c*D/4 + 4kk + 2h + e.  A permutation of k leaves
+// sum_k K Q^T unchanged when Q^T is loaded in the same order, and in this
+// one a thread's A-fragment pairs are consecutive elements of its own
+// group: K is dequantised straight into A-operand registers, with no
+// shared-memory round trip.
+
+// Q^T fragments (B operand) in the permuted k order: qb[kk] holds head g's
+// columns c*D/4 + 4kk .. + 4, i.e. 16 consecutive bytes per two k-steps.
 template <typename T, int D, int STAGES>
-__device__ __forceinline__ void mma_tile_t(float scale_log2, uint32_t kbase, uint32_t vbase,
+__device__ __forceinline__ void load_qT_frags_perm(const char* qslot, uint32_t (&qb)[D / 16][2]) {
+  using Gm = Geom<T, D, STAGES>;
+  const int lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
+  const uint32_t base = smem_addr(qslot);
+#pragma unroll
+  for (int m = 0; m < D / 32; ++m)
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(qb[2 * m][0]), "=r"(qb[2 * m][1]), "=r"(qb[2 * m + 1][0]),
+                   "=r"(qb[2 * m + 1][1])
+                 : "r"(base + swz<Gm::kInner, Gm::kGpb>(g, c * (D / 32) + m)));
+}
+
+// This thread's packed K codes (rows g, g + 8; D/4 codes each, interleaved
+// as the packed format stores them: element 16w + 4k + b of a group at bit
+// 8b + 2k of word w) and the value tables {v0, v1 | v2, v3} of their group.
+template <int D>
+struct KRegs {
+  uint32_t words[2][D / 64];
+  uint32_t t01[2], t23[2];
+};
+
+template <typename T, int D>
+__device__ __forceinline__ void load_k_regs(const char* pack, int code_tile, int sz_tile,
+                                            KRegs<D>& kr) {
+  constexpr int kSpan = D / 4;          // head-dim columns of one thread
+  constexpr int kCB = D / 4;            // 2-bit code bytes per row
+  constexpr int kGS = D / 32;           // groups per row
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int g = lane >> 2, c = lane & 3;
+  const int gi = (c * kSpan) / 32;      // the thread's quantisation group
+  const uint32_t s_codes = smem_addr(pack) + c * (kSpan / 4);
+  const uint32_t s_sc = smem_addr(pack + code_tile) + 2 * gi;
+  const uint32_t s_ze = smem_addr(pack + code_tile + sz_tile) + 2 * gi;
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int row = warp * 16 + g + 8 * r;
+    if constexpr (D == 128)
+      asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];"
+                   : "=r"(kr.words[r][0]), "=r"(kr.words[r][1])
+                   : "r"(s_codes + row * kCB));
+    else
+      asm volatile("ld.shared.u32 %0, [%1];" : "=r"(kr.words[r][0]) : "r"(s_codes + row * kCB));
+    uint16_t sb, zb;
+    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(sb) : "r"(s_sc + row * kGS * 2));
+    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(zb) : "r"(s_ze + row * kGS * 2));
+    const float sc = Elem<T>::to_f32(*reinterpret_cast<const T*>(&sb));
+    const float z = Elem<T>::to_f32(*reinterpret_cast<const T*>(&zb));
+    kr.t01[r] = Elem<T>::pack(__fadd_rn(__fmul_rn(0.f, sc), z), __fadd_rn(sc, z));
+    kr.t23[r] = Elem<T>::pack(__fadd_rn(__fmul_rn(2.f, sc), z), __fadd_rn(__fmul_rn(3.f, sc), z));
+  }
+}
+
+// A fragments of k-step kk: elements 4kk .. 4kk+3 of the thread's span, rows
+// g (a0, a2) and g + 8 (a1, a3); c * 0x22 + 0x10 is the byte-permute
+// selector of value c's two bytes in the table.
+template <int D>
+__device__ __forceinline__ void k_frag(const KRegs<D>& kr, int kk, uint32_t (&a)[4]) {
+  const int w = kk >> 2, sh = 2 * (kk & 3);
+  uint32_t lo[2], hi[2];
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const uint32_t sel = ((kr.words[r][w] >> sh) & 0x03030303u) * 0x22u + 0x10101010u;
+    lo[r] = __byte_perm(kr.t01[r], kr.t23[r], sel);
+    hi[r] = __byte_perm(kr.t01[r], kr.t23[r], sel >> 16);
+  }
+  a[0] = lo[0];
+  a[1] = lo[1];
+  a[2] = hi[0];
+  a[3] = hi[1];
+}
+
+template <typename T, int D, int STAGES, class KFrag>
+__device__ __forceinline__ void mma_tile_t(float scale_log2, const KFrag& kfrag, uint32_t vbase,
                                            const uint32_t (&qb)[D / 16][2],
                                            float (&o)[D / 16][4], float& m0, float& m1, float& l0,
                                            float& l1, int valid, int64_t pos0, bool causal,
@@ -417,16 +502,14 @@ __device__ __forceinline__ void mma_tile_t(float scale_log2, uint32_t kbase, uin
   const int wrow = (threadIdx.x >> 5) * 16;
   const int g = lane >> 2;
 
-  // ---- S^T = K Q^T (16 keys x 8 heads)
+  // ---- S^T = K Q^T (16 keys x 8 heads); kfrag(kk, a) gives k-step kk's
+  // A fragments (the warp's 16 keys)
   float s[4] = {0.f, 0.f, 0.f, 0.f};
-  {
-    const int key = wrow + (lane & 15);
 #pragma unroll
-    for (int kk = 0; kk < D / 16; ++kk) {
-      uint32_t a[4];
-      ldsm_x4(kbase + swz<Gm::kInner>(key, kk * 2 + (lane >> 4)), a[0], a[1], a[2], a[3]);
-      mma_16816(s, a, qb[kk][0], qb[kk][1], (T*)nullptr);
-    }
+  for (int kk = 0; kk < D / 16; ++kk) {
+    uint32_t a[4];
+    kfrag(kk, a);
+    mma_16816(s, a, qb[kk][0], qb[kk][1], (T*)nullptr);
   }
 
   // ---- scale + mask: s[0], s[1] are key g, s[2], s[3] key g + 8
@@ -536,7 +619,10 @@ __device__ __forceinline__ bool consume_mma_t(const P& p, const Unit& un, const 
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   uint32_t qb[D / 16][2];
-  load_qT_frags<T, D, STAGES>(qslot, qb);
+  if constexpr (Tiles::kKDirect)
+    load_qT_frags_perm<T, D, STAGES>(qslot, qb);
+  else
+    load_qT_frags<T, D, STAGES>(qslot, qb);
   __syncwarp();
   if (lane == 0) mbar_arrive(qempty);
 
@@ -548,9 +634,21 @@ __device__ __forceinline__ bool consume_mma_t(const P& p, const Unit& un, const 
   for (int t = 0; t < n_tiles; ++t, ++gt) {
     uint32_t kbase, vbase;
     if (!tiles.acquire(t, gt, kbase, vbase)) { ok = false; ++gt; break; }
-    mma_tile_t<T, D, STAGES>(p.scale_log2, kbase, vbase, qb, o, m0, m1, l0, l1,
-                             it.rows - t * kBlockN, it.start + (int64_t)t * kBlockN,
-                             it.causal != 0, qpos);
+    const int valid = it.rows - t * kBlockN;
+    const int64_t pos0 = it.start + (int64_t)t * kBlockN;
+    if constexpr (Tiles::kKDirect) {
+      auto kf = [&](int kk, uint32_t (&a)[4]) { k_frag<D>(tiles.kr, kk, a); };
+      mma_tile_t<T, D, STAGES>(p.scale_log2, kf, vbase, qb, o, m0, m1, l0, l1, valid, pos0,
+                               it.causal != 0, qpos);
+    } else {
+      using Gm = Geom<T, D, STAGES>;
+      const int key = warp * 16 + (lane & 15);
+      auto kf = [&](int kk, uint32_t (&a)[4]) {
+        ldsm_x4(kbase + swz<Gm::kInner>(key, kk * 2 + (lane >> 4)), a[0], a[1], a[2], a[3]);
+      };
+      mma_tile_t<T, D, STAGES>(p.scale_log2, kf, vbase, qb, o, m0, m1, l0, l1, valid, pos0,
+                               it.causal != 0, qpos);
+    }
     tiles.release(gt);
   }
   store_partial_t<D>(p, un, it.slot + warp, o, m0, m1, l0, l1);
@@ -1057,8 +1155,11 @@ struct alignas(64) KiviParams {
 };
 
 // Packed-tile geometry of kk_kernel.  TR (the transposed tile math) runs
-// 4 CTAs per SM, whose shared memory leaves room for a 2-stage packed ring;
-// the other variant runs 2 CTAs per SM with 4 stages.
+// 4 CTAs per SM.  With 2-bit codes it dequantises K straight into MMA
+// registers (kKDirect) and keeps only the V tile in shared memory, which
+// leaves room for a 4-stage packed ring; with 4/8-bit codes both tiles are
+// staged and the ring has 2 stages.  The row-layout variant runs 2 CTAs per
+// SM with 4 stages.
 template <typename T, int D, int BITS, bool TR = false>
 struct KGeom {
   using Gm = Geom<T, D, 1>;
@@ -1067,9 +1168,10 @@ struct KGeom {
   static constexpr int kCodeTile = 64 * kCB;
   static constexpr int kSZTile = 64 * kGS * 2;
   static constexpr int kPackBytes = kCodeTile + 2 * kSZTile;
-  static constexpr int kStages = TR ? 2 : 4;
+  static constexpr bool kKDirect = TR && BITS == 2;
+  static constexpr int kStages = (TR && !kKDirect) ? 2 : 4;
   static constexpr int kStageBytes = 2 * kPackBytes;
-  static constexpr int kDqBytes = 2 * Gm::kTileBytes;
+  static constexpr int kDqBytes = (kKDirect ? 1 : 2) * Gm::kTileBytes;
   static constexpr int kSmemBytes =
       kDqBytes + 2 * Gm::kQSlotBytes + kStages * kStageBytes + 128 + 1024;
   static_assert(kPackBytes % 16 == 0, "bulk copies need 16-byte multiples");
@@ -1151,6 +1253,7 @@ __device__ __forceinline__ void dequant_rows(const char* pack, char* dq) {
 template <typename T, int D, int BITS, bool TR>
 struct DequantTiles {
   using KG = KGeom<T, D, BITS, TR>;
+  static constexpr bool kKDirect = false;
   char* stages;
   char* kdq;
   char* vdq;
@@ -1172,6 +1275,34 @@ struct DequantTiles {
   __device__ __forceinline__ void release(int) { __syncwarp(); }
 };
 
+// K-direct tile provider (2-bit, transposed): K's codes and value tables go
+// to registers (KRegs), V is dequantised into the 16-bit tile; the packed
+// stage is freed once both are done.
+template <typename T, int D>
+struct DequantTilesKD {
+  using KG = KGeom<T, D, 2, true>;
+  static constexpr bool kKDirect = true;
+  char* stages;
+  char* vdq;
+  uint64_t* full;
+  uint64_t* empty;
+  unsigned int* err;
+  KRegs<D> kr;
+  __device__ __forceinline__ bool acquire(int t, int gt, uint32_t& kbase, uint32_t& vbase) {
+    const int s = gt % KG::kStages;
+    if (!mbar_wait(&full[s], (gt / KG::kStages) & 1, err)) return false;
+    const char* st = stages + s * KG::kStageBytes;
+    load_k_regs<T, D>(st, KG::kCodeTile, KG::kSZTile, kr);
+    dequant_rows<T, D, 2>(st + KG::kPackBytes, vdq);
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) mbar_arrive(&empty[s]);
+    kbase = 0;
+    vbase = smem_addr(vdq);
+    return true;
+  }
+  __device__ __forceinline__ void release(int) { __syncwarp(); }
+};
+
 // TR: transposed tile math (GQA groups of at most 8 q-heads), 4 CTAs per SM.
 template <typename T, int D, int BITS, bool TR>
 __global__ void __launch_bounds__(kThreads, TR ? 4 : 2) kk_kernel(const __grid_constant__ KiviParams p) {
@@ -1179,9 +1310,10 @@ __global__ void __launch_bounds__(kThreads, TR ? 4 : 2) kk_kernel(const __grid_c
   using Gm = typename KG::Gm;
   constexpr int STAGES = KG::kStages;
   extern __shared__ char smem_raw[];
+  // 16-bit tiles (K then V; V only with K-direct) | q ring | packed ring
   char* kdq = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                       ~uintptr_t(1023));
-  char* vdq = kdq + Gm::kTileBytes;
+  char* vdq = KG::kKDirect ? kdq : kdq + Gm::kTileBytes;
   char* qring = kdq + KG::kDqBytes;
   char* stages = qring + 2 * Gm::kQSlotBytes;
   uint64_t* full = reinterpret_cast<uint64_t*>(stages + STAGES * KG::kStageBytes);
@@ -1257,14 +1389,20 @@ __global__ void __launch_bounds__(kThreads, TR ? 4 : 2) kk_kernel(const __grid_c
     if (!mbar_wait(&qfull[qs], (ut >> 1) & 1, p.err)) return;
     const int64_t qpos = (it.causal && p.q_pos != nullptr) ? p.q_pos[un.b] : INT64_MAX;
     const int n_tiles = (it.rows + kBlockN - 1) / kBlockN;
-    DequantTiles<T, D, BITS, TR> tiles{stages, kdq, vdq, full, empty, p.err};
     bool ok;
-    if constexpr (TR)
+    if constexpr (KG::kKDirect) {
+      DequantTilesKD<T, D> tiles{stages, vdq, full, empty, p.err, {}};
       ok = consume_mma_t<T, D, STAGES>(p, un, it, tiles, qring + qs * Gm::kQSlotBytes, &qempty[qs],
                                        n_tiles, gt, qpos);
-    else
+    } else if constexpr (TR) {
+      DequantTiles<T, D, BITS, TR> tiles{stages, kdq, vdq, full, empty, p.err};
+      ok = consume_mma_t<T, D, STAGES>(p, un, it, tiles, qring + qs * Gm::kQSlotBytes, &qempty[qs],
+                                       n_tiles, gt, qpos);
+    } else {
+      DequantTiles<T, D, BITS, TR> tiles{stages, kdq, vdq, full, empty, p.err};
       ok = consume_mma<T, D, STAGES>(p, un, it, tiles, qring + qs * Gm::kQSlotBytes, &qempty[qs],
                                      n_tiles, gt, qpos);
+    }
     if (!ok) return;
   }
 }
