@@ -17,9 +17,11 @@
 //     time from per-pair counters and writes one combined partial per CTA;
 //     kd_kernel splits them statically (fp32, short contexts, or a fixed
 //     max_split_rows, which is bit-reproducible).
-//   * kk: the same pipeline over KIVI-packed K/V, dequantised per tile in
-//     shared memory; GQA groups of at most 8 q-heads use transposed tile
-//     math (keys as the MMA rows).
+//   * kk: the same pipeline over KIVI-packed K/V, dequantised per tile; GQA
+//     groups of at most 8 q-heads use transposed tile math (keys as the MMA
+//     rows), where 2-bit K goes straight into MMA registers (a permuted k
+//     order gives each thread one quantisation group) and only V is staged
+//     as a 16-bit tile in shared memory.
 //   * km: one CTA per (b, q-head) row folds all partial states (and
 //     optionally a prior running state) into the final output + LSE, or
 //     into the running (m, l, o) accumulators of update_chunk.
