@@ -136,3 +136,60 @@ def test_scorer_arguments_are_checked_before_any_launch():
     rc = lib.halo_page_score_topk(0x1000, 0, 0, 0, 1, 8, 1, 2, 64, L.DTYPE_BF16, 0x2000, 0x3000,
                                   0, 0, 0, 16385, 0x4000, None, 4, None, 0x5000, None)
     assert rc == L.HALO_ERR_UNSUPPORTED                          # top-k holds 16384 pages
+
+
+def test_kivi_arguments_are_checked_before_any_launch():
+    from halo_b200 import _lib as L
+    lib = L.lib()
+
+    def quant(dtype=L.DTYPE_F16, bits=2, group=32, T=64, D=128):
+        return lib.halo_kivi_quantize(0x1000, 0, 0, 0, 1, 2, T, D, dtype, bits, group, 0x2000, 0,
+                                      0, 0, 0x3000, 0x4000, 0, 0, 0, None)
+    assert quant(dtype=L.DTYPE_F32) == L.HALO_ERR_UNSUPPORTED    # fp16 / bf16 only
+    assert quant(bits=3) == L.HALO_ERR_UNSUPPORTED
+    assert quant(group=48) == L.HALO_ERR_INVALID_ARG             # must divide D
+    assert quant(bits=2, group=8, D=64) == L.HALO_ERR_UNSUPPORTED   # 2-bit groups: x16
+    assert quant(T=0) == L.HALO_OK                               # nothing to do
+
+    prob = L.DecodeProblem()
+    prob.B, prob.H, prob.H_kv, prob.D, prob.Dv, prob.dtype = 1, 8, 2, 128, 128, L.DTYPE_F16
+    prob.q = 0x2000
+    kt = L.KiviTensor(0x10000, 0x20000, 0x30000, 64 * 32, 64 * 32, 64 * 4, 64 * 4, 64)
+    mg = L.MergeArgs()
+    mg.mode, mg.out_dtype, mg.out = L.MERGE_FINALIZE, L.DTYPE_F32, 0x40000
+
+    def decode(p=prob, k=kt, rows=64, bits=2, causal=0, merge=mg):
+        return lib.halo_kivi_decode(ctypes.byref(p), ctypes.byref(k), ctypes.byref(kt), rows, bits,
+                                    0, causal, 0x50000, 1 << 20, ctypes.byref(merge), None)
+    assert decode(bits=3) == L.HALO_ERR_UNSUPPORTED
+    assert decode(rows=65) == L.HALO_ERR_INVALID_ARG             # t_cap 64 does not cover 65
+    bad = L.KiviTensor(0x10008, 0x20000, 0x30000, 64 * 32, 64 * 32, 64 * 4, 64 * 4, 64)
+    assert decode(k=bad) == L.HALO_ERR_MISALIGNED
+    assert decode(causal=1) == L.HALO_ERR_INVALID_ARG            # causal needs q_pos
+    acc = L.MergeArgs()
+    acc.mode = L.MERGE_ACCUMULATE                                # without m, l, o
+    assert decode(merge=acc) == L.HALO_ERR_INVALID_ARG
+    p96 = L.DecodeProblem()
+    p96.B, p96.H, p96.H_kv, p96.D, p96.Dv, p96.dtype = 1, 8, 2, 96, 96, L.DTYPE_F16
+    assert decode(p=p96) == L.HALO_ERR_UNSUPPORTED               # head_dim 64 / 128 only
+
+
+def test_merge_arguments_are_checked_before_any_launch():
+    from halo_b200 import _lib as L
+    lib = L.lib()
+    mg = L.MergeArgs()
+    mg.mode, mg.out_dtype, mg.out = L.MERGE_FINALIZE, L.DTYPE_F32, 0x40000
+
+    def merge(B=1, H=8, Dv=128, P=4, m=0x100, o=0x200, args=mg):
+        return lib.halo_lse_merge(B, H, Dv, P, m, None, o, 1, P, Dv, P * Dv,
+                                  ctypes.byref(args), None)
+    assert merge(B=0) == L.HALO_ERR_INVALID_ARG
+    assert merge(m=None) == L.HALO_ERR_INVALID_ARG
+    assert merge(Dv=300) == L.HALO_ERR_UNSUPPORTED
+    assert merge(Dv=130) == L.HALO_ERR_UNSUPPORTED               # 5 columns a lane: no kernel
+    bad = L.MergeArgs()
+    bad.mode = 7
+    assert merge(args=bad) == L.HALO_ERR_INVALID_ARG
+    prior = L.MergeArgs()
+    prior.mode, prior.out_dtype, prior.out, prior.m = L.MERGE_FINALIZE, L.DTYPE_F32, 0x40000, 0x8
+    assert merge(args=prior) == L.HALO_ERR_INVALID_ARG           # m without l and o
