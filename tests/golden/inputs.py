@@ -170,6 +170,33 @@ WITH_OVERRIDES_CASES = [
 ]
 
 
+# Host control flow (halo/scorer.py, refetcher.py, demoter.py, kv_cache.py,
+# memory_tier.py): the configuration of the reference's unit-test fixtures,
+# hotness snapshots (K, step, seed) and a multi-step update_hotness trace.
+HOST_CONFIG = dict(hot_ratio=0.25, score_alpha=1.0, score_beta=0.5, score_gamma=2.0,
+                   sink_tokens=2, refresh_window=8, tiers=("gpu", "dram"), block_size=4,
+                   async_refetch=False, lookahead=1)
+HOST_SCORE_CASES = [(64, 0, 0), (64, 10, 1), (37, 100, 2), (5, 3, 3), (1, 0, 4), (200, 7, 5)]
+HOST_TRACE = dict(layers=2, K=64, steps=6, max_blocks=16, head_dim=8, kv_heads=2)
+
+
+def host_attention(K: int, seed: int) -> torch.Tensor:
+    """A head-mean attention snapshot: softmax of seeded N(0, 1) logits."""
+    g = torch.Generator().manual_seed(seed)
+    return torch.softmax(torch.randn(K, generator=g), dim=0)
+
+
+def host_trace_attention(step: int, layer: int, K: int) -> torch.Tensor:
+    """Trace snapshots: a window of extra mass sweeps the context (front to
+    back, then wraps), so hot sets change and blocks move both ways."""
+    base = host_attention(K, 1000 + 10 * step + layer)
+    focus = torch.zeros(K)
+    lo = (step * K // 4) % K
+    focus[lo:lo + K // 4] = 1.0
+    a = base + 4.0 * focus / focus.sum()
+    return a / a.sum()
+
+
 def load(name: str) -> dict:
     """Load ``tests/golden/<name>.npz`` as ``{case: {key: array}}``."""
     out: dict = {}

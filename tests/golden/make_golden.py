@@ -202,6 +202,56 @@ def gen_policy(P) -> dict:
     }
 
 
+def run_host_trace(mods, hot_ratio: float) -> dict:
+    """HALOCache.update_hotness over HOST_TRACE with a CPU TieredStorage:
+    telemetry and the tier directory after every call.  ``mods`` =
+    (HALOConfig, HALOScorer, HALODemoter, HALORefetcher, HALOCache,
+    MemoryTier, TieredStorage) of either implementation."""
+    Cfg, Scorer, Demoter, Refetcher, Cache, Tier, Storage = mods
+    tr = I.HOST_TRACE
+    cfg = Cfg(**{**I.HOST_CONFIG, "hot_ratio": hot_ratio})
+    st = Storage(tiers=[Tier.GPU, Tier.DRAM], num_layers=tr["layers"],
+                 num_kv_heads=tr["kv_heads"], head_dim=tr["head_dim"],
+                 block_size=cfg.block_size, dtype=torch.float32, device=torch.device("cpu"),
+                 max_blocks=tr["max_blocks"])
+    cache = Cache(config=cfg, storage=st, scorer=Scorer(cfg), demoter=Demoter(cfg, storage=st),
+                  refetcher=Refetcher(cfg, storage=st))
+    n_blocks = tr["K"] // cfg.block_size
+    out = []
+    for step in range(tr["steps"]):
+        for layer in range(tr["layers"]):
+            cache.update_hotness(layer, I.host_trace_attention(step, layer, tr["K"]))
+            out.append({"telemetry": cache.telemetry(),
+                        "directory": [st.locate_block(layer=layer, block=b)
+                                      for b in range(n_blocks)],
+                        "hot": cache._last_hot_indices[layer].tolist()})
+        cache.step()
+    return {"trace": out}
+
+
+def gen_host(mods) -> dict:
+    """The reference's host control flow: scorer snapshots (score, hot
+    sets, jaccard), refetcher predictions, and update_hotness traces."""
+    Cfg, Scorer, _, Refetcher = mods[:4]
+    cfg = Cfg(**I.HOST_CONFIG)
+    sc, rf = Scorer(cfg), Refetcher(cfg, storage=None)
+    snaps = []
+    for K, step, seed in I.HOST_SCORE_CASES:
+        a = I.host_attention(K, seed)
+        s = sc.score(a, step=step)
+        hot = sc.topk_hot(s)
+        snaps.append({"score": [float(x) for x in s.tolist()], "hot": hot.tolist(),
+                      "hot_half": sc.topk_hot(s, ratio=0.5).tolist(),
+                      "hot_all": sc.topk_hot(s, ratio=1.0).tolist(),
+                      "predicted": rf.predict_hot(layer=0, last_hot_indices=hot,
+                                                  last_score=s).tolist()})
+    jac = [sc.jaccard(torch.tensor(a, dtype=torch.long), torch.tensor(b, dtype=torch.long))
+           for a, b in (([], []), ([1, 2, 3], [2, 3, 4]), ([5], [6]), ([0, 1], [0, 1]))]
+    return {"snapshots": snaps, "jaccard": jac,
+            "trace_quarter": run_host_trace(mods, 0.25)["trace"],
+            "trace_identity": run_host_trace(mods, 1.0)["trace"]}
+
+
 def save_json(name: str, obj: dict) -> None:
     import json
     path = os.path.join(I.HERE, name)
@@ -242,8 +292,14 @@ def main() -> None:
     if args.only == "press":
         save("press.npz", gen_press(A))
         return
+    from halo.kv_cache import HALOCache as HC
+    host_mods = (HALOConfig, HALOScorer, HALODemoter, HALORefetcher, HC, MemoryTier,
+                 TieredStorage)
     if args.only == "policy":
         save_json("policy.json", gen_policy(P))
+        return
+    if args.only == "host":
+        save_json("host.json", gen_host(host_mods))
         return
 
     def make_cache(chunk, H_kv, D, dtype):
@@ -265,6 +321,7 @@ def main() -> None:
     save("scorer.npz", gen_scorer(Q))
     save("press.npz", gen_press(A))
     save_json("policy.json", gen_policy(P))
+    save_json("host.json", gen_host(host_mods))
 
 
 if __name__ == "__main__":
