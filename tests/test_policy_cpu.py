@@ -94,3 +94,22 @@ def test_chunked_cache_refuses_cpu_tensors():
     with pytest.raises(RuntimeError, match="CUDA"):
         m.generate(ids, attention_mask=torch.ones_like(ids), max_new_tokens=2, do_sample=False,
                    pad_token_id=0)
+
+
+def test_unchunked_wrap_is_identity_at_full_hot_ratio():
+    """Path A (``HALOCache``, no chunking) passes the ``DynamicCache`` rows
+    through untouched: greedy decoding with the wrapped model equals the
+    unwrapped one (the identity claim of the reference's
+    ``tests/test_integration_identity.py``, on a random-weight model)."""
+    base = _tiny_llama()
+    ids = torch.randint(0, 64, (1, 24), generator=torch.Generator().manual_seed(3))
+    mask = torch.ones_like(ids)
+    with torch.no_grad():
+        want = base.generate(ids, attention_mask=mask, max_new_tokens=8, do_sample=False,
+                             pad_token_id=0)
+    m = wrap_with_halo(_tiny_llama(), HALOConfig(hot_ratio=1.0))
+    assert type(m._halo_cache).__name__ == "HALOCache"
+    with torch.no_grad():
+        got = m.generate(ids, attention_mask=mask, max_new_tokens=8, do_sample=False,
+                         pad_token_id=0)
+    assert torch.equal(got, want)
