@@ -214,11 +214,10 @@ class ShardedDecoder:
 
     @property
     def launches_per_call(self) -> int:
-        """Kernels of this library per call (at most): split-KV + merge on
-        one GPU, split-KV + exchange merge (p2p) or split-KV + local merge +
-        merge of the gathered parts (nccl) when sharded.  With the dynamic
-        schedule the split-KV kernel merges (and exchanges) itself: one
-        launch per call, counted by ``halo_launch_count``."""
+        """Kernels of this library per call, as counted by
+        ``halo_launch_count``: split-KV + merge on one GPU, split-KV +
+        exchange merge (p2p) or split-KV + local merge + merge of the
+        gathered parts (nccl) when sharded."""
         if self.world == 1:
             return 2
         return 2 if self.exchange == "p2p" else 3
