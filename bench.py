@@ -63,12 +63,11 @@ METRIC = "decode-attn tokens/s & achieved HBM GB/s at 32K-1M ctx, 1/2/4/8 B200"
 # DRAM traffic per algorithmic byte, from one ncu capture of each kernel
 # (dram__bytes_read.sum + dram__bytes_write.sum of the launch over the bytes
 # it must read); the captures and their commands are summarised under
-# profiles/.  kd_kernel: cfg5 reduced to 262144 tokens (1.0738 GB read +
-# 5.3 MB written over 1.0737 GB), scaled to a full launch by the K/V bytes it
-# processes.  kk_kernel: the cfg4 launch itself (201.0 MB + 4.8 MB over
-# 200.9 MB).
+# profiles/.  kd_dyn_kernel: cfg5 reduced to 262144 tokens, scaled to a full
+# launch by the K/V bytes it processes.  kk_kernel: the cfg4 launch itself
+# (transposed tile math; 201.0 MB read + 7.4 MB written over 200.9 MB).
 NCU_TRAFFIC_RATIO = 1.0040      # kd_dyn_kernel, ncu at 262144 tokens: (1073.795 + 4.311) MB read+write / 1073.742 MB algorithmic
-NCU_TRAFFIC_RATIO_KK = 1.0243
+NCU_TRAFFIC_RATIO_KK = 1.0373
 
 
 def _tensor_peak():
