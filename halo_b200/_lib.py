@@ -20,6 +20,7 @@ HALO_ERR_MISALIGNED = -3
 HALO_ERR_CUDA = -4
 HALO_ERR_TIMEOUT = -5
 HALO_ERR_WORKSPACE = -6
+HALO_ERR_SPLIT = -7
 
 DTYPE_F32, DTYPE_BF16, DTYPE_F16 = 0, 1, 2
 MERGE_FINALIZE, MERGE_ACCUMULATE = 0, 1

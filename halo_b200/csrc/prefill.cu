@@ -711,6 +711,50 @@ static int launch_kp2(const prefill::Params& prm, int grid, cudaStream_t st) {
   return HALO_OK;
 }
 
+// One coalesced run of chunks: the first chunk's pointers, strides, start
+// and causal flag, its total length and whether the batch broadcasts.
+struct PfSeg {
+  halo_kv_chunk_t c;
+  int64_t len;
+  bool bcast;
+};
+
+// K/V tiles of a segment visible to query positions <= qmax (host copy of
+// prefill::seg_tiles).
+static int pf_seg_tiles(const PfSeg& sg, int64_t qmax) {
+  int64_t n = (sg.len + prefill::kBN - 1) / prefill::kBN;
+  if (sg.c.causal) {
+    const int64_t lim = qmax - sg.c.start;
+    if (lim < 0) return 0;
+    n = std::min<int64_t>(n, lim / prefill::kBN + 1);
+  }
+  return (int)n;
+}
+
+// Whether every query-tile pair (A, B) of the call sees, along the union
+// walk of its K/V tiles, at most one tile in a row that A sits out.  A run
+// of two or more can stall A's MMA issuer: it waits for the K tile after the
+// run while the producer, one ring stage later, waits for A's pending P V
+// to free a V stage.  Within one segment A sits out at most the last tile
+// (query tiles are 128 rows, K/V tiles 128 keys apart), so runs only form
+// across segments.
+static bool pf_order_ok(const PfSeg* segs, int n, int T_q, int64_t q_pos0) {
+  const int n_qtiles = (T_q + prefill::kBM - 1) / prefill::kBM;
+  for (int pair = 0; 2 * pair + 1 < n_qtiles; ++pair) {
+    const int qA0 = 2 * pair * prefill::kBM;
+    const int64_t qmaxA = q_pos0 + qA0 + prefill::kBM - 1;   // A is full when B exists
+    const int validB = std::min(prefill::kBM, T_q - (qA0 + prefill::kBM));
+    const int64_t qmaxB = q_pos0 + qA0 + prefill::kBM + validB - 1;
+    int64_t run = 0;
+    for (int i = 0; i < n; ++i) {
+      const int ntU = pf_seg_tiles(segs[i], qmaxB), ntA = pf_seg_tiles(segs[i], qmaxA);
+      run = (ntA > 0 ? 0 : run) + (ntU - ntA);
+      if (run > 1) return false;
+    }
+  }
+  return true;
+}
+
 }  // namespace halo
 
 using namespace halo;
@@ -755,6 +799,7 @@ extern "C" int32_t halo_prefill_attention(const halo_prefill_problem_t* pb,
 
   // ---- segments: coalesce chunks contiguous in memory and position
   static thread_local prefill::Params prm;
+  PfSeg segs[prefill::kMaxSegs];
   int n_seg = 0;
   halo_kv_chunk_t cur{};
   int64_t cur_len = 0;
@@ -765,23 +810,7 @@ extern "C" int32_t halo_prefill_attention(const halo_prefill_problem_t* pb,
                   prefill::kMaxSegs);
     const bool bk = cur.k_stride_b == 0, bv = cur.v_stride_b == 0;
     if (bk != bv) return fail(HALO_ERR_INVALID_ARG, "k and v must both broadcast the batch or neither");
-    const uint64_t dims[4] = {(uint64_t)D, (uint64_t)cur_len, (uint64_t)pb->H_kv,
-                              (uint64_t)(bk ? 1 : pb->B)};
-    const uint64_t ks[3] = {(uint64_t)cur.k_stride_t * 2, (uint64_t)cur.k_stride_h * 2,
-                            (uint64_t)(bk || pb->B == 1 ? cur.k_stride_h * 2 * pb->H_kv
-                                                        : cur.k_stride_b * 2)};
-    const uint64_t vs[3] = {(uint64_t)cur.v_stride_t * 2, (uint64_t)cur.v_stride_h * 2,
-                            (uint64_t)(bv || pb->B == 1 ? cur.v_stride_h * 2 * pb->H_kv
-                                                        : cur.v_stride_b * 2)};
-    int rc = pf_encode(cur.k, pb->dtype, dims, ks, &prm.kmap[n_seg]);
-    if (rc != HALO_OK) return rc;
-    rc = pf_encode(cur.v, pb->dtype, dims, vs, &prm.vmap[n_seg]);
-    if (rc != HALO_OK) return rc;
-    prm.seg[n_seg].start = cur.start;
-    prm.seg[n_seg].len = (int32_t)cur_len;
-    prm.seg[n_seg].causal = cur.causal ? 1 : 0;
-    prm.seg[n_seg].bcast = bk ? 1 : 0;
-    ++n_seg;
+    segs[n_seg++] = PfSeg{cur, cur_len, bk};
     cur_len = 0;
     return HALO_OK;
   };
@@ -805,6 +834,29 @@ extern "C" int32_t halo_prefill_attention(const halo_prefill_problem_t* pb,
   }
   int rc = flush();
   if (rc != HALO_OK) return rc;
+  if (!pf_order_ok(segs, n_seg, pb->T_q, pb->q_pos0))
+    return fail(HALO_ERR_SPLIT, "chunk order: a query tile would sit out two or more K/V tiles "
+                "in a row; pass the chunks in smaller calls");
+  for (int i = 0; i < n_seg; ++i) {
+    const halo_kv_chunk_t& c = segs[i].c;
+    const bool bk = segs[i].bcast;
+    const uint64_t dims[4] = {(uint64_t)D, (uint64_t)segs[i].len, (uint64_t)pb->H_kv,
+                              (uint64_t)(bk ? 1 : pb->B)};
+    const uint64_t ks[3] = {(uint64_t)c.k_stride_t * 2, (uint64_t)c.k_stride_h * 2,
+                            (uint64_t)(bk || pb->B == 1 ? c.k_stride_h * 2 * pb->H_kv
+                                                        : c.k_stride_b * 2)};
+    const uint64_t vs[3] = {(uint64_t)c.v_stride_t * 2, (uint64_t)c.v_stride_h * 2,
+                            (uint64_t)(bk || pb->B == 1 ? c.v_stride_h * 2 * pb->H_kv
+                                                        : c.v_stride_b * 2)};
+    rc = pf_encode(c.k, pb->dtype, dims, ks, &prm.kmap[i]);
+    if (rc != HALO_OK) return rc;
+    rc = pf_encode(c.v, pb->dtype, dims, vs, &prm.vmap[i]);
+    if (rc != HALO_OK) return rc;
+    prm.seg[i].start = c.start;
+    prm.seg[i].len = (int32_t)segs[i].len;
+    prm.seg[i].causal = c.causal ? 1 : 0;
+    prm.seg[i].bcast = bk ? 1 : 0;
+  }
 
   // ---- Q map {D, T_q, H, B}
   {

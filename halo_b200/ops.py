@@ -302,7 +302,9 @@ def prefill_attention(q: torch.Tensor, chunks: Sequence[tuple], *, query_pos_off
     ``state = (m, l, o)``: fp32 running state, ``m, l (B, H, T_q)`` and
     ``o (B, H, T_q, D)`` contiguous.  ``accumulate=True`` folds the chunks
     into it in place and returns ``None``; otherwise the state (if given) is
-    folded in and ``(out (B, H, T_q, D), lse (B, H, T_q))`` is returned."""
+    folded in and ``(out (B, H, T_q, D), lse (B, H, T_q))`` is returned.
+    Lists longer than one call takes, or in an order the kernel refuses
+    (``HALO_ERR_SPLIT``), run as several calls through a running state."""
     _require_cuda(q, "q")
     B, H, T_q, D = q.shape
     if q.stride(-1) != 1:
@@ -325,8 +327,10 @@ def prefill_attention(q: torch.Tensor, chunks: Sequence[tuple], *, query_pos_off
         if lse is None:
             lse = torch.empty(B, H, T_q, dtype=torch.float32, device=q.device)
     lib = L.lib()
-    for gi, grp in enumerate(groups):
-        last = gi == len(groups) - 1
+    pending = list(groups)
+    while pending:
+        grp = pending.pop(0)
+        last = not pending
         prob = L.PrefillProblem()
         prob.B, prob.H, prob.H_kv, prob.T_q, prob.D = B, H, H_kv, T_q, D
         prob.dtype = L.halo_dtype(q.dtype)
@@ -359,6 +363,16 @@ def prefill_attention(q: torch.Tensor, chunks: Sequence[tuple], *, query_pos_off
         with torch.cuda.device(q.device):
             rc = lib.halo_prefill_attention(ctypes.byref(prob), arr, len(structs), ctypes.byref(po),
                                             L.stream_handle(q.device))
+        if rc == L.HALO_ERR_SPLIT and len(grp) > 1:
+            # a chunk order that could stall the kernel (refused before any
+            # launch): one chunk per call, through a running state
+            if state is None:
+                state = (torch.full((B, H, T_q), float("-inf"), dtype=torch.float32,
+                                    device=q.device),
+                         torch.zeros(B, H, T_q, dtype=torch.float32, device=q.device),
+                         torch.zeros(B, H, T_q, D, dtype=torch.float32, device=q.device))
+            pending = [[c] for c in grp] + pending
+            continue
         L.check(rc, "halo_prefill_attention")
     return None if accumulate else (out, lse)
 

@@ -42,6 +42,7 @@ extern "C" {
 #define HALO_ERR_CUDA (-4)          /* a CUDA runtime call failed            */
 #define HALO_ERR_TIMEOUT (-5)       /* a device-side bounded wait expired    */
 #define HALO_ERR_WORKSPACE (-6)     /* workspace missing or too small        */
+#define HALO_ERR_SPLIT (-7)         /* pass the chunks in smaller calls      */
 
 /* ------------------------------------------------------------------ dtypes */
 #define HALO_DTYPE_F32 0
@@ -374,6 +375,14 @@ typedef struct halo_prefill_out {
   float* o;
 } halo_prefill_out_t;
 
+/* Chunk order: the two query tiles of a CTA walk the union of their K/V
+ * tiles, and the earlier tile sits out the tiles only the later one can see.
+ * A run of two or more such tiles in a row can stall the earlier tile's MMA
+ * issuer behind the shared K/V ring (it would end in HALO_ERR_TIMEOUT), so a
+ * call whose coalesced segments produce one is refused with HALO_ERR_SPLIT
+ * before anything is launched.  Chunks in increasing position, contiguous
+ * chunks and single-chunk calls never produce one; otherwise pass the chunks
+ * in smaller calls and carry the running state (the Python wrapper does). */
 int32_t halo_prefill_attention(const halo_prefill_problem_t* problem,
                                const halo_kv_chunk_t* chunks, int32_t n_chunks,
                                const halo_prefill_out_t* out, halo_stream_t stream);
