@@ -71,10 +71,8 @@ constexpr int kConsumerWarps = 4;    // each owns 16 rows of every stage
 constexpr int kThreads = (kConsumerWarps + 1) * 32;
 constexpr int kMaxSegs = 48;         // tensor-map pairs per launch
 constexpr int kMaxItems = 512;       // work items per launch
-// Control block at the start of every decode workspace: the dynamic
-// schedule's per-pair piece counters and its exit counter.  It must be zero
-// before a workspace's first use; every call leaves it zero.
-constexpr int64_t kCtrlBytes = 4096;
+// kCtrlBytes (halo_common.cuh): the control block at the start of every
+// decode workspace.
 constexpr int kMaxDynPairs = (int)(kCtrlBytes / 4) - 1;
 constexpr int kPieceTiles = 2;       // 64-row tiles per piece of the dynamic schedule
 

@@ -40,6 +40,11 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 // Wall-clock limit of every bounded wait (nanoseconds).
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
 
+// Control block at the start of every decode workspace: the dynamic
+// schedule's per-pair piece counters and its exit counter.  It must be zero
+// before a workspace's first use; every call that completes leaves it zero.
+constexpr int64_t kCtrlBytes = 4096;
+
 // System-scope relaxed 64-bit accesses (peer GPU memory through NVLink): an
 // aligned 64-bit access is single-copy atomic.
 __device__ __forceinline__ uint64_t ld_relaxed_sys(const uint64_t* p) {

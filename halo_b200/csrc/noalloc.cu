@@ -14,9 +14,13 @@
 //    is enqueued; use halo_chunked_decode with a caller workspace instead.
 //  * Every GPU that loads the library keeps this array until process exit.
 //  * All calls on a device share the one array and it keeps the last call's
-//    contents.  Nothing in it has to start at zero: each call writes every
-//    partial it later reads.  Calls whose work overlaps on the GPU (other
-//    streams, other host threads) race on the array; serialise them.
+//    contents.  Its first 4096 bytes are the split-KV scheduler's counters,
+//    which must be zero when a call starts: each call clears them on its
+//    stream (cudaMemsetAsync, no allocation) before the kernels, so a call
+//    that ended early (a timed-out wait) cannot leave stale counters for the
+//    next.  The partials after them are written before they are read.
+//    Calls whose work overlaps on the GPU (other streams, other host
+//    threads) race on the array; serialise them.
 //  * The first call on each device looks up the array's device address
 //    (cudaGetSymbolAddress, with that device current).  Make that first call
 //    before any stream capture.
@@ -81,6 +85,9 @@ extern "C" int32_t halo_chunked_decode_noalloc(const halo_decode_problem_t* prob
                       (long long)need, (long long)halo::kNoAllocScratchBytes);
   void* ptr = halo::scratch_ptr();
   if (!ptr) return HALO_ERR_CUDA;
+  cudaError_t e = cudaMemsetAsync(ptr, 0, halo::kCtrlBytes,
+                                  static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return halo::cuda_fail(e, "clear no-alloc scratch counters");
   return halo_chunked_decode(problem, chunks, n_chunks, ptr, halo::kNoAllocScratchBytes, merge,
                              stream);
 }

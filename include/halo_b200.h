@@ -156,9 +156,10 @@ int32_t halo_lse_merge(int32_t B, int32_t H, int32_t Dv, int32_t P,
  * callers without an allocator.  Problems needing more than 8 MiB of scratch
  * (halo_decode_workspace_bytes) are rejected with HALO_ERR_WORKSPACE.  Every
  * GPU that loads the library holds the array until exit.  All calls on a
- * device share it, so calls that overlap on the GPU race: serialise them.
- * The first call on each device looks up the array's address (make it before
- * any stream capture). */
+ * device share it and it keeps the last call's contents; each call clears
+ * its leading scheduler counters on `stream` before the kernels.  Calls that
+ * overlap on the GPU race: serialise them.  The first call on each device
+ * looks up the array's address (make it before any stream capture). */
 int32_t halo_chunked_decode_noalloc(const halo_decode_problem_t* problem,
                                     const halo_kv_chunk_t* chunks, int32_t n_chunks,
                                     const halo_merge_args_t* merge, halo_stream_t stream);

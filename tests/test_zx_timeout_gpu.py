@@ -5,8 +5,8 @@ whose second rank never runs: the rows it should store into this rank's
 exchange buffer never arrive.  The kernel's polls are bounded (2 s of
 ``%globaltimer``); on expiry it records ``HALO_ERR_TIMEOUT`` in the device
 error word, writes no output and returns.  The host reads the status, and the
-context stays usable for the next call.  Runs last: it holds the GPU for the
-length of the wait."""
+context stays usable for the next call.  Collected near the end (it holds
+the GPU for the length of the wait); the no-alloc test comes after it."""
 from __future__ import annotations
 
 import ctypes
