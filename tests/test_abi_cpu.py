@@ -230,6 +230,8 @@ def test_prefill_refuses_chunk_orders_that_could_stall():
     rc = lib.halo_prefill_attention(ctypes.byref(prob), risky, 3, ctypes.byref(po), None)
     assert rc == L.HALO_ERR_SPLIT
     assert b"chunk order" in lib.halo_last_error_string()
-    fine = (L.KVChunk * 2)(old, pg1)
-    rc = lib.halo_prefill_attention(ctypes.byref(prob), fine, 2, ctypes.byref(po), None)
-    assert rc != L.HALO_ERR_SPLIT
+    import torch
+    if not torch.cuda.is_available():      # with a GPU this would launch on fake pointers
+        fine = (L.KVChunk * 2)(old, pg1)
+        rc = lib.halo_prefill_attention(ctypes.byref(prob), fine, 2, ctypes.byref(po), None)
+        assert rc != L.HALO_ERR_SPLIT
