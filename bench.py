@@ -1,42 +1,47 @@
 """Benchmark of the HALO chunked-attention hot path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload cfg5|cfg2]
+                    [--workload all|cfg5|cfg2|cfg3|cfg4] [--no-cpu-baseline]
 
-Default workload (all N): BASELINE config 5 -- 1M-token sequence-sharded
-decode of one Llama-3-70B-shaped attention layer (B1, 64 q-heads / 8 KV
-heads, head_dim 128, bf16, 256 chunks of 4096 rows).  Rank r of N owns a
-contiguous 1/N of the chunks; a step is one decode query: split-KV kernel over
-the local chunks, then one fused kernel that merges the local splits, pushes
-the fp32 (o, lse) row to every rank over NVLink peer stores and merges the N
-parts (halo_sharded_merge).
-Total context is fixed as N grows (strong scaling).  K/V are seeded N(0,1)
-synthetic data resident in HBM; the working set per GPU (4.3 GB / N) is far
-larger than L2, so no flush is needed between steps.
+Headline workload (all N): 1M-token sequence-sharded decode of one
+Llama-3-70B-shaped attention layer (B1, 64 q-heads / 8 KV heads, head_dim
+128, bf16, 256 chunks of 4096 rows).  Rank r of N owns a contiguous 1/N of
+the chunks; a step is one decode query: split-KV kernel over the local
+chunks, then one fused kernel that merges the local splits, pushes the fp32
+(o, lse) row to every rank over NVLink peer stores and merges the N parts
+(halo_sharded_merge).  Total context is fixed as N grows (strong scaling).
+K/V are seeded N(0,1) synthetic data resident in HBM; the working set per
+GPU (4.3 GB / N) is far larger than L2, so no flush is needed between steps.
+After timing, one KV-head group of the last output is checked against a
+float64 attention (``parity`` in the line).
+
+With N = 1 the default run (``--workload all``) also measures the other
+three workloads and reports them under ``workloads`` in the same line:
+
+* ``cfg2`` -- tiered decode: 32 layers of B8 / 32 q-heads / 8 KV heads /
+  32K context in chunks of 1024; hot chunks (first + 7 most recent) in HBM,
+  24 cold chunks per layer in pinned host DRAM; per layer and step the chunk
+  scorer picks the top-8 cold chunks for a fresh query, the ones not already
+  in the layer's GPU slot cache are refetched on a copy stream while the hot
+  chunks are attended, then the selected chunks are folded in
+  (``halo_b200.tiered.TieredLayer``);
+* ``cfg3`` -- chunked prefill of a 131072-token prompt in 32 slices of 4096
+  queries against the accumulated KV, causal, 32 q-heads / 8 KV heads,
+  head_dim 128, on the tcgen05 prefill kernel; a step is the whole prompt of
+  one layer;
+* ``cfg4`` -- KIVI 2-bit decode of B4 / 32 q-heads / 8 KV heads / head_dim
+  128 over a 65536-token context -- 65408 quantised rows (packed 2-bit
+  codes, fp16 scale and zero per group of 32 along head_dim) plus the 128
+  most recent rows in fp16 -- through ``KIVICache.compute_attention``.
+
+and, under ``reference_gpu``, the reference's own Triton decode kernel
+(``halo/triton_chunked.py`` from the reference installed in
+``baseline/_ref``) timed on the same GPU and inputs.  ``--workload cfgX``
+runs one workload alone and prints its own line.
 
 ``--seq-len T`` shrinks the cfg5 context (a multiple of 4096 x N) or the cfg3
-prompt (a multiple of 4096) for small profiling captures; the line then names
-the reduced workload.
-
-``--workload cfg2`` runs BASELINE config 2 (one GPU): 32 layers of B8 /
-32 q-heads / 8 KV heads / 32K context in chunks of 1024; hot chunks (first +
-7 most recent) in HBM, 24 cold chunks per layer in pinned host DRAM; per
-layer and step the chunk scorer picks the top-8 cold chunks for a fresh
-query, the ones not already in the layer's GPU slot cache are refetched on a
-copy stream while the hot chunks are attended, then the selected chunks are
-folded in (``halo_b200.tiered.TieredLayer``).
-
-``--workload cfg3`` runs BASELINE config 3 (one GPU): chunked prefill of a
-131072-token prompt in 32 slices of 4096 queries against the accumulated KV,
-causal, 32 q-heads / 8 KV heads, head_dim 128, on the tcgen05 prefill kernel;
-a step is the whole prompt of one layer.
-
-``--workload cfg4`` runs BASELINE config 4 instead (one GPU): KIVI 2-bit
-decode of B4 / 32 q-heads / 8 KV heads / head_dim 128 over a 65536-token
-context -- 65408 quantised rows (packed 2-bit codes, fp16 scale and zero per
-group of 32 along head_dim) plus the 128 most recent rows in fp16 -- through
-``KIVICache.compute_attention`` (fused dequant-and-attend kernel, then the
-recent rows folded in by the split-KV kernel).
+prompt (a multiple of 4096), and ``--layers L`` the cfg2 layer count, for
+small profiling captures; the line then names the reduced workload.
 
 Rank 0 prints one JSON line.  ``--impl reference`` times the reference's CPU
 implementation of the path (its torch ops restated in ``oracle/``) on this
@@ -56,7 +61,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
-# cfg5 shapes
+# 1M-token sequence-sharded decode of one Llama-3-70B-shaped layer
 CFG5 = dict(B=1, H=64, H_kv=8, D=128, T=1 << 20, chunk=4096)
 METRIC = "decode-attn tokens/s & achieved HBM GB/s at 32K-1M ctx, 1/2/4/8 B200"
 
@@ -68,6 +73,7 @@ METRIC = "decode-attn tokens/s & achieved HBM GB/s at 32K-1M ctx, 1/2/4/8 B200"
 # (transposed tile math; 201.0 MB read + 7.4 MB written over 200.9 MB).
 NCU_TRAFFIC_RATIO = 1.0040      # kd_dyn_kernel, ncu at 262144 tokens: (1073.795 + 4.311) MB read+write / 1073.742 MB algorithmic
 NCU_TRAFFIC_RATIO_KK = 1.0373
+NCU_TRAFFIC_RATIO_KD_CFG2 = None   # kd_kernel on the tiered-decode launches: not captured yet
 
 
 def _tensor_peak():
@@ -101,7 +107,7 @@ class ClockSampler:
         0x100: "display_clock_setting",
     }
 
-    def __init__(self, device_index: int, period_s: float = 0.02):
+    def __init__(self, device_index: int, period_s: float = 0.002):
         self.idx, self.period = device_index, period_s
         self.samples, self.reasons, self.max_mhz = [], 0, None
         self._stop = threading.Event()
@@ -351,10 +357,15 @@ def run_ours_cfg5(args):
     e2e_ms = float(e2e_ms.item())
     barrier()
 
-    # parity self-check of the final state on rank 0 (cheap, outside timing)
+    # parity of the last output (outside timing): one KV-head group against
+    # float64 attention, each rank over its own shard, merged across ranks
+    parity = _cfg5_parity(q, k, v, out, lse, world, group_kv=0)
     local_bytes = 2 * k.numel() * k.element_size()
     peak, peak_kind = _peaks()
     achieved = local_bytes / (kd_ms_max / 1e3) / 1e9
+    ref_gpu = None
+    if world == 1 and not args.no_reference_gpu:
+        ref_gpu = reference_gpu_cfg5(q, k, v, out)
     line = None
     if rank == 0:
         cpu = cpu_baseline_cfg5() if world == 1 and not args.no_cpu_baseline else None
@@ -378,13 +389,140 @@ def run_ours_cfg5(args):
                         "h2d_bytes_per_step": q.numel() * q.element_size(),
                         "d2h_bytes_per_step": out.numel() * out.element_size()},
                 "clocks": clocks.summary(),
-                "gpu_launches": launches}
-        print(json.dumps(line), flush=True)
+                "gpu_launches": launches,
+                "parity": parity}
+        if ref_gpu is not None:
+            line["reference_gpu"] = ref_gpu
     dec.close()
     if world > 1:
         dist.barrier(device_ids=[local])
         dist.destroy_process_group()
     return line
+
+
+def _cfg5_parity(q, k, v, out, lse, world: int, group_kv: int = 0):
+    """Max |error| of the decode output and LSE of one KV-head group against
+    float64 attention computed with torch on this GPU.  Each rank attends
+    its own shard; the ranks' (out, lse) rows are all-gathered (a few KB)
+    and merged with log-sum-exp, so every rank takes the same collective
+    step.  ``out`` is the bf16 output the timed loop kept, so its error
+    includes one bf16 rounding."""
+    import torch
+    import torch.distributed as dist
+    B, H, D = q.shape
+    H_kv = k.shape[1]
+    G = H // H_kv
+    hs = slice(group_kv * G, (group_kv + 1) * G)
+    scale = 1.0 / (D ** 0.5)
+    qg = q[:, hs].double()                                   # (B, G, D)
+    o_loc = torch.empty(B, G, D, dtype=torch.float64, device=q.device)
+    l_loc = torch.empty(B, G, dtype=torch.float64, device=q.device)
+    for b in range(B):
+        s = torch.matmul(qg[b], k[b, group_kv].double().T) * scale      # (G, T_local)
+        l = torch.logsumexp(s, dim=-1)
+        o_loc[b] = torch.matmul(torch.exp(s - l[:, None]), v[b, group_kv].double())
+        l_loc[b] = l
+        del s
+    row = torch.cat([o_loc.reshape(-1), l_loc.reshape(-1)])
+    if world > 1:
+        rows = torch.empty(world * row.numel(), dtype=row.dtype, device=row.device)
+        dist.all_gather_into_tensor(rows, row)
+        rows = rows.view(world, -1)
+    else:
+        rows = row.view(1, -1)
+    o_parts = rows[:, :B * G * D].view(-1, B, G, D)
+    l_parts = rows[:, B * G * D:].view(-1, B, G)
+    l_all = torch.logsumexp(l_parts, dim=0)
+    o_all = (torch.exp(l_parts - l_all)[..., None] * o_parts).sum(dim=0)
+    err_o = (out[:, hs].double() - o_all).abs().max().item()
+    err_l = (lse[:, hs].double() - l_all).abs().max().item()
+    return {"kv_head_group": group_kv, "max_abs_out": err_o, "max_abs_lse": err_l,
+            "checker": "float64 torch attention on the GPU (per-rank shard, LSE-merged)",
+            "tolerance": {"out": 2e-3 + 2 ** -8 * o_all.abs().max().item(), "lse": 1e-4},
+            "ok": bool(err_o <= 2e-3 + 2 ** -8 * o_all.abs().max().item() and err_l <= 1e-4)}
+
+
+def _reference_triton():
+    """The reference's Triton module from its unmodified install under
+    ``baseline/_ref`` (``pip install --target baseline/_ref``), or a reason
+    why it cannot run here."""
+    ref_root = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref_root, "halo")):
+        return None, "reference not installed under baseline/_ref"
+    if ref_root not in sys.path:
+        sys.path.append(ref_root)
+    try:
+        from halo import triton_chunked as RT
+    except Exception as e:          # noqa: BLE001 - reported in the line
+        return None, f"import halo.triton_chunked failed: {type(e).__name__}: {e}"
+    if not getattr(RT, "HAS_TRITON", False):
+        return None, "triton is not importable on this box"
+    return RT, None
+
+
+def _time_events(fn, steps: int, warmup: int):
+    """Mean ms per call of ``fn`` on the current stream (CUDA events)."""
+    import torch
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        res = fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps, res
+
+
+def reference_gpu_cfg5(q, k, v, ours_out, steps: int = 5, warmup: int = 3):
+    """The reference's own GPU decode path (its Triton kernel,
+    ``halo/triton_chunked.py:47-138``) on this GPU and on the same resident
+    inputs as the timed decode: (a) ``update_chunk`` once over the whole
+    context (the kernel alone, grid B x H) + ``finalize``; (b) its
+    single-launch driver ``triton_chunked_attention_single_launch`` with the
+    context passed as its GPU part (it stages the rows into one buffer with a
+    device-to-device copy, then launches the kernel once).  Not causal (the
+    query sits after every key).  Also reports the largest difference
+    between the reference kernel's output and this build's."""
+    import torch
+    RT, why = _reference_triton()
+    if RT is None:
+        return {"unavailable": why}
+    B, H, D = q.shape
+    T = k.shape[-2]
+    scale = 1.0 / (D ** 0.5)
+    q_pos = torch.full((B,), T - 1, dtype=torch.int64, device=q.device)
+    nbytes = 2 * k.numel() * k.element_size()
+
+    def kernel_only():
+        m, l, o = RT.init_acc(B=B, H=H, D_v=v.shape[-1], device=q.device)
+        RT.update_chunk(q=q, k=k, v=v, m=m, l=l, o=o, scale=scale, chunk_start=0, q_pos=q_pos,
+                        apply_causal=False)
+        return RT.finalize(m=m, l=l, o=o, out_dtype=torch.float32)
+
+    def single_launch():
+        return RT.triton_chunked_attention_single_launch(q.unsqueeze(2), None, None, k, v,
+                                                         scale=scale, q_pos=q_pos,
+                                                         apply_causal=False)
+
+    try:
+        ms_k, o_ref = _time_events(kernel_only, steps, warmup)
+        ms_s, _ = _time_events(single_launch, steps, warmup)
+    except Exception as e:          # noqa: BLE001 - reported in the line
+        return {"unavailable": f"reference Triton kernel failed: {type(e).__name__}: {e}"}
+    diff = (o_ref - ours_out.float()).abs().max().item()
+    return {"impl": "reference halo/triton_chunked.py (unmodified, baseline/_ref), Triton on "
+                    "this B200",
+            "workload": "the timed 1M-token decode: same q, K, V in HBM",
+            "kernel_only": {"ms_per_step": ms_k, "tokens_per_s": B / (ms_k / 1e3),
+                            "algorithmic_gbs": nbytes / (ms_k / 1e3) / 1e9,
+                            "call": "init_acc + update_chunk over all rows + finalize"},
+            "single_launch": {"ms_per_step": ms_s, "tokens_per_s": B / (ms_s / 1e3),
+                              "algorithmic_gbs": nbytes / (ms_s / 1e3) / 1e9,
+                              "call": "triton_chunked_attention_single_launch (includes its "
+                                      "device-to-device staging copy)"},
+            "max_abs_vs_ours": diff, "steps": steps, "warmup": warmup}
 
 
 # ---------------------------------------------------------------- cfg2 (tiered decode)
@@ -402,7 +540,8 @@ def _cfg2_hot(P: int):
 def _cfg2_config():
     c = CFG2
     P = c["T"] // c["chunk"]
-    return {"workload": f"cfg2: tiered decode, {c['L']} layers, B{c['B']}, 32 q-heads / 8 KV "
+    name = "cfg2: tiered decode" if c["L"] == 32 else "cfg2 reduced (profiling case): tiered decode"
+    return {"workload": f"{name}, {c['L']} layers, B{c['B']}, 32 q-heads / 8 KV "
                         f"heads, head_dim 128, {c['T']} ctx in {P} chunks of {c['chunk']}; hot = "
                         f"chunk 0 + {len(_cfg2_hot(P)) - 1} most recent (HBM), {P - len(_cfg2_hot(P))} "
                         f"cold chunks in pinned host DRAM; per layer and step the chunk scorer picks "
@@ -473,10 +612,11 @@ def run_ours_cfg2(args):
     out = torch.empty(c["B"], c["H"], c["D"], device=dev, dtype=torch.bfloat16)
     lse = torch.empty(c["B"], c["H"], device=dev)
 
-    def step(i, evs=None):
+    def step(i, evs=None, cevs=None):
         for li, lay in enumerate(layers):
             lay.step(qs[i, li], k_sel=c["k_sel"], out=out, lse=lse,
-                     events=evs[li] if evs else None)
+                     events=evs[li] if evs else None,
+                     copy_events=cevs[li] if cevs else None)
 
     for i in range(args.warmup):
         step(i)
@@ -492,18 +632,29 @@ def run_ours_cfg2(args):
     torch.cuda.synchronize()
     raw = [[((a.cuda_event, b.cuda_event), (c2.cuda_event, d.cuda_event))
             for (a, b), (c2, d) in s_] for s_ in evs]
+    cevs = [[(mk(), mk()) for _ in range(c["L"])] for _ in range(K)]
+    for e in (x for s_ in cevs for pr in s_ for x in pr):
+        e.record()
+    torch.cuda.synchronize()
     t0, t1 = mk(), mk()
     n0 = L.launch_count()
     with ClockSampler(0) as clocks:
         t0.record()
         for i in range(K):
-            step(args.warmup + i, raw[i])
+            step(args.warmup + i, raw[i], cevs[i])
         t1.record()
         torch.cuda.synchronize()
     launches = L.launch_count() - n0
     ms_step = t0.elapsed_time(t1) / K
     kd_ms = sum(a.elapsed_time(b) + c2.elapsed_time(d)
                 for s_ in evs for (a, b), (c2, d) in s_) / K
+    hot_ms = sum(a.elapsed_time(b) for s_ in evs for (a, b), _ in s_) / K
+    copy_ms = sum(a.elapsed_time(b) for s_ in cevs for (a, b) in s_) / K
+    # compute-stream idle time between the hot attention and the fold of
+    # the selected chunks: waiting for the indices on the host and for the
+    # refetch copies (the part of the refetch not hidden behind attention)
+    exposed_ms = sum(max(0.0, hb.elapsed_time(sb)) for s_ in evs
+                     for (_ha, hb), (sb, _se) in s_) / K
     refetched = sum(l_.stats["refetched_chunks"] for l_ in layers) / K
     refetch_bytes = sum(l_.stats["refetch_bytes"] for l_ in layers) / K
     att_bytes = (len(hot) + c["k_sel"]) * layers[0].chunk_bytes * c["L"]
@@ -541,18 +692,79 @@ def run_ours_cfg2(args):
                          "frac": achieved / peak, "peak_kind": f"of {peak_kind}",
                          "kernel": "kd_kernel (split-KV decode), hot + selected launches",
                          "bytes_per_step": att_bytes, "kernel_ms_per_step": kd_ms,
-                         "traffic": att_bytes * NCU_TRAFFIC_RATIO},
+                         "traffic": (att_bytes * NCU_TRAFFIC_RATIO_KD_CFG2
+                                     if NCU_TRAFFIC_RATIO_KD_CFG2 else None)},
             "refetch": {"chunks_per_step": refetched, "bytes_per_step": refetch_bytes,
                         "chunks_selected_per_step": c["k_sel"] * c["L"],
-                        "host_link_bound_ms": refetch_bytes / 54e9 * 1e3},
+                        "copy_stream_ms_per_step": copy_ms,
+                        "copy_gbs": refetch_bytes / max(copy_ms, 1e-9) / 1e6,
+                        "hot_attention_ms_per_step": hot_ms,
+                        "attention_ms_per_step": kd_ms,
+                        "exposed_ms_per_step": exposed_ms,
+                        "hidden": exposed_ms <= 0.05 * ms_step,
+                        "exposed_note": "compute-stream gap between the hot-chunk attention "
+                                        "and the fold of the selected chunks, summed over "
+                                        "layers (host wait for the indices + copies)"},
             "cpu_baseline": cpu and {kk: cpu[kk] for kk in ("value", "unit", "cores", "kind",
                                                            "sample")},
             "e2e": {"value": c["B"] / (e2e_ms / 1e3), "unit": "tokens/s",
                     "h2d_bytes_per_step": qs[0].numel() * 2,
                     "d2h_bytes_per_step": out.numel() * 2},
             "clocks": clocks.summary(), "gpu_launches": launches}
-    print(json.dumps(line), flush=True)
+    if not args.no_reference_gpu:
+        line["reference_gpu"] = reference_gpu_cfg2(layers[0], qs[0, 0])
+    del layers
     return line
+
+
+def reference_gpu_cfg2(lay, q, steps: int = 10, warmup: int = 3):
+    """One layer's attention of the tiered decode on the reference's Triton
+    kernel (``halo/triton_chunked.py:47-138``): the 16 chunks a step attends
+    (8 hot + the 8 in the refetch slots, 16384 rows) staged in one buffer,
+    one ``update_chunk`` over it, against this build's split-KV decode over
+    the same chunks in place."""
+    import torch
+    from halo_b200 import ops
+    RT, why = _reference_triton()
+    if RT is None:
+        return {"unavailable": why}
+    C = lay.C
+    ks = [lay.k_hot] + [lay.k_slots[i] for i in range(lay.n_slots)]
+    vs = [lay.v_hot] + [lay.v_slots[i] for i in range(lay.n_slots)]
+    k = torch.cat(ks, dim=2)
+    v = torch.cat(vs, dim=2)
+    B, H, D = q.shape
+    T = k.shape[2]
+    scale = 1.0 / (D ** 0.5)
+    q_pos = torch.full((B,), T - 1, dtype=torch.int64, device=q.device)
+    nbytes = 2 * k.numel() * k.element_size()
+    chunks = [(k[:, :, a:a + C], v[:, :, a:a + C], a, False) for a in range(0, T, C)]
+    table = ops.ChunkTable(chunks)
+    out = torch.empty(B, H, D, device=q.device)
+    lse = torch.empty(B, H, device=q.device)
+
+    def ref():
+        m, l, o = RT.init_acc(B=B, H=H, D_v=D, device=q.device)
+        RT.update_chunk(q=q, k=k, v=v, m=m, l=l, o=o, scale=scale, chunk_start=0, q_pos=q_pos,
+                        apply_causal=False)
+        return RT.finalize(m=m, l=l, o=o, out_dtype=torch.float32)
+
+    def ours():
+        ops.chunked_decode(q, table, scale=scale, out=out, lse=lse)
+        return out
+
+    try:
+        ms_r, o_r = _time_events(ref, steps, warmup)
+    except Exception as e:          # noqa: BLE001 - reported in the line
+        return {"unavailable": f"reference Triton kernel failed: {type(e).__name__}: {e}"}
+    ms_o, o_o = _time_events(ours, steps, warmup)
+    return {"impl": "reference halo/triton_chunked.py (unmodified, baseline/_ref), Triton on "
+                    "this B200",
+            "workload": f"one layer's attended chunks: B{B}, {H}/{k.shape[1]} heads, {T} rows",
+            "reference_ms_per_layer": ms_r, "reference_gbs": nbytes / (ms_r / 1e3) / 1e9,
+            "ours_ms_per_layer": ms_o, "ours_gbs": nbytes / (ms_o / 1e3) / 1e9,
+            "max_abs_vs_ours": (o_r - o_o).abs().max().item(), "steps": steps,
+            "call": "init_acc + update_chunk over the staged rows + finalize"}
 
 
 def run_reference_cfg2(args):
@@ -576,7 +788,7 @@ METRIC4 = "KIVI 2-bit decode tokens/s & achieved HBM GB/s (packed bytes), B4 x 6
 
 
 def _outlier_keys(k, seed: int):
-    """Scale 4 seeded channels of every KV head by 10 (BASELINE key outliers)."""
+    """Scale 4 seeded channels of every KV head by 10 (outlier key channels)."""
     import torch
     g = torch.Generator().manual_seed(seed)
     for h in range(k.shape[1]):
@@ -734,7 +946,7 @@ def run_ours_cfg4(args):
                     "h2d_bytes_per_step": q.numel() * q.element_size(),
                     "d2h_bytes_per_step": out_host.numel() * out_host.element_size()},
             "clocks": clocks.summary(), "gpu_launches": launches}
-    print(json.dumps(line), flush=True)
+    del cache
     return line
 
 
@@ -904,7 +1116,6 @@ def run_ours_cfg3(args):
                     "h2d_bytes_per_step": (q.numel() + k.numel() + v.numel()) * 2,
                     "d2h_bytes_per_step": out.numel() * 2},
             "clocks": clocks.summary(), "gpu_launches": launches}
-    print(json.dumps(line), flush=True)
     return line
 
 
@@ -923,23 +1134,56 @@ def run_reference_cfg3(args):
     print(json.dumps(line), flush=True)
 
 
+def run_ours_all(args):
+    """The headline decode line; with one GPU, the other three workloads
+    measured after it (each with its own roofline, CPU baseline, e2e and
+    clock record) under ``workloads``."""
+    import torch
+    line = run_ours_cfg5(args)
+    if int(os.environ.get("WORLD_SIZE", "1")) != 1 or args.gpus != 1 or args.no_workloads:
+        return line
+    sub = argparse.Namespace(**vars(args))
+    sub.steps = min(args.steps, 20)
+    sub.warmup = max(3, min(args.warmup, 5))
+    workloads = {}
+    for name, fn in (("cfg4", run_ours_cfg4), ("cfg3", run_ours_cfg3), ("cfg2", run_ours_cfg2)):
+        torch.cuda.empty_cache()
+        try:
+            workloads[name] = fn(sub if name != "cfg4" else args)
+        except Exception as e:      # noqa: BLE001 - one workload failing is reported, not fatal
+            workloads[name] = {"error": f"{type(e).__name__}: {e}"}
+    line["workloads"] = workloads
+    return line
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=300)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["cfg5", "cfg4", "cfg3", "cfg2"], default="cfg5")
+    ap.add_argument("--workload", choices=["all", "cfg5", "cfg4", "cfg3", "cfg2"], default="all")
     ap.add_argument("--seq-len", type=int, default=0)
+    ap.add_argument("--layers", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-workloads", action="store_true",
+                    help="headline decode only (skip cfg2/3/4 in the default run)")
+    ap.add_argument("--no-reference-gpu", action="store_true",
+                    help="skip timing the reference's Triton kernel")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
-    if args.seq_len and args.workload == "cfg5":
+    if args.seq_len and args.workload in ("cfg5", "all"):
         n = args.gpus * CFG5["chunk"]
         if args.seq_len % n:
             raise SystemExit(f"--seq-len must be a multiple of {n}")
         CFG5["T"] = args.seq_len
+    if args.seq_len and args.workload == "cfg3":
+        if args.seq_len % CFG3["slice"]:
+            raise SystemExit(f"--seq-len must be a multiple of {CFG3['slice']}")
+        CFG3["T"] = args.seq_len
+    if args.layers:
+        CFG2["L"] = args.layers
     if args.impl == "reference":
         if args.workload == "cfg4":
             return run_reference_cfg4(args)
@@ -948,17 +1192,12 @@ def main():
         if args.workload == "cfg3":
             return run_reference_cfg3(args)
         return run_reference(args)
-    if args.workload == "cfg4":
-        return run_ours_cfg4(args)
-    if args.workload == "cfg2":
-        return run_ours_cfg2(args)
-    if args.workload == "cfg3":
-        if args.seq_len:
-            if args.seq_len % CFG3["slice"]:
-                raise SystemExit(f"--seq-len must be a multiple of {CFG3['slice']}")
-            CFG3["T"] = args.seq_len
-        return run_ours_cfg3(args)
-    return run_ours_cfg5(args)
+    runner = {"cfg4": run_ours_cfg4, "cfg2": run_ours_cfg2, "cfg3": run_ours_cfg3,
+              "cfg5": run_ours_cfg5, "all": run_ours_all}[args.workload]
+    line = runner(args)
+    if line is not None:
+        print(json.dumps(line), flush=True)
+    return line
 
 
 if __name__ == "__main__":

@@ -124,9 +124,11 @@ class TieredLayer:
         L.check(rc, "halo_page_score_topk")
         return self._topk[:k_sel]
 
-    def _refetch(self, chunks: Sequence[int]) -> int:
+    def _refetch(self, chunks: Sequence[int], copy_events: Optional[tuple] = None) -> int:
         """Copy the chunks not resident into slots (copy stream); returns how
-        many were copied.  The compute stream must wait on ``self._copied``."""
+        many were copied.  The compute stream must wait on ``self._copied``.
+        ``copy_events = (begin, end)`` (``torch.cuda.Event``) are recorded
+        on the copy stream around the copies."""
         need = [c for c in chunks if c not in self._slot_of]
         for c in chunks:
             if c in self._slot_of:
@@ -134,6 +136,8 @@ class TieredLayer:
         keep = set(chunks)
         cs = self.copy_stream
         cs.wait_stream(torch.cuda.current_stream(self.dev))   # slots are free on the compute stream
+        if copy_events is not None:
+            copy_events[0].record(cs)
         lib = L.lib()
         esz = self.k_hot.element_size()
         width = self.C * self.D * esz
@@ -151,17 +155,21 @@ class TieredLayer:
                 rc = lib.halo_copy2d_async(dst.data_ptr(), width, src.data_ptr() + off, src_pitch,
                                            width, rows, ctypes.c_void_p(cs.cuda_stream))
                 L.check(rc, "halo_copy2d_async")
+        if copy_events is not None:
+            copy_events[1].record(cs)
         self._copied.record(cs)
         return len(need)
 
     def step(self, q: torch.Tensor, *, k_sel: int, scale: Optional[float] = None,
              out: Optional[torch.Tensor] = None, lse: Optional[torch.Tensor] = None,
-             events: Optional[tuple] = None):
+             events: Optional[tuple] = None, copy_events: Optional[tuple] = None):
         """One decode query ``q (B, H, D)`` (or ``(B, H, 1, D)``): attention
         over the hot chunks and the ``k_sel`` best cold chunks.  Returns
         ``(out (B, H, D) in q.dtype, lse (B, H), selected chunk ids)``.
         ``events = (begin, end)`` bracket each split-KV launch pair (hot,
-        selected) when given as two lists of raw event handles."""
+        selected) when given as two lists of raw event handles;
+        ``copy_events = (begin, end)`` (``torch.cuda.Event``) bracket the
+        refetch copies on the copy stream."""
         q3 = q.squeeze(2) if q.dim() == 4 else q
         q3 = q3 if q3.is_contiguous() else q3.contiguous()
         B, H, D = q3.shape
@@ -180,7 +188,7 @@ class TieredLayer:
         # 3. delta refetch of the selected cold chunks
         self._idx_ready.synchronize()
         chosen = [int(x) for x in self._idx_host[:k_sel].tolist()]
-        n_new = self._refetch(chosen)
+        n_new = self._refetch(chosen, copy_events)
         # 4. selected chunks folded into the hot state
         cur.wait_event(self._copied)
         if self._ones is None or self._ones.shape != (B, H):

@@ -83,7 +83,7 @@ def prefill_inputs(name):
 
 
 def config1_inputs():
-    """fp32, B1, H32/H_kv8, D128, T8192, seed 0."""
+    """The fp32 CPU-runnable decode case: B1, H32/H_kv8, D128, T8192, seed 0."""
     g = torch.Generator().manual_seed(0)
     q = torch.randn(1, 32, 1, 128, generator=g)
     k = torch.randn(1, 8, 8192, 128, generator=g)

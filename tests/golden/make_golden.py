@@ -118,7 +118,8 @@ def gen_prefill(C, make_cache) -> dict:
 
 
 def gen_config1(C) -> dict:
-    """BASELINE config 1, hot = chunks {0, 13, 14, 15}, cold = 1..12; walk
+    """The fp32 CPU-runnable decode case (B1, H32/8, D128, 16 chunks of 512),
+    hot = chunks {0, 13, 14, 15}, cold = 1..12; walk
     order cold then hot, as compute_attention walks its tiers."""
     q, k, v = I.config1_inputs()
     chunk = 512

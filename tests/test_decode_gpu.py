@@ -1,7 +1,7 @@
 """GPU parity: split-KV decode + LSE merge (sm_100a) vs the CPU oracle and the
 reference's golden vectors.
 
-Tolerances (BASELINE north_star): attention output within 2e-3 max-abs of the
+Tolerances: attention output within 2e-3 max-abs of the
 fp32 reference for 16-bit inputs (compared on the fp32 output, before any
 rounding to the storage dtype), LSE within 1e-4; fp32 inputs within 1e-5.
 """
@@ -59,7 +59,8 @@ def test_decode_matches_reference_golden(cuda_device, name):
 
 
 def test_decode_config1_full(cuda_device):
-    """BASELINE config 1 (fp32, B1, H32/8, D128, T8192, 16 x 512, hot {0,13,14,15})."""
+    """The fp32 CPU-runnable decode case at full size (B1, H32/8, D128, T8192,
+    16 chunks of 512, hot chunks {0, 13, 14, 15} walked first)."""
     ops = _ops()
     g = I.load("config1.npz")["config1"]
     q, k, v = I.config1_inputs()

@@ -83,6 +83,54 @@ def test_noalloc_matches_workspace_entry_point_twice(cuda_device):
     assert L.device_error() == 0
 
 
+@pytest.mark.gpu
+def test_noalloc_dynamic_schedule_twice_matches_oracle(cuda_device):
+    """A context long enough for the dynamically scheduled split-KV kernel
+    (B1, 64 q-heads / 8 KV heads, head_dim 128, 32768 rows: 512 tiles per
+    KV head against 8 x 37 needed), whose CTAs take row pieces from counters
+    kept in the first 4 KB of the scratch.  Two calls in a row must both
+    match the workspace entry point and the float64 oracle: the second call
+    only works if the counters the first one used were cleared."""
+    from halo_b200 import _lib as L
+    from oracle import attention as OA
+    lib = L.lib()
+    dev = cuda_device
+    B, H, H_kv, D, T, chunk = 1, 64, 8, 128, 32768, 4096
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    g = torch.Generator().manual_seed(12)
+    k = torch.randn(B, H_kv, T, D, generator=g).bfloat16()
+    v = torch.randn(B, H_kv, T, D, generator=g).bfloat16()
+    kd, vd = k.to(dev), v.to(dev)
+    arr, n = _chunks(L, kd, vd, chunk, causal=False)
+    G = H // H_kv
+    for call in range(2):
+        q = torch.randn(B, H, D, generator=g).bfloat16()
+        qd = q.to(dev)
+        prob = _problem(L, qd, H_kv, None, 1.0 / math.sqrt(D))
+        need = lib.halo_decode_workspace_bytes(ctypes.byref(prob), arr, n)
+        assert 0 < need <= 8 << 20
+        ws = torch.zeros(need, dtype=torch.uint8, device=dev)
+        out_ref = torch.empty(B, H, D, dtype=torch.float32, device=dev)
+        lse_ref = torch.empty(B, H, dtype=torch.float32, device=dev)
+        L.check(lib.halo_chunked_decode(ctypes.byref(prob), arr, n, ws.data_ptr(), need,
+                                        ctypes.byref(_merge(L, out_ref, lse_ref)), stream),
+                "halo_chunked_decode")
+        out = torch.full((B, H, D), float("nan"), dtype=torch.float32, device=dev)
+        lse = torch.full((B, H), float("nan"), dtype=torch.float32, device=dev)
+        L.check(lib.halo_chunked_decode_noalloc(ctypes.byref(prob), arr, n,
+                                                ctypes.byref(_merge(L, out, lse)), stream),
+                "halo_chunked_decode_noalloc")
+        torch.cuda.synchronize(dev)
+        assert (out - out_ref).abs().max().item() <= 2e-3
+        assert (lse - lse_ref).abs().max().item() <= 1e-4
+        for hk in range(H_kv):
+            hs = slice(hk * G, (hk + 1) * G)
+            ro, rl = OA.full_attention_f64(q[:, hs], k[:, hk:hk + 1], v[:, hk:hk + 1])
+            assert (out[:, hs].cpu().double() - ro[:, :, 0]).abs().max().item() <= 2e-3
+            assert (lse[:, hs].cpu().double() - rl[:, :, 0]).abs().max().item() <= 1e-4
+    assert L.device_error() == 0
+
+
 def test_noalloc_rejects_problems_beyond_its_scratch():
     """A problem whose partials exceed the fixed 8 MiB scratch is refused
     before anything is enqueued (no GPU work, no allocation)."""
