@@ -70,10 +70,11 @@ METRIC = "decode-attn tokens/s & achieved HBM GB/s at 32K-1M ctx, 1/2/4/8 B200"
 # it must read); the captures and their commands are summarised under
 # profiles/.  kd_dyn_kernel: cfg5 reduced to 262144 tokens, scaled to a full
 # launch by the K/V bytes it processes.  kk_kernel: the cfg4 launch itself
-# (transposed tile math; 201.0 MB read + 7.4 MB written over 200.9 MB).
+# (transposed tile math, K into MMA registers).  kd_kernel at cfg2: the hot
+# and selected launches of one layer.
 NCU_TRAFFIC_RATIO = 1.0040      # kd_dyn_kernel, ncu at 262144 tokens: (1073.795 + 4.311) MB read+write / 1073.742 MB algorithmic
-NCU_TRAFFIC_RATIO_KK = 1.0373
-NCU_TRAFFIC_RATIO_KD_CFG2 = None   # kd_kernel on the tiered-decode launches: not captured yet
+NCU_TRAFFIC_RATIO_KK = 1.0284      # kk_kernel, ncu of the cfg4 launch: (201.13 + 5.50) MB / 200.93 MB
+NCU_TRAFFIC_RATIO_KD_CFG2 = 1.0139  # kd_kernel, ncu of one layer's hot + selected launches (cfg2)
 
 
 def _tensor_peak():
