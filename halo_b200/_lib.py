@@ -165,6 +165,12 @@ SIGNATURES = {
     "halo_prefill_attention": (ctypes.c_int32, [ctypes.POINTER(PrefillProblem),
                                                 ctypes.POINTER(KVChunk), ctypes.c_int32,
                                                 ctypes.POINTER(PrefillOut), ctypes.c_void_p]),
+    "halo_prefill_workspace_bytes": (ctypes.c_int64, [ctypes.POINTER(PrefillProblem),
+                                                      ctypes.POINTER(KVChunk), ctypes.c_int32]),
+    "halo_prefill_attention_ws": (ctypes.c_int32, [ctypes.POINTER(PrefillProblem),
+                                                   ctypes.POINTER(KVChunk), ctypes.c_int32,
+                                                   ctypes.POINTER(PrefillOut), ctypes.c_void_p,
+                                                   ctypes.c_int64, ctypes.c_void_p]),
     "halo_chunked_decode_partials": (ctypes.c_int32, [ctypes.POINTER(DecodeProblem),
                                                       ctypes.POINTER(KVChunk), ctypes.c_int32,
                                                       ctypes.c_void_p, ctypes.c_int64,

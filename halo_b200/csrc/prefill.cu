@@ -4,16 +4,22 @@
 // chunks (the accumulated cache of halo/kv_cache_chunked.py:873-942 and the
 // slices of halo/chunked_prefill.py:73-135 in lzbaclz/HALO) with an online
 // softmax; there is no split over keys, so results leave a CTA merged.  The
-// kernel (kp2_kernel below) gives each CTA two 128-row query tiles of one
+// kernel (kp3_kernel below) gives each CTA two 128-row query tiles of one
 // q-head; its layout, warp roles and synchronisation are described at the
 // kernel.
 //
 // Numerics: scores and outputs accumulate in fp32 (TMEM).  P = exp2(s*c - m)
 // with a running max m that is only moved when it grows by more than 2^8
-// (O is then rescaled in TMEM), so P <= 256.  bf16 inputs feed P to the
-// tensor core as hi + lo 16-bit parts (two MMAs; ~16 significant bits): a
-// single bf16 P puts errors up to ~2^-9 |v| on peaked rows, above the 2e-3
-// budget.  fp16 inputs use one fp16 P (11 bits, |err| <~ 2^-12 |v|).
+// (O is then rescaled in TMEM), so P <= 256.  P enters the P V product as
+// one fp16 operand (11 significant bits, |err| <~ 2^-12 |v| per term) with V
+// in fp16: fp16 inputs as they are, bf16 inputs through an fp16 copy of V
+// that a pre-pass (v16_kernel) writes into the caller's workspace.  That
+// copy is exact for 2^-14 <= |v| < 2^16 and loses at most 2^-25 in absolute
+// terms below; a call whose V holds a finite |v| >= 2^16 is flagged by the
+// pre-pass and runs the bf16 route instead: bf16 V and P as a truncated bf16
+// high part plus a bf16 residual (two MMAs, ~16 significant bits).  A single
+// bf16 P would put errors up to ~2^-9 |v| on peaked rows, above the 2e-3
+// budget.  Calls without a workspace take the bf16 route.
 #include <algorithm>
 #include <cmath>
 #include <cstdarg>
@@ -33,11 +39,12 @@ int device_sms();
 
 namespace prefill {
 
-constexpr int kBM = 128;            // query rows per CTA (TMEM lanes)
-constexpr int kBN = 128;            // keys per tile
+constexpr int kBM = 128;            // query rows per tile (TMEM lanes)
+constexpr int kBN = 128;            // keys per K/V tile and per score tile
 constexpr int kMaxSegs = 48;
 constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleLog2 = 8.f;
+constexpr int64_t kWsHeader = 256;  // workspace: flag word, then the fp16 V copies
 
 struct Seg {
   int64_t start;   // global position of row 0
@@ -50,7 +57,9 @@ struct alignas(64) Params {
   CUtensorMap qmap;                 // {D, T_q, H, B}
   CUtensorMap kmap[kMaxSegs];       // {D, len, H_kv, B}
   CUtensorMap vmap[kMaxSegs];
+  CUtensorMap v16map[kMaxSegs];     // fp16 copy of V (workspace), bf16 inputs only
   Seg seg[kMaxSegs];
+  const unsigned int* v16_flag;     // non-NULL: fp16 copies exist; *flag != 0: out of range
   int32_t n_seg;
   int32_t B, H, G, T_q, n_qtiles;
   int64_t q_pos0;
@@ -73,6 +82,20 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+// Non-blocking probe of an mbarrier phase (true: the phase with this parity
+// has completed).
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // K/V tiles of segment `sg` visible to query positions <= qmax.
 __device__ __forceinline__ int seg_tiles(const Seg& sg, int64_t qmax) {
   int n = (sg.len + kBN - 1) / kBN;
@@ -85,68 +108,81 @@ __device__ __forceinline__ int seg_tiles(const Seg& sg, int64_t qmax) {
   return n;
 }
 
-template <typename T>
-__device__ __forceinline__ uint32_t pack2(float a, float b) {
-  return Elem<T>::pack(a, b);
+// The value itself, opaque to the compiler: keeps the issuer from hoisting
+// every unrolled MMA's descriptor out of its polling loop into registers.
+__device__ __forceinline__ uint64_t opaque(uint64_t v) {
+  asm volatile("mov.b64 %0, %0;" : "+l"(v));
+  return v;
+}
+
+// Two floats as one 32-bit register of two fp16 values (round to nearest).
+__device__ __forceinline__ uint32_t pack_h2(float a, float b) {
+  const __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+__device__ __forceinline__ uint32_t pack_bf2(float a, float b) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&h);
 }
 
 // ======================================================================
-// kp2_kernel: two query tiles per CTA, double-buffered 64-key score tiles.
+// kp3_kernel: two query tiles per CTA, 128-key score tiles, one MMA issuer
+// that polls.
 //
 // CTA = query tiles A = 2*pair and B = 2*pair + 1 (B may be absent) of one
-// q-head; both walk the same K/V tiles (B's causal range; A joins the tiles
-// it can see).  K/V arrive as 128-key TMA tiles; scores are computed per
-// 64-key sub-tile j (half j%2 of K/V tile j/2).  384 threads:
-//   WG0  warp 0 TMA producer; warp 1 TMEM owner and MMA issuer of tile A
-//        (lane 0); warp 2 MMA issuer of tile B; warp 3 idle.  Registers
-//        lowered to 104 per thread.
-//   WG1  softmax of tile A (thread r = TMEM lane r), 200 registers.
-//   WG2  softmax of tile B, 200 registers.
-// TMEM (512 columns): tile X has two 64-column score buffers S_X[0..1] and a
-// D-column output accumulator O_X: S_A[b] = [64b, 64b+64), S_B[b] =
-// [128+64b, ...), O_A = [256, 256+D), O_B = [256+D, 256+2D).  P of sub-tile
-// j overwrites S_X[j%2] in place as 16-bit pairs (keys 32c..32c+31: hi in
-// columns [32c, 32c+16), lo in [32c+16, 32c+32)) and is the A operand of
-// O_X += P V (tcgen05.mma with A in TMEM).  With two score buffers the MMA
-// issuer computes S_X(j+1) while the softmax of S_X(j) runs; S_X(j+2) waits
-// for O_X += P_X(j) V to finish reading P.  A softmax that must rescale O_X
-// first waits for the previous PV_X.
-// Each tile's issuer runs PV(j), QK(j+2), PV(j+1), QK(j+3), ... on its own
-// commit chain; the two chains interleave on the tensor pipe.
-// Descriptors are precomputed (one add per MMA) so an issuing thread keeps
-// pace with the pipe.
-// Barriers: q_full; k_full/v_full/k_empty/v_empty [stages]; per tile X and
-// buffer b: s_full (commit after QK), p_full (128 softmax arrivals), pv_done
-// (commit after PV); mma_done per issuer.  K/V empty barriers take one
-// arrival per issuer (the producer stands in for an issuer whose tile sits
-// that K/V tile out).  All waits bounded.
-constexpr int kThreads2 = 384;
-constexpr int kSub = 64;                 // keys per score sub-tile
+// q-head; both walk the same K/V tiles (B's causal range; A takes part in
+// the tiles it can see, a prefix of each segment's).  384 threads:
+//   WG0  warp 0 lane 0: TMA producer (Q once, then K and V tiles of 128
+//        keys through ST-stage rings); warp 1: TMEM owner, lane 0 issues
+//        every MMA of both tiles; warps 2-3 idle.  88 registers.
+//   WG1  softmax of tile A (thread r = TMEM lane r = query row r), 208 regs.
+//   WG2  softmax of tile B.
+// TMEM (512 columns): per tile X a 128-column score buffer S_X = [128X,
+// 128X + 128) and a D-column output accumulator O_X = [256 + D X, ...).
+// QK_X(j): S_X = Q_X K(j)^T, M128 N128, both operands in shared memory.
+// The softmax writes P_X(j) back into S_X's columns as 16-bit pairs (fp16
+// route: keys 2c, 2c+1 in column c < 64; bf16 route: the high parts there
+// and the residuals in column 64 + c) and PV_X(j): O_X += P_X(j) V(j) takes
+// P from TMEM as the A operand (M128 N=D), so P never touches shared memory.
+// With one score buffer per tile, QK_X(j+1) is issued only once PV_X(j) has
+// completed; the issuer keeps the tensor pipe busy with the other tile's
+// work meanwhile, so the two softmax groups alternate with the MMAs.
+// Issuer: a single thread polls (mbarrier.test_wait) and issues whichever
+// of the four next steps (QK/PV of A/B) has its inputs ready; it never waits
+// on one step while another could go, so no order of chunks can stall it.
+// Ring barriers: k_full/v_full (one arrival + the copy's bytes), k_empty /
+// v_empty (two arrivals: a tcgen05.commit per query tile that reads the
+// tile, the producer arriving for a tile that sits it out).  Per tile X:
+// s_full (commit after QK), p_full (128 softmax arrivals), pv_done (commit
+// after PV).  All waits bounded; TMEM freed on every exit path.
+constexpr int kThreads = 384;
 
 template <int D>
-struct Geom2 {
-  static constexpr int kBlocks = D / 64;
-  static constexpr int kBlockBytes = kBM * 128;
+struct Geom {
+  static constexpr int kBlocks = D / 64;                  // 128-byte column blocks
+  static constexpr int kBlockBytes = kBN * 128;           // one block of a 128-row tile
   static constexpr int kTileBytes = kBlocks * kBlockBytes;
   static constexpr int kStages = D == 64 ? 4 : 2;
   static constexpr int kOffQ = 0;                         // Q_A, Q_B
   static constexpr int kOffK = 2 * kTileBytes;
   static constexpr int kOffV = kOffK + kStages * kTileBytes;
   static constexpr int kOffBar = kOffV + kStages * kTileBytes;
-  static constexpr int kSmemBytes = kOffBar + 512 + 1024;
+  static constexpr int kSmemBytes = kOffBar + 512 + 1024;   // barriers + tile table, alignment
   static constexpr uint32_t kColO = 256;
 };
 
-struct Bars2 {
+struct Bars {
   uint64_t q_full;
   uint64_t k_full[4], v_full[4], k_empty[4], v_empty[4];
-  uint64_t s_full[2][2], p_full[2][2], pv_done[2][2], mma_done[2];
+  uint64_t s_full[2], p_full[2], pv_done[2], mma_done;
   uint32_t tmem_base;
   int abort_flag;
+  int nU, nA;                        // K/V tiles of the walk, and tile A's share
+  int16_t ntU[kMaxSegs], ntA[kMaxSegs];   // per segment: tiles B (the walk) / A see
 };
 
-__device__ __forceinline__ bool wait_bar2(uint64_t* bar, uint32_t parity, Bars2* bs,
-                                          unsigned int* err) {
+__device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, Bars* bs,
+                                         unsigned int* err) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   while (true) {
@@ -161,24 +197,21 @@ __device__ __forceinline__ bool wait_bar2(uint64_t* bar, uint32_t parity, Bars2*
   }
 }
 
-// Sub-tile walk shared by every role: K/V tile index g (within segment s,
-// tile t of that segment) and which query tiles take part.
-struct Walk {
-  int s, t, g;          // segment, tile in segment, global K/V tile
-  int ntU, ntA;         // tiles of segment s for the union / tile A
+// Position in the walk over the K/V tiles of a CTA (segment s, tile t of
+// that segment, global tile index g counting every tile of the walk).
+struct Cursor {
+  int s, t, g;
 };
 
 template <typename T, int D>
-__global__ void __launch_bounds__(kThreads2, 1) kp2_kernel(const __grid_constant__ Params p) {
-  using Gm = Geom2<D>;
+__global__ void __launch_bounds__(kThreads, 1) kp3_kernel(const __grid_constant__ Params p) {
+  using Gm = Geom<D>;
   constexpr int ST = Gm::kStages;
-  // bf16 keeps P as hi + lo (two MMAs); fp16's 11-bit P alone keeps the
-  // output within the error budget (|err| <~ 2^-12 |v|), so one MMA.
-  constexpr bool kSplitP = Elem<T>::kDtype == HALO_DTYPE_BF16;
+  constexpr bool kBf16 = Elem<T>::kDtype == HALO_DTYPE_BF16;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  Bars2* bs = reinterpret_cast<Bars2*>(smem + Gm::kOffBar);
+  Bars* bs = reinterpret_cast<Bars*>(smem + Gm::kOffBar);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   const int BH = p.B * p.H;
@@ -193,6 +226,10 @@ __global__ void __launch_bounds__(kThreads2, 1) kp2_kernel(const __grid_constant
   const int64_t qminA = p.q_pos0 + qA0, qmaxA = qminA + validA - 1;
   const int64_t qminB = qminA + kBM, qmaxB = qminB + validB - 1;
   const int64_t qmaxU = hasB ? qmaxB : qmaxA;
+  // P as one fp16 operand with fp16 V (fp16 inputs, or bf16 inputs whose
+  // fp16 V copy is in range); otherwise bf16 hi + lo with bf16 V
+  const bool p16 = !kBf16 || (p.v16_flag != nullptr && *p.v16_flag == 0u);
+  const CUtensorMap* vmaps = (kBf16 && p16) ? p.v16map : p.vmap;
 
   if (threadIdx.x == 0) {
     mbar_init(&bs->q_full, 1);
@@ -203,14 +240,22 @@ __global__ void __launch_bounds__(kThreads2, 1) kp2_kernel(const __grid_constant
       mbar_init(&bs->v_empty[i], 2);
     }
     for (int x = 0; x < 2; ++x) {
-      for (int k = 0; k < 2; ++k) {
-        mbar_init(&bs->s_full[x][k], 1);
-        mbar_init(&bs->p_full[x][k], kBM);
-        mbar_init(&bs->pv_done[x][k], 1);
-      }
-      mbar_init(&bs->mma_done[x], 1);
+      mbar_init(&bs->s_full[x], 1);
+      mbar_init(&bs->p_full[x], kBM);
+      mbar_init(&bs->pv_done[x], 1);
     }
+    mbar_init(&bs->mma_done, 1);
     bs->abort_flag = 0;
+    int nu = 0, na = 0;
+    for (int s = 0; s < p.n_seg; ++s) {
+      const int tu = seg_tiles(p.seg[s], qmaxU), ta = seg_tiles(p.seg[s], qmaxA);
+      bs->ntU[s] = (int16_t)tu;
+      bs->ntA[s] = (int16_t)ta;
+      nu += tu;
+      na += ta;
+    }
+    bs->nU = nu;
+    bs->nA = na;
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -223,21 +268,17 @@ __global__ void __launch_bounds__(kThreads2, 1) kp2_kernel(const __grid_constant
   const uint32_t tmem = bs->tmem_base;
 
   // K/V tiles of the union walk and tile A's share of them
-  int nU = 0, nA = 0;
-  for (int s = 0; s < p.n_seg; ++s) {
-    nU += seg_tiles(p.seg[s], qmaxU);
-    nA += seg_tiles(p.seg[s], qmaxA);
-  }
+  const int nU = bs->nU, nA = bs->nA;
 
   const uint32_t sQ = smem_addr(smem + Gm::kOffQ);
   const uint32_t sK = smem_addr(smem + Gm::kOffK);
   const uint32_t sV = smem_addr(smem + Gm::kOffV);
 
-  // Register split (128 x 104 + 256 x 200 = 384 x 168, the launch budget),
+  // Register split (128 x 88 + 256 x 208 = 384 x 168, the launch budget),
   // made inside each role's branch so the compiler sizes each role's code
   // for its own budget.
   if (warp < 4) {
-    umma::regs_dec<104>();
+    umma::regs_dec<88>();
     if (warp == 0) {
       // ---------------------------------------------------------- producer
       if (lane == 0 && nU > 0) {
@@ -246,29 +287,29 @@ __global__ void __launch_bounds__(kThreads2, 1) kp2_kernel(const __grid_constant
           for (int blk = 0; blk < Gm::kBlocks; ++blk)
             tma_load_4d(smem + Gm::kOffQ + x * Gm::kTileBytes + blk * Gm::kBlockBytes, &p.qmap,
                         blk * 64, qA0 + x * kBM, h, b, &bs->q_full);
-        int nk = 0, nv = 0;
+        int nk = 0, nv = 0;   // K and V tile loads issued
         bool ok = true;
         for (int s = 0; s < p.n_seg && ok; ++s) {
-          const int nt = seg_tiles(p.seg[s], qmaxU);
-          const int ntA = seg_tiles(p.seg[s], qmaxA);
+          const int nt = bs->ntU[s];
+          const int ntA = bs->ntA[s];
           const int bb = p.seg[s].bcast ? 0 : b;
           for (int t = 0; t < nt; ++t) {
-            // the empty barriers take one arrival per issuer; the issuer of a
-            // tile that sits this K/V tile out is arrived for here
+            // the empty barriers take one arrival per query tile; a tile
+            // that sits this K/V tile out is arrived for here
             const uint32_t absent = (t < ntA ? 0u : 1u) + (hasB ? 0u : 1u);
             const int st = nk % ST, use = nk / ST;
-            if (use > 0 && !(ok = wait_bar2(&bs->k_empty[st], (use - 1) & 1, bs, p.err))) break;
+            if (use > 0 && !(ok = wait_bar(&bs->k_empty[st], (use - 1) & 1, bs, p.err))) break;
             mbar_arrive_expect_tx(&bs->k_full[st], Gm::kTileBytes);
             for (int blk = 0; blk < Gm::kBlocks; ++blk)
               tma_load_4d(smem + Gm::kOffK + st * Gm::kTileBytes + blk * Gm::kBlockBytes,
                           &p.kmap[s], blk * 64, t * kBN, hk, bb, &bs->k_full[st]);
             if (absent) mbar_arrive_n(&bs->k_empty[st], absent);
             ++nk;
-            if (use > 0 && !(ok = wait_bar2(&bs->v_empty[st], (use - 1) & 1, bs, p.err))) break;
+            if (use > 0 && !(ok = wait_bar(&bs->v_empty[st], (use - 1) & 1, bs, p.err))) break;
             mbar_arrive_expect_tx(&bs->v_full[st], Gm::kTileBytes);
             for (int blk = 0; blk < Gm::kBlocks; ++blk)
               tma_load_4d(smem + Gm::kOffV + st * Gm::kTileBytes + blk * Gm::kBlockBytes,
-                          &p.vmap[s], blk * 64, t * kBN, hk, bb, &bs->v_full[st]);
+                          &vmaps[s], blk * 64, t * kBN, hk, bb, &bs->v_full[st]);
             if (absent) mbar_arrive_n(&bs->v_empty[st], absent);
             ++nv;
           }
@@ -281,178 +322,161 @@ __global__ void __launch_bounds__(kThreads2, 1) kp2_kernel(const __grid_constant
           if (uv > 0) mbar_wait(&bs->v_full[st], (uv - 1) & 1, p.err);
         }
       }
-    } else if ((warp == 1 || (warp == 2 && hasB)) && lane == 0 && nU > 0) {
-      // ---------------------------------------------------------- MMA issuers
-      // warp 1 issues tile A's MMAs, warp 2 tile B's: two independent
-      // commit chains, so one tile's waits never idle the other's work.
-      // Both walk every K/V tile: they wait on its full barriers (keeping
-      // the phase parity in step) and commit to its empty barriers when
-      // they read it; the producer arrives for an issuer that sits it out.
-      const int x = warp - 1;
-      constexpr bool kBf16 = Elem<T>::kDtype == HALO_DTYPE_BF16;
-      constexpr uint32_t kIdQK = umma::instr_desc_f16(kBM, kSub, kBf16, false, false);
-      constexpr uint32_t kIdPV = umma::instr_desc_f16(kBM, D, kBf16, false, true);
-      const uint64_t qdesc = umma::smem_desc_sw128(sQ + x * Gm::kTileBytes, 16, 1024);
+    } else if (warp == 1 && lane == 0 && nU > 0) {
+      // ---------------------------------------------------------- MMA issuer
+      constexpr uint32_t kIdQK = umma::instr_desc_f16(kBM, kBN, kBf16, false, false);
+      const uint32_t kIdPV = umma::instr_desc_f16(kBM, D, !p16, false, true);
       const uint64_t kdesc0 = umma::smem_desc_sw128(sK, 16, 1024);
       const uint64_t vdesc0 = umma::smem_desc_sw128(sV, Gm::kBlockBytes, 1024);
-      const uint32_t scol0 = tmem + x * 128;
-      const uint32_t ocol = tmem + Gm::kColO + x * D;
-      bool ok = wait_bar2(&bs->q_full, 0, bs, p.err);
-      // Two cursors walk the K/V tiles: QK runs two sub-tiles ahead of PV
-      // (QK(j+2) is issued right after PV(j), whose completion frees the
-      // score buffer it reuses), so the softmax of S(j+1) overlaps PV(j)
-      // and QK(j+2).  Tiles this tile sits out are only waited on.
-      struct Cursor {
-        int s, t, g, ntU, ntA;
-      };
-      auto load = [&](Cursor& c) {
-        while (c.s < p.n_seg) {
-          c.ntU = seg_tiles(p.seg[c.s], qmaxU);
-          c.ntA = seg_tiles(p.seg[c.s], qmaxA);
-          if (c.t < c.ntU) return;
+      const int nX[2] = {nA, hasB ? nU : 0};
+      // cursors: next K/V tile each query tile takes part in, for QK and PV
+      const int n_seg = p.n_seg;
+      auto seek = [&](Cursor& c, int x) {
+        while (c.s < n_seg) {
+          const int ntU = bs->ntU[c.s];
+          const int ntX = x ? ntU : bs->ntA[c.s];
+          if (c.t < ntX) return;
+          c.g += ntU - c.t;   // the rest of this segment is sat out
           ++c.s;
           c.t = 0;
         }
       };
-      auto next = [&](Cursor& c) {
-        ++c.t;
-        ++c.g;
-        if (c.t >= c.ntU) {
-          ++c.s;
-          c.t = 0;
-          load(c);
-        }
-      };
-      auto takes_part = [&](const Cursor& c) { return x ? hasB : (c.t < c.ntA); };
-      Cursor cq{0, 0, 0, 0, 0}, cp{0, 0, 0, 0, 0};
-      load(cq);
-      load(cp);
-      int jq = 0, jp = 0, hq = 0, hp = 0;
-      // K side: skip tiles this tile sits out, then QK of the next sub-tile
-      auto qk_step = [&]() -> int {   // 1 issued, 0 walk finished, -1 error
-        while (cq.s < p.n_seg && !takes_part(cq)) {
-          const int st = cq.g % ST;
-          if (!wait_bar2(&bs->k_full[st], (cq.g / ST) & 1, bs, p.err)) return -1;
-          next(cq);
-        }
-        if (cq.s >= p.n_seg) return 0;
-        const int st = cq.g % ST;
-        if (hq == 0 && !wait_bar2(&bs->k_full[st], (cq.g / ST) & 1, bs, p.err)) return -1;
-        const int j = jq, bf = j & 1;
-        if (j >= 2 && !wait_bar2(&bs->pv_done[x][bf], ((j - 2) >> 1) & 1, bs, p.err)) return -1;
-        umma::fence_after_sync();
-        const uint64_t kd = kdesc0 + (uint64_t)((st * Gm::kTileBytes + hq * kSub * 128) >> 4);
+      Cursor qc[2] = {{0, 0, 0}, {0, 0, 0}}, pc[2] = {{0, 0, 0}, {0, 0, 0}};
+      for (int x = 0; x < 2; ++x) {
+        seek(qc[x], x);
+        seek(pc[x], x);
+      }
+      int jq[2] = {0, 0}, jp[2] = {0, 0};
+      // Tile B's first QK waits for tile A's first P V when both start on
+      // the walk's first K/V tile, so the two softmax groups run half a
+      // step apart.  (Only then: if A starts later, A's first V tile may
+      // need a ring stage that B's early tiles must free first.)
+      const bool gateB = nX[0] > 0 && qc[0].g == 0;
+      bool ok = wait_bar(&bs->q_full, 0, bs, p.err);
+      uint64_t t_idle = 0;
+      int idle = 0;
+      while (ok) {
+        bool did = false;
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = ((kk >> 2) * Gm::kBlockBytes + (kk & 3) * 32) >> 4;
-          umma::mma_ss(scol0 + bf * kSub, qdesc + off, kd + off, kIdQK, kk > 0);
-        }
-        umma::commit(&bs->s_full[x][bf]);
-        ++jq;
-        if (hq == 1) {
-          umma::commit(&bs->k_empty[st]);
-          next(cq);
-          hq = 0;
-        } else {
-          hq = 1;
-        }
-        return 1;
-      };
-      // V side: skip tiles this tile sits out, then PV of the next sub-tile
-      auto pv_step = [&]() -> bool {
-        while (!takes_part(cp)) {
-          const int st = cp.g % ST;
-          if (!wait_bar2(&bs->v_full[st], (cp.g / ST) & 1, bs, p.err)) return false;
-          next(cp);
-        }
-        const int st = cp.g % ST;
-        if (hp == 0 && !wait_bar2(&bs->v_full[st], (cp.g / ST) & 1, bs, p.err)) return false;
-        const int j = jp, bf = j & 1;
-        if (!wait_bar2(&bs->p_full[x][bf], (j >> 1) & 1, bs, p.err)) return false;
-        umma::fence_after_sync();
-        const uint32_t pcol = scol0 + bf * kSub;
-        const uint64_t vd = vdesc0 + (uint64_t)((st * Gm::kTileBytes + hp * kSub * 128) >> 4);
+        for (int x = 0; x < 2; ++x) {
+          // O_X += P_X(j) V(j): P written and V landed
+          if (jp[x] < jq[x]) {
+            const int g = pc[x].g, st = g % ST;
+            if (mbar_test(&bs->p_full[x], jp[x] & 1) &&
+                mbar_test(&bs->v_full[st], (g / ST) & 1)) {
+              umma::fence_after_sync();
+              const uint32_t pcol = tmem + x * 128;
+              const uint32_t ocol = tmem + Gm::kColO + x * D;
+              const uint64_t vd = opaque(vdesc0 + (uint64_t)((st * Gm::kTileBytes) >> 4));
+              const bool acc0 = jp[x] > 0;
 #pragma unroll
-        for (int part = 0; part < (kSplitP ? 2 : 1); ++part)
+              for (int kk = 0; kk < kBN / 16; ++kk)
+                umma::mma_ts(ocol, pcol + kk * 8, vd + (uint64_t)((kk * 16 * 128) >> 4), kIdPV,
+                             acc0 || kk > 0);
+              if (!p16) {
 #pragma unroll
-          for (int kk = 0; kk < kSub / 16; ++kk)
-            umma::mma_ts(ocol, pcol + (kk >> 1) * 32 + part * 16 + (kk & 1) * 8,
-                         vd + (uint64_t)((kk * 16 * 128) >> 4), kIdPV, (j > 0) || part || kk);
-        umma::commit(&bs->pv_done[x][bf]);
-        ++jp;
-        if (hp == 1) {
-          umma::commit(&bs->v_empty[st]);
-          next(cp);
-          hp = 0;
-        } else {
-          hp = 1;
+                for (int kk = 0; kk < kBN / 16; ++kk)
+                  umma::mma_ts(ocol, pcol + 64 + kk * 8, vd + (uint64_t)((kk * 16 * 128) >> 4),
+                               kIdPV, true);
+              }
+              umma::commit(&bs->pv_done[x]);
+              umma::commit(&bs->v_empty[st]);
+              ++jp[x];
+              ++pc[x].t;
+              ++pc[x].g;
+              seek(pc[x], x);
+              did = true;
+            }
+          }
+          // S_X = Q_X K(j)^T: S_X free (previous PV_X completed) and K landed
+          if (jq[x] < nX[x] && jq[x] == jp[x] &&
+              (x == 0 || jq[1] > 0 || !gateB || jp[0] > 0)) {
+            const int g = qc[x].g, st = g % ST;
+            if ((jq[x] == 0 || mbar_test(&bs->pv_done[x], (jq[x] - 1) & 1)) &&
+                mbar_test(&bs->k_full[st], (g / ST) & 1)) {
+              umma::fence_after_sync();
+              const uint64_t qd = opaque(umma::smem_desc_sw128(sQ + x * Gm::kTileBytes, 16, 1024));
+              const uint64_t kd = opaque(kdesc0 + (uint64_t)((st * Gm::kTileBytes) >> 4));
+#pragma unroll
+              for (int kk = 0; kk < D / 16; ++kk) {
+                const uint32_t off = ((kk >> 2) * Gm::kBlockBytes + (kk & 3) * 32) >> 4;
+                umma::mma_ss(tmem + x * 128, qd + off, kd + off, kIdQK, kk > 0);
+              }
+              umma::commit(&bs->s_full[x]);
+              umma::commit(&bs->k_empty[st]);
+              ++jq[x];
+              ++qc[x].t;
+              ++qc[x].g;
+              seek(qc[x], x);
+              did = true;
+            }
+          }
         }
-        return true;
-      };
-      // Offset tile B by one softmax: its chain starts once tile A's first P
-      // is out, so the two softmax warpgroups alternate with the MMAs
-      // instead of competing at the same moments.
-      if (x == 1 && ok && p.seg[0].len > 0 && seg_tiles(p.seg[0], qmaxA) > 0)
-        ok = wait_bar2(&bs->p_full[0][0], 0, bs, p.err);
-      int rq = ok ? qk_step() : -1;
-      if (rq > 0) rq = qk_step();
-      ok = rq >= 0;
-      while (ok && jp < jq) {
-        if (!(ok = pv_step())) break;
-        if (rq > 0) {
-          rq = qk_step();
-          ok = rq >= 0;
+        if (jp[0] >= nX[0] && jp[1] >= nX[1]) break;
+        if (did) {
+          idle = 0;
+          continue;
+        }
+        // nothing ready: back off briefly (the softmax warps share this
+        // warp's scheduler), bounded idle time, stop if another role aborted
+        if (idle >= 4) __nanosleep(32);
+        if (++idle == 64) t_idle = globaltimer_ns();
+        if (idle > 64 && (idle & 63) == 0) {
+          if (*reinterpret_cast<volatile int*>(&bs->abort_flag)) {
+            ok = false;
+          } else if (globaltimer_ns() - t_idle > kWaitLimitNs) {
+            set_device_error(p.err, static_cast<unsigned int>(-HALO_ERR_TIMEOUT));
+            *reinterpret_cast<volatile int*>(&bs->abort_flag) = 1;
+            ok = false;
+          }
         }
       }
       // this thread's MMAs complete before the CTA can free TMEM
-      umma::commit(&bs->mma_done[x]);
-      mbar_wait(&bs->mma_done[x], 0, p.err);
+      umma::commit(&bs->mma_done);
+      mbar_wait(&bs->mma_done, 0, p.err);
     }
   } else {
-    umma::regs_inc<200>();
+    umma::regs_inc<208>();
     // ------------------------------------------------------------ softmax X
     const int x = (warp - 4) >> 2;              // 0: tile A, 1: tile B
     const int sub = warp & 3;
     const int r = sub * 32 + lane;
     const uint32_t trow = tmem + ((uint32_t)(sub * 32) << 16);
+    const uint32_t scol = x * 128;
     const uint32_t ocol = Gm::kColO + x * D;
     const bool active = x == 0 || hasB;
     const int64_t qmin = x ? qminB : qminA;
     const int64_t qmaxX = x ? qmaxB : qmaxA;
     const int64_t qpos = qmin + r;
-    int nX = 0;                                  // sub-tiles of tile X
     float m = -INFINITY, l = 0.f;
     bool ok = true;
     int j = 0;
     for (int s = 0; s < p.n_seg && ok && active; ++s) {
       const Seg sg = p.seg[s];
-      const int nt = seg_tiles(sg, qmaxX);
-      for (int t = 0; t < nt * 2; ++t, ++j) {
-        const int bf = j & 1;
-        const uint32_t scol = x * 128 + bf * kSub;
-        ok = __all_sync(0xffffffffu, wait_bar2(&bs->s_full[x][bf], (j >> 1) & 1, bs, p.err));
+      const int nt = x ? bs->ntU[s] : bs->ntA[s];
+      for (int t = 0; t < nt; ++t, ++j) {
+        ok = __all_sync(0xffffffffu, wait_bar(&bs->s_full[x], j & 1, bs, p.err));
         if (!ok) break;
         umma::fence_after_sync();
-        const int row0 = (t >> 1) * kBN + (t & 1) * kSub;
+        const int row0 = t * kBN;
         const int64_t kpos0 = sg.start + row0;
-        const bool full = (row0 + kSub <= sg.len) && (!sg.causal || kpos0 + kSub - 1 <= qmin);
+        const bool full = (row0 + kBN <= sg.len) && (!sg.causal || kpos0 + kBN - 1 <= qmin);
         const int lim_len = sg.len - row0;
-        const int64_t lim_pos = sg.causal ? qpos - kpos0 : (int64_t)kSub;
-        // the sub-tile's 64 scores: two loads, one wait
-        float sv[kSub];
-        umma::tmem_ld32(trow + scol, sv);
-        umma::tmem_ld32(trow + scol + 32, sv + 32);
+        const int64_t lim_pos = sg.causal ? qpos - kpos0 : (int64_t)kBN;
+        float sv[kBN];
+#pragma unroll
+        for (int c = 0; c < kBN / 32; ++c) umma::tmem_ld32(trow + scol + c * 32, sv + c * 32);
         umma::tmem_wait_ld();
         if (!full) {
 #pragma unroll
-          for (int c = 0; c < kSub; ++c)
+          for (int c = 0; c < kBN; ++c)
             if (!(c < lim_len && (int64_t)c <= lim_pos)) sv[c] = -INFINITY;
         }
         float mx8[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) mx8[e] = sv[e];
 #pragma unroll
-        for (int c = 8; c < kSub; ++c) mx8[c & 7] = fmaxf(mx8[c & 7], sv[c]);
+        for (int c = 8; c < kBN; ++c) mx8[c & 7] = fmaxf(mx8[c & 7], sv[c]);
         const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
                                fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]))) *
                          p.scale_log2;
@@ -464,11 +488,8 @@ __global__ void __launch_bounds__(kThreads2, 1) kp2_kernel(const __grid_constant
           m = mx;
         }
         if (j > 0 && __any_sync(0xffffffffu, grow)) {
-          // O_X must be quiescent: wait for O_X += P_X(j-1) V
-          ok = __all_sync(0xffffffffu, wait_bar2(&bs->pv_done[x][bf ^ 1], ((j - 1) >> 1) & 1,
-                                                  bs, p.err));
-          if (!ok) break;
-          umma::fence_after_sync();
+          // O_X is quiescent: QK_X(j) was issued after PV_X(j-1) completed,
+          // and PV_X(j) waits for this P
 #pragma unroll
           for (int c = 0; c < D / 32; ++c) {
             float ov[32];
@@ -483,40 +504,50 @@ __global__ void __launch_bounds__(kThreads2, 1) kp2_kernel(const __grid_constant
         const float nmu = (m == -INFINITY) ? 0.f : -m;
         const float sl2 = p.scale_log2;
         float rs4[4] = {0.f, 0.f, 0.f, 0.f};
+        if (p16) {
 #pragma unroll
-        for (int c = 0; c < kSub / 32; ++c) {
-          uint32_t hi[16], lo[16];
+          for (int c = 0; c < kBN / 32; ++c) {
+            uint32_t hv[16];
 #pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            const float p0 = ex2(fmaf(sv[c * 32 + 2 * e], sl2, nmu));
-            const float p1 = ex2(fmaf(sv[c * 32 + 2 * e + 1], sl2, nmu));
-            rs4[e & 3] += p0 + p1;
-            if constexpr (kSplitP) {
-              // hi = p truncated to bf16 (upper halves, one byte permute
-              // per pair), lo = rnd(p - hi): ~16 significant bits in all
-              const uint32_t b0 = __float_as_uint(p0), b1 = __float_as_uint(p1);
-              hi[e] = __byte_perm(b0, b1, 0x7632);
-              lo[e] = pack2<T>(p0 - __uint_as_float(b0 & 0xFFFF0000u),
-                               p1 - __uint_as_float(b1 & 0xFFFF0000u));
-            } else {
-              hi[e] = pack2<T>(p0, p1);
+            for (int e = 0; e < 16; ++e) {
+              const float p0 = ex2(fmaf(sv[c * 32 + 2 * e], sl2, nmu));
+              const float p1 = ex2(fmaf(sv[c * 32 + 2 * e + 1], sl2, nmu));
+              rs4[e & 3] += p0 + p1;
+              hv[e] = pack_h2(p0, p1);
             }
+            umma::tmem_st16u(trow + scol + c * 16, hv);
           }
-          umma::tmem_st16u(trow + scol + c * 32, hi);
-          if constexpr (kSplitP) umma::tmem_st16u(trow + scol + c * 32 + 16, lo);
+        } else {
+#pragma unroll
+          for (int c = 0; c < kBN / 32; ++c) {
+            uint32_t hv[16], lv[16];
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              const float p0 = ex2(fmaf(sv[c * 32 + 2 * e], sl2, nmu));
+              const float p1 = ex2(fmaf(sv[c * 32 + 2 * e + 1], sl2, nmu));
+              rs4[e & 3] += p0 + p1;
+              // hi = p truncated to bf16 (upper halves, one byte permute per
+              // pair), lo = rnd(p - hi): ~16 significant bits in all
+              const uint32_t b0 = __float_as_uint(p0), b1 = __float_as_uint(p1);
+              hv[e] = __byte_perm(b0, b1, 0x7632);
+              lv[e] = pack_bf2(p0 - __uint_as_float(b0 & 0xFFFF0000u),
+                               p1 - __uint_as_float(b1 & 0xFFFF0000u));
+            }
+            umma::tmem_st16u(trow + scol + c * 16, hv);
+            umma::tmem_st16u(trow + scol + 64 + c * 16, lv);
+          }
         }
         l += (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
         umma::tmem_wait_st();
         umma::fence_before_sync();
-        mbar_arrive(&bs->p_full[x][bf]);
+        mbar_arrive(&bs->p_full[x]);
       }
     }
-    nX = j;
+    const int nX = j;
 
     // ---- epilogue of tile X: thread r finalises query row q0 + r
     if (active && ok && nX > 0) {
-      ok = __all_sync(0xffffffffu, wait_bar2(&bs->pv_done[x][(nX - 1) & 1], ((nX - 1) >> 1) & 1,
-                                              bs, p.err));
+      ok = __all_sync(0xffffffffu, wait_bar(&bs->pv_done[x], (nX - 1) & 1, bs, p.err));
       if (ok) umma::fence_after_sync();
     }
     const int validX = x ? validB : validA;
@@ -572,10 +603,10 @@ __global__ void __launch_bounds__(kThreads2, 1) kp2_kernel(const __grid_constant
           uint4* od = reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.out) + off + c * 32);
 #pragma unroll
           for (int e = 0; e < 32; e += 8)
-            od[e / 8] = make_uint4(pack2<T>(ov[e] * inv, ov[e + 1] * inv),
-                                   pack2<T>(ov[e + 2] * inv, ov[e + 3] * inv),
-                                   pack2<T>(ov[e + 4] * inv, ov[e + 5] * inv),
-                                   pack2<T>(ov[e + 6] * inv, ov[e + 7] * inv));
+            od[e / 8] = make_uint4(Elem<T>::pack(ov[e] * inv, ov[e + 1] * inv),
+                                   Elem<T>::pack(ov[e + 2] * inv, ov[e + 3] * inv),
+                                   Elem<T>::pack(ov[e + 4] * inv, ov[e + 5] * inv),
+                                   Elem<T>::pack(ov[e + 6] * inv, ov[e + 7] * inv));
         }
       }
     }
@@ -588,6 +619,60 @@ __global__ void __launch_bounds__(kThreads2, 1) kp2_kernel(const __grid_constant
     umma::fence_after_sync();
     umma::tmem_dealloc(tmem, kTmemCols);
   }
+}
+
+// ======================================================================
+// v16_kernel: fp16 copy of each segment's bf16 V rows into the workspace
+// (layout [batch'][H_kv][len][D] per segment, batch' = 1 for a segment that
+// broadcasts the batch) and a flag raised when a finite |v| >= 2^16 would
+// overflow fp16.  Memory-bound: 16-byte loads and stores, grid (row blocks,
+// segment, batch' x H_kv).
+struct V16Seg {
+  const uint16_t* src;    // bf16 bits
+  int64_t sb, sh, st;     // element strides
+  uint16_t* dst;          // fp16 bits
+  int32_t len;
+  int32_t nb;             // batch rows stored (1 when broadcast)
+};
+
+struct V16Params {
+  V16Seg seg[kMaxSegs];
+  int32_t H_kv, D;
+  unsigned int* flag;
+};
+
+constexpr int kV16Rows = 64;     // rows per CTA
+constexpr int kV16Threads = 128;
+
+__global__ void __launch_bounds__(kV16Threads) v16_kernel(const __grid_constant__ V16Params p) {
+  const V16Seg& sg = p.seg[blockIdx.y];
+  const int bh = blockIdx.z;
+  if (bh >= sg.nb * p.H_kv) return;
+  const int b = bh / p.H_kv, hk = bh % p.H_kv;
+  const int r0 = blockIdx.x * kV16Rows;
+  if (r0 >= sg.len) return;
+  const int rows = min(kV16Rows, sg.len - r0);
+  const int vpr = p.D / 8;                      // 16-byte vectors per row
+  const uint16_t* src = sg.src + (int64_t)b * sg.sb + (int64_t)hk * sg.sh;
+  uint16_t* dst = sg.dst + ((int64_t)bh * sg.len) * p.D;
+  unsigned int bad = 0;
+  for (int i = threadIdx.x; i < rows * vpr; i += kV16Threads) {
+    const int r = r0 + i / vpr, c = i % vpr;
+    const uint4 w = *reinterpret_cast<const uint4*>(src + (int64_t)r * sg.st + c * 8);
+    const uint32_t in[4] = {w.x, w.y, w.z, w.w};
+    uint32_t out[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const uint32_t lo = in[k] & 0xFFFFu, hi = in[k] >> 16;
+      // finite magnitude at or above 2^16 (bf16 0x4780) overflows fp16
+      bad |= (((lo & 0x7FFFu) >= 0x4780u) & ((lo & 0x7FFFu) < 0x7F80u)) |
+             (((hi & 0x7FFFu) >= 0x4780u) & ((hi & 0x7FFFu) < 0x7F80u));
+      out[k] = pack_h2(__uint_as_float(lo << 16), __uint_as_float(hi << 16));
+    }
+    *reinterpret_cast<uint4*>(dst + (int64_t)r * p.D + c * 8) =
+        make_uint4(out[0], out[1], out[2], out[3]);
+  }
+  if (__syncthreads_or(bad) && threadIdx.x == 0) atomicOr(p.flag, 1u);
 }
 
 }  // namespace prefill
@@ -693,20 +778,20 @@ static bool pf_continues(const halo_kv_chunk_t& a, int64_t a_len, const halo_kv_
 }
 
 template <typename T, int D>
-static int launch_kp2(const prefill::Params& prm, int grid, cudaStream_t st) {
-  using Gm = prefill::Geom2<D>;
+static int launch_kp3(const prefill::Params& prm, int grid, cudaStream_t st) {
+  using Gm = prefill::Geom<D>;
   static std::once_flag once[64];
   int dev = 0;
   cudaGetDevice(&dev);
   cudaError_t attr_err = cudaSuccess;
   std::call_once(once[dev & 63], [&] {
-    attr_err = cudaFuncSetAttribute(prefill::kp2_kernel<T, D>,
+    attr_err = cudaFuncSetAttribute(prefill::kp3_kernel<T, D>,
                                     cudaFuncAttributeMaxDynamicSharedMemorySize, Gm::kSmemBytes);
   });
-  if (attr_err != cudaSuccess) return cuda_fail(attr_err, "kp2_kernel shared-memory attribute");
-  prefill::kp2_kernel<T, D><<<grid, prefill::kThreads2, Gm::kSmemBytes, st>>>(prm);
+  if (attr_err != cudaSuccess) return cuda_fail(attr_err, "kp3_kernel shared-memory attribute");
+  prefill::kp3_kernel<T, D><<<grid, prefill::kThreads, Gm::kSmemBytes, st>>>(prm);
   cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, "kp2_kernel launch");
+  if (e != cudaSuccess) return cuda_fail(e, "kp3_kernel launch");
   count_launches();
   return HALO_OK;
 }
@@ -719,50 +804,10 @@ struct PfSeg {
   bool bcast;
 };
 
-// K/V tiles of a segment visible to query positions <= qmax (host copy of
-// prefill::seg_tiles).
-static int pf_seg_tiles(const PfSeg& sg, int64_t qmax) {
-  int64_t n = (sg.len + prefill::kBN - 1) / prefill::kBN;
-  if (sg.c.causal) {
-    const int64_t lim = qmax - sg.c.start;
-    if (lim < 0) return 0;
-    n = std::min<int64_t>(n, lim / prefill::kBN + 1);
-  }
-  return (int)n;
-}
-
-// Whether every query-tile pair (A, B) of the call sees, along the union
-// walk of its K/V tiles, at most one tile in a row that A sits out.  A run
-// of two or more can stall A's MMA issuer: it waits for the K tile after the
-// run while the producer, one ring stage later, waits for A's pending P V
-// to free a V stage.  Within one segment A sits out at most the last tile
-// (query tiles are 128 rows, K/V tiles 128 keys apart), so runs only form
-// across segments.
-static bool pf_order_ok(const PfSeg* segs, int n, int T_q, int64_t q_pos0) {
-  const int n_qtiles = (T_q + prefill::kBM - 1) / prefill::kBM;
-  for (int pair = 0; 2 * pair + 1 < n_qtiles; ++pair) {
-    const int qA0 = 2 * pair * prefill::kBM;
-    const int64_t qmaxA = q_pos0 + qA0 + prefill::kBM - 1;   // A is full when B exists
-    const int validB = std::min(prefill::kBM, T_q - (qA0 + prefill::kBM));
-    const int64_t qmaxB = q_pos0 + qA0 + prefill::kBM + validB - 1;
-    int64_t run = 0;
-    for (int i = 0; i < n; ++i) {
-      const int ntU = pf_seg_tiles(segs[i], qmaxB), ntA = pf_seg_tiles(segs[i], qmaxA);
-      run = (ntA > 0 ? 0 : run) + (ntU - ntA);
-      if (run > 1) return false;
-    }
-  }
-  return true;
-}
-
-}  // namespace halo
-
-using namespace halo;
-
-extern "C" int32_t halo_prefill_attention(const halo_prefill_problem_t* pb,
-                                          const halo_kv_chunk_t* chunks, int32_t n_chunks,
-                                          const halo_prefill_out_t* po, halo_stream_t stream) {
-  if (!pb || !po) return fail(HALO_ERR_INVALID_ARG, "problem/out is NULL");
+// Validate the problem and the output description (everything but the
+// chunks).
+static int pf_check(const halo_prefill_problem_t* pb, const halo_prefill_out_t* po, bool need_out) {
+  if (!pb || (need_out && !po)) return fail(HALO_ERR_INVALID_ARG, "problem/out is NULL");
   if (pb->B <= 0 || pb->H <= 0 || pb->H_kv <= 0 || pb->T_q < 0 || pb->D <= 0)
     return fail(HALO_ERR_INVALID_ARG, "non-positive dimension (B=%d H=%d H_kv=%d T_q=%d D=%d)",
                 pb->B, pb->H, pb->H_kv, pb->T_q, pb->D);
@@ -773,7 +818,7 @@ extern "C" int32_t halo_prefill_attention(const halo_prefill_problem_t* pb,
     return fail(HALO_ERR_UNSUPPORTED, "prefill kernel head_dim %d (64 or 128)", pb->D);
   if (!(pb->scale > 0.f) || !std::isfinite(pb->scale))
     return fail(HALO_ERR_UNSUPPORTED, "prefill kernel needs a positive finite scale");
-  if (n_chunks < 0 || (n_chunks > 0 && !chunks)) return fail(HALO_ERR_INVALID_ARG, "bad chunk list");
+  if (!need_out) return HALO_OK;
   if (po->mode != HALO_MERGE_FINALIZE && po->mode != HALO_MERGE_ACCUMULATE)
     return fail(HALO_ERR_INVALID_ARG, "bad mode %d", po->mode);
   const bool have_state = po->m || po->l || po->o;
@@ -782,7 +827,6 @@ extern "C" int32_t halo_prefill_attention(const halo_prefill_problem_t* pb,
   if (po->mode == HALO_MERGE_ACCUMULATE && !have_state)
     return fail(HALO_ERR_INVALID_ARG, "accumulate needs m, l, o");
   if (po->o && !aligned16(po->o)) return fail(HALO_ERR_MISALIGNED, "o must be 16-byte aligned");
-  const int D = pb->D;
   if (po->mode == HALO_MERGE_FINALIZE) {
     if (!po->out) return fail(HALO_ERR_INVALID_ARG, "out is NULL");
     const int oe = po->out_dtype == HALO_DTYPE_F32 ? 4 : 2;
@@ -792,14 +836,13 @@ extern "C" int32_t halo_prefill_attention(const halo_prefill_problem_t* pb,
         (po->out_stride_t * oe) % 16)
       return fail(HALO_ERR_MISALIGNED, "out rows must be 16-byte aligned");
   }
-  if (pb->T_q == 0) return HALO_OK;
-  if (!pb->q || !aligned16(pb->q) || (pb->q_stride_t * 2) % 16 || (pb->q_stride_h * 2) % 16 ||
-      (pb->B > 1 && (pb->q_stride_b * 2) % 16) || pb->q_stride_t <= 0 || pb->q_stride_h <= 0)
-    return fail(HALO_ERR_MISALIGNED, "q must be 16-byte aligned with 16-byte row strides");
+  return HALO_OK;
+}
 
-  // ---- segments: coalesce chunks contiguous in memory and position
-  static thread_local prefill::Params prm;
-  PfSeg segs[prefill::kMaxSegs];
+// Coalesce chunks contiguous in memory and position into segments (at most
+// kMaxSegs), validating each chunk.
+static int pf_segments(const halo_kv_chunk_t* chunks, int32_t n_chunks, PfSeg* segs, int* n_out) {
+  if (n_chunks < 0 || (n_chunks > 0 && !chunks)) return fail(HALO_ERR_INVALID_ARG, "bad chunk list");
   int n_seg = 0;
   halo_kv_chunk_t cur{};
   int64_t cur_len = 0;
@@ -834,14 +877,57 @@ extern "C" int32_t halo_prefill_attention(const halo_prefill_problem_t* pb,
   }
   int rc = flush();
   if (rc != HALO_OK) return rc;
-  if (!pf_order_ok(segs, n_seg, pb->T_q, pb->q_pos0))
-    return fail(HALO_ERR_SPLIT, "chunk order: a query tile would sit out two or more K/V tiles "
-                "in a row; pass the chunks in smaller calls");
+  *n_out = n_seg;
+  return HALO_OK;
+}
+
+static int64_t align256(int64_t x) { return (x + 255) & ~int64_t(255); }
+
+// Bytes of segment i's fp16 V copy in the workspace.
+static int64_t pf_v16_bytes(const PfSeg& sg, const halo_prefill_problem_t* pb) {
+  return align256((int64_t)(sg.bcast ? 1 : pb->B) * pb->H_kv * sg.len * pb->D * 2);
+}
+
+static int64_t pf_workspace_bytes(const PfSeg* segs, int n_seg, const halo_prefill_problem_t* pb) {
+  if (pb->dtype != HALO_DTYPE_BF16 || n_seg == 0) return 0;
+  int64_t n = prefill::kWsHeader;
+  for (int i = 0; i < n_seg; ++i) n += pf_v16_bytes(segs[i], pb);
+  return n;
+}
+
+static int pf_run(const halo_prefill_problem_t* pb, const halo_kv_chunk_t* chunks,
+                  int32_t n_chunks, const halo_prefill_out_t* po, void* workspace,
+                  int64_t workspace_bytes, halo_stream_t stream) {
+  int rc = pf_check(pb, po, true);
+  if (rc != HALO_OK) return rc;
+  PfSeg segs[prefill::kMaxSegs];
+  int n_seg = 0;
+  rc = pf_segments(chunks, n_chunks, segs, &n_seg);
+  if (rc != HALO_OK) return rc;
+  if (pb->T_q == 0) return HALO_OK;
+  if (!pb->q || !aligned16(pb->q) || (pb->q_stride_t * 2) % 16 || (pb->q_stride_h * 2) % 16 ||
+      (pb->B > 1 && (pb->q_stride_b * 2) % 16) || pb->q_stride_t <= 0 || pb->q_stride_h <= 0)
+    return fail(HALO_ERR_MISALIGNED, "q must be 16-byte aligned with 16-byte row strides");
+  const int D = pb->D;
+  const bool v16 = workspace != nullptr && pb->dtype == HALO_DTYPE_BF16 && n_seg > 0;
+  if (v16) {
+    const int64_t need = pf_workspace_bytes(segs, n_seg, pb);
+    if (workspace_bytes < need)
+      return fail(HALO_ERR_WORKSPACE, "prefill workspace has %lld bytes, needs %lld",
+                  (long long)workspace_bytes, (long long)need);
+    if (reinterpret_cast<uintptr_t>(workspace) & 255)
+      return fail(HALO_ERR_MISALIGNED, "prefill workspace must be 256-byte aligned");
+  }
+
+  static thread_local prefill::Params prm;
+  static thread_local prefill::V16Params vp;
+  char* ws = static_cast<char*>(workspace);
+  int64_t ws_off = prefill::kWsHeader;
   for (int i = 0; i < n_seg; ++i) {
     const halo_kv_chunk_t& c = segs[i].c;
     const bool bk = segs[i].bcast;
-    const uint64_t dims[4] = {(uint64_t)D, (uint64_t)segs[i].len, (uint64_t)pb->H_kv,
-                              (uint64_t)(bk ? 1 : pb->B)};
+    const uint64_t nb = bk ? 1 : pb->B;
+    const uint64_t dims[4] = {(uint64_t)D, (uint64_t)segs[i].len, (uint64_t)pb->H_kv, nb};
     const uint64_t ks[3] = {(uint64_t)c.k_stride_t * 2, (uint64_t)c.k_stride_h * 2,
                             (uint64_t)(bk || pb->B == 1 ? c.k_stride_h * 2 * pb->H_kv
                                                         : c.k_stride_b * 2)};
@@ -852,6 +938,23 @@ extern "C" int32_t halo_prefill_attention(const halo_prefill_problem_t* pb,
     if (rc != HALO_OK) return rc;
     rc = pf_encode(c.v, pb->dtype, dims, vs, &prm.vmap[i]);
     if (rc != HALO_OK) return rc;
+    if (v16) {
+      // contiguous fp16 copy [nb][H_kv][len][D]
+      void* dst = ws + ws_off;
+      const uint64_t s16[3] = {(uint64_t)D * 2, (uint64_t)segs[i].len * D * 2,
+                               (uint64_t)pb->H_kv * segs[i].len * D * 2};
+      rc = pf_encode(dst, HALO_DTYPE_F16, dims, s16, &prm.v16map[i]);
+      if (rc != HALO_OK) return rc;
+      prefill::V16Seg& vsg = vp.seg[i];
+      vsg.src = static_cast<const uint16_t*>(c.v);
+      vsg.sb = bk ? 0 : c.v_stride_b;
+      vsg.sh = c.v_stride_h;
+      vsg.st = c.v_stride_t;
+      vsg.dst = static_cast<uint16_t*>(dst);
+      vsg.len = (int32_t)segs[i].len;
+      vsg.nb = (int32_t)nb;
+      ws_off += pf_v16_bytes(segs[i], pb);
+    }
     prm.seg[i].start = c.start;
     prm.seg[i].len = (int32_t)segs[i].len;
     prm.seg[i].causal = c.causal ? 1 : 0;
@@ -868,6 +971,7 @@ extern "C" int32_t halo_prefill_attention(const halo_prefill_problem_t* pb,
     if (rc != HALO_OK) return rc;
   }
   prm.n_seg = n_seg;
+  prm.v16_flag = v16 ? reinterpret_cast<const unsigned int*>(ws) : nullptr;
   prm.B = pb->B;
   prm.H = pb->H;
   prm.G = pb->H / pb->H_kv;
@@ -890,12 +994,60 @@ extern "C" int32_t halo_prefill_attention(const halo_prefill_problem_t* pb,
   if (grid > INT32_MAX) return fail(HALO_ERR_UNSUPPORTED, "grid too large");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (pb->event_begin) cudaEventRecord(static_cast<cudaEvent_t>(pb->event_begin), st);
+  if (v16) {
+    // the fp16 V copies and the range flag, on the same stream
+    cudaError_t e = cudaMemsetAsync(ws, 0, sizeof(unsigned int), st);
+    if (e != cudaSuccess) return cuda_fail(e, "clear prefill range flag");
+    int64_t max_len = 0, max_bh = 0;
+    for (int i = 0; i < n_seg; ++i) {
+      max_len = std::max<int64_t>(max_len, segs[i].len);
+      max_bh = std::max<int64_t>(max_bh, (int64_t)vp.seg[i].nb * pb->H_kv);
+    }
+    if (max_bh > 65535) return fail(HALO_ERR_UNSUPPORTED, "batch x H_kv too large");
+    vp.H_kv = pb->H_kv;
+    vp.D = D;
+    vp.flag = reinterpret_cast<unsigned int*>(ws);
+    const dim3 vgrid((unsigned)((max_len + prefill::kV16Rows - 1) / prefill::kV16Rows),
+                     (unsigned)n_seg, (unsigned)max_bh);
+    prefill::v16_kernel<<<vgrid, prefill::kV16Threads, 0, st>>>(vp);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "v16_kernel launch");
+    count_launches();
+  }
   if (pb->dtype == HALO_DTYPE_BF16)
-    rc = D == 128 ? launch_kp2<__nv_bfloat16, 128>(prm, (int)grid, st)
-                  : launch_kp2<__nv_bfloat16, 64>(prm, (int)grid, st);
+    rc = D == 128 ? launch_kp3<__nv_bfloat16, 128>(prm, (int)grid, st)
+                  : launch_kp3<__nv_bfloat16, 64>(prm, (int)grid, st);
   else
-    rc = D == 128 ? launch_kp2<__half, 128>(prm, (int)grid, st)
-                  : launch_kp2<__half, 64>(prm, (int)grid, st);
+    rc = D == 128 ? launch_kp3<__half, 128>(prm, (int)grid, st)
+                  : launch_kp3<__half, 64>(prm, (int)grid, st);
   if (rc == HALO_OK && pb->event_end) cudaEventRecord(static_cast<cudaEvent_t>(pb->event_end), st);
   return rc;
+}
+
+}  // namespace halo
+
+using namespace halo;
+
+extern "C" int32_t halo_prefill_attention(const halo_prefill_problem_t* pb,
+                                          const halo_kv_chunk_t* chunks, int32_t n_chunks,
+                                          const halo_prefill_out_t* po, halo_stream_t stream) {
+  return pf_run(pb, chunks, n_chunks, po, nullptr, 0, stream);
+}
+
+extern "C" int64_t halo_prefill_workspace_bytes(const halo_prefill_problem_t* pb,
+                                                const halo_kv_chunk_t* chunks, int32_t n_chunks) {
+  int rc = pf_check(pb, nullptr, false);
+  if (rc != HALO_OK) return rc;
+  PfSeg segs[prefill::kMaxSegs];
+  int n_seg = 0;
+  rc = pf_segments(chunks, n_chunks, segs, &n_seg);
+  if (rc != HALO_OK) return rc;
+  return pf_workspace_bytes(segs, n_seg, pb);
+}
+
+extern "C" int32_t halo_prefill_attention_ws(const halo_prefill_problem_t* pb,
+                                             const halo_kv_chunk_t* chunks, int32_t n_chunks,
+                                             const halo_prefill_out_t* po, void* workspace,
+                                             int64_t workspace_bytes, halo_stream_t stream) {
+  return pf_run(pb, chunks, n_chunks, po, workspace, workspace_bytes, stream);
 }

@@ -34,6 +34,9 @@ class _Workspaces:
 
 
 WORKSPACES = _Workspaces()
+# prefill's staging workspace (fp16 copies of V): kept apart from the decode
+# workspaces, whose leading control block must stay zero between calls
+PREFILL_WORKSPACES = _Workspaces()
 
 
 def _require_cuda(t: torch.Tensor, name: str) -> None:
@@ -295,16 +298,17 @@ def prefill_attention(q: torch.Tensor, chunks: Sequence[tuple], *, query_pos_off
                       state: Optional[tuple] = None, accumulate: bool = False,
                       events: Optional[tuple] = None):
     """Chunked-prefill attention on the tcgen05 kernel
-    (``halo_prefill_attention``): ``q (B, H, T_q, D)`` with query row ``i`` at
-    global position ``query_pos_offset + i`` over ``(k, v, start, causal)``
+    (``halo_prefill_attention_ws``): ``q (B, H, T_q, D)`` with query row ``i``
+    at global position ``query_pos_offset + i`` over ``(k, v, start, causal)``
     chunks (``halo/kv_cache_chunked.py:873-942``).
 
     ``state = (m, l, o)``: fp32 running state, ``m, l (B, H, T_q)`` and
     ``o (B, H, T_q, D)`` contiguous.  ``accumulate=True`` folds the chunks
     into it in place and returns ``None``; otherwise the state (if given) is
-    folded in and ``(out (B, H, T_q, D), lse (B, H, T_q))`` is returned.
-    Lists longer than one call takes, or in an order the kernel refuses
-    (``HALO_ERR_SPLIT``), run as several calls through a running state."""
+    folded in and ``(out (B, H, T_q, D), lse (B, H, T_q))`` is returned, and
+    the caller's state is left as it was.  Lists longer than one call takes
+    (more than ``PREFILL_MAX_CHUNKS`` non-contiguous chunks) run as several
+    calls through a running state of their own."""
     _require_cuda(q, "q")
     B, H, T_q, D = q.shape
     if q.stride(-1) != 1:
@@ -317,20 +321,23 @@ def prefill_attention(q: torch.Tensor, chunks: Sequence[tuple], *, query_pos_off
         groups = [[]]
     if accumulate and state is None:
         raise L.HaloError("accumulate needs state=(m, l, o)", L.HALO_ERR_INVALID_ARG)
-    if len(groups) > 1 and state is None:
-        state = (torch.full((B, H, T_q), float("-inf"), dtype=torch.float32, device=q.device),
-                 torch.zeros(B, H, T_q, dtype=torch.float32, device=q.device),
-                 torch.zeros(B, H, T_q, D, dtype=torch.float32, device=q.device))
+    if len(groups) > 1 and not accumulate:
+        # the groups fold into a state of this call's own (a copy of the
+        # caller's, if given): the caller's tensors are only read
+        if state is None:
+            state = (torch.full((B, H, T_q), float("-inf"), dtype=torch.float32, device=q.device),
+                     torch.zeros(B, H, T_q, dtype=torch.float32, device=q.device),
+                     torch.zeros(B, H, T_q, D, dtype=torch.float32, device=q.device))
+        else:
+            state = tuple(t.clone() for t in state)
     if not accumulate:
         if out is None:
             out = torch.empty(B, H, T_q, D, dtype=out_dtype or q.dtype, device=q.device)
         if lse is None:
             lse = torch.empty(B, H, T_q, dtype=torch.float32, device=q.device)
     lib = L.lib()
-    pending = list(groups)
-    while pending:
-        grp = pending.pop(0)
-        last = not pending
+    for gi, grp in enumerate(groups):
+        last = gi == len(groups) - 1
         prob = L.PrefillProblem()
         prob.B, prob.H, prob.H_kv, prob.T_q, prob.D = B, H, H_kv, T_q, D
         prob.dtype = L.halo_dtype(q.dtype)
@@ -361,19 +368,16 @@ def prefill_attention(q: torch.Tensor, chunks: Sequence[tuple], *, query_pos_off
                 out.stride(2)
             po.lse = lse.data_ptr()
         with torch.cuda.device(q.device):
-            rc = lib.halo_prefill_attention(ctypes.byref(prob), arr, len(structs), ctypes.byref(po),
-                                            L.stream_handle(q.device))
-        if rc == L.HALO_ERR_SPLIT and len(grp) > 1:
-            # a chunk order that could stall the kernel (refused before any
-            # launch): one chunk per call, through a running state
-            if state is None:
-                state = (torch.full((B, H, T_q), float("-inf"), dtype=torch.float32,
-                                    device=q.device),
-                         torch.zeros(B, H, T_q, dtype=torch.float32, device=q.device),
-                         torch.zeros(B, H, T_q, D, dtype=torch.float32, device=q.device))
-            pending = [[c] for c in grp] + pending
-            continue
-        L.check(rc, "halo_prefill_attention")
+            need = lib.halo_prefill_workspace_bytes(ctypes.byref(prob), arr, len(structs))
+            if need < 0:
+                L.check(int(need), "halo_prefill_workspace_bytes")
+            ws = PREFILL_WORKSPACES.get(q.device, int(need)) if need > 0 else None
+            rc = lib.halo_prefill_attention_ws(ctypes.byref(prob), arr, len(structs),
+                                               ctypes.byref(po),
+                                               ws.data_ptr() if ws is not None else None,
+                                               ws.numel() if ws is not None else 0,
+                                               L.stream_handle(q.device))
+        L.check(rc, "halo_prefill_attention_ws")
     return None if accumulate else (out, lse)
 
 

@@ -42,7 +42,7 @@ extern "C" {
 #define HALO_ERR_CUDA (-4)          /* a CUDA runtime call failed            */
 #define HALO_ERR_TIMEOUT (-5)       /* a device-side bounded wait expired    */
 #define HALO_ERR_WORKSPACE (-6)     /* workspace missing or too small        */
-#define HALO_ERR_SPLIT (-7)         /* pass the chunks in smaller calls      */
+#define HALO_ERR_SPLIT (-7)         /* reserved (no longer returned)          */
 
 /* ------------------------------------------------------------------ dtypes */
 #define HALO_DTYPE_F32 0
@@ -376,17 +376,36 @@ typedef struct halo_prefill_out {
   float* o;
 } halo_prefill_out_t;
 
-/* Chunk order: the two query tiles of a CTA walk the union of their K/V
- * tiles, and the earlier tile sits out the tiles only the later one can see.
- * A run of two or more such tiles in a row can stall the earlier tile's MMA
- * issuer behind the shared K/V ring (it would end in HALO_ERR_TIMEOUT), so a
- * call whose coalesced segments produce one is refused with HALO_ERR_SPLIT
- * before anything is launched.  Chunks in increasing position, contiguous
- * chunks and single-chunk calls never produce one; otherwise pass the chunks
- * in smaller calls and carry the running state (the Python wrapper does). */
+/* Any chunk order is accepted: the kernel's single MMA issuer polls its
+ * inputs and never waits on one step while another could go (a CTA's two
+ * query tiles walk the union of their K/V tiles; the earlier tile sits out
+ * the tiles only the later one can see).  Without a workspace, bf16 inputs
+ * run P V as two bf16 MMAs (P as high part + residual); see
+ * halo_prefill_attention_ws for the single-MMA route. */
 int32_t halo_prefill_attention(const halo_prefill_problem_t* problem,
                                const halo_kv_chunk_t* chunks, int32_t n_chunks,
                                const halo_prefill_out_t* out, halo_stream_t stream);
+
+/* Workspace bytes halo_prefill_attention_ws needs for this problem and chunk
+ * list: 0 for fp16 inputs (nothing to stage), else 256 bytes of flags plus
+ * an fp16 copy of V (B x H_kv x rows x D x 2 bytes per coalesced segment,
+ * each rounded up to 256).  Negative status on bad arguments. */
+int64_t halo_prefill_workspace_bytes(const halo_prefill_problem_t* problem,
+                                     const halo_kv_chunk_t* chunks, int32_t n_chunks);
+
+/* halo_prefill_attention with a caller workspace (256-byte aligned, at least
+ * halo_prefill_workspace_bytes; its contents need no initialisation and are
+ * overwritten).  For bf16 inputs a pre-pass writes an fp16 copy of V into
+ * the workspace, so P enters P V as one fp16 operand (one MMA instead of
+ * two; max error well inside 2e-3).  If V holds a finite |v| >= 65536, which
+ * fp16 cannot represent, the pre-pass raises a flag in the workspace and the
+ * kernel takes the two-MMA bf16 route with the original V: same result
+ * contract, no host round trip.  Same semantics as halo_prefill_attention
+ * otherwise.  Same reference interface as halo_prefill_attention. */
+int32_t halo_prefill_attention_ws(const halo_prefill_problem_t* problem,
+                                  const halo_kv_chunk_t* chunks, int32_t n_chunks,
+                                  const halo_prefill_out_t* out, void* workspace,
+                                  int64_t workspace_bytes, halo_stream_t stream);
 
 /* ------------------------------------------------------------------ tiers */
 

@@ -1,22 +1,29 @@
-"""Discrete-event model of the prefill kernel's barrier protocol
-(``kp2_kernel`` in ``halo_b200/csrc/prefill.cu``), for the CPU tests.
+"""Discrete-event models of the prefill kernel's barrier protocol
+(``kp3_kernel`` in ``halo_b200/csrc/prefill.cu``), for the CPU tests.
 
-Roles as in the kernel: one producer streams K/V tiles through an ST-stage
-ring (full barriers: one arrival + the copy's bytes; empty barriers: one
-arrival per MMA issuer, the producer arriving for an issuer that sits the
-tile out); per query tile X an MMA issuer (QK into NB score buffers, P V into
-O, ``tcgen05.commit`` arrivals completing in issue order) and a softmax group
-(waits S, may rescale O after the previous P V, writes P).  Query tile A sees
-a prefix of each segment's K/V tiles; tile B sees all of them.
+Roles: one producer streams K/V tiles through an ST-stage ring (full
+barriers: one arrival + the copy's bytes; empty barriers: one arrival per
+query tile, the producer arriving for a tile that sits the K/V tile out);
+MMA issuers (QK into score buffers, P V into O; ``tcgen05.commit`` arrivals
+complete in issue order per issuing thread) and per query tile X a softmax
+group (waits S, writes P).  Query tile A sees a prefix of each segment's
+K/V tiles; tile B sees all of them.
 
 Barriers count completed phases.  A wait for phase n by parity succeeds when
 n has completed; it is an error (in hardware: a stall or an early return) if
 the barrier is then at neither n nor n + 1 completed phases.
 
-``issuer="blocking"`` is the kernel's issuer: QK two score tiles ahead of
-P V, each step waiting for its inputs, waiting on the full barriers of tiles
-it sits out.  ``issuer="polling"`` issues whichever of its next QK and next
-P V is ready and skips sat-out tiles without waiting."""
+``simulate_kernel`` is the kernel: ONE issuing thread for both query tiles
+that polls and issues whichever of the four next steps (QK / P V of A / B)
+has its inputs ready, one 128-key score buffer per tile (QK_X(j+1) after
+PV_X(j) completed), tile B's first QK after tile A's first P V when both
+start on the walk's first K/V tile.
+
+``simulate`` models the alternative of one issuing thread per query tile
+with score buffers ``NB`` deep and ``SPT`` score tiles per K/V tile:
+``issuer="blocking"`` (QK NB score tiles ahead of P V, each step waiting for
+its inputs, waiting on the full barriers of tiles it sits out) stalls when
+tile A sits out two K/V tiles in a row; ``issuer="polling"`` does not."""
 from __future__ import annotations
 
 import random
@@ -245,3 +252,131 @@ def max_sit_out_run(segs):
         run = 0 if takes else run + 1
         best = max(best, run)
     return best
+
+
+def simulate_kernel(segs, ST, seed=0, has_b=True, max_steps=200000):
+    """One random schedule of ``kp3_kernel``'s protocol; raise Stall on a
+    deadlock or an aliased wait.  ``segs``: [(tiles B sees, tiles A sees)];
+    with ``has_b=False`` only tile A exists (its tiles form the walk)."""
+    rng = random.Random(seed)
+    if not has_b:
+        segs = [(n_a, n_a) for _n_u, n_a in segs]
+    takes_a = tiles_of(segs)
+    n = len(takes_a)
+    n_x = [sum(takes_a), n if has_b else 0]
+    bars = []
+
+    def bar(name, count):
+        bars.append(_Bar(name, count))
+        return bars[-1]
+    q_full = bar("q_full", 1)
+    k_full = [bar(f"k_full{i}", 1) for i in range(ST)]
+    v_full = [bar(f"v_full{i}", 1) for i in range(ST)]
+    k_empty = [bar(f"k_empty{i}", 2) for i in range(ST)]
+    v_empty = [bar(f"v_empty{i}", 2) for i in range(ST)]
+    s_full = [bar(f"s_full{x}", 1) for x in range(2)]
+    p_full = [bar(f"p_full{x}", 1) for x in range(2)]
+    pv_done = [bar(f"pv_done{x}", 1) for x in range(2)]
+    now, seq, events = [0], [0], []
+    last_commit = [0]
+
+    def later(delay, fn):
+        seq[0] += 1
+        events.append((now[0] + delay, seq[0], fn))
+
+    def commit(b):
+        # one issuing thread: its commits complete in issue order
+        t = max(now[0] + rng.randint(1, 6), last_commit[0])
+        last_commit[0] = t
+        seq[0] += 1
+        events.append((t, seq[0], b.arrive))
+
+    def producer():
+        if n == 0:
+            return
+        q_full.expect_tx()
+        later(rng.randint(1, 5), q_full.land)
+        for g, ta in enumerate(takes_a):
+            st, use = g % ST, g // ST
+            absent = (0 if ta else 1) + (0 if has_b else 1)
+            if use > 0:
+                yield from _wait(k_empty[st], use - 1)
+            k_full[st].expect_tx()
+            later(rng.randint(1, 8), k_full[st].land)
+            if absent:
+                k_empty[st].arrive(absent)
+            if use > 0:
+                yield from _wait(v_empty[st], use - 1)
+            v_full[st].expect_tx()
+            later(rng.randint(1, 8), v_full[st].land)
+            if absent:
+                v_empty[st].arrive(absent)
+
+    def issuer():
+        if n == 0:
+            return
+        takes = [lambda g: takes_a[g], lambda g: has_b]
+        qc, pc = [0, 0], [0, 0]
+        jq, jp = [0, 0], [0, 0]
+
+        def seek(c, x):
+            while c < n and not takes[x](c):
+                c += 1
+            return c
+        for x in range(2):
+            qc[x] = seek(0, x)
+            pc[x] = seek(0, x)
+        gate_b = n_x[0] > 0 and qc[0] == 0
+        yield from _wait(q_full, 0)
+        while True:
+            did = False
+            for x in range(2):
+                if jp[x] < jq[x]:
+                    g = pc[x]
+                    if _done(p_full[x], jp[x]) and _done(v_full[g % ST], g // ST):
+                        commit(pv_done[x])
+                        commit(v_empty[g % ST])
+                        jp[x] += 1
+                        pc[x] = seek(g + 1, x)
+                        did = True
+                if jq[x] < n_x[x] and jq[x] == jp[x] and \
+                        (x == 0 or jq[1] > 0 or not gate_b or jp[0] > 0):
+                    g = qc[x]
+                    if (jq[x] == 0 or _done(pv_done[x], jq[x] - 1)) and \
+                            _done(k_full[g % ST], g // ST):
+                        commit(s_full[x])
+                        commit(k_empty[g % ST])
+                        jq[x] += 1
+                        qc[x] = seek(g + 1, x)
+                        did = True
+            if jp[0] >= n_x[0] and jp[1] >= n_x[1]:
+                return
+            if not did:
+                yield
+
+    def softmax(x):
+        for j in range(n_x[x]):
+            yield from _wait(s_full[x], j)
+            p_full[x].arrive()
+        if n_x[x] > 0:
+            yield from _wait(pv_done[x], n_x[x] - 1)
+
+    live = {"producer": producer(), "issuer": issuer(), "softmaxA": softmax(0),
+            "softmaxB": softmax(1)}
+    for _step in range(max_steps):
+        if not live and not events:
+            # every barrier of the ring ends balanced: each stage's empty
+            # phases match the loads that used it
+            return
+        for name in rng.sample(list(live), len(live)):
+            try:
+                next(live[name])
+            except StopIteration:
+                del live[name]
+        if events and (rng.random() < 0.5 or not live):
+            events.sort()
+            t, _, fn = events.pop(0)
+            now[0] = max(now[0], t)
+            fn()
+    raise Stall("deadlock: " + ", ".join(sorted(live)) + "; " +
+                ", ".join(f"{b.name}={b.phase}" for b in bars))
