@@ -150,6 +150,8 @@ __device__ __forceinline__ uint32_t pack_bf2(float a, float b) {
 // Issuer: a single thread polls (mbarrier.test_wait) and issues whichever
 // of the four next steps (QK/PV of A/B) has its inputs ready; it never waits
 // on one step while another could go, so no order of chunks can stall it.
+// It observes K and V landings in walk order (landed prefixes), so no ring
+// stage is probed before its previous use was seen to land.
 // Ring barriers: k_full/v_full (one arrival + the copy's bytes), k_empty /
 // v_empty (two arrivals: a tcgen05.commit per query tile that reads the
 // tile, the producer arriving for a tile that sits it out).  Per tile X:
@@ -352,18 +354,26 @@ __global__ void __launch_bounds__(kThreads, 1) kp3_kernel(const __grid_constant_
       // step apart.  (Only then: if A starts later, A's first V tile may
       // need a ring stage that B's early tiles must free first.)
       const bool gateB = nX[0] > 0 && qc[0].g == 0;
+      // Landed prefixes: K (V) tiles below kpre (vpre) are known to have
+      // landed.  The next tile's full barrier is probed in walk order, so a
+      // stage is only probed after its previous use was seen to land: a
+      // parity probe of phase n while phase n-1 is still open would read
+      // as complete (a query tile that sits tiles out would otherwise
+      // probe ahead of the ring).
+      int kpre = 0, vpre = 0;
       bool ok = wait_bar(&bs->q_full, 0, bs, p.err);
       uint64_t t_idle = 0;
       int idle = 0;
       while (ok) {
         bool did = false;
+        while (kpre < nU && mbar_test(&bs->k_full[kpre % ST], (kpre / ST) & 1)) ++kpre;
+        while (vpre < nU && mbar_test(&bs->v_full[vpre % ST], (vpre / ST) & 1)) ++vpre;
 #pragma unroll
         for (int x = 0; x < 2; ++x) {
           // O_X += P_X(j) V(j): P written and V landed
           if (jp[x] < jq[x]) {
             const int g = pc[x].g, st = g % ST;
-            if (mbar_test(&bs->p_full[x], jp[x] & 1) &&
-                mbar_test(&bs->v_full[st], (g / ST) & 1)) {
+            if (g < vpre && mbar_test(&bs->p_full[x], jp[x] & 1)) {
               umma::fence_after_sync();
               const uint32_t pcol = tmem + x * 128;
               const uint32_t ocol = tmem + Gm::kColO + x * D;
@@ -392,8 +402,7 @@ __global__ void __launch_bounds__(kThreads, 1) kp3_kernel(const __grid_constant_
           if (jq[x] < nX[x] && jq[x] == jp[x] &&
               (x == 0 || jq[1] > 0 || !gateB || jp[0] > 0)) {
             const int g = qc[x].g, st = g % ST;
-            if ((jq[x] == 0 || mbar_test(&bs->pv_done[x], (jq[x] - 1) & 1)) &&
-                mbar_test(&bs->k_full[st], (g / ST) & 1)) {
+            if (g < kpre && (jq[x] == 0 || mbar_test(&bs->pv_done[x], (jq[x] - 1) & 1))) {
               umma::fence_after_sync();
               const uint64_t qd = opaque(umma::smem_desc_sw128(sQ + x * Gm::kTileBytes, 16, 1024));
               const uint64_t kd = opaque(kdesc0 + (uint64_t)((st * Gm::kTileBytes) >> 4));

@@ -11,13 +11,16 @@ K/V tiles; tile B sees all of them.
 
 Barriers count completed phases.  A wait for phase n by parity succeeds when
 n has completed; it is an error (in hardware: a stall or an early return) if
-the barrier is then at neither n nor n + 1 completed phases.
+the barrier is then at neither n nor n + 1 completed phases -- in particular
+a probe of phase n while phase n - 1 is still open reads as complete.
 
 ``simulate_kernel`` is the kernel: ONE issuing thread for both query tiles
 that polls and issues whichever of the four next steps (QK / P V of A / B)
 has its inputs ready, one 128-key score buffer per tile (QK_X(j+1) after
 PV_X(j) completed), tile B's first QK after tile A's first P V when both
-start on the walk's first K/V tile.
+start on the walk's first K/V tile.  K and V landings are observed in walk
+order (a landed prefix per ring), so a tile that sits K/V tiles out never
+probes a ring stage whose previous use has not been seen to land.
 
 ``simulate`` models the alternative of one issuing thread per query tile
 with score buffers ``NB`` deep and ``SPT`` score tiles per K/V tile:
@@ -57,9 +60,13 @@ class _Bar:
 
 
 def _done(bar, n):
+    """A parity probe for the completion of phase ``n`` (hardware: true iff
+    the current phase's parity differs from n's).  With c phases completed
+    it answers correctly only for c in {n, n + 1}: c = n - 1 would read as
+    done, c >= n + 2 as done or not by parity alone."""
     c = bar.phase
-    if c >= n + 2:
-        raise Stall(f"aliased wait: {bar.name} waits phase {n}, {c} completed")
+    if c >= n + 2 or c == n - 1:
+        raise Stall(f"aliased wait: {bar.name} probes phase {n}, {c} completed")
     return c == n + 1
 
 
@@ -327,13 +334,21 @@ def simulate_kernel(segs, ST, seed=0, has_b=True, max_steps=200000):
             qc[x] = seek(0, x)
             pc[x] = seek(0, x)
         gate_b = n_x[0] > 0 and qc[0] == 0
+        # landed prefixes: K/V tiles below kpre / vpre are known to have
+        # landed; the next one is probed in walk order, so every probe of a
+        # stage follows the observed landing of its previous use
+        kpre = vpre = 0
         yield from _wait(q_full, 0)
         while True:
             did = False
+            while kpre < n and _done(k_full[kpre % ST], kpre // ST):
+                kpre += 1
+            while vpre < n and _done(v_full[vpre % ST], vpre // ST):
+                vpre += 1
             for x in range(2):
                 if jp[x] < jq[x]:
                     g = pc[x]
-                    if _done(p_full[x], jp[x]) and _done(v_full[g % ST], g // ST):
+                    if g < vpre and _done(p_full[x], jp[x]):
                         commit(pv_done[x])
                         commit(v_empty[g % ST])
                         jp[x] += 1
@@ -342,8 +357,7 @@ def simulate_kernel(segs, ST, seed=0, has_b=True, max_steps=200000):
                 if jq[x] < n_x[x] and jq[x] == jp[x] and \
                         (x == 0 or jq[1] > 0 or not gate_b or jp[0] > 0):
                     g = qc[x]
-                    if (jq[x] == 0 or _done(pv_done[x], jq[x] - 1)) and \
-                            _done(k_full[g % ST], g // ST):
+                    if g < kpre and (jq[x] == 0 or _done(pv_done[x], jq[x] - 1)):
                         commit(s_full[x])
                         commit(k_empty[g % ST])
                         jq[x] += 1
