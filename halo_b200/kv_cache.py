@@ -1,45 +1,55 @@
-"""``HALOCache``: a ``transformers`` ``DynamicCache`` with HALO's tiering
-handles (``halo/kv_cache.py`` in lzbaclz/HALO, :69-219).
+"""``HALOCache``: a ``transformers`` ``DynamicCache`` that carries HALO's
+tiering handles (the interface of ``halo/kv_cache.py`` in lzbaclz/HALO,
+:69-219).
 
-It returns exactly what ``DynamicCache.update`` returns, so attention sees
-the same keys and values; HALO state changes only through
-:meth:`update_hotness` (demote what cooled, prefetch what is predicted hot).
+Attention sees exactly what ``DynamicCache.update`` returns; the tiers
+change only through :meth:`update_hotness`, which works on index tensors:
+the positions that left the hot set (``torch.isin``) become the blocks to
+demote one tier down, then the refetcher's prediction for the next step is
+scheduled.  That order -- demote what cooled, then refetch what is
+predicted -- is the policy's, and the telemetry counts follow from it.
 """
 from __future__ import annotations
 
 try:
     from transformers.cache_utils import DynamicCache as _BaseCache
-    _HAS_TRANSFORMERS = True
-except Exception:  # pragma: no cover
-    _HAS_TRANSFORMERS = False
-
+except Exception:  # pragma: no cover - transformers is part of the runtime image
     class _BaseCache:  # type: ignore[no-redef]
-        """Minimal per-layer concatenating cache when transformers is absent."""
+        """Per-layer append-only K/V lists, concatenated on read (used only
+        when transformers is not importable)."""
 
         def __init__(self) -> None:
-            self.key_cache: list = []
-            self.value_cache: list = []
+            self._parts: list = []
 
         def update(self, key_states, value_states, layer_idx, *args, **kwargs):
             import torch
-            while len(self.key_cache) <= layer_idx:
-                self.key_cache.append(None)
-                self.value_cache.append(None)
-            if self.key_cache[layer_idx] is None:
-                self.key_cache[layer_idx], self.value_cache[layer_idx] = key_states, value_states
-            else:
-                self.key_cache[layer_idx] = torch.cat([self.key_cache[layer_idx], key_states], -2)
-                self.value_cache[layer_idx] = torch.cat([self.value_cache[layer_idx], value_states], -2)
-            return self.key_cache[layer_idx], self.value_cache[layer_idx]
+            while len(self._parts) <= layer_idx:
+                self._parts.append(([], []))
+            ks, vs = self._parts[layer_idx]
+            ks.append(key_states)
+            vs.append(value_states)
+            if len(ks) > 1:       # keep one tensor per layer
+                ks[:] = [torch.cat(ks, dim=-2)]
+                vs[:] = [torch.cat(vs, dim=-2)]
+            return ks[0], vs[0]
 
         def get_seq_length(self, layer_idx: int = 0) -> int:
-            if layer_idx >= len(self.key_cache) or self.key_cache[layer_idx] is None:
+            if layer_idx >= len(self._parts) or not self._parts[layer_idx][0]:
                 return 0
-            return self.key_cache[layer_idx].shape[-2]
+            return int(self._parts[layer_idx][0][0].shape[-2])
+
+
+def _tier_below(tiers, name: str) -> str:
+    """The next slower tier after ``name`` in ``tiers`` (itself if last or
+    absent)."""
+    order = [str(getattr(t, "value", t)) for t in tiers]
+    if name not in order:
+        return name
+    return order[min(order.index(name) + 1, len(order) - 1)]
 
 
 class HALOCache(_BaseCache):
-    """KV cache carrying HALO's scorer, demoter and refetcher."""
+    """KV cache with HALO's scorer, demoter and refetcher attached."""
 
     def __init__(self, *, config, storage, scorer, demoter, refetcher) -> None:
         super().__init__()
@@ -49,22 +59,17 @@ class HALOCache(_BaseCache):
         self.demoter = demoter
         self.refetcher = refetcher
         self._step = 0
-        self._last_hot_indices: dict = {}
-        self._last_score: dict = {}
+        self._last_hot_indices: dict = {}    # layer -> hot positions (int64, sorted)
+        self._last_score: dict = {}          # layer -> hotness score (K,)
         self.demoted_blocks_total = 0
         self.refetched_blocks_total = 0
 
     def reset(self) -> None:
-        """Forget all cached layers and HALO bookkeeping (one per ``generate``)."""
-        try:
-            _BaseCache.__init__(self)
-        except Exception:  # pragma: no cover
-            for name in ("key_cache", "value_cache"):
-                if isinstance(getattr(self, name, None), list):
-                    getattr(self, name).clear()
+        """Empty the cache and the HALO bookkeeping (one call per generate)."""
+        _BaseCache.__init__(self)
         self._step = 0
-        self._last_hot_indices.clear()
-        self._last_score.clear()
+        self._last_hot_indices = {}
+        self._last_score = {}
         self.demoted_blocks_total = 0
         self.refetched_blocks_total = 0
 
@@ -76,42 +81,36 @@ class HALOCache(_BaseCache):
         return self._step
 
     def update_hotness(self, layer_idx: int, attn_weights) -> None:
-        """Score the head-mean attention ``(K,)``, demote blocks that left the
-        hot set, prefetch the predicted next hot set."""
+        """Score this step's head-mean attention ``(K,)``; demote the blocks
+        of positions that left the hot set, then schedule the refetch of the
+        predicted next hot set."""
+        import torch
         score = self.scorer.score(attn_weights, step=self._step)
         hot = self.scorer.topk_hot(score)
         prev = self._last_hot_indices.get(layer_idx)
         if prev is not None:
-            cooled = sorted(set(prev.tolist()) - set(hot.tolist()))
-            if cooled:
-                blocks = sorted({c // self.cfg.block_size for c in cooled})
+            cooled = prev[~torch.isin(prev, hot)]
+            if cooled.numel():
+                blocks = torch.unique(torch.div(cooled, self.cfg.block_size,
+                                                 rounding_mode="floor")).tolist()
                 self.demoter.demote(layer=layer_idx, block_indices=blocks, src="gpu",
-                                    dst=self._next_tier_after("gpu"))
+                                    dst=_tier_below(self.cfg.tiers, "gpu"))
                 self.demoted_blocks_total += len(blocks)
-        predicted = self.refetcher.predict_hot(layer=layer_idx, last_hot_indices=hot,
-                                               last_score=score)
-        before = self.refetcher.misses
-        self.refetcher.schedule(layer=layer_idx, predicted_indices=predicted)
-        self.refetched_blocks_total += self.refetcher.misses - before
+        misses = self.refetcher.misses
+        self.refetcher.schedule(layer=layer_idx,
+                                predicted_indices=self.refetcher.predict_hot(
+                                    layer=layer_idx, last_hot_indices=hot, last_score=score))
+        self.refetched_blocks_total += self.refetcher.misses - misses
         self._last_hot_indices[layer_idx] = hot
         self._last_score[layer_idx] = score
 
     def telemetry(self) -> dict:
-        tot = self.refetcher.hits + self.refetcher.misses
-        return {
-            "step": self._step,
-            "demoted_blocks": self.demoted_blocks_total,
-            "refetched_blocks": self.refetched_blocks_total,
-            "refetch_hits": self.refetcher.hits,
-            "refetch_misses": self.refetcher.misses,
-            "refetch_hit_rate": (self.refetcher.hits / tot) if tot else 0.0,
-        }
-
-    def _next_tier_after(self, current: str) -> str:
-        names = list(self.cfg.tiers)
-        if current not in names:
-            return current
-        return names[min(names.index(current) + 1, len(names) - 1)]
+        """JSON-able counters (the reference's keys)."""
+        rf = self.refetcher
+        n = rf.hits + rf.misses
+        return {"step": self._step, "demoted_blocks": self.demoted_blocks_total,
+                "refetched_blocks": self.refetched_blocks_total, "refetch_hits": rf.hits,
+                "refetch_misses": rf.misses, "refetch_hit_rate": rf.hits / n if n else 0.0}
 
 
 __all__ = ["HALOCache"]

@@ -128,6 +128,40 @@ class TieredStorage:
     def locate_block(self, *, layer: int, block: int) -> str:
         return self._directory.get((layer, block), MemoryTier.GPU).value
 
+    def locate_blocks(self, *, layer: int, blocks) -> list:
+        """Tier names of several blocks of one layer, in order."""
+        d = self._directory
+        return [d.get((layer, int(b)), MemoryTier.GPU).value for b in blocks]
+
+    def move_blocks(self, *, layer: int, blocks, src, dst) -> int:
+        """Move several blocks of one layer between two tiers; returns how
+        many moved.  Block ids are deduplicated and sorted, and each run of
+        consecutive ids is one slab of the tier buffers
+        ``(L, max_blocks, H_kv, block, D)``, so it moves with one copy per
+        tensor (one DMA when one side is HBM and the other pinned host
+        memory); the NVMe tier still moves block by block."""
+        s, d = MemoryTier.from_name(src), MemoryTier.from_name(dst)
+        ids = sorted({int(b) for b in blocks})
+        if not ids or s == d:
+            return 0
+        sb, db = self._ensure(s), self._ensure(d)
+        if isinstance(sb, _FileTier) or isinstance(db, _FileTier):
+            for b in ids:
+                self.move_block(layer=layer, block=b, src=s, dst=d)
+            return len(ids)
+        lo = 0
+        while lo < len(ids):
+            hi = lo
+            while hi + 1 < len(ids) and ids[hi + 1] == ids[hi] + 1:
+                hi += 1
+            a, z = ids[lo], ids[hi] + 1
+            for src_t, dst_t in zip(sb, db):
+                dst_t[layer, a:z].copy_(src_t[layer, a:z], non_blocking=True)
+            lo = hi + 1
+        for b in ids:
+            self._directory[(layer, b)] = d
+        return len(ids)
+
     def write_new_block(self, *, layer: int, block: int, keys, values, tier: str = "gpu") -> None:
         t = MemoryTier.from_name(tier)
         self._store(layer, block, keys, values, t)
@@ -202,4 +236,40 @@ class TieredStorage:
         return f"TieredStorage(tiers=[{','.join(t.value for t in self.tiers)}], blocks={self.max_blocks})"
 
 
-__all__ = ["MemoryTier", "TieredStorage"]
+class TierMover:
+    """Runs a storage's batched block moves, on a side CUDA stream of its
+    own when ``asynchronous`` (and CUDA is up) so the caller's stream never
+    waits for them: the side stream first waits for the work already queued
+    on the caller's stream (which may still read the source blocks), then
+    copies; :meth:`fence` makes the caller's stream wait for every move
+    issued so far.  The tier directory is updated when a move is issued."""
+
+    def __init__(self, storage, *, asynchronous: bool) -> None:
+        self.storage = storage
+        self.asynchronous = asynchronous
+        self._side = None
+
+    def _stream(self):
+        import torch
+        if not (self.asynchronous and torch.cuda.is_available()):
+            return None
+        if self._side is None:
+            self._side = torch.cuda.Stream()
+        return self._side
+
+    def move(self, layer: int, blocks, src, dst) -> int:
+        import torch
+        side = self._stream()
+        if side is None:
+            return self.storage.move_blocks(layer=layer, blocks=blocks, src=src, dst=dst)
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            return self.storage.move_blocks(layer=layer, blocks=blocks, src=src, dst=dst)
+
+    def fence(self) -> None:
+        import torch
+        if self._side is not None:
+            torch.cuda.current_stream().wait_stream(self._side)
+
+
+__all__ = ["MemoryTier", "TieredStorage", "TierMover"]
