@@ -115,6 +115,61 @@ __device__ __forceinline__ uint64_t opaque(uint64_t v) {
   return v;
 }
 
+// ---- packed fp32 pairs (sm_100 f32x2 instructions: two lanes per issue)
+__device__ __forceinline__ uint64_t f2pack(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void f2unpack(uint64_t r, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
+}
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// 2^x for a pair on the FMA pipe instead of the special-function unit
+// (which the softmax otherwise saturates: one exponential per score).
+// Range reduction x = j + f with j = rint(x) (adding 1.5 * 2^23 rounds to an
+// integer), f in [-1/2, 1/2]; 2^f by a degree-4 polynomial whose
+// coefficients are a relative-error least-squares fit (iteratively
+// reweighted towards the minimax solution) on Chebyshev nodes of
+// [-1/2, 1/2], max relative error 2.7e-6 in fp32 evaluation; 2^j enters
+// as an integer add to the exponent field.  x is clamped at -126 (results
+// below 2^-126 are far under fp16's range and l's rounding).
+__device__ __forceinline__ void exp2_poly2(float x0, float x1, float& y0, float& y1) {
+  const uint64_t x = f2pack(fmaxf(x0, -126.f), fmaxf(x1, -126.f));
+  const uint64_t t = fadd2(x, f2pack(12582912.f, 12582912.f));
+  const uint64_t j = fadd2(t, f2pack(-12582912.f, -12582912.f));
+  const uint64_t f = ffma2(j, f2pack(-1.f, -1.f), x);
+  uint64_t q = ffma2(f2pack(0.009570101276f, 0.009570101276f), f,
+                     f2pack(0.05591785908f, 0.05591785908f));
+  q = ffma2(q, f, f2pack(0.2402474433f, 0.2402474433f));
+  q = ffma2(q, f, f2pack(0.6931217909f, 0.6931217909f));
+  q = ffma2(q, f, f2pack(0.9999992847f, 0.9999992847f));
+  float q0, q1, t0, t1;
+  f2unpack(q, q0, q1);
+  f2unpack(t, t0, t1);
+  y0 = __int_as_float(__float_as_int(q0) + (__float_as_int(t0) << 23));
+  y1 = __int_as_float(__float_as_int(q1) + (__float_as_int(t1) << 23));
+}
+
+// One pair of P: pairs e with (e % 4) == 3 of each 16 go through the FMA
+// pipe polynomial, the rest through ex2 on the special-function unit.
+constexpr int kPolyEvery = 4;
+
 // Two floats as one 32-bit register of two fp16 values (round to nearest).
 __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
   const __half2 h = __floats2half2_rn(a, b);
@@ -123,6 +178,43 @@ __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
 __device__ __forceinline__ uint32_t pack_bf2(float a, float b) {
   const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
   return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// P = exp2(s * scale_log2 - m) of one row's 128 scores into TMEM columns
+// [col, col + 64) as fp16 pairs (kSplit = false), or as bf16 high parts
+// there and bf16 residuals in [col + 64, col + 128) (kSplit = true); the
+// fp32 row sum accumulates into rs2 (two pairs).
+template <bool kSplit>
+__device__ __forceinline__ void write_p(const float (&sv)[kBN], uint64_t sl2, uint64_t nm2,
+                                        uint32_t col, uint64_t (&rs2)[2]) {
+#pragma unroll
+  for (int c = 0; c < kBN / 32; ++c) {
+    uint32_t hv[16], lv[16];
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      float x0, x1, p0, p1;
+      f2unpack(ffma2(f2pack(sv[c * 32 + 2 * e], sv[c * 32 + 2 * e + 1]), sl2, nm2), x0, x1);
+      if ((e % kPolyEvery) == kPolyEvery - 1) {
+        exp2_poly2(x0, x1, p0, p1);
+      } else {
+        p0 = ex2(x0);
+        p1 = ex2(x1);
+      }
+      rs2[e & 1] = fadd2(rs2[e & 1], f2pack(p0, p1));
+      if constexpr (!kSplit) {
+        hv[e] = pack_h2(p0, p1);
+      } else {
+        // hi = p truncated to bf16 (upper halves, one byte permute per pair),
+        // lo = rnd(p - hi): ~16 significant bits in all
+        const uint32_t b0 = __float_as_uint(p0), b1 = __float_as_uint(p1);
+        hv[e] = __byte_perm(b0, b1, 0x7632);
+        lv[e] = pack_bf2(p0 - __uint_as_float(b0 & 0xFFFF0000u),
+                         p1 - __uint_as_float(b1 & 0xFFFF0000u));
+      }
+    }
+    umma::tmem_st16u(col + c * 16, hv);
+    if constexpr (kSplit) umma::tmem_st16u(col + 64 + c * 16, lv);
+  }
 }
 
 // ======================================================================
@@ -455,7 +547,6 @@ __global__ void __launch_bounds__(kThreads, 1) kp3_kernel(const __grid_constant_
     const uint32_t ocol = Gm::kColO + x * D;
     const bool active = x == 0 || hasB;
     const int64_t qmin = x ? qminB : qminA;
-    const int64_t qmaxX = x ? qmaxB : qmaxA;
     const int64_t qpos = qmin + r;
     float m = -INFINITY, l = 0.f;
     bool ok = true;
@@ -485,9 +576,12 @@ __global__ void __launch_bounds__(kThreads, 1) kp3_kernel(const __grid_constant_
 #pragma unroll
         for (int e = 0; e < 8; ++e) mx8[e] = sv[e];
 #pragma unroll
-        for (int c = 8; c < kBN; ++c) mx8[c & 7] = fmaxf(mx8[c & 7], sv[c]);
-        const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                               fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]))) *
+        for (int c = 8; c < kBN; c += 16) {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) mx8[e] = fmax3(mx8[e], sv[c + e], sv[c + 8 + e]);
+        }
+        const float mx = fmax3(fmax3(mx8[0], mx8[1], mx8[2]), fmax3(mx8[3], mx8[4], mx8[5]),
+                               fmaxf(mx8[6], mx8[7])) *
                          p.scale_log2;
         const bool grow = mx > m + kRescaleLog2 || (m == -INFINITY && mx > -INFINITY);
         float fac = 1.f;
@@ -511,41 +605,15 @@ __global__ void __launch_bounds__(kThreads, 1) kp3_kernel(const __grid_constant_
         }
         // P = exp2(s * scale_log2 - m) as 16-bit pairs into S's columns
         const float nmu = (m == -INFINITY) ? 0.f : -m;
-        const float sl2 = p.scale_log2;
-        float rs4[4] = {0.f, 0.f, 0.f, 0.f};
-        if (p16) {
-#pragma unroll
-          for (int c = 0; c < kBN / 32; ++c) {
-            uint32_t hv[16];
-#pragma unroll
-            for (int e = 0; e < 16; ++e) {
-              const float p0 = ex2(fmaf(sv[c * 32 + 2 * e], sl2, nmu));
-              const float p1 = ex2(fmaf(sv[c * 32 + 2 * e + 1], sl2, nmu));
-              rs4[e & 3] += p0 + p1;
-              hv[e] = pack_h2(p0, p1);
-            }
-            umma::tmem_st16u(trow + scol + c * 16, hv);
-          }
-        } else {
-#pragma unroll
-          for (int c = 0; c < kBN / 32; ++c) {
-            uint32_t hv[16], lv[16];
-#pragma unroll
-            for (int e = 0; e < 16; ++e) {
-              const float p0 = ex2(fmaf(sv[c * 32 + 2 * e], sl2, nmu));
-              const float p1 = ex2(fmaf(sv[c * 32 + 2 * e + 1], sl2, nmu));
-              rs4[e & 3] += p0 + p1;
-              // hi = p truncated to bf16 (upper halves, one byte permute per
-              // pair), lo = rnd(p - hi): ~16 significant bits in all
-              const uint32_t b0 = __float_as_uint(p0), b1 = __float_as_uint(p1);
-              hv[e] = __byte_perm(b0, b1, 0x7632);
-              lv[e] = pack_bf2(p0 - __uint_as_float(b0 & 0xFFFF0000u),
-                               p1 - __uint_as_float(b1 & 0xFFFF0000u));
-            }
-            umma::tmem_st16u(trow + scol + c * 16, hv);
-            umma::tmem_st16u(trow + scol + 64 + c * 16, lv);
-          }
-        }
+        const uint64_t sl2 = f2pack(p.scale_log2, p.scale_log2), nm2 = f2pack(nmu, nmu);
+        uint64_t rs2[2] = {0ull, 0ull};   // row-sum pairs (+0.f bits)
+        if (p16)
+          write_p<false>(sv, sl2, nm2, trow + scol, rs2);
+        else
+          write_p<true>(sv, sl2, nm2, trow + scol, rs2);
+        float rs4[4];
+        f2unpack(rs2[0], rs4[0], rs4[1]);
+        f2unpack(rs2[1], rs4[2], rs4[3]);
         l += (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
         umma::tmem_wait_st();
         umma::fence_before_sync();
