@@ -140,36 +140,6 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   return d;
 }
 
-// 2^x for a pair on the FMA pipe instead of the special-function unit
-// (which the softmax otherwise saturates: one exponential per score).
-// Range reduction x = j + f with j = rint(x) (adding 1.5 * 2^23 rounds to an
-// integer), f in [-1/2, 1/2]; 2^f by a degree-4 polynomial whose
-// coefficients are a relative-error least-squares fit (iteratively
-// reweighted towards the minimax solution) on Chebyshev nodes of
-// [-1/2, 1/2], max relative error 2.7e-6 in fp32 evaluation; 2^j enters
-// as an integer add to the exponent field.  x is clamped at -126 (results
-// below 2^-126 are far under fp16's range and l's rounding).
-__device__ __forceinline__ void exp2_poly2(float x0, float x1, float& y0, float& y1) {
-  const uint64_t x = f2pack(fmaxf(x0, -126.f), fmaxf(x1, -126.f));
-  const uint64_t t = fadd2(x, f2pack(12582912.f, 12582912.f));
-  const uint64_t j = fadd2(t, f2pack(-12582912.f, -12582912.f));
-  const uint64_t f = ffma2(j, f2pack(-1.f, -1.f), x);
-  uint64_t q = ffma2(f2pack(0.009570101276f, 0.009570101276f), f,
-                     f2pack(0.05591785908f, 0.05591785908f));
-  q = ffma2(q, f, f2pack(0.2402474433f, 0.2402474433f));
-  q = ffma2(q, f, f2pack(0.6931217909f, 0.6931217909f));
-  q = ffma2(q, f, f2pack(0.9999992847f, 0.9999992847f));
-  float q0, q1, t0, t1;
-  f2unpack(q, q0, q1);
-  f2unpack(t, t0, t1);
-  y0 = __int_as_float(__float_as_int(q0) + (__float_as_int(t0) << 23));
-  y1 = __int_as_float(__float_as_int(q1) + (__float_as_int(t1) << 23));
-}
-
-// One pair of P: pairs e with (e % 4) == 3 of each 16 go through the FMA
-// pipe polynomial, the rest through ex2 on the special-function unit.
-constexpr int kPolyEvery = 4;
-
 // Two floats as one 32-bit register of two fp16 values (round to nearest).
 __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
   const __half2 h = __floats2half2_rn(a, b);
@@ -194,12 +164,8 @@ __device__ __forceinline__ void write_p(const float (&sv)[kBN], uint64_t sl2, ui
     for (int e = 0; e < 16; ++e) {
       float x0, x1, p0, p1;
       f2unpack(ffma2(f2pack(sv[c * 32 + 2 * e], sv[c * 32 + 2 * e + 1]), sl2, nm2), x0, x1);
-      if ((e % kPolyEvery) == kPolyEvery - 1) {
-        exp2_poly2(x0, x1, p0, p1);
-      } else {
-        p0 = ex2(x0);
-        p1 = ex2(x1);
-      }
+      p0 = ex2(x0);
+      p1 = ex2(x1);
       rs2[e & 1] = fadd2(rs2[e & 1], f2pack(p0, p1));
       if constexpr (!kSplit) {
         hv[e] = pack_h2(p0, p1);

@@ -330,11 +330,16 @@ def prefill_attention(q: torch.Tensor, chunks: Sequence[tuple], *, query_pos_off
                      torch.zeros(B, H, T_q, D, dtype=torch.float32, device=q.device))
         else:
             state = tuple(t.clone() for t in state)
+    lse_view = None
     if not accumulate:
         if out is None:
             out = torch.empty(B, H, T_q, D, dtype=out_dtype or q.dtype, device=q.device)
         if lse is None:
             lse = torch.empty(B, H, T_q, dtype=torch.float32, device=q.device)
+        elif not lse.is_contiguous():
+            # the kernel writes lse as contiguous (B, H, T_q); a strided
+            # view (e.g. one slice of a whole prompt's lse) is filled after
+            lse_view, lse = lse, torch.empty(B, H, T_q, dtype=torch.float32, device=q.device)
     lib = L.lib()
     for gi, grp in enumerate(groups):
         last = gi == len(groups) - 1
@@ -378,7 +383,12 @@ def prefill_attention(q: torch.Tensor, chunks: Sequence[tuple], *, query_pos_off
                                                ws.numel() if ws is not None else 0,
                                                L.stream_handle(q.device))
         L.check(rc, "halo_prefill_attention_ws")
-    return None if accumulate else (out, lse)
+    if accumulate:
+        return None
+    if lse_view is not None:
+        lse_view.copy_(lse)
+        lse = lse_view
+    return out, lse
 
 
 def multi_query_attention(q: torch.Tensor, chunks: Sequence[tuple], *, scale: Optional[float] = None,
