@@ -96,6 +96,20 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Suspend in hardware (the warp issues nothing) until the phase with this
+// parity completes or about `ns` nanoseconds pass; true when it completed.
+__device__ __forceinline__ bool mbar_sleep_wait(uint64_t* bar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
+
 // K/V tiles of segment `sg` visible to query positions <= qmax.
 __device__ __forceinline__ int seg_tiles(const Seg& sg, int64_t qmax) {
   int n = (sg.len + kBN - 1) / kBN;
@@ -419,6 +433,7 @@ __global__ void __launch_bounds__(kThreads, 1) kp3_kernel(const __grid_constant_
       // as complete (a query tile that sits tiles out would otherwise
       // probe ahead of the ring).
       int kpre = 0, vpre = 0;
+      int qseq[2] = {0, 0}, seq = 0;       // issue order of each tile's latest QK
       bool ok = wait_bar(&bs->q_full, 0, bs, p.err);
       uint64_t t_idle = 0;
       int idle = 0;
@@ -471,6 +486,7 @@ __global__ void __launch_bounds__(kThreads, 1) kp3_kernel(const __grid_constant_
               }
               umma::commit(&bs->s_full[x]);
               umma::commit(&bs->k_empty[st]);
+              qseq[x] = ++seq;
               ++jq[x];
               ++qc[x].t;
               ++qc[x].g;
@@ -484,9 +500,41 @@ __global__ void __launch_bounds__(kThreads, 1) kp3_kernel(const __grid_constant_
           idle = 0;
           continue;
         }
-        // nothing ready: back off briefly (the softmax warps share this
-        // warp's scheduler), bounded idle time, stop if another role aborted
-        if (idle >= 4) __nanosleep(32);
+        // Nothing ready.  Sleep in hardware on the event expected first, so
+        // the issuer takes no issue slots from the softmax warps that share
+        // its scheduler: a P V completing (it frees a score buffer for the
+        // next QK), else the oldest pending P (its softmax started first),
+        // else the next K or V tile to land (probed in walk order); every
+        // probe stays within one phase of its barrier, as above.
+        {
+          bool slept = false;
+#pragma unroll
+          for (int x = 0; x < 2 && !slept; ++x) {
+            if (jq[x] < nX[x] && jq[x] == jp[x] && jq[x] > 0 &&
+                (x == 0 || !gateB || jp[0] > 0) &&
+                !mbar_test(&bs->pv_done[x], (jq[x] - 1) & 1)) {
+              mbar_sleep_wait(&bs->pv_done[x], (jq[x] - 1) & 1, 1000);
+              slept = true;
+            }
+          }
+          if (!slept) {
+            int xo = -1;
+            if (jp[0] < jq[0]) xo = 0;
+            if (jp[1] < jq[1] && (xo < 0 || qseq[1] < qseq[0])) xo = 1;
+            if (xo >= 0 && !mbar_test(&bs->p_full[xo], jp[xo] & 1)) {
+              mbar_sleep_wait(&bs->p_full[xo], jp[xo] & 1, 1000);
+              slept = true;
+            } else if (xo >= 0 && vpre < nU) {
+              mbar_sleep_wait(&bs->v_full[vpre % ST], (vpre / ST) & 1, 1000);
+              slept = true;
+            } else if (kpre < nU) {
+              mbar_sleep_wait(&bs->k_full[kpre % ST], (kpre / ST) & 1, 1000);
+              slept = true;
+            }
+          }
+          if (!slept) __nanosleep(64);
+        }
+        // bounded idle time; stop if another role aborted
         if (++idle == 64) t_idle = globaltimer_ns();
         if (idle > 64 && (idle & 63) == 0) {
           if (*reinterpret_cast<volatile int*>(&bs->abort_flag)) {
