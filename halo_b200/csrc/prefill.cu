@@ -353,50 +353,65 @@ __global__ void __launch_bounds__(kThreads, 1) kp3_kernel(const __grid_constant_
   // for its own budget.
   if (warp < 4) {
     umma::regs_dec<88>();
-    if (warp == 0) {
+    // Warps 0 and 1 run their roles with all 32 lanes (lane 0 issues the
+    // copies and MMAs, every lane takes the same branches), so no lane of
+    // theirs sits at the CTA's closing barrier while another lane works.
+    if (warp == 0 && nU > 0) {
       // ---------------------------------------------------------- producer
-      if (lane == 0 && nU > 0) {
+      if (lane == 0) {
         mbar_arrive_expect_tx(&bs->q_full, (hasB ? 2 : 1) * Gm::kTileBytes);
         for (int x = 0; x < (hasB ? 2 : 1); ++x)
           for (int blk = 0; blk < Gm::kBlocks; ++blk)
             tma_load_4d(smem + Gm::kOffQ + x * Gm::kTileBytes + blk * Gm::kBlockBytes, &p.qmap,
                         blk * 64, qA0 + x * kBM, h, b, &bs->q_full);
-        int nk = 0, nv = 0;   // K and V tile loads issued
-        bool ok = true;
-        for (int s = 0; s < p.n_seg && ok; ++s) {
-          const int nt = bs->ntU[s];
-          const int ntA = bs->ntA[s];
-          const int bb = p.seg[s].bcast ? 0 : b;
-          for (int t = 0; t < nt; ++t) {
-            // the empty barriers take one arrival per query tile; a tile
-            // that sits this K/V tile out is arrived for here
-            const uint32_t absent = (t < ntA ? 0u : 1u) + (hasB ? 0u : 1u);
-            const int st = nk % ST, use = nk / ST;
-            if (use > 0 && !(ok = wait_bar(&bs->k_empty[st], (use - 1) & 1, bs, p.err))) break;
+      }
+      __syncwarp();
+      int nk = 0, nv = 0;   // K and V tile loads issued
+      bool ok = true;
+      for (int s = 0; s < p.n_seg && ok; ++s) {
+        const int nt = bs->ntU[s];
+        const int ntA = bs->ntA[s];
+        const int bb = p.seg[s].bcast ? 0 : b;
+        for (int t = 0; t < nt; ++t) {
+          // the empty barriers take one arrival per query tile; a tile that
+          // sits this K/V tile out is arrived for here
+          const uint32_t absent = (t < ntA ? 0u : 1u) + (hasB ? 0u : 1u);
+          const int st = nk % ST, use = nk / ST;
+          if (use > 0 &&
+              !(ok = __all_sync(0xffffffffu, wait_bar(&bs->k_empty[st], (use - 1) & 1, bs, p.err))))
+            break;
+          if (lane == 0) {
             mbar_arrive_expect_tx(&bs->k_full[st], Gm::kTileBytes);
             for (int blk = 0; blk < Gm::kBlocks; ++blk)
               tma_load_4d(smem + Gm::kOffK + st * Gm::kTileBytes + blk * Gm::kBlockBytes,
                           &p.kmap[s], blk * 64, t * kBN, hk, bb, &bs->k_full[st]);
             if (absent) mbar_arrive_n(&bs->k_empty[st], absent);
-            ++nk;
-            if (use > 0 && !(ok = wait_bar(&bs->v_empty[st], (use - 1) & 1, bs, p.err))) break;
+          }
+          __syncwarp();
+          ++nk;
+          if (use > 0 &&
+              !(ok = __all_sync(0xffffffffu, wait_bar(&bs->v_empty[st], (use - 1) & 1, bs, p.err))))
+            break;
+          if (lane == 0) {
             mbar_arrive_expect_tx(&bs->v_full[st], Gm::kTileBytes);
             for (int blk = 0; blk < Gm::kBlocks; ++blk)
               tma_load_4d(smem + Gm::kOffV + st * Gm::kTileBytes + blk * Gm::kBlockBytes,
                           &vmaps[s], blk * 64, t * kBN, hk, bb, &bs->v_full[st]);
             if (absent) mbar_arrive_n(&bs->v_empty[st], absent);
-            ++nv;
           }
-        }
-        // let every issued copy land before the CTA can exit
-        mbar_wait(&bs->q_full, 0, p.err);
-        for (int st = 0; st < ST; ++st) {
-          const int uk = (nk - st + ST - 1) / ST, uv = (nv - st + ST - 1) / ST;
-          if (uk > 0) mbar_wait(&bs->k_full[st], (uk - 1) & 1, p.err);
-          if (uv > 0) mbar_wait(&bs->v_full[st], (uv - 1) & 1, p.err);
+          __syncwarp();
+          ++nv;
         }
       }
-    } else if (warp == 1 && lane == 0 && nU > 0) {
+      // let every issued copy land before the CTA can exit
+      mbar_wait(&bs->q_full, 0, p.err);
+      for (int st = 0; st < ST; ++st) {
+        const int uk = (nk - st + ST - 1) / ST, uv = (nv - st + ST - 1) / ST;
+        if (uk > 0) mbar_wait(&bs->k_full[st], (uk - 1) & 1, p.err);
+        if (uv > 0) mbar_wait(&bs->v_full[st], (uv - 1) & 1, p.err);
+      }
+      __syncwarp();
+    } else if (warp == 1 && nU > 0) {
       // ---------------------------------------------------------- MMA issuer
       constexpr uint32_t kIdQK = umma::instr_desc_f16(kBM, kBN, kBf16, false, false);
       const uint32_t kIdPV = umma::instr_desc_f16(kBM, D, !p16, false, true);
@@ -414,6 +429,10 @@ __global__ void __launch_bounds__(kThreads, 1) kp3_kernel(const __grid_constant_
           ++c.s;
           c.t = 0;
         }
+      };
+      // every lane sees the same barrier state: lane 0's probe decides
+      auto probe = [&](uint64_t* bar, uint32_t parity) {
+        return __shfl_sync(0xffffffffu, mbar_test(bar, parity) ? 1 : 0, 0) != 0;
       };
       Cursor qc[2] = {{0, 0, 0}, {0, 0, 0}}, pc[2] = {{0, 0, 0}, {0, 0, 0}};
       for (int x = 0; x < 2; ++x) {
@@ -434,36 +453,39 @@ __global__ void __launch_bounds__(kThreads, 1) kp3_kernel(const __grid_constant_
       // probe ahead of the ring).
       int kpre = 0, vpre = 0;
       int qseq[2] = {0, 0}, seq = 0;       // issue order of each tile's latest QK
-      bool ok = wait_bar(&bs->q_full, 0, bs, p.err);
+      bool ok = __all_sync(0xffffffffu, wait_bar(&bs->q_full, 0, bs, p.err));
       uint64_t t_idle = 0;
       int idle = 0;
       while (ok) {
         bool did = false;
-        while (kpre < nU && mbar_test(&bs->k_full[kpre % ST], (kpre / ST) & 1)) ++kpre;
-        while (vpre < nU && mbar_test(&bs->v_full[vpre % ST], (vpre / ST) & 1)) ++vpre;
+        while (kpre < nU && probe(&bs->k_full[kpre % ST], (kpre / ST) & 1)) ++kpre;
+        while (vpre < nU && probe(&bs->v_full[vpre % ST], (vpre / ST) & 1)) ++vpre;
 #pragma unroll
         for (int x = 0; x < 2; ++x) {
           // O_X += P_X(j) V(j): P written and V landed
           if (jp[x] < jq[x]) {
             const int g = pc[x].g, st = g % ST;
-            if (g < vpre && mbar_test(&bs->p_full[x], jp[x] & 1)) {
-              umma::fence_after_sync();
-              const uint32_t pcol = tmem + x * 128;
-              const uint32_t ocol = tmem + Gm::kColO + x * D;
-              const uint64_t vd = opaque(vdesc0 + (uint64_t)((st * Gm::kTileBytes) >> 4));
-              const bool acc0 = jp[x] > 0;
-#pragma unroll
-              for (int kk = 0; kk < kBN / 16; ++kk)
-                umma::mma_ts(ocol, pcol + kk * 8, vd + (uint64_t)((kk * 16 * 128) >> 4), kIdPV,
-                             acc0 || kk > 0);
-              if (!p16) {
+            if (g < vpre && probe(&bs->p_full[x], jp[x] & 1)) {
+              if (lane == 0) {
+                umma::fence_after_sync();
+                const uint32_t pcol = tmem + x * 128;
+                const uint32_t ocol = tmem + Gm::kColO + x * D;
+                const uint64_t vd = opaque(vdesc0 + (uint64_t)((st * Gm::kTileBytes) >> 4));
+                const bool acc0 = jp[x] > 0;
 #pragma unroll
                 for (int kk = 0; kk < kBN / 16; ++kk)
-                  umma::mma_ts(ocol, pcol + 64 + kk * 8, vd + (uint64_t)((kk * 16 * 128) >> 4),
-                               kIdPV, true);
+                  umma::mma_ts(ocol, pcol + kk * 8, vd + (uint64_t)((kk * 16 * 128) >> 4), kIdPV,
+                               acc0 || kk > 0);
+                if (!p16) {
+#pragma unroll
+                  for (int kk = 0; kk < kBN / 16; ++kk)
+                    umma::mma_ts(ocol, pcol + 64 + kk * 8, vd + (uint64_t)((kk * 16 * 128) >> 4),
+                                 kIdPV, true);
+                }
+                umma::commit(&bs->pv_done[x]);
+                umma::commit(&bs->v_empty[st]);
               }
-              umma::commit(&bs->pv_done[x]);
-              umma::commit(&bs->v_empty[st]);
+              __syncwarp();
               ++jp[x];
               ++pc[x].t;
               ++pc[x].g;
@@ -475,17 +497,21 @@ __global__ void __launch_bounds__(kThreads, 1) kp3_kernel(const __grid_constant_
           if (jq[x] < nX[x] && jq[x] == jp[x] &&
               (x == 0 || jq[1] > 0 || !gateB || jp[0] > 0)) {
             const int g = qc[x].g, st = g % ST;
-            if (g < kpre && (jq[x] == 0 || mbar_test(&bs->pv_done[x], (jq[x] - 1) & 1))) {
-              umma::fence_after_sync();
-              const uint64_t qd = opaque(umma::smem_desc_sw128(sQ + x * Gm::kTileBytes, 16, 1024));
-              const uint64_t kd = opaque(kdesc0 + (uint64_t)((st * Gm::kTileBytes) >> 4));
+            if (g < kpre && (jq[x] == 0 || probe(&bs->pv_done[x], (jq[x] - 1) & 1))) {
+              if (lane == 0) {
+                umma::fence_after_sync();
+                const uint64_t qd =
+                    opaque(umma::smem_desc_sw128(sQ + x * Gm::kTileBytes, 16, 1024));
+                const uint64_t kd = opaque(kdesc0 + (uint64_t)((st * Gm::kTileBytes) >> 4));
 #pragma unroll
-              for (int kk = 0; kk < D / 16; ++kk) {
-                const uint32_t off = ((kk >> 2) * Gm::kBlockBytes + (kk & 3) * 32) >> 4;
-                umma::mma_ss(tmem + x * 128, qd + off, kd + off, kIdQK, kk > 0);
+                for (int kk = 0; kk < D / 16; ++kk) {
+                  const uint32_t off = ((kk >> 2) * Gm::kBlockBytes + (kk & 3) * 32) >> 4;
+                  umma::mma_ss(tmem + x * 128, qd + off, kd + off, kIdQK, kk > 0);
+                }
+                umma::commit(&bs->s_full[x]);
+                umma::commit(&bs->k_empty[st]);
               }
-              umma::commit(&bs->s_full[x]);
-              umma::commit(&bs->k_empty[st]);
+              __syncwarp();
               qseq[x] = ++seq;
               ++jq[x];
               ++qc[x].t;
@@ -512,7 +538,7 @@ __global__ void __launch_bounds__(kThreads, 1) kp3_kernel(const __grid_constant_
           for (int x = 0; x < 2 && !slept; ++x) {
             if (jq[x] < nX[x] && jq[x] == jp[x] && jq[x] > 0 &&
                 (x == 0 || !gateB || jp[0] > 0) &&
-                !mbar_test(&bs->pv_done[x], (jq[x] - 1) & 1)) {
+                !probe(&bs->pv_done[x], (jq[x] - 1) & 1)) {
               mbar_sleep_wait(&bs->pv_done[x], (jq[x] - 1) & 1, 1000);
               slept = true;
             }
@@ -521,7 +547,7 @@ __global__ void __launch_bounds__(kThreads, 1) kp3_kernel(const __grid_constant_
             int xo = -1;
             if (jp[0] < jq[0]) xo = 0;
             if (jp[1] < jq[1] && (xo < 0 || qseq[1] < qseq[0])) xo = 1;
-            if (xo >= 0 && !mbar_test(&bs->p_full[xo], jp[xo] & 1)) {
+            if (xo >= 0 && !probe(&bs->p_full[xo], jp[xo] & 1)) {
               mbar_sleep_wait(&bs->p_full[xo], jp[xo] & 1, 1000);
               slept = true;
             } else if (xo >= 0 && vpre < nU) {
@@ -533,22 +559,30 @@ __global__ void __launch_bounds__(kThreads, 1) kp3_kernel(const __grid_constant_
             }
           }
           if (!slept) __nanosleep(64);
+          __syncwarp();
         }
         // bounded idle time; stop if another role aborted
         if (++idle == 64) t_idle = globaltimer_ns();
         if (idle > 64 && (idle & 63) == 0) {
-          if (*reinterpret_cast<volatile int*>(&bs->abort_flag)) {
-            ok = false;
-          } else if (globaltimer_ns() - t_idle > kWaitLimitNs) {
-            set_device_error(p.err, static_cast<unsigned int>(-HALO_ERR_TIMEOUT));
-            *reinterpret_cast<volatile int*>(&bs->abort_flag) = 1;
-            ok = false;
+          int stop = 0;
+          if (lane == 0) {
+            if (*reinterpret_cast<volatile int*>(&bs->abort_flag)) {
+              stop = 1;
+            } else if (globaltimer_ns() - t_idle > kWaitLimitNs) {
+              set_device_error(p.err, static_cast<unsigned int>(-HALO_ERR_TIMEOUT));
+              *reinterpret_cast<volatile int*>(&bs->abort_flag) = 1;
+              stop = 1;
+            }
           }
+          if (__shfl_sync(0xffffffffu, stop, 0)) ok = false;
         }
       }
       // this thread's MMAs complete before the CTA can free TMEM
-      umma::commit(&bs->mma_done);
-      mbar_wait(&bs->mma_done, 0, p.err);
+      if (lane == 0) {
+        umma::commit(&bs->mma_done);
+        mbar_wait(&bs->mma_done, 0, p.err);
+      }
+      __syncwarp();
     }
   } else {
     umma::regs_inc<208>();
