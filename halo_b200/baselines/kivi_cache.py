@@ -85,13 +85,16 @@ def dequantize_packed(codes, scale, zero, *, bits: int, group_size: int, out=Non
 def unpack_codes(codes: torch.Tensor, bits: int) -> torch.Tensor:
     """Packed codes ``(..., D*bits/8)`` -> uint8 codes ``(..., D)``.  4/8
     bits: code ``i`` at byte ``i*bits/8``, bit ``(i*bits)%8``.  2 bits: 16
-    codes per 32-bit word, code ``i`` at word ``i/16``, byte ``(i%16)%4``,
-    bits ``2*((i%16)/4)`` (the decoder's interleaved layout)."""
+    codes per little-endian 32-bit word, code ``i`` at word ``i/16``, bit
+    ``16*(e&1) + 2*(e>>1)`` with ``e = i%16`` (the decoder's pair layout:
+    codes 2q and 2q+1 share bit 2q of the word's two halves)."""
     lead, nb = codes.shape[:-1], codes.shape[-1]
     if bits == 2:
-        w = codes.reshape(*lead, nb // 4, 1, 4)
-        sh = (2 * torch.arange(4, device=codes.device, dtype=torch.uint8)).view(4, 1)
-        return ((w >> sh) & 3).reshape(*lead, nb * 4)
+        e = torch.arange(16, device=codes.device)
+        pos = 16 * (e & 1) + 2 * (e >> 1)
+        byte, shift = (pos // 8), (pos % 8).to(torch.uint8)
+        w = codes.reshape(*lead, nb // 4, 4)
+        return ((w[..., byte] >> shift) & 3).reshape(*lead, nb * 4)
     per = 8 // bits
     c = codes.unsqueeze(-1).expand(*codes.shape, per)
     shifts = torch.arange(per, device=codes.device, dtype=torch.uint8) * bits

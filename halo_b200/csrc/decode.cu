@@ -409,7 +409,7 @@ __device__ __forceinline__ void load_qT_frags(const char* qslot, uint32_t (&qb)[
 // ---- K-direct (2-bit codes, transposed tile math).  Thread (g, c) of a
 // warp (g = lane / 4, c = lane % 4) owns the K elements of its rows g and
 // g + 8 in head-dim columns [c*D/4, (c+1)*D/4): one quantisation group
-// (half of one for D = 64), so one 4-entry value table per row.  The S^T
+// (half of one for D = 64), so one scale and zero per row.  The S^T
 // MMAs take K in a permuted k order: logical column 2c + e + 8h of k-step kk
 // is head-dim column c*D/4 + 4kk + 2h + e.  A permutation of k leaves
 // sum_k K Q^T unchanged when Q^T is loaded in the same order, and in this
@@ -432,13 +432,78 @@ __device__ __forceinline__ void load_qT_frags_perm(const char* qslot, uint32_t (
                  : "r"(base + swz<Gm::kInner, Gm::kGpb>(g, c * (D / 32) + m)));
 }
 
-// This thread's packed K codes (rows g, g + 8; D/4 codes each, interleaved
-// as the packed format stores them: element 16w + 4k + b of a group at bit
-// 8b + 2k of word w) and the value tables {v0, v1 | v2, v3} of their group.
+// ---- 2-bit codes to 16-bit values without the integer pipe
+// Packed 2-bit layout: code e (0..15) of each 16-code block at bit
+// 16*(e & 1) + 2*(e >> 1) of the block's little-endian 32-bit word, so the
+// two codes of pair q = (2q, 2q+1) sit at the same bit 2q of the word's two
+// 16-bit halves.  One LOP3 ((w & (0x00030003 << 2q)) | M_q) puts them into
+// the mantissas of two 16-bit floats whose exponent makes bit 2q worth 1:
+// each half reads E_q + c exactly, and a packed subtract of E_q leaves the
+// codes as exact small floats; one packed FMA then gives c*s + z rounded once
+// to the 16-bit type (the reference rounds c*s + z to fp32 first; with
+// c <= 3 and s, z 16-bit that only differs when the exact sum lies within
+// 2^-23 of a 16-bit rounding midpoint).  Pairs whose bits would reach the
+// exponent field are taken from the word shifted right first.  Two 16-bit
+// values per LOP3 and two per FMA-pipe instruction, instead of byte permutes
+// on the integer pipe.
+template <typename T>
+struct Code2;
+template <>
+struct Code2<__half> {
+  static constexpr int kPairsPerShift = 5;         // bits 0..9 of the mantissa
+  static constexpr int kShiftBits = 10;
+  __device__ static __forceinline__ uint32_t magic(int q) {
+    const uint32_t m = (uint32_t)(25 - 2 * q) << 10;  // 2^(10 - 2q)
+    return m | (m << 16);
+  }
+  __device__ static __forceinline__ uint32_t decode(uint32_t bits, int q, uint32_t s2,
+                                                    uint32_t z2) {
+    const __half2 e = __halves2half2(__ushort_as_half((unsigned short)(magic(q) & 0xFFFF)),
+                                     __ushort_as_half((unsigned short)(magic(q) & 0xFFFF)));
+    const __half2 v = __hsub2(*reinterpret_cast<const __half2*>(&bits), e);
+    const __half2 r = __hfma2(v, *reinterpret_cast<const __half2*>(&s2),
+                              *reinterpret_cast<const __half2*>(&z2));
+    return *reinterpret_cast<const uint32_t*>(&r);
+  }
+};
+template <>
+struct Code2<__nv_bfloat16> {
+  static constexpr int kPairsPerShift = 3;         // bits 0..5 of the mantissa
+  static constexpr int kShiftBits = 6;
+  __device__ static __forceinline__ uint32_t magic(int q) {
+    const uint32_t m = (uint32_t)(134 - 2 * q) << 7;  // 2^(7 - 2q)
+    return m | (m << 16);
+  }
+  __device__ static __forceinline__ uint32_t decode(uint32_t bits, int q, uint32_t s2,
+                                                    uint32_t z2) {
+    const uint32_t mm = magic(q) & 0xFFFF;
+    const __nv_bfloat162 e = __halves2bfloat162(__ushort_as_bfloat16((unsigned short)mm),
+                                                __ushort_as_bfloat16((unsigned short)mm));
+    const __nv_bfloat162 v = __hsub2(*reinterpret_cast<const __nv_bfloat162*>(&bits), e);
+    const __nv_bfloat162 r = __hfma2(v, *reinterpret_cast<const __nv_bfloat162*>(&s2),
+                                     *reinterpret_cast<const __nv_bfloat162*>(&z2));
+    return *reinterpret_cast<const uint32_t*>(&r);
+  }
+};
+
+// Values of pair p (0..7) of a 16-code word: codes 2p and 2p+1 as one
+// register of two 16-bit values c*s + z.
+template <typename T>
+__device__ __forceinline__ uint32_t code2_pair(uint32_t word, int p, uint32_t s2, uint32_t z2) {
+  using C = Code2<T>;
+  const int seg = p / C::kPairsPerShift, q = p % C::kPairsPerShift;
+  const uint32_t w = seg ? (word >> (seg * C::kShiftBits)) : word;
+  const uint32_t bits = (w & (0x00030003u << (2 * q))) | C::magic(q);
+  return C::decode(bits, q, s2, z2);
+}
+
+// This thread's packed K codes (rows g, g + 8; D/4 codes each, the span of
+// one quantisation group, as the packed format stores them) and the group's
+// scale and zero of each row, duplicated into both 16-bit halves.
 template <int D>
 struct KRegs {
   uint32_t words[2][D / 64];
-  uint32_t t01[2], t23[2];
+  uint32_t s2[2], z2[2];
 };
 
 template <typename T, int D>
@@ -465,30 +530,21 @@ __device__ __forceinline__ void load_k_regs(const char* pack, int code_tile, int
     uint16_t sb, zb;
     asm volatile("ld.shared.u16 %0, [%1];" : "=h"(sb) : "r"(s_sc + row * kGS * 2));
     asm volatile("ld.shared.u16 %0, [%1];" : "=h"(zb) : "r"(s_ze + row * kGS * 2));
-    const float sc = Elem<T>::to_f32(*reinterpret_cast<const T*>(&sb));
-    const float z = Elem<T>::to_f32(*reinterpret_cast<const T*>(&zb));
-    kr.t01[r] = Elem<T>::pack(__fadd_rn(__fmul_rn(0.f, sc), z), __fadd_rn(sc, z));
-    kr.t23[r] = Elem<T>::pack(__fadd_rn(__fmul_rn(2.f, sc), z), __fadd_rn(__fmul_rn(3.f, sc), z));
+    kr.s2[r] = (uint32_t)sb | ((uint32_t)sb << 16);
+    kr.z2[r] = (uint32_t)zb | ((uint32_t)zb << 16);
   }
 }
 
-// A fragments of k-step kk: elements 4kk .. 4kk+3 of the thread's span, rows
-// g (a0, a2) and g + 8 (a1, a3); c * 0x22 + 0x10 is the byte-permute
-// selector of value c's two bytes in the table.
-template <int D>
+// A fragments of k-step kk: span elements 4kk + 2h + {0, 1} (pair 2kk + h of
+// the span) of rows g (a0, a2) and g + 8 (a1, a3).
+template <typename T, int D>
 __device__ __forceinline__ void k_frag(const KRegs<D>& kr, int kk, uint32_t (&a)[4]) {
-  const int w = kk >> 2, sh = 2 * (kk & 3);
-  uint32_t lo[2], hi[2];
+  const int w = kk >> 2, p = 2 * (kk & 3);
 #pragma unroll
   for (int r = 0; r < 2; ++r) {
-    const uint32_t sel = ((kr.words[r][w] >> sh) & 0x03030303u) * 0x22u + 0x10101010u;
-    lo[r] = __byte_perm(kr.t01[r], kr.t23[r], sel);
-    hi[r] = __byte_perm(kr.t01[r], kr.t23[r], sel >> 16);
+    a[r] = code2_pair<T>(kr.words[r][w], p, kr.s2[r], kr.z2[r]);
+    a[2 + r] = code2_pair<T>(kr.words[r][w], p + 1, kr.s2[r], kr.z2[r]);
   }
-  a[0] = lo[0];
-  a[1] = lo[1];
-  a[2] = hi[0];
-  a[3] = hi[1];
 }
 
 template <typename T, int D, int STAGES, class KFrag>
@@ -637,7 +693,7 @@ __device__ __forceinline__ bool consume_mma_t(const P& p, const Unit& un, const 
     const int valid = it.rows - t * kBlockN;
     const int64_t pos0 = it.start + (int64_t)t * kBlockN;
     if constexpr (Tiles::kKDirect) {
-      auto kf = [&](int kk, uint32_t (&a)[4]) { k_frag<D>(tiles.kr, kk, a); };
+      auto kf = [&](int kk, uint32_t (&a)[4]) { k_frag<T, D>(tiles.kr, kk, a); };
       mma_tile_t<T, D, STAGES>(p.scale_log2, kf, vbase, qb, o, m0, m1, l0, l1, valid, pos0,
                                it.causal != 0, qpos);
     } else {
@@ -1205,24 +1261,16 @@ __device__ __forceinline__ void dequant_rows(const char* pack, char* dq) {
     const float z = Elem<T>::to_f32(*reinterpret_cast<const T*>(&zb));
     uint32_t out[16];
     if constexpr (BITS == 2) {
-      // 4-entry table of this group's values {v0, v1 | v2, v3}; codes are
-      // interleaved so (word >> 2k) & 0x03030303 holds the codes of elements
-      // 4k..4k+3, one per byte, and c * 0x22 + 0x10 is the byte-permute
-      // selector of value c's two bytes.
-      const uint32_t t01 = Elem<T>::pack(__fadd_rn(__fmul_rn(0.f, s), z), __fadd_rn(s, z));
-      const uint32_t t23 =
-          Elem<T>::pack(__fadd_rn(__fmul_rn(2.f, s), z), __fadd_rn(__fmul_rn(3.f, s), z));
+      // two 16-code words: pair p of word w is columns 16w + 2p, 16w + 2p + 1
+      const uint32_t s2 = (uint32_t)sb | ((uint32_t)sb << 16);
+      const uint32_t z2 = (uint32_t)zb | ((uint32_t)zb << 16);
       uint32_t words[2];
       asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];"
                    : "=r"(words[0]), "=r"(words[1]) : "r"(s_codes + col0 / 4));
 #pragma unroll
       for (int w = 0; w < 2; ++w)
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const uint32_t sel = ((words[w] >> (2 * k)) & 0x03030303u) * 0x22u + 0x10101010u;
-          out[w * 8 + 2 * k] = __byte_perm(t01, t23, sel);
-          out[w * 8 + 2 * k + 1] = __byte_perm(t01, t23, sel >> 16);
-        }
+        for (int q = 0; q < 8; ++q) out[w * 8 + q] = code2_pair<T>(words[w], q, s2, z2);
     } else {
       constexpr uint32_t kMask = (1u << BITS) - 1u;
       constexpr int kPer = 8 / BITS;
@@ -1275,7 +1323,7 @@ struct DequantTiles {
   __device__ __forceinline__ void release(int) { __syncwarp(); }
 };
 
-// K-direct tile provider (2-bit, transposed): K's codes and value tables go
+// K-direct tile provider (2-bit, transposed): K's codes, scales and zeros go
 // to registers (KRegs), V is dequantised into the 16-bit tile; the packed
 // stage is freed once both are done.
 template <typename T, int D>

@@ -11,12 +11,13 @@
 //   q         = clamp(rint(rnd(rnd(x - z) / s)), 0, qmax)   (NaN -> 0)
 //   dequant   = rnd(fl32(q * s) + z)                        (no fused multiply-add)
 // Codes are packed 8/bits per byte along head_dim.  4 and 8 bits: code i of
-// a row sits in byte i*bits/8 at bit (i*bits) % 8.  2 bits: each 32-bit word
-// holds 16 codes interleaved for the decoder -- code i of the row sits in
-// word i/16, byte (i%16)%4, bits 2*((i%16)/4) -- so one shift and mask give
-// the codes of four consecutive elements, one per byte (halo_b200.h
-// documents the layout).  Scale and zero are stored per group in the 16-bit
-// type, as the reference stores them.
+// a row sits in byte i*bits/8 at bit (i*bits) % 8.  2 bits: each
+// little-endian 32-bit word holds 16 codes laid out for the decoder -- code
+// i of the row sits in word i/16 at bit 16*(e & 1) + 2*(e >> 1), e = i % 16
+// -- so the two codes of each consecutive pair (2q, 2q+1) share bit 2q of
+// the word's two 16-bit halves and one mask yields both as a packed pair
+// (halo_b200.h documents the layout).  Scale and zero are stored per group
+// in the 16-bit type, as the reference stores them.
 #include <cstdint>
 
 #include "halo_common.cuh"
@@ -84,7 +85,7 @@ __global__ void __launch_bounds__(256) kivi_quantize_kernel(const QuantParams p)
     // groups are whole 16-code words (group % 16 == 0 is checked)
     for (int w = 0; w < p.group / 16; ++w) {
       uint32_t word = 0;
-      for (int e = 0; e < 16; ++e) word |= code(16 * w + e) << (8 * (e & 3) + 2 * (e >> 2));
+      for (int e = 0; e < 16; ++e) word |= code(16 * w + e) << (16 * (e & 1) + 2 * (e >> 1));
       for (int bb = 0; bb < 4; ++bb) out[4 * w + bb] = (uint8_t)(word >> (8 * bb));
     }
     return;
@@ -122,7 +123,7 @@ __global__ void __launch_bounds__(256) kivi_dequantize_kernel(const QuantParams 
   for (int i = 0; i < p.group; ++i) {
     const int e = i & 15;
     const uint32_t c =
-        p.bits == 2 ? (in[4 * (i >> 4) + (e & 3)] >> (2 * (e >> 2))) & 3u
+        p.bits == 2 ? (in[4 * (i >> 4) + 2 * (e & 1) + (e >> 3)] >> (2 * ((e >> 1) & 3))) & 3u
                     : (in[i / per_byte] >> ((i % per_byte) * p.bits)) & mask;
     x[i] = Elem<T>::from_f32(__fadd_rn(__fmul_rn((float)c, s), z));
   }

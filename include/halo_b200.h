@@ -236,7 +236,7 @@ int32_t halo_sharded_decode(const halo_decode_problem_t* problem,
  * x_sb, x_sh, x_st, fp16 or bf16) along head_dim in groups of `group`, to
  * `bits` (2/4/8) codes packed 8/bits per byte (4/8 bits: code i of a row at
  * byte i*bits/8, bit (i*bits)%8; 2 bits: 16 codes per little-endian 32-bit
- * word, code i at word i/16, byte (i%16)%4, bit 2*((i%16)/4), group a
+ * word, code i at word i/16, bit 16*(e&1) + 2*(e>>1) with e = i%16, group a
  * multiple of 16; byte strides c_sb/c_sh/c_st) plus per-group
  * scale and zero in x's dtype (element strides s_sb/s_sh/s_st).  Bit-exact
  * with _quantize_per_group (baselines/kivi_cache.py:44-69), whose every op

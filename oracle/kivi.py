@@ -81,26 +81,27 @@ def dequantize_per_group(codes: np.ndarray, scale: np.ndarray, zero: np.ndarray,
     return x.reshape(*codes.shape[:-2], codes.shape[-2] * codes.shape[-1])
 
 
+_POS2 = 16 * (np.arange(16) & 1) + 2 * (np.arange(16) >> 1)   # bit of code e in its word
+
+
 def pack_codes_2bit(codes: np.ndarray) -> np.ndarray:
     """Pack codes 0..3 of each row (flattened last two axes) into the device
     layout: 16 codes per little-endian 32-bit word, code ``i`` in word
-    ``i // 16``, byte ``(i % 16) % 4``, bits ``2 * ((i % 16) // 4)``."""
+    ``i // 16`` at bit ``16 * (e & 1) + 2 * (e >> 1)``, ``e = i % 16``."""
     c = codes.reshape(*codes.shape[:-2], -1).astype(np.uint32)
     n = c.shape[-1]
     assert n % 16 == 0
-    c = c.reshape(*c.shape[:-1], n // 16, 4, 4)           # (..., word, k, byte)
-    sh = (2 * np.arange(4, dtype=np.uint32)).reshape(4, 1)
-    byte = np.bitwise_or.reduce(c << sh, axis=-2)        # (..., word, byte)
-    return byte.astype(np.uint8).reshape(*c.shape[:-3], n // 4)
+    c = c.reshape(*c.shape[:-1], n // 16, 16)              # (..., word, e)
+    word = np.bitwise_or.reduce(c << _POS2.astype(np.uint32), axis=-1).astype("<u4")
+    return word.view(np.uint8).reshape(*c.shape[:-2], n // 4)
 
 
 def unpack_codes_2bit(packed: np.ndarray, group_size: int) -> np.ndarray:
     """Inverse of :func:`pack_codes_2bit`, back to ``(..., G, group_size)``."""
-    p = packed.astype(np.uint8)
+    p = np.ascontiguousarray(packed.astype(np.uint8))
     nb = p.shape[-1]
-    w = p.reshape(*p.shape[:-1], nb // 4, 1, 4)           # (..., word, 1, byte)
-    sh = (2 * np.arange(4, dtype=np.uint8)).reshape(4, 1)
-    c = (w >> sh) & 3                                     # (..., word, k, byte)
+    w = p.reshape(*p.shape[:-1], nb // 4, 4).view("<u4")   # (..., word, 1)
+    c = (w >> _POS2.astype(np.uint32)) & 3                 # (..., word, e)
     c = c.reshape(*p.shape[:-1], nb * 4)
     return c.reshape(*c.shape[:-1], c.shape[-1] // group_size, group_size).astype(np.int8)
 

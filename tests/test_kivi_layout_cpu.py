@@ -63,21 +63,39 @@ def test_permuted_fragments_give_k_q_transpose(D):
     np.testing.assert_allclose(S, K @ Q.T, rtol=1e-12, atol=1e-12)
 
 
-def test_code_word_selectors_follow_the_packed_order():
-    """Packed 2-bit format: element 16w + 4k + b of a group at bit 8b + 2k of
-    word w.  The selector ``((word >> 2k) & 0x03030303) * 0x22 + 0x10101010``
-    then names, per byte, the two table bytes of elements 4k .. 4k+3 --
-    k-step kk of a thread uses shift k = kk % 4 of word kk / 4."""
+def test_code_pairs_decode_through_16_bit_exponent_magic():
+    """Packed 2-bit format: element 16w + e of a group at bit 16*(e & 1) +
+    2*(e >> 1) of word w, so pair q = (2q, 2q+1) sits at bit 2q of both
+    16-bit halves.  The decoder's LOP3 ((w & (0x00030003 << 2q)) | M_q),
+    with M_q a 16-bit float whose exponent makes bit 2q worth 1, gives
+    E_q + c in each half; subtracting E_q leaves c exactly.  Pairs past the
+    mantissa (q >= 5 for fp16, q >= 3 for bf16) are read from the word
+    shifted right by 10 (fp16) or 6 (bf16) bits, in steps.  k-step kk of a
+    thread uses pairs 2kk and 2kk + 1 of its span: word kk / 4."""
     rng = np.random.default_rng(7)
     codes = rng.integers(0, 4, 32)
     words = [0, 0]
     for j, code in enumerate(codes):
-        w, rem = divmod(j, 16)
-        k, b = divmod(rem, 4)
-        words[w] |= int(code) << (8 * b + 2 * k)
+        w, e = divmod(j, 16)
+        words[w] |= int(code) << (16 * (e & 1) + 2 * (e >> 1))
+    for name, mant, per, shift, bias in (("f16", 10, 5, 10, 15), ("bf16", 7, 3, 6, 127)):
+        dt = np.float16 if name == "f16" else None
+        for p in range(16):
+            w, q8 = divmod(p, 8)
+            seg, q = divmod(q8, per)
+            word = words[w] >> (seg * shift)
+            m = (bias + mant - 2 * q) << mant            # 2^(mant - 2q) as 16-bit bits
+            bits = (word & (0x00030003 << (2 * q))) | (m | (m << 16))
+            lo, hi = bits & 0xFFFF, bits >> 16
+            if name == "f16":
+                vals = [float(np.array([x], dtype=np.uint16).view(dt)[0]) for x in (lo, hi)]
+            else:
+                vals = [float(np.array([x << 16], dtype=np.uint32).view(np.float32)[0])
+                        for x in (lo, hi)]
+            E = 2.0 ** (mant - 2 * q)
+            assert [v - E for v in vals] == [codes[2 * p], codes[2 * p + 1]], (name, p)
+    # k-step kk: pairs 2kk + h of the span (h = 0 -> a0/a1, h = 1 -> a2/a3)
     for kk in range(8):
-        w, k = divmod(kk, 4)
-        sel = ((words[w] >> (2 * k)) & 0x03030303) * 0x22 + 0x10101010
-        for b in range(4):
-            lo, hi = (sel >> (8 * b)) & 0xF, (sel >> (8 * b + 4)) & 0xF
-            assert (lo, hi) == (2 * codes[4 * kk + b], 2 * codes[4 * kk + b] + 1)
+        for h in (0, 1):
+            p = 2 * kk + h
+            assert p // 8 == kk // 4 and 2 * p == 4 * kk + 2 * h

@@ -29,11 +29,15 @@ def _check_digest(d, *ts):
 
 
 def test_kivi_2bit_device_layout_known_answers():
-    """16 codes per 32-bit word, code i at byte i % 4, bits 2 * (i // 4)."""
+    """16 codes per little-endian 32-bit word, code e at bit 16*(e & 1) +
+    2*(e >> 1): even codes fill the low half, odd codes the high half, pair
+    (2q, 2q+1) at bit 2q of each half.  Codes e % 4 put 0/2 in the low half
+    (0x8888) and 1/3 in the high half (0xDDDD); codes (e % 16) // 4 give
+    0, 0, 1, 1, 2, 2, 3, 3 in both halves (0xFA50)."""
     row = np.array([e % 4 for e in range(32)], dtype=np.int8).reshape(1, 32)
-    np.testing.assert_array_equal(OK.pack_codes_2bit(row), [0, 85, 170, 255] * 2)
+    np.testing.assert_array_equal(OK.pack_codes_2bit(row), [0x88, 0x88, 0xDD, 0xDD] * 2)
     row = np.array([(e % 16) // 4 for e in range(32)], dtype=np.int8).reshape(1, 32)
-    np.testing.assert_array_equal(OK.pack_codes_2bit(row), [228] * 8)
+    np.testing.assert_array_equal(OK.pack_codes_2bit(row), [0x50, 0xFA, 0x50, 0xFA] * 2)
     rng = np.random.default_rng(0)
     c = rng.integers(0, 4, size=(3, 4, 32)).astype(np.int8)
     np.testing.assert_array_equal(OK.unpack_codes_2bit(OK.pack_codes_2bit(c), 32), c)
