@@ -294,6 +294,14 @@ def run_ours_cfg5(args):
     for _ in range(args.warmup):
         dec(q, out=out, lse=lse)
     torch.cuda.synchronize()
+    # a decode step as a serving loop runs it: one CUDA graph replay per step
+    # (split-KV kernel + merge, or + the NVLink exchange merge when sharded);
+    # --eager times plain calls instead
+    graph = None if args.eager else dec.capture(q, out=out, lse=lse)
+    step = graph.replay if graph is not None else (lambda: dec(q, out=out, lse=lse))
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
 
     # ---- device throughput: K steps, events only around the whole loop (an
     # event between the split-KV kernel and its dependent merge would cancel
@@ -306,10 +314,12 @@ def run_ours_cfg5(args):
     with ClockSampler(local) as clocks:
         t0.record()
         for i in range(K):
-            dec(q, out=out, lse=lse)
+            step()
         t1.record()
         torch.cuda.synchronize()
-    launches = L.launch_count() - n0
+    # graph replays launch the captured kernels without passing the host
+    # counter: count them from the kernels one step holds
+    launches = (K * dec.launches_per_call if graph is not None else L.launch_count() - n0)
     barrier()
     ms = t0.elapsed_time(t1)
     # ---- roofline pass: the same K steps with the split-KV kernel bracketed
@@ -332,13 +342,14 @@ def run_ours_cfg5(args):
     ms, kd_ms_max = ms_t.tolist()
     ms_step = ms / K
 
-    # ---- end to end through the public API with host buffers
+    # ---- end to end through the public API with host buffers: the query
+    # comes from pinned host memory into the step's input buffer, the output
+    # goes back, every step synchronised
     q_host = q.cpu().pin_memory()
     out_host = torch.empty_like(out, device="cpu").pin_memory()
-    q_dev = torch.empty_like(q)
     for _ in range(3):
-        q_dev.copy_(q_host, non_blocking=True)
-        dec(q_dev, out=out, lse=lse)
+        q.copy_(q_host, non_blocking=True)
+        step()
         out_host.copy_(out, non_blocking=True)
         torch.cuda.current_stream().synchronize()
     barrier()
@@ -346,8 +357,8 @@ def run_ours_cfg5(args):
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(K):
-        q_dev.copy_(q_host, non_blocking=True)
-        dec(q_dev, out=out, lse=lse)
+        q.copy_(q_host, non_blocking=True)
+        step()
         out_host.copy_(out, non_blocking=True)
         torch.cuda.current_stream().synchronize()
     e1.record()
@@ -394,6 +405,10 @@ def run_ours_cfg5(args):
                 "parity": parity}
         if ref_gpu is not None:
             line["reference_gpu"] = ref_gpu
+        line["config"]["step"] = ("one CUDA graph replay per step" if graph is not None
+                                  else "eager calls")
+    del graph, step
+    torch.cuda.synchronize()
     dec.close()
     if world > 1:
         dist.barrier(device_ids=[local])
@@ -1172,6 +1187,8 @@ def main():
                     help="headline decode only (skip cfg2/3/4 in the default run)")
     ap.add_argument("--no-reference-gpu", action="store_true",
                     help="skip timing the reference's Triton kernel")
+    ap.add_argument("--eager", action="store_true",
+                    help="time the decode step as eager calls instead of CUDA graph replays")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")

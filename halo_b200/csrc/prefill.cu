@@ -110,16 +110,6 @@ __device__ __forceinline__ bool mbar_sleep_wait(uint64_t* bar, uint32_t parity, 
   return ok != 0;
 }
 
-// Shared-memory int with release / acquire ordering at CTA scope.
-__device__ __forceinline__ void st_release_shared(int* p, int v) {
-  asm volatile("st.release.cta.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(p)), "r"(v) : "memory");
-}
-__device__ __forceinline__ int ld_acquire_shared(const int* p) {
-  int v;
-  asm volatile("ld.acquire.cta.shared::cta.b32 %0, [%1];" : "=r"(v) : "r"(smem_addr(p)) : "memory");
-  return v;
-}
-
 // K/V tiles of segment `sg` visible to query positions <= qmax.
 __device__ __forceinline__ int seg_tiles(const Seg& sg, int64_t qmax) {
   int n = (sg.len + kBN - 1) / kBN;
@@ -130,6 +120,13 @@ __device__ __forceinline__ int seg_tiles(const Seg& sg, int64_t qmax) {
     if (nv < n) n = (int)nv;
   }
   return n;
+}
+
+// The value itself, opaque to the compiler: keeps the issuer from hoisting
+// every unrolled MMA's descriptor out of its polling loop into registers.
+__device__ __forceinline__ uint64_t opaque(uint64_t v) {
+  asm volatile("mov.b64 %0, %0;" : "+l"(v));
+  return v;
 }
 
 // ---- packed fp32 pairs (sm_100 f32x2 instructions: two lanes per issue)
@@ -201,19 +198,17 @@ __device__ __forceinline__ void write_p(const float (&sv)[kBN], uint64_t sl2, ui
 }
 
 // ======================================================================
-// kp3_kernel: two query tiles per CTA, 128-key score tiles, each softmax
-// group issuing its own tile's MMAs.
+// kp3_kernel: two query tiles per CTA, 128-key score tiles, one MMA issuer
+// that polls.
 //
 // CTA = query tiles A = 2*pair and B = 2*pair + 1 (B may be absent) of one
 // q-head; both walk the same K/V tiles (B's causal range; A takes part in
 // the tiles it can see, a prefix of each segment's).  384 threads:
-//   WG0  warp 0: TMA producer (Q once, then K and V tiles of 128 keys
-//        through ST-stage rings; lane 0 issues); warp 1: TMEM owner and
-//        landing observer (publishes how many K and V tiles have landed,
-//        in walk order); warps 2-3 idle.  56 registers.
-//   WG1  softmax of tile A (thread r = TMEM lane r = query row r); its
-//        thread 0 also issues tile A's MMAs.  224 registers.
-//   WG2  the same for tile B.
+//   WG0  warp 0 lane 0: TMA producer (Q once, then K and V tiles of 128
+//        keys through ST-stage rings); warp 1: TMEM owner, lane 0 issues
+//        every MMA of both tiles; warps 2-3 idle.  88 registers.
+//   WG1  softmax of tile A (thread r = TMEM lane r = query row r), 208 regs.
+//   WG2  softmax of tile B.
 // TMEM (512 columns): per tile X a 128-column score buffer S_X = [128X,
 // 128X + 128) and a D-column output accumulator O_X = [256 + D X, ...).
 // QK_X(j): S_X = Q_X K(j)^T, M128 N128, both operands in shared memory.
@@ -221,22 +216,19 @@ __device__ __forceinline__ void write_p(const float (&sv)[kBN], uint64_t sl2, ui
 // route: keys 2c, 2c+1 in column c < 64; bf16 route: the high parts there
 // and the residuals in column 64 + c) and PV_X(j): O_X += P_X(j) V(j) takes
 // P from TMEM as the A operand (M128 N=D), so P never touches shared memory.
-// Per tile the chain is QK(j) -> softmax(j) -> PV(j) -> QK(j+1), the last
-// step once PV(j) has completed (one score buffer per tile); the two tiles'
-// chains interleave on the tensor pipe, tile B starting half a step after
-// tile A.  Each softmax group issues its own tile's MMAs (thread 0, after a
-// group barrier), so a P reaches the tensor pipe without a hand-off.
+// With one score buffer per tile, QK_X(j+1) is issued only once PV_X(j) has
+// completed; the issuer keeps the tensor pipe busy with the other tile's
+// work meanwhile, so the two softmax groups alternate with the MMAs.
+// Issuer: a single thread polls (mbarrier.test_wait) and issues whichever
+// of the four next steps (QK/PV of A/B) has its inputs ready; it never waits
+// on one step while another could go, so no order of chunks can stall it.
+// It observes K and V landings in walk order (landed prefixes), so no ring
+// stage is probed before its previous use was seen to land.
 // Ring barriers: k_full/v_full (one arrival + the copy's bytes), k_empty /
 // v_empty (two arrivals: a tcgen05.commit per query tile that reads the
-// tile, the producer arriving for a tile that sits it out).  The landing
-// observer is the only reader of the full barriers in walk order; an
-// issuing thread takes a full barrier only after the observer published
-// that tile, so every parity wait stays within one phase (a tile that sits
-// K/V tiles out never probes ahead of the ring), and no order of chunks
-// can stall the CTA (each tile's chain is sequential; the ring only waits
-// on earlier tiles).  Per tile X: s_full (commit after QK), pv_done (commit
-// after PV); gate: tile A's first PV issued.  All waits bounded; TMEM freed
-// on every exit path.
+// tile, the producer arriving for a tile that sits it out).  Per tile X:
+// s_full (commit after QK), p_full (128 softmax arrivals), pv_done (commit
+// after PV).  All waits bounded; TMEM freed on every exit path.
 constexpr int kThreads = 384;
 
 template <int D>
@@ -256,11 +248,9 @@ struct Geom {
 struct Bars {
   uint64_t q_full;
   uint64_t k_full[4], v_full[4], k_empty[4], v_empty[4];
-  uint64_t s_full[2], pv_done[2], mma_done[2];
+  uint64_t s_full[2], p_full[2], pv_done[2], mma_done;
   uint32_t tmem_base;
   int abort_flag;
-  uint64_t gate;                     // tile A's first P V issued (tile B starts after it)
-  int kpub, vpub;                    // K / V tiles seen landed, in walk order
   int nU, nA;                        // K/V tiles of the walk, and tile A's share
   int16_t ntU[kMaxSegs], ntA[kMaxSegs];   // per segment: tiles B (the walk) / A see
 };
@@ -325,14 +315,11 @@ __global__ void __launch_bounds__(kThreads, 1) kp3_kernel(const __grid_constant_
     }
     for (int x = 0; x < 2; ++x) {
       mbar_init(&bs->s_full[x], 1);
+      mbar_init(&bs->p_full[x], kBM);
       mbar_init(&bs->pv_done[x], 1);
     }
-    mbar_init(&bs->mma_done[0], 1);
-    mbar_init(&bs->mma_done[1], 1);
-    mbar_init(&bs->gate, 1);
+    mbar_init(&bs->mma_done, 1);
     bs->abort_flag = 0;
-    bs->kpub = 0;
-    bs->vpub = 0;
     int nu = 0, na = 0;
     for (int s = 0; s < p.n_seg; ++s) {
       const int tu = seg_tiles(p.seg[s], qmaxU), ta = seg_tiles(p.seg[s], qmaxA);
@@ -361,102 +348,211 @@ __global__ void __launch_bounds__(kThreads, 1) kp3_kernel(const __grid_constant_
   const uint32_t sK = smem_addr(smem + Gm::kOffK);
   const uint32_t sV = smem_addr(smem + Gm::kOffV);
 
-  // Register split (128 x 56 + 256 x 224 = 384 x 168, the launch budget),
+  // Register split (128 x 88 + 256 x 208 = 384 x 168, the launch budget),
   // made inside each role's branch so the compiler sizes each role's code
   // for its own budget.
   if (warp < 4) {
-    umma::regs_dec<56>();
-    // Warps 0 and 1 run their roles with all 32 lanes (lane 0 issues the
-    // copies and MMAs, every lane takes the same branches), so no lane of
-    // theirs sits at the CTA's closing barrier while another lane works.
-    if (warp == 0 && nU > 0) {
+    umma::regs_dec<88>();
+    if (warp == 0) {
       // ---------------------------------------------------------- producer
-      if (lane == 0) {
+      if (lane == 0 && nU > 0) {
         mbar_arrive_expect_tx(&bs->q_full, (hasB ? 2 : 1) * Gm::kTileBytes);
         for (int x = 0; x < (hasB ? 2 : 1); ++x)
           for (int blk = 0; blk < Gm::kBlocks; ++blk)
             tma_load_4d(smem + Gm::kOffQ + x * Gm::kTileBytes + blk * Gm::kBlockBytes, &p.qmap,
                         blk * 64, qA0 + x * kBM, h, b, &bs->q_full);
-      }
-      __syncwarp();
-      int nk = 0, nv = 0;   // K and V tile loads issued
-      bool ok = true;
-      for (int s = 0; s < p.n_seg && ok; ++s) {
-        const int nt = bs->ntU[s];
-        const int ntA = bs->ntA[s];
-        const int bb = p.seg[s].bcast ? 0 : b;
-        for (int t = 0; t < nt; ++t) {
-          // the empty barriers take one arrival per query tile; a tile that
-          // sits this K/V tile out is arrived for here
-          const uint32_t absent = (t < ntA ? 0u : 1u) + (hasB ? 0u : 1u);
-          const int st = nk % ST, use = nk / ST;
-          if (use > 0 &&
-              !(ok = __all_sync(0xffffffffu, wait_bar(&bs->k_empty[st], (use - 1) & 1, bs, p.err))))
-            break;
-          if (lane == 0) {
+        int nk = 0, nv = 0;   // K and V tile loads issued
+        bool ok = true;
+        for (int s = 0; s < p.n_seg && ok; ++s) {
+          const int nt = bs->ntU[s];
+          const int ntA = bs->ntA[s];
+          const int bb = p.seg[s].bcast ? 0 : b;
+          for (int t = 0; t < nt; ++t) {
+            // the empty barriers take one arrival per query tile; a tile
+            // that sits this K/V tile out is arrived for here
+            const uint32_t absent = (t < ntA ? 0u : 1u) + (hasB ? 0u : 1u);
+            const int st = nk % ST, use = nk / ST;
+            if (use > 0 && !(ok = wait_bar(&bs->k_empty[st], (use - 1) & 1, bs, p.err))) break;
             mbar_arrive_expect_tx(&bs->k_full[st], Gm::kTileBytes);
             for (int blk = 0; blk < Gm::kBlocks; ++blk)
               tma_load_4d(smem + Gm::kOffK + st * Gm::kTileBytes + blk * Gm::kBlockBytes,
                           &p.kmap[s], blk * 64, t * kBN, hk, bb, &bs->k_full[st]);
             if (absent) mbar_arrive_n(&bs->k_empty[st], absent);
-          }
-          __syncwarp();
-          ++nk;
-          if (use > 0 &&
-              !(ok = __all_sync(0xffffffffu, wait_bar(&bs->v_empty[st], (use - 1) & 1, bs, p.err))))
-            break;
-          if (lane == 0) {
+            ++nk;
+            if (use > 0 && !(ok = wait_bar(&bs->v_empty[st], (use - 1) & 1, bs, p.err))) break;
             mbar_arrive_expect_tx(&bs->v_full[st], Gm::kTileBytes);
             for (int blk = 0; blk < Gm::kBlocks; ++blk)
               tma_load_4d(smem + Gm::kOffV + st * Gm::kTileBytes + blk * Gm::kBlockBytes,
                           &vmaps[s], blk * 64, t * kBN, hk, bb, &bs->v_full[st]);
             if (absent) mbar_arrive_n(&bs->v_empty[st], absent);
+            ++nv;
           }
-          __syncwarp();
-          ++nv;
+        }
+        // let every issued copy land before the CTA can exit
+        mbar_wait(&bs->q_full, 0, p.err);
+        for (int st = 0; st < ST; ++st) {
+          const int uk = (nk - st + ST - 1) / ST, uv = (nv - st + ST - 1) / ST;
+          if (uk > 0) mbar_wait(&bs->k_full[st], (uk - 1) & 1, p.err);
+          if (uv > 0) mbar_wait(&bs->v_full[st], (uv - 1) & 1, p.err);
         }
       }
-      // let every issued copy land before the CTA can exit
-      mbar_wait(&bs->q_full, 0, p.err);
-      for (int st = 0; st < ST; ++st) {
-        const int uk = (nk - st + ST - 1) / ST, uv = (nv - st + ST - 1) / ST;
-        if (uk > 0) mbar_wait(&bs->k_full[st], (uk - 1) & 1, p.err);
-        if (uv > 0) mbar_wait(&bs->v_full[st], (uv - 1) & 1, p.err);
+    } else if (warp == 1 && lane == 0 && nU > 0) {
+      // ---------------------------------------------------------- MMA issuer
+      constexpr uint32_t kIdQK = umma::instr_desc_f16(kBM, kBN, kBf16, false, false);
+      const uint32_t kIdPV = umma::instr_desc_f16(kBM, D, !p16, false, true);
+      const uint64_t kdesc0 = umma::smem_desc_sw128(sK, 16, 1024);
+      const uint64_t vdesc0 = umma::smem_desc_sw128(sV, Gm::kBlockBytes, 1024);
+      const int nX[2] = {nA, hasB ? nU : 0};
+      // cursors: next K/V tile each query tile takes part in, for QK and PV
+      const int n_seg = p.n_seg;
+      auto seek = [&](Cursor& c, int x) {
+        while (c.s < n_seg) {
+          const int ntU = bs->ntU[c.s];
+          const int ntX = x ? ntU : bs->ntA[c.s];
+          if (c.t < ntX) return;
+          c.g += ntU - c.t;   // the rest of this segment is sat out
+          ++c.s;
+          c.t = 0;
+        }
+      };
+      Cursor qc[2] = {{0, 0, 0}, {0, 0, 0}}, pc[2] = {{0, 0, 0}, {0, 0, 0}};
+      for (int x = 0; x < 2; ++x) {
+        seek(qc[x], x);
+        seek(pc[x], x);
       }
-      __syncwarp();
-    } else if (warp == 1 && nU > 0) {
-      // ---------------------------------------------------------- landing observer
-      // Publishes how many K and V tiles have landed, each in walk order
-      // (kpub / vpub).  Each full barrier is waited on only after its
-      // previous use was seen to land, and no use of a stage can be
-      // reloaded before this warp saw it land (the MMAs that free it are
-      // issued after the publication), so every parity wait here and in
-      // the issuing threads stays within one phase of its barrier: a parity
-      // probe of phase n while phase n-1 is open would read as complete.
+      int jq[2] = {0, 0}, jp[2] = {0, 0};
+      // Tile B's first QK waits for tile A's first P V when both start on
+      // the walk's first K/V tile, so the two softmax groups run half a
+      // step apart.  (Only then: if A starts later, A's first V tile may
+      // need a ring stage that B's early tiles must free first.)
+      const bool gateB = nX[0] > 0 && qc[0].g == 0;
+      // Landed prefixes: K (V) tiles below kpre (vpre) are known to have
+      // landed.  The next tile's full barrier is probed in walk order, so a
+      // stage is only probed after its previous use was seen to land: a
+      // parity probe of phase n while phase n-1 is still open would read
+      // as complete (a query tile that sits tiles out would otherwise
+      // probe ahead of the ring).
       int kpre = 0, vpre = 0;
-      bool ok = true;
-      while (ok && (kpre < nU || vpre < nU)) {
-        const bool doK = kpre < nU && (kpre <= vpre || vpre >= nU);
-        const int n = doK ? kpre : vpre;
-        uint64_t* bar = doK ? &bs->k_full[n % ST] : &bs->v_full[n % ST];
-        ok = __all_sync(0xffffffffu, wait_bar(bar, (n / ST) & 1, bs, p.err));
-        if (!ok) break;
-        if (lane == 0) st_release_shared(doK ? &bs->kpub : &bs->vpub, n + 1);
-        __syncwarp();
-        if (doK)
-          ++kpre;
-        else
-          ++vpre;
+      int qseq[2] = {0, 0}, seq = 0;       // issue order of each tile's latest QK
+      bool ok = wait_bar(&bs->q_full, 0, bs, p.err);
+      uint64_t t_idle = 0;
+      int idle = 0;
+      while (ok) {
+        bool did = false;
+        while (kpre < nU && mbar_test(&bs->k_full[kpre % ST], (kpre / ST) & 1)) ++kpre;
+        while (vpre < nU && mbar_test(&bs->v_full[vpre % ST], (vpre / ST) & 1)) ++vpre;
+#pragma unroll
+        for (int x = 0; x < 2; ++x) {
+          // O_X += P_X(j) V(j): P written and V landed
+          if (jp[x] < jq[x]) {
+            const int g = pc[x].g, st = g % ST;
+            if (g < vpre && mbar_test(&bs->p_full[x], jp[x] & 1)) {
+              umma::fence_after_sync();
+              const uint32_t pcol = tmem + x * 128;
+              const uint32_t ocol = tmem + Gm::kColO + x * D;
+              const uint64_t vd = opaque(vdesc0 + (uint64_t)((st * Gm::kTileBytes) >> 4));
+              const bool acc0 = jp[x] > 0;
+#pragma unroll
+              for (int kk = 0; kk < kBN / 16; ++kk)
+                umma::mma_ts(ocol, pcol + kk * 8, vd + (uint64_t)((kk * 16 * 128) >> 4), kIdPV,
+                             acc0 || kk > 0);
+              if (!p16) {
+#pragma unroll
+                for (int kk = 0; kk < kBN / 16; ++kk)
+                  umma::mma_ts(ocol, pcol + 64 + kk * 8, vd + (uint64_t)((kk * 16 * 128) >> 4),
+                               kIdPV, true);
+              }
+              umma::commit(&bs->pv_done[x]);
+              umma::commit(&bs->v_empty[st]);
+              ++jp[x];
+              ++pc[x].t;
+              ++pc[x].g;
+              seek(pc[x], x);
+              did = true;
+            }
+          }
+          // S_X = Q_X K(j)^T: S_X free (previous PV_X completed) and K landed
+          if (jq[x] < nX[x] && jq[x] == jp[x] &&
+              (x == 0 || jq[1] > 0 || !gateB || jp[0] > 0)) {
+            const int g = qc[x].g, st = g % ST;
+            if (g < kpre && (jq[x] == 0 || mbar_test(&bs->pv_done[x], (jq[x] - 1) & 1))) {
+              umma::fence_after_sync();
+              const uint64_t qd = opaque(umma::smem_desc_sw128(sQ + x * Gm::kTileBytes, 16, 1024));
+              const uint64_t kd = opaque(kdesc0 + (uint64_t)((st * Gm::kTileBytes) >> 4));
+#pragma unroll
+              for (int kk = 0; kk < D / 16; ++kk) {
+                const uint32_t off = ((kk >> 2) * Gm::kBlockBytes + (kk & 3) * 32) >> 4;
+                umma::mma_ss(tmem + x * 128, qd + off, kd + off, kIdQK, kk > 0);
+              }
+              umma::commit(&bs->s_full[x]);
+              umma::commit(&bs->k_empty[st]);
+              qseq[x] = ++seq;
+              ++jq[x];
+              ++qc[x].t;
+              ++qc[x].g;
+              seek(qc[x], x);
+              did = true;
+            }
+          }
+        }
+        if (jp[0] >= nX[0] && jp[1] >= nX[1]) break;
+        if (did) {
+          idle = 0;
+          continue;
+        }
+        // Nothing ready.  Sleep in hardware on the event expected first, so
+        // the issuer takes no issue slots from the softmax warps that share
+        // its scheduler: a P V completing (it frees a score buffer for the
+        // next QK), else the oldest pending P (its softmax started first),
+        // else the next K or V tile to land (probed in walk order); every
+        // probe stays within one phase of its barrier, as above.
+        {
+          bool slept = false;
+#pragma unroll
+          for (int x = 0; x < 2 && !slept; ++x) {
+            if (jq[x] < nX[x] && jq[x] == jp[x] && jq[x] > 0 &&
+                (x == 0 || !gateB || jp[0] > 0) &&
+                !mbar_test(&bs->pv_done[x], (jq[x] - 1) & 1)) {
+              mbar_sleep_wait(&bs->pv_done[x], (jq[x] - 1) & 1, 1000);
+              slept = true;
+            }
+          }
+          if (!slept) {
+            int xo = -1;
+            if (jp[0] < jq[0]) xo = 0;
+            if (jp[1] < jq[1] && (xo < 0 || qseq[1] < qseq[0])) xo = 1;
+            if (xo >= 0 && !mbar_test(&bs->p_full[xo], jp[xo] & 1)) {
+              mbar_sleep_wait(&bs->p_full[xo], jp[xo] & 1, 1000);
+              slept = true;
+            } else if (xo >= 0 && vpre < nU) {
+              mbar_sleep_wait(&bs->v_full[vpre % ST], (vpre / ST) & 1, 1000);
+              slept = true;
+            } else if (kpre < nU) {
+              mbar_sleep_wait(&bs->k_full[kpre % ST], (kpre / ST) & 1, 1000);
+              slept = true;
+            }
+          }
+          if (!slept) __nanosleep(64);
+        }
+        // bounded idle time; stop if another role aborted
+        if (++idle == 64) t_idle = globaltimer_ns();
+        if (idle > 64 && (idle & 63) == 0) {
+          if (*reinterpret_cast<volatile int*>(&bs->abort_flag)) {
+            ok = false;
+          } else if (globaltimer_ns() - t_idle > kWaitLimitNs) {
+            set_device_error(p.err, static_cast<unsigned int>(-HALO_ERR_TIMEOUT));
+            *reinterpret_cast<volatile int*>(&bs->abort_flag) = 1;
+            ok = false;
+          }
+        }
       }
+      // this thread's MMAs complete before the CTA can free TMEM
+      umma::commit(&bs->mma_done);
+      mbar_wait(&bs->mma_done, 0, p.err);
     }
   } else {
-    umma::regs_inc<224>();
+    umma::regs_inc<208>();
     // ------------------------------------------------------------ softmax X
-    // and, on thread r = 0, the MMAs of tile X: P V as soon as the group's
-    // P is written, then QK of the next K/V tile once that P V completed.
-    // Issuing from the group that produces P needs no hand-off to another
-    // warp (an issuing warp beside two busy softmax warps on one scheduler
-    // was measured to react about a microsecond late).
     const int x = (warp - 4) >> 2;              // 0: tile A, 1: tile B
     const int sub = warp & 3;
     const int r = sub * 32 + lane;
@@ -466,175 +562,77 @@ __global__ void __launch_bounds__(kThreads, 1) kp3_kernel(const __grid_constant_
     const bool active = x == 0 || hasB;
     const int64_t qmin = x ? qminB : qminA;
     const int64_t qpos = qmin + r;
-    const int nXt = active ? (x ? nU : nA) : 0;   // K/V tiles this tile takes part in
-    constexpr uint32_t kIdQK = umma::instr_desc_f16(kBM, kBN, kBf16, false, false);
-    const uint32_t kIdPV = umma::instr_desc_f16(kBM, D, !p16, false, true);
-
-    // thread r = 0: wait until the observer has seen K/V tile g land, then
-    // take the (now alias-free) full barrier itself
-    auto landed = [&](int* pub, uint64_t* full, int g) -> bool {
-      if (ld_acquire_shared(pub) <= g) {
-        const uint64_t t0 = globaltimer_ns();
-        while (ld_acquire_shared(pub) <= g) {
-          __nanosleep(32);
-          if (*reinterpret_cast<volatile int*>(&bs->abort_flag)) return false;
-          if (globaltimer_ns() - t0 > kWaitLimitNs) {
-            set_device_error(p.err, static_cast<unsigned int>(-HALO_ERR_TIMEOUT));
-            *reinterpret_cast<volatile int*>(&bs->abort_flag) = 1;
-            return false;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    int j = 0;
+    for (int s = 0; s < p.n_seg && ok && active; ++s) {
+      const Seg sg = p.seg[s];
+      const int nt = x ? bs->ntU[s] : bs->ntA[s];
+      for (int t = 0; t < nt; ++t, ++j) {
+        ok = __all_sync(0xffffffffu, wait_bar(&bs->s_full[x], j & 1, bs, p.err));
+        if (!ok) break;
+        umma::fence_after_sync();
+        const int row0 = t * kBN;
+        const int64_t kpos0 = sg.start + row0;
+        const bool full = (row0 + kBN <= sg.len) && (!sg.causal || kpos0 + kBN - 1 <= qmin);
+        const int lim_len = sg.len - row0;
+        const int64_t lim_pos = sg.causal ? qpos - kpos0 : (int64_t)kBN;
+        float sv[kBN];
+#pragma unroll
+        for (int c = 0; c < kBN / 32; ++c) umma::tmem_ld32(trow + scol + c * 32, sv + c * 32);
+        umma::tmem_wait_ld();
+        if (!full) {
+#pragma unroll
+          for (int c = 0; c < kBN; ++c)
+            if (!(c < lim_len && (int64_t)c <= lim_pos)) sv[c] = -INFINITY;
+        }
+        float mx8[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) mx8[e] = sv[e];
+#pragma unroll
+        for (int c = 8; c < kBN; c += 16) {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) mx8[e] = fmax3(mx8[e], sv[c + e], sv[c + 8 + e]);
+        }
+        const float mx = fmax3(fmax3(mx8[0], mx8[1], mx8[2]), fmax3(mx8[3], mx8[4], mx8[5]),
+                               fmaxf(mx8[6], mx8[7])) *
+                         p.scale_log2;
+        const bool grow = mx > m + kRescaleLog2 || (m == -INFINITY && mx > -INFINITY);
+        float fac = 1.f;
+        if (grow) {
+          fac = (m == -INFINITY) ? 0.f : ex2(m - mx);
+          l *= fac;
+          m = mx;
+        }
+        if (j > 0 && __any_sync(0xffffffffu, grow)) {
+          // O_X is quiescent: QK_X(j) was issued after PV_X(j-1) completed,
+          // and PV_X(j) waits for this P
+#pragma unroll
+          for (int c = 0; c < D / 32; ++c) {
+            float ov[32];
+            umma::tmem_ld32(trow + ocol + c * 32, ov);
+            umma::tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) ov[e] *= fac;
+            umma::tmem_st32(trow + ocol + c * 32, ov);
           }
         }
+        // P = exp2(s * scale_log2 - m) as 16-bit pairs into S's columns
+        const float nmu = (m == -INFINITY) ? 0.f : -m;
+        const uint64_t sl2 = f2pack(p.scale_log2, p.scale_log2), nm2 = f2pack(nmu, nmu);
+        uint64_t rs2[2] = {0ull, 0ull};   // row-sum pairs (+0.f bits)
+        if (p16)
+          write_p<false>(sv, sl2, nm2, trow + scol, rs2);
+        else
+          write_p<true>(sv, sl2, nm2, trow + scol, rs2);
+        float rs4[4];
+        f2unpack(rs2[0], rs4[0], rs4[1]);
+        f2unpack(rs2[1], rs4[2], rs4[3]);
+        l += (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
+        umma::tmem_wait_st();
+        umma::fence_before_sync();
+        mbar_arrive(&bs->p_full[x]);
       }
-      return wait_bar(&full[g % ST], (g / ST) & 1, bs, p.err);
-    };
-    auto issue_qk = [&](int g) -> bool {
-      if (!landed(&bs->kpub, bs->k_full, g)) return false;
-      umma::fence_after_sync();
-      const int st = g % ST;
-      const uint64_t qd = umma::smem_desc_sw128(sQ + x * Gm::kTileBytes, 16, 1024);
-      const uint64_t kd = umma::smem_desc_sw128(sK + st * Gm::kTileBytes, 16, 1024);
-#pragma unroll
-      for (int kk = 0; kk < D / 16; ++kk) {
-        const uint32_t off = ((kk >> 2) * Gm::kBlockBytes + (kk & 3) * 32) >> 4;
-        umma::mma_ss(tmem + x * 128, qd + off, kd + off, kIdQK, kk > 0);
-      }
-      umma::commit(&bs->s_full[x]);
-      umma::commit(&bs->k_empty[st]);
-      return true;
-    };
-    auto issue_pv = [&](int g, bool first) -> bool {
-      if (!landed(&bs->vpub, bs->v_full, g)) return false;
-      umma::fence_after_sync();
-      const int st = g % ST;
-      const uint32_t pcol = tmem + x * 128;
-      const uint32_t oc = tmem + ocol;
-      const uint64_t vd = umma::smem_desc_sw128(sV + st * Gm::kTileBytes, Gm::kBlockBytes, 1024);
-#pragma unroll
-      for (int kk = 0; kk < kBN / 16; ++kk)
-        umma::mma_ts(oc, pcol + kk * 8, vd + (uint64_t)((kk * 16 * 128) >> 4), kIdPV,
-                     !first || kk > 0);
-      if (!p16) {
-#pragma unroll
-        for (int kk = 0; kk < kBN / 16; ++kk)
-          umma::mma_ts(oc, pcol + 64 + kk * 8, vd + (uint64_t)((kk * 16 * 128) >> 4), kIdPV,
-                       true);
-      }
-      umma::commit(&bs->pv_done[x]);
-      umma::commit(&bs->v_empty[st]);
-      return true;
-    };
-    // walk position of this tile's next K/V tile after (s, t): segment,
-    // tile in segment and global tile index; s = n_seg when none is left
-    auto advance = [&](int& s, int& t, int& g) {
-      ++t;
-      ++g;
-      while (s < p.n_seg) {
-        const int ntU = bs->ntU[s];
-        const int ntX = x ? ntU : bs->ntA[s];
-        if (t < ntX) return;
-        g += ntU - t;        // tiles of this segment that tile X sits out
-        ++s;
-        t = 0;
-      }
-    };
-
-    bool ok = true;
-    int s = 0, t = -1, g = -1;                   // this tile's first K/V tile
-    advance(s, t, g);
-    if (r == 0 && nXt > 0) {
-      bool go = wait_bar(&bs->q_full, 0, bs, p.err);
-      // Tile B's first QK waits for tile A's first P V when both start on
-      // the walk's first K/V tile, so the two softmax groups run half a
-      // step apart.  (Only then: if A starts later, A's first V tile may
-      // need a ring stage that B's early tiles must free first.)
-      if (go && x == 1 && nA > 0 && bs->ntA[0] > 0) go = wait_bar(&bs->gate, 0, bs, p.err);
-      ok = go && issue_qk(g);
-    }
-    ok = __shfl_sync(0xffffffffu, ok, 0);        // warp-uniform (thread 0's outcome)
-    float m = -INFINITY, l = 0.f;
-    int j = 0;
-    for (; j < nXt && ok; ++j) {
-      const Seg sg = p.seg[s];
-      ok = __all_sync(0xffffffffu, wait_bar(&bs->s_full[x], j & 1, bs, p.err));
-      if (!ok) break;
-      umma::fence_after_sync();
-      const int row0 = t * kBN;
-      const int64_t kpos0 = sg.start + row0;
-      const bool full = (row0 + kBN <= sg.len) && (!sg.causal || kpos0 + kBN - 1 <= qmin);
-      const int lim_len = sg.len - row0;
-      const int64_t lim_pos = sg.causal ? qpos - kpos0 : (int64_t)kBN;
-      float sv[kBN];
-#pragma unroll
-      for (int c = 0; c < kBN / 32; ++c) umma::tmem_ld32(trow + scol + c * 32, sv + c * 32);
-      umma::tmem_wait_ld();
-      if (!full) {
-#pragma unroll
-        for (int c = 0; c < kBN; ++c)
-          if (!(c < lim_len && (int64_t)c <= lim_pos)) sv[c] = -INFINITY;
-      }
-      float mx8[8];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) mx8[e] = sv[e];
-#pragma unroll
-      for (int c = 8; c < kBN; c += 16) {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) mx8[e] = fmax3(mx8[e], sv[c + e], sv[c + 8 + e]);
-      }
-      const float mx = fmax3(fmax3(mx8[0], mx8[1], mx8[2]), fmax3(mx8[3], mx8[4], mx8[5]),
-                             fmaxf(mx8[6], mx8[7])) *
-                       p.scale_log2;
-      const bool grow = mx > m + kRescaleLog2 || (m == -INFINITY && mx > -INFINITY);
-      float fac = 1.f;
-      if (grow) {
-        fac = (m == -INFINITY) ? 0.f : ex2(m - mx);
-        l *= fac;
-        m = mx;
-      }
-      if (j > 0 && __any_sync(0xffffffffu, grow)) {
-        // O_X is quiescent: QK_X(j) was issued after PV_X(j-1) completed,
-        // and PV_X(j) waits for this P
-#pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
-          float ov[32];
-          umma::tmem_ld32(trow + ocol + c * 32, ov);
-          umma::tmem_wait_ld();
-#pragma unroll
-          for (int e = 0; e < 32; ++e) ov[e] *= fac;
-          umma::tmem_st32(trow + ocol + c * 32, ov);
-        }
-      }
-      // P = exp2(s * scale_log2 - m) as 16-bit pairs into S's columns
-      const float nmu = (m == -INFINITY) ? 0.f : -m;
-      const uint64_t sl2 = f2pack(p.scale_log2, p.scale_log2), nm2 = f2pack(nmu, nmu);
-      uint64_t rs2[2] = {0ull, 0ull};   // row-sum pairs (+0.f bits)
-      if (p16)
-        write_p<false>(sv, sl2, nm2, trow + scol, rs2);
-      else
-        write_p<true>(sv, sl2, nm2, trow + scol, rs2);
-      float rs4[4];
-      f2unpack(rs2[0], rs4[0], rs4[1]);
-      f2unpack(rs2[1], rs4[2], rs4[3]);
-      l += (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
-      umma::tmem_wait_st();
-      umma::fence_before_sync();
-      // every row's P is in TMEM: the group's thread 0 issues P V, then the
-      // next QK once this P V has completed (it frees the score buffer)
-      named_bar_sync(1 + x, kBM);
-      int sn = s, tn = t, gn = g;
-      advance(sn, tn, gn);
-      if (r == 0) {
-        bool go = issue_pv(g, j == 0);
-        if (go && j == 0 && x == 0) mbar_arrive(&bs->gate);
-        if (go && j + 1 < nXt) {
-          go = wait_bar(&bs->pv_done[x], j & 1, bs, p.err);
-          if (go) go = issue_qk(gn);
-        }
-        ok = go;
-      }
-      ok = __shfl_sync(0xffffffffu, ok, 0);
-      s = sn;
-      t = tn;
-      g = gn;
     }
     const int nX = j;
 
@@ -702,12 +700,6 @@ __global__ void __launch_bounds__(kThreads, 1) kp3_kernel(const __grid_constant_
                                    Elem<T>::pack(ov[e + 6] * inv, ov[e + 7] * inv));
         }
       }
-    }
-    // this group's MMAs (also those of an aborted walk) complete before the
-    // CTA can free TMEM
-    if (r == 0 && nXt > 0) {
-      umma::commit(&bs->mma_done[x]);
-      mbar_wait(&bs->mma_done[x], 0, p.err);
     }
   }
 

@@ -14,13 +14,13 @@ n has completed; it is an error (in hardware: a stall or an early return) if
 the barrier is then at neither n nor n + 1 completed phases -- in particular
 a probe of phase n while phase n - 1 is still open reads as complete.
 
-``simulate_kernel`` is the kernel: a landing observer waits on the K and V
-full barriers in walk order and publishes the counts; per query tile one
-softmax group whose thread 0 issues that tile's MMAs in a sequential chain
-(QK(j) -> softmax -> PV(j) -> PV(j) complete -> QK(j+1)), taking a full
-barrier only for a published tile, so no parity probe runs ahead of or
-behind its ring stage; tile B's first QK after tile A's first P V when both
-start on the walk's first K/V tile.
+``simulate_kernel`` is the kernel: ONE issuing thread for both query tiles
+that polls and issues whichever of the four next steps (QK / P V of A / B)
+has its inputs ready, one 128-key score buffer per tile (QK_X(j+1) after
+PV_X(j) completed), tile B's first QK after tile A's first P V when both
+start on the walk's first K/V tile.  K and V landings are observed in walk
+order (a landed prefix per ring), so a tile that sits K/V tiles out never
+probes a ring stage whose previous use has not been seen to land.
 
 ``simulate`` models the alternative of one issuing thread per query tile
 with score buffers ``NB`` deep and ``SPT`` score tiles per K/V tile:
@@ -264,19 +264,13 @@ def max_sit_out_run(segs):
 def simulate_kernel(segs, ST, seed=0, has_b=True, max_steps=200000):
     """One random schedule of ``kp3_kernel``'s protocol; raise Stall on a
     deadlock or an aliased wait.  ``segs``: [(tiles B sees, tiles A sees)];
-    with ``has_b=False`` only tile A exists (its tiles form the walk).
-
-    Roles: the producer; the landing observer (waits on the K and V full
-    barriers in walk order and publishes the counts); per query tile one
-    softmax group whose thread 0 issues that tile's MMAs: QK(first), then
-    per tile softmax -> PV(j) -> [PV(j) complete] -> QK(j+1), taking a full
-    barrier only for a tile the observer has published."""
+    with ``has_b=False`` only tile A exists (its tiles form the walk)."""
     rng = random.Random(seed)
     if not has_b:
         segs = [(n_a, n_a) for _n_u, n_a in segs]
     takes_a = tiles_of(segs)
     n = len(takes_a)
-    tiles = [[g for g in range(n) if takes_a[g]], list(range(n)) if has_b else []]
+    n_x = [sum(takes_a), n if has_b else 0]
     bars = []
 
     def bar(name, count):
@@ -288,20 +282,19 @@ def simulate_kernel(segs, ST, seed=0, has_b=True, max_steps=200000):
     k_empty = [bar(f"k_empty{i}", 2) for i in range(ST)]
     v_empty = [bar(f"v_empty{i}", 2) for i in range(ST)]
     s_full = [bar(f"s_full{x}", 1) for x in range(2)]
+    p_full = [bar(f"p_full{x}", 1) for x in range(2)]
     pv_done = [bar(f"pv_done{x}", 1) for x in range(2)]
-    gate = bar("gate", 1)
-    pub = {"k": 0, "v": 0}
     now, seq, events = [0], [0], []
-    last_commit = [0, 0]
+    last_commit = [0]
 
     def later(delay, fn):
         seq[0] += 1
         events.append((now[0] + delay, seq[0], fn))
 
-    def commit(x, b):
-        # one issuing thread per tile: its commits complete in issue order
-        t = max(now[0] + rng.randint(1, 6), last_commit[x])
-        last_commit[x] = t
+    def commit(b):
+        # one issuing thread: its commits complete in issue order
+        t = max(now[0] + rng.randint(1, 6), last_commit[0])
+        last_commit[0] = t
         seq[0] += 1
         events.append((t, seq[0], b.arrive))
 
@@ -326,55 +319,68 @@ def simulate_kernel(segs, ST, seed=0, has_b=True, max_steps=200000):
             if absent:
                 v_empty[st].arrive(absent)
 
-    def observer():
-        kpre = vpre = 0
-        while kpre < n or vpre < n:
-            if kpre < n and (kpre <= vpre or vpre >= n):
-                yield from _wait(k_full[kpre % ST], kpre // ST)
-                kpre += 1
-                pub["k"] = kpre
-            else:
-                yield from _wait(v_full[vpre % ST], vpre // ST)
-                vpre += 1
-                pub["v"] = vpre
-
-    def landed(key, full, g):
-        while pub[key] <= g:
-            yield
-        yield from _wait(full[g % ST], g // ST)
-
-    gate_b = bool(tiles[0]) and tiles[0][0] == 0
-
-    def tile(x):
-        mine = tiles[x]
-        if not mine:
+    def issuer():
+        if n == 0:
             return
-        yield from _wait(q_full, 0)
-        if x == 1 and gate_b:
-            yield from _wait(gate, 0)
-        yield from landed("k", k_full, mine[0])
-        commit(x, s_full[x])
-        commit(x, k_empty[mine[0] % ST])
-        for j, g in enumerate(mine):
-            yield from _wait(s_full[x], j)          # softmax of tile j
-            if rng.random() < 0.5:
-                yield
-            yield from landed("v", v_full, g)
-            commit(x, pv_done[x])
-            commit(x, v_empty[g % ST])
-            if j == 0 and x == 0:
-                gate.arrive()
-            if j + 1 < len(mine):
-                yield from _wait(pv_done[x], j)
-                gn = mine[j + 1]
-                yield from landed("k", k_full, gn)
-                commit(x, s_full[x])
-                commit(x, k_empty[gn % ST])
-        yield from _wait(pv_done[x], len(mine) - 1)
+        takes = [lambda g: takes_a[g], lambda g: has_b]
+        qc, pc = [0, 0], [0, 0]
+        jq, jp = [0, 0], [0, 0]
 
-    live = {"producer": producer(), "observer": observer(), "tileA": tile(0), "tileB": tile(1)}
+        def seek(c, x):
+            while c < n and not takes[x](c):
+                c += 1
+            return c
+        for x in range(2):
+            qc[x] = seek(0, x)
+            pc[x] = seek(0, x)
+        gate_b = n_x[0] > 0 and qc[0] == 0
+        # landed prefixes: K/V tiles below kpre / vpre are known to have
+        # landed; the next one is probed in walk order, so every probe of a
+        # stage follows the observed landing of its previous use
+        kpre = vpre = 0
+        yield from _wait(q_full, 0)
+        while True:
+            did = False
+            while kpre < n and _done(k_full[kpre % ST], kpre // ST):
+                kpre += 1
+            while vpre < n and _done(v_full[vpre % ST], vpre // ST):
+                vpre += 1
+            for x in range(2):
+                if jp[x] < jq[x]:
+                    g = pc[x]
+                    if g < vpre and _done(p_full[x], jp[x]):
+                        commit(pv_done[x])
+                        commit(v_empty[g % ST])
+                        jp[x] += 1
+                        pc[x] = seek(g + 1, x)
+                        did = True
+                if jq[x] < n_x[x] and jq[x] == jp[x] and \
+                        (x == 0 or jq[1] > 0 or not gate_b or jp[0] > 0):
+                    g = qc[x]
+                    if g < kpre and (jq[x] == 0 or _done(pv_done[x], jq[x] - 1)):
+                        commit(s_full[x])
+                        commit(k_empty[g % ST])
+                        jq[x] += 1
+                        qc[x] = seek(g + 1, x)
+                        did = True
+            if jp[0] >= n_x[0] and jp[1] >= n_x[1]:
+                return
+            if not did:
+                yield
+
+    def softmax(x):
+        for j in range(n_x[x]):
+            yield from _wait(s_full[x], j)
+            p_full[x].arrive()
+        if n_x[x] > 0:
+            yield from _wait(pv_done[x], n_x[x] - 1)
+
+    live = {"producer": producer(), "issuer": issuer(), "softmaxA": softmax(0),
+            "softmaxB": softmax(1)}
     for _step in range(max_steps):
         if not live and not events:
+            # every barrier of the ring ends balanced: each stage's empty
+            # phases match the loads that used it
             return
         for name in rng.sample(list(live), len(live)):
             try:
