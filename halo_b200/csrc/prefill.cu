@@ -437,16 +437,21 @@ __global__ void __launch_bounds__(kThreads, 1) kp3_kernel(const __grid_constant_
       bool ok = wait_bar(&bs->q_full, 0, bs, p.err);
       uint64_t t_idle = 0;
       int idle = 0;
+      // advance a landed prefix up to tile g, probing only as far as needed
+      // (each probe is a shared-memory access that queues behind the MMAs'
+      // operand reads)
+      auto landed = [&](int& pre, uint64_t* full, int g) {
+        while (pre <= g && mbar_test(&full[pre % ST], (pre / ST) & 1)) ++pre;
+        return g < pre;
+      };
       while (ok) {
         bool did = false;
-        while (kpre < nU && mbar_test(&bs->k_full[kpre % ST], (kpre / ST) & 1)) ++kpre;
-        while (vpre < nU && mbar_test(&bs->v_full[vpre % ST], (vpre / ST) & 1)) ++vpre;
 #pragma unroll
         for (int x = 0; x < 2; ++x) {
           // O_X += P_X(j) V(j): P written and V landed
           if (jp[x] < jq[x]) {
             const int g = pc[x].g, st = g % ST;
-            if (g < vpre && mbar_test(&bs->p_full[x], jp[x] & 1)) {
+            if (mbar_test(&bs->p_full[x], jp[x] & 1) && landed(vpre, bs->v_full, g)) {
               umma::fence_after_sync();
               const uint32_t pcol = tmem + x * 128;
               const uint32_t ocol = tmem + Gm::kColO + x * D;
@@ -475,7 +480,8 @@ __global__ void __launch_bounds__(kThreads, 1) kp3_kernel(const __grid_constant_
           if (jq[x] < nX[x] && jq[x] == jp[x] &&
               (x == 0 || jq[1] > 0 || !gateB || jp[0] > 0)) {
             const int g = qc[x].g, st = g % ST;
-            if (g < kpre && (jq[x] == 0 || mbar_test(&bs->pv_done[x], (jq[x] - 1) & 1))) {
+            if ((jq[x] == 0 || mbar_test(&bs->pv_done[x], (jq[x] - 1) & 1)) &&
+                landed(kpre, bs->k_full, g)) {
               umma::fence_after_sync();
               const uint64_t qd = opaque(umma::smem_desc_sw128(sQ + x * Gm::kTileBytes, 16, 1024));
               const uint64_t kd = opaque(kdesc0 + (uint64_t)((st * Gm::kTileBytes) >> 4));
