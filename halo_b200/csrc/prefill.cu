@@ -227,8 +227,8 @@ __device__ __forceinline__ void write_p(const float (&sv)[kBN], uint64_t sl2, ui
 // Ring barriers: k_full/v_full (one arrival + the copy's bytes), k_empty /
 // v_empty (two arrivals: a tcgen05.commit per query tile that reads the
 // tile, the producer arriving for a tile that sits it out).  Per tile X:
-// s_full (commit after QK), p_full (128 softmax arrivals), pv_done (commit
-// after PV).  All waits bounded; TMEM freed on every exit path.
+// s_full (commit after QK), p_full (one arrival per softmax warp), pv_done
+// (commit after PV).  All waits bounded; TMEM freed on every exit path.
 constexpr int kThreads = 384;
 
 template <int D>
@@ -275,6 +275,7 @@ __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, Bars* b
 // that segment, global tile index g counting every tile of the walk).
 struct Cursor {
   int s, t, g;
+  int end;     // tiles of segment s this query tile takes part in (cached)
 };
 
 template <typename T, int D>
@@ -315,7 +316,7 @@ __global__ void __launch_bounds__(kThreads, 1) kp3_kernel(const __grid_constant_
     }
     for (int x = 0; x < 2; ++x) {
       mbar_init(&bs->s_full[x], 1);
-      mbar_init(&bs->p_full[x], kBM);
+      mbar_init(&bs->p_full[x], kBM / 32);
       mbar_init(&bs->pv_done[x], 1);
     }
     mbar_init(&bs->mma_done, 1);
@@ -405,21 +406,31 @@ __global__ void __launch_bounds__(kThreads, 1) kp3_kernel(const __grid_constant_
       const int nX[2] = {nA, hasB ? nU : 0};
       // cursors: next K/V tile each query tile takes part in, for QK and PV
       const int n_seg = p.n_seg;
+      // (re)enter a segment: skip the tiles and segments tile x sits out
       auto seek = [&](Cursor& c, int x) {
         while (c.s < n_seg) {
           const int ntU = bs->ntU[c.s];
           const int ntX = x ? ntU : bs->ntA[c.s];
-          if (c.t < ntX) return;
+          if (c.t < ntX) {
+            c.end = ntX;
+            return;
+          }
           c.g += ntU - c.t;   // the rest of this segment is sat out
           ++c.s;
           c.t = 0;
         }
       };
-      Cursor qc[2] = {{0, 0, 0}, {0, 0, 0}}, pc[2] = {{0, 0, 0}, {0, 0, 0}};
-      for (int x = 0; x < 2; ++x) {
-        seek(qc[x], x);
-        seek(pc[x], x);
-      }
+      // next tile: stays in the segment without touching shared memory
+      auto step = [&](Cursor& c, int x) {
+        ++c.t;
+        ++c.g;
+        if (c.t >= c.end) seek(c, x);
+      };
+      // qc: next K/V tile each query tile's QK takes; pg: the tile of its
+      // pending P V (one at most: QK(j+1) waits for PV(j))
+      Cursor qc[2] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
+      int pg[2] = {0, 0};
+      for (int x = 0; x < 2; ++x) seek(qc[x], x);
       int jq[2] = {0, 0}, jp[2] = {0, 0};
       // Tile B's first QK waits for tile A's first P V when both start on
       // the walk's first K/V tile, so the two softmax groups run half a
@@ -450,7 +461,7 @@ __global__ void __launch_bounds__(kThreads, 1) kp3_kernel(const __grid_constant_
         for (int x = 0; x < 2; ++x) {
           // O_X += P_X(j) V(j): P written and V landed
           if (jp[x] < jq[x]) {
-            const int g = pc[x].g, st = g % ST;
+            const int g = pg[x], st = g % ST;
             if (mbar_test(&bs->p_full[x], jp[x] & 1) && landed(vpre, bs->v_full, g)) {
               umma::fence_after_sync();
               const uint32_t pcol = tmem + x * 128;
@@ -470,9 +481,6 @@ __global__ void __launch_bounds__(kThreads, 1) kp3_kernel(const __grid_constant_
               umma::commit(&bs->pv_done[x]);
               umma::commit(&bs->v_empty[st]);
               ++jp[x];
-              ++pc[x].t;
-              ++pc[x].g;
-              seek(pc[x], x);
               did = true;
             }
           }
@@ -493,10 +501,9 @@ __global__ void __launch_bounds__(kThreads, 1) kp3_kernel(const __grid_constant_
               umma::commit(&bs->s_full[x]);
               umma::commit(&bs->k_empty[st]);
               qseq[x] = ++seq;
+              pg[x] = g;
               ++jq[x];
-              ++qc[x].t;
-              ++qc[x].g;
-              seek(qc[x], x);
+              step(qc[x], x);
               did = true;
             }
           }
@@ -637,7 +644,8 @@ __global__ void __launch_bounds__(kThreads, 1) kp3_kernel(const __grid_constant_
         l += (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
         umma::tmem_wait_st();
         umma::fence_before_sync();
-        mbar_arrive(&bs->p_full[x]);
+        __syncwarp();                    // the warp's P is in TMEM: one arrival
+        if (lane == 0) mbar_arrive(&bs->p_full[x]);
       }
     }
     const int nX = j;
