@@ -444,6 +444,7 @@ __global__ void __launch_bounds__(kThreads, 1) kp3_kernel(const __grid_constant_
       // as complete (a query tile that sits tiles out would otherwise
       // probe ahead of the ring).
       int kpre = 0, vpre = 0;
+      int qseq[2] = {0, 0}, seq = 0;       // issue order of each tile's latest QK
       bool ok = wait_bar(&bs->q_full, 0, bs, p.err);
       uint64_t t_idle = 0;
       int idle = 0;
@@ -468,11 +469,14 @@ __global__ void __launch_bounds__(kThreads, 1) kp3_kernel(const __grid_constant_
               const uint64_t vd = opaque(vdesc0 + (uint64_t)((st * Gm::kTileBytes) >> 4));
               const bool acc0 = jp[x] > 0;
 #pragma unroll
-              for (int kk = 0; kk < kBN / 16; ++kk) {
-                const uint64_t vk = vd + (uint64_t)((kk * 16 * 128) >> 4);
-                umma::mma_ts(ocol, pcol + kk * 8, vk, kIdPV, acc0 || kk > 0);
-                // bf16 route: the residual part of P, same V rows
-                if (!p16) umma::mma_ts(ocol, pcol + 64 + kk * 8, vk, kIdPV, true);
+              for (int kk = 0; kk < kBN / 16; ++kk)
+                umma::mma_ts(ocol, pcol + kk * 8, vd + (uint64_t)((kk * 16 * 128) >> 4), kIdPV,
+                             acc0 || kk > 0);
+              if (!p16) {
+#pragma unroll
+                for (int kk = 0; kk < kBN / 16; ++kk)
+                  umma::mma_ts(ocol, pcol + 64 + kk * 8, vd + (uint64_t)((kk * 16 * 128) >> 4),
+                               kIdPV, true);
               }
               umma::commit(&bs->pv_done[x]);
               umma::commit(&bs->v_empty[st]);
@@ -496,6 +500,7 @@ __global__ void __launch_bounds__(kThreads, 1) kp3_kernel(const __grid_constant_
               }
               umma::commit(&bs->s_full[x]);
               umma::commit(&bs->k_empty[st]);
+              qseq[x] = ++seq;
               pg[x] = g;
               ++jq[x];
               step(qc[x], x);
@@ -528,7 +533,7 @@ __global__ void __launch_bounds__(kThreads, 1) kp3_kernel(const __grid_constant_
           if (!slept) {
             int xo = -1;
             if (jp[0] < jq[0]) xo = 0;
-            if (jp[1] < jq[1] && (xo < 0 || jq[1] < jq[0])) xo = 1;   // older QK first
+            if (jp[1] < jq[1] && (xo < 0 || qseq[1] < qseq[0])) xo = 1;
             if (xo >= 0 && !mbar_test(&bs->p_full[xo], jp[xo] & 1)) {
               mbar_sleep_wait(&bs->p_full[xo], jp[xo] & 1, 1000);
               slept = true;
