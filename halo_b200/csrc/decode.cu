@@ -70,6 +70,7 @@ constexpr int kBlockN = 64;          // K/V rows per pipeline stage (one TMA box
 constexpr int kConsumerWarps = 4;    // each owns 16 rows of every stage
 constexpr int kThreads = (kConsumerWarps + 1) * 32;
 constexpr int kMaxSegs = 48;         // tensor-map pairs per launch
+constexpr float kLazyMax = 8.f;      // KIVI decode: log2 headroom before the running max moves
 constexpr int kMaxItems = 512;       // work items per launch
 // kCtrlBytes (halo_common.cuh): the control block at the start of every
 // decode workspace.
@@ -568,32 +569,35 @@ __device__ __forceinline__ void mma_tile_t(float scale_log2, const KFrag& kfrag,
     mma_16816(s, a, qb[kk][0], qb[kk][1], (T*)nullptr);
   }
 
-  // ---- scale + mask: s[0], s[1] are key g, s[2], s[3] key g + 8
+  // ---- mask, only on a tile that ends early or crosses the causal limit
+  // (warp-uniform test): s[0], s[1] are key g, s[2], s[3] key g + 8
+  if (valid < kBlockN || (causal && pos0 + (kBlockN - 1) > qpos)) {
 #pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    const int r = wrow + g + ((e >> 1) << 3);
-    const bool ok = r < valid && (!causal || pos0 + r <= qpos);
-    s[e] = ok ? s[e] * scale_log2 : -INFINITY;
+    for (int e = 0; e < 4; ++e) {
+      const int r = wrow + g + ((e >> 1) << 3);
+      if (!(r < valid && (!causal || pos0 + r <= qpos))) s[e] = -INFINITY;
+    }
   }
 
-  // ---- online softmax per head (columns 2c, 2c+1): max over the 16 keys
-  float t0 = fmaxf(s[0], s[2]), t1 = fmaxf(s[1], s[3]);
+  // ---- online softmax per head (columns 2c, 2c+1) in log2 units.  The
+  // running max moves only when a key exceeds it by more than kLazyMax:
+  // P = exp2(s - m) then stays <= 2^kLazyMax (exact to 16-bit rounding, far
+  // from fp16 overflow) and most tiles skip the cross-lane max and the
+  // rescale of O.
+  float t0 = fmaxf(s[0], s[2]) * scale_log2, t1 = fmaxf(s[1], s[3]) * scale_log2;
+  if (__any_sync(0xffffffffu, t0 > m0 + kLazyMax || t1 > m1 + kLazyMax)) {
 #pragma unroll
-  for (int off = 4; off < 32; off <<= 1) {
-    t0 = fmaxf(t0, __shfl_xor_sync(0xffffffffu, t0, off));
-    t1 = fmaxf(t1, __shfl_xor_sync(0xffffffffu, t1, off));
-  }
-  const float mn0 = fmaxf(m0, t0), mn1 = fmaxf(m1, t1);
-  const float mu0 = (mn0 == -INFINITY) ? 0.f : mn0;
-  const float mu1 = (mn1 == -INFINITY) ? 0.f : mn1;
-  const float a0 = exp2f(m0 - mu0), a1 = exp2f(m1 - mu1);
-  m0 = mn0;
-  m1 = mn1;
-  const float p0 = exp2f(s[0] - mu0), p1 = exp2f(s[1] - mu1);
-  const float p2 = exp2f(s[2] - mu0), p3 = exp2f(s[3] - mu1);
-  l0 = l0 * a0 + (p0 + p2);      // this thread's keys; reduced over lanes at the end
-  l1 = l1 * a1 + (p1 + p3);
-  if (__any_sync(0xffffffffu, a0 != 1.f || a1 != 1.f)) {
+    for (int off = 4; off < 32; off <<= 1) {
+      t0 = fmaxf(t0, __shfl_xor_sync(0xffffffffu, t0, off));
+      t1 = fmaxf(t1, __shfl_xor_sync(0xffffffffu, t1, off));
+    }
+    const float mn0 = fmaxf(m0, t0), mn1 = fmaxf(m1, t1);
+    const float a0 = (m0 == -INFINITY) ? 0.f : ex2(m0 - mn0);
+    const float a1 = (m1 == -INFINITY) ? 0.f : ex2(m1 - mn1);
+    m0 = mn0;
+    m1 = mn1;
+    l0 *= a0;
+    l1 *= a1;
 #pragma unroll
     for (int i = 0; i < D / 16; ++i) {
       o[i][0] *= a0;
@@ -602,6 +606,13 @@ __device__ __forceinline__ void mma_tile_t(float scale_log2, const KFrag& kfrag,
       o[i][3] *= a1;
     }
   }
+  // -m (0 while a head has seen no key, so masked scores give exp2(-inf) = 0)
+  const float nm0 = (m0 == -INFINITY) ? 0.f : -m0;
+  const float nm1 = (m1 == -INFINITY) ? 0.f : -m1;
+  const float p0 = ex2(fmaf(s[0], scale_log2, nm0)), p1 = ex2(fmaf(s[1], scale_log2, nm1));
+  const float p2 = ex2(fmaf(s[2], scale_log2, nm0)), p3 = ex2(fmaf(s[3], scale_log2, nm1));
+  l0 += p0 + p2;      // this thread's keys; reduced over lanes at the end
+  l1 += p1 + p3;
 
   // ---- P^T transposed into the B operand (keys x heads).  fp16 keeps 11
   // significant bits of P (relative error <= 2^-11) in one MMA; bf16 keeps

@@ -31,6 +31,14 @@ __device__ __forceinline__ void set_device_error(unsigned int* err, unsigned int
   if (err) atomicCAS(err, 0u, code);
 }
 
+// exp2 on the special-function unit (relative error ~2^-22; subnormal
+// results flush to zero).
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));

@@ -75,13 +75,6 @@ struct alignas(64) Params {
   unsigned int* err;
 };
 
-// exp2 on the special-function unit (relative error ~2^-22).
-__device__ __forceinline__ float ex2(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-
 // Non-blocking probe of an mbarrier phase (true: the phase with this parity
 // has completed).
 __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
