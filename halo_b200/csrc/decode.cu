@@ -453,39 +453,42 @@ template <>
 struct Code2<__half> {
   static constexpr int kPairsPerShift = 5;         // bits 0..9 of the mantissa
   static constexpr int kShiftBits = 10;
-  __device__ static __forceinline__ uint32_t magic(int q) {
-    const uint32_t m = (uint32_t)(25 - 2 * q) << 10;  // 2^(10 - 2q)
-    return m | (m << 16);
-  }
-  __device__ static __forceinline__ uint32_t decode(uint32_t bits, int q, uint32_t s2,
-                                                    uint32_t z2) {
-    const __half2 e = __halves2half2(__ushort_as_half((unsigned short)(magic(q) & 0xFFFF)),
-                                     __ushort_as_half((unsigned short)(magic(q) & 0xFFFF)));
-    const __half2 v = __hsub2(*reinterpret_cast<const __half2*>(&bits), e);
-    const __half2 r = __hfma2(v, *reinterpret_cast<const __half2*>(&s2),
-                              *reinterpret_cast<const __half2*>(&z2));
-    return *reinterpret_cast<const uint32_t*>(&r);
+  // 2^(10 - 2q) in both halves: exponent 25 - 2q
+  __host__ __device__ static constexpr uint32_t magic(int q) {
+    return ((uint32_t)(25 - 2 * q) << 10) | ((uint32_t)(25 - 2 * q) << 26);
   }
 };
 template <>
 struct Code2<__nv_bfloat16> {
   static constexpr int kPairsPerShift = 3;         // bits 0..5 of the mantissa
   static constexpr int kShiftBits = 6;
-  __device__ static __forceinline__ uint32_t magic(int q) {
-    const uint32_t m = (uint32_t)(134 - 2 * q) << 7;  // 2^(7 - 2q)
-    return m | (m << 16);
-  }
-  __device__ static __forceinline__ uint32_t decode(uint32_t bits, int q, uint32_t s2,
-                                                    uint32_t z2) {
-    const uint32_t mm = magic(q) & 0xFFFF;
-    const __nv_bfloat162 e = __halves2bfloat162(__ushort_as_bfloat16((unsigned short)mm),
-                                                __ushort_as_bfloat16((unsigned short)mm));
-    const __nv_bfloat162 v = __hsub2(*reinterpret_cast<const __nv_bfloat162*>(&bits), e);
-    const __nv_bfloat162 r = __hfma2(v, *reinterpret_cast<const __nv_bfloat162*>(&s2),
-                                     *reinterpret_cast<const __nv_bfloat162*>(&z2));
-    return *reinterpret_cast<const uint32_t*>(&r);
+  // 2^(7 - 2q) in both halves: exponent 134 - 2q
+  __host__ __device__ static constexpr uint32_t magic(int q) {
+    return ((uint32_t)(134 - 2 * q) << 7) | ((uint32_t)(134 - 2 * q) << 23);
   }
 };
+
+// (w & mask) | magic, minus magic as two 16-bit floats, times s plus z: one
+// LOP3 and two packed 16-bit instructions, with the magic constant as the
+// operand of both the LOP3 and the subtract.
+template <typename T>
+__device__ __forceinline__ uint32_t code2_decode(uint32_t w, uint32_t mask, uint32_t magic,
+                                                 uint32_t s2, uint32_t z2) {
+  uint32_t r;
+  if constexpr (std::is_same<T, __half>::value)
+    asm("{\n\t.reg .b32 t;\n\t"
+        "lop3.b32 t, %1, %2, %3, 0xEA;\n\t"
+        "sub.f16x2 t, t, %3;\n\t"
+        "fma.rn.f16x2 %0, t, %4, %5;\n\t}"
+        : "=r"(r) : "r"(w), "r"(mask), "r"(magic), "r"(s2), "r"(z2));
+  else
+    asm("{\n\t.reg .b32 t;\n\t"
+        "lop3.b32 t, %1, %2, %3, 0xEA;\n\t"
+        "sub.bf16x2 t, t, %3;\n\t"
+        "fma.rn.bf16x2 %0, t, %4, %5;\n\t}"
+        : "=r"(r) : "r"(w), "r"(mask), "r"(magic), "r"(s2), "r"(z2));
+  return r;
+}
 
 // Values of pair p (0..7) of a 16-code word: codes 2p and 2p+1 as one
 // register of two 16-bit values c*s + z.
@@ -494,8 +497,7 @@ __device__ __forceinline__ uint32_t code2_pair(uint32_t word, int p, uint32_t s2
   using C = Code2<T>;
   const int seg = p / C::kPairsPerShift, q = p % C::kPairsPerShift;
   const uint32_t w = seg ? (word >> (seg * C::kShiftBits)) : word;
-  const uint32_t bits = (w & (0x00030003u << (2 * q))) | C::magic(q);
-  return C::decode(bits, q, s2, z2);
+  return code2_decode<T>(w, 0x00030003u << (2 * q), C::magic(q), s2, z2);
 }
 
 // This thread's packed K codes (rows g, g + 8; D/4 codes each, the span of
