@@ -1249,7 +1249,12 @@ struct KGeom {
 // Warp w dequantises rows [16w, 16w+16) of one packed K or V tile into the
 // swizzled 64-row 16-bit tile `dq`.  Lane: row 16w + lane/2, half of the
 // row's columns by lane parity; one group (32 columns) at a time.  All
-// accesses are explicit shared-memory loads and stores.
+// accesses are explicit shared-memory loads and stores, free of bank
+// conflicts: with two groups per half-row the odd half stores its groups in
+// reverse order, so the 8 lanes of each 128-byte store phase (4 rows x 2
+// halves) hit 8 different 16-byte bank groups of the swizzled tile, and
+// 2-bit codes are read as one 16-byte load per lane (a quarter-warp reads
+// 128 contiguous bytes).
 template <typename T, int D, int BITS>
 __device__ __forceinline__ void dequant_rows(const char* pack, char* dq) {
   using KG = KGeom<T, D, BITS>;
@@ -1259,32 +1264,49 @@ __device__ __forceinline__ void dequant_rows(const char* pack, char* dq) {
   const int half = lane & 1;
   constexpr int kCols = D / 2;
   constexpr int kGroups = kCols / 32;
+  static_assert(kGroups == 1 || kGroups == 2, "64 or 128 columns");
   const uint32_t s_codes = smem_addr(pack) + row * KG::kCB;
   const uint32_t s_sc = smem_addr(pack + KG::kCodeTile) + row * KG::kGS * 2;
   const uint32_t s_ze = smem_addr(pack + KG::kCodeTile + KG::kSZTile) + row * KG::kGS * 2;
   const uint32_t s_dq = smem_addr(dq);
+  // 2-bit: this half-row's code words (two per group), in store order
+  uint32_t words[2 * kGroups];
+  if constexpr (BITS == 2) {
+    const uint32_t a = s_codes + half * (kCols / 4);
+    if constexpr (kGroups == 2) {
+      asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                   : "=r"(words[0]), "=r"(words[1]), "=r"(words[2]), "=r"(words[3]) : "r"(a));
+      if (half) {
+        const uint32_t t0 = words[0], t1 = words[1];
+        words[0] = words[2];
+        words[1] = words[3];
+        words[2] = t0;
+        words[3] = t1;
+      }
+    } else {
+      asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(words[0]), "=r"(words[1]) : "r"(a));
+    }
+  }
 #pragma unroll
   for (int j = 0; j < kGroups; ++j) {
-    const int col0 = half * kCols + j * 32;
+    const int jj = kGroups == 2 ? (j ^ half) : j;
+    const int col0 = half * kCols + jj * 32;
     const int g = col0 / 32;
     uint16_t sb, zb;
     asm volatile("ld.shared.u16 %0, [%1];" : "=h"(sb) : "r"(s_sc + 2 * g));
     asm volatile("ld.shared.u16 %0, [%1];" : "=h"(zb) : "r"(s_ze + 2 * g));
-    const float s = Elem<T>::to_f32(*reinterpret_cast<const T*>(&sb));
-    const float z = Elem<T>::to_f32(*reinterpret_cast<const T*>(&zb));
     uint32_t out[16];
     if constexpr (BITS == 2) {
-      // two 16-code words: pair p of word w is columns 16w + 2p, 16w + 2p + 1
+      // pair p of word w is columns 16w + 2p, 16w + 2p + 1 of the group
       const uint32_t s2 = (uint32_t)sb | ((uint32_t)sb << 16);
       const uint32_t z2 = (uint32_t)zb | ((uint32_t)zb << 16);
-      uint32_t words[2];
-      asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];"
-                   : "=r"(words[0]), "=r"(words[1]) : "r"(s_codes + col0 / 4));
 #pragma unroll
       for (int w = 0; w < 2; ++w)
 #pragma unroll
-        for (int q = 0; q < 8; ++q) out[w * 8 + q] = code2_pair<T>(words[w], q, s2, z2);
+        for (int q = 0; q < 8; ++q) out[w * 8 + q] = code2_pair<T>(words[2 * j + w], q, s2, z2);
     } else {
+      const float s = Elem<T>::to_f32(*reinterpret_cast<const T*>(&sb));
+      const float z = Elem<T>::to_f32(*reinterpret_cast<const T*>(&zb));
       constexpr uint32_t kMask = (1u << BITS) - 1u;
       constexpr int kPer = 8 / BITS;
       uint32_t cw[32 * BITS / 32];
