@@ -23,7 +23,10 @@
 //    threads) race on the array; serialise them.
 //  * The first call on each device looks up the array's device address
 //    (cudaGetSymbolAddress, with that device current).  Make that first call
-//    before any stream capture.
+//    before any stream capture.  The address is cached for the life of the
+//    process: after cudaDeviceReset (or any teardown of the device's primary
+//    context) it is stale, so this entry point must not be used on that
+//    device again in the same process.
 //  * No cudaMalloc, cudaFree or other device allocation happens here.
 #include <mutex>
 

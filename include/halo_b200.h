@@ -159,7 +159,10 @@ int32_t halo_lse_merge(int32_t B, int32_t H, int32_t Dv, int32_t P,
  * device share it and it keeps the last call's contents; each call clears
  * its leading scheduler counters on `stream` before the kernels.  Calls that
  * overlap on the GPU race: serialise them.  The first call on each device
- * looks up the array's address (make it before any stream capture). */
+ * looks up the array's address (make it before any stream capture); the
+ * address is kept for the life of the process, so do not use this entry
+ * point on a device after cudaDeviceReset (or any other teardown of its
+ * primary context) in the same process. */
 int32_t halo_chunked_decode_noalloc(const halo_decode_problem_t* problem,
                                     const halo_kv_chunk_t* chunks, int32_t n_chunks,
                                     const halo_merge_args_t* merge, halo_stream_t stream);
