@@ -333,7 +333,6 @@ def simulate_kernel(segs, ST, seed=0, has_b=True, max_steps=200000):
         for x in range(2):
             qc[x] = seek(0, x)
             pc[x] = seek(0, x)
-        gate_b = n_x[0] > 0 and qc[0] == 0
         # landed prefixes: K/V tiles below kpre / vpre are known to have
         # landed; the next one is probed in walk order, so every probe of a
         # stage follows the observed landing of its previous use
@@ -354,8 +353,7 @@ def simulate_kernel(segs, ST, seed=0, has_b=True, max_steps=200000):
                         jp[x] += 1
                         pc[x] = seek(g + 1, x)
                         did = True
-                if jq[x] < n_x[x] and jq[x] == jp[x] and \
-                        (x == 0 or jq[1] > 0 or not gate_b or jp[0] > 0):
+                if jq[x] < n_x[x] and jq[x] == jp[x]:
                     g = qc[x]
                     if g < kpre and (jq[x] == 0 or _done(pv_done[x], jq[x] - 1)):
                         commit(s_full[x])
