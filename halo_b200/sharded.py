@@ -221,3 +221,94 @@ class ShardedDecoder:
         if self.world == 1:
             return 2
         return 2 if self.exchange == "p2p" else 3
+
+
+class ShardedKiviDecoder:
+    """KIVI decode over a sequence-sharded quantised cache (the packed
+    2/4/8-bit format of ``baselines.kivi_cache``; the reference's KIVI cache,
+    ``baselines/kivi_cache.py:121-195``, is single-GPU).
+
+    Rank ``r`` quantises and holds its contiguous rows ``k_shard`` /
+    ``v_shard`` ``(B, H_kv, T_local, D)`` (``T_local`` a multiple of
+    ``group_size``; quantisation is per row, so the codes equal those a
+    single cache would hold for the same rows); the rank holding the end of
+    the context may also pass the most recent rows in 16 bits
+    (``recent_k`` / ``recent_v``).  A call attends this rank's rows with the
+    fused packed kernel (and the recent rows with the split-KV kernel, folded
+    in by LSE), then all-gathers every rank's normalised fp32 ``(o, lse)``
+    and merges them, as :class:`ShardedDecoder` does with
+    ``exchange="nccl"``.  The keys are not causal-masked against each other:
+    every cached row precedes the decode query.
+    """
+
+    def __init__(self, k_shard: torch.Tensor, v_shard: torch.Tensor, *, bits: int = 2,
+                 group_size: int = 32, recent_k: Optional[torch.Tensor] = None,
+                 recent_v: Optional[torch.Tensor] = None, group=None):
+        import torch.distributed as dist
+        from halo_b200.baselines.kivi_cache import _Packed
+        if k_shard.shape[-2] % group_size:
+            raise ValueError("rows per shard must be a multiple of group_size")
+        self.group = group
+        self.world = dist.get_world_size(group) if (group is not None or (
+            dist.is_available() and dist.is_initialized())) else 1
+        self.bits = bits
+        B, H_kv, T, D = k_shard.shape
+        self.kq = _Packed(B, H_kv, D, k_shard.dtype, k_shard.device, bits, group_size)
+        self.vq = _Packed(B, H_kv, v_shard.shape[-1], v_shard.dtype, v_shard.device, bits,
+                          group_size)
+        if T:
+            self.kq.append(k_shard)
+            self.vq.append(v_shard)
+        self.recent = []
+        if recent_k is not None and recent_k.shape[-2]:
+            self.recent = [(recent_k, recent_v, 0, False)]
+        self._bufs: dict = {}
+
+    def _buffers(self, B: int, H: int, D_v: int, dev: torch.device):
+        key = (B, H, D_v)
+        if key not in self._bufs:
+            R = B * H
+            local = torch.empty(R * D_v + R, dtype=torch.float32, device=dev)
+            gathered = torch.empty(self.world * (R * D_v + R), dtype=torch.float32, device=dev)
+            ones = torch.ones(B, H, dtype=torch.float32, device=dev)
+            self._bufs[key] = (local, gathered, ones)
+        return self._bufs[key]
+
+    def __call__(self, q: torch.Tensor, *, scale: Optional[float] = None,
+                 out: Optional[torch.Tensor] = None):
+        """``q (B, H, D)`` or ``(B, H, 1, D)``; returns ``(out (B, H, D_v) in
+        q.dtype, lse (B, H) fp32)`` over the rows of every rank."""
+        from halo_b200.baselines.kivi_cache import kivi_decode
+        q3 = q.squeeze(2) if q.dim() == 4 else q
+        q3 = q3 if q3.is_contiguous() else q3.contiguous()
+        B, H, D = q3.shape
+        D_v = self.vq.D
+        if scale is None:
+            scale = 1.0 / math.sqrt(D)
+        R = B * H
+        local, gathered, ones = self._buffers(B, H, D_v, q3.device)
+        o_loc, l_loc = local[:R * D_v].view(B, H, D_v), local[R * D_v:].view(B, H)
+        if self.kq.T:
+            if self.recent:
+                o_p = torch.empty(B, H, D_v, dtype=torch.float32, device=q3.device)
+                l_p = torch.empty(B, H, dtype=torch.float32, device=q3.device)
+                kivi_decode(q3, self.kq, self.vq, self.kq.T, self.bits, scale=scale, out=o_p,
+                            lse=l_p)
+                ops.chunked_decode(q3, self.recent, scale=scale, out=o_loc, lse=l_loc,
+                                   prior=(l_p, ones, o_p))
+            else:
+                kivi_decode(q3, self.kq, self.vq, self.kq.T, self.bits, scale=scale, out=o_loc,
+                            lse=l_loc)
+        elif self.recent:
+            ops.chunked_decode(q3, self.recent, scale=scale, out=o_loc, lse=l_loc)
+        else:
+            # no rows on this rank: a part that the merge gives zero weight
+            o_loc.zero_()
+            l_loc.fill_(float("-inf"))
+        if out is None:
+            out = torch.empty(B, H, D_v, dtype=q3.dtype, device=q3.device)
+        if self.world == 1:
+            out.copy_(o_loc)
+            return out, l_loc.clone()
+        m_parts, o_parts = gather_partials(o_loc, l_loc, self.group, buffers=(local, gathered))
+        return ops.lse_merge(m_parts, None, o_parts, out=out, parts_major=True)

@@ -111,3 +111,90 @@ def test_sharded_decode_two_gpus_matches_single_gpu_and_oracle():
             for key, (out, lse) in res.items():
                 if key[0] == large:
                     assert (out - o1.cpu()).abs().max().item() <= 1e-5, key
+
+
+def _kivi_inputs():
+    """A cfg4-shaped KIVI cache cut short: B2, 32 q-heads / 8 KV heads,
+    D 128, 8192 quantised rows + 128 fp16 recent rows, keys with outlier
+    channels."""
+    g = torch.Generator().manual_seed(555)
+    B, H, H_kv, D, T, R = 2, 32, 8, 128, 8192, 128
+    q = torch.randn(B, H, D, generator=g).half()
+    k = torch.randn(B, H_kv, T + R, D, generator=g)
+    for h in range(H_kv):
+        k[:, h, :, torch.randperm(D, generator=g)[:4]] *= 10
+    v = torch.randn(B, H_kv, T + R, D, generator=g).half()
+    return q, k.half(), v, T
+
+
+def _kivi_rank_main(rank: int, port: int, result_q):
+    import torch.distributed as dist
+    from datetime import timedelta
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=WORLD, timeout=timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        from halo_b200.sharded import ShardedKiviDecoder
+        dev = torch.device("cuda", rank)
+        q, k, v, T = _kivi_inputs()
+        lo, hi = rank * T // WORLD, (rank + 1) * T // WORLD
+        last = rank == WORLD - 1
+        dec = ShardedKiviDecoder(k[..., lo:hi, :].to(dev), v[..., lo:hi, :].to(dev), bits=2,
+                                 group_size=32,
+                                 recent_k=k[..., T:, :].to(dev) if last else None,
+                                 recent_v=v[..., T:, :].to(dev) if last else None)
+        outs = []
+        for _ in range(2):
+            out, lse = dec(q.to(dev))
+            torch.cuda.synchronize()
+            outs.append((out.float().cpu(), lse.cpu()))
+        from halo_b200 import _lib as L
+        result_q.put((rank, outs, L.device_error()))
+        dist.barrier(device_ids=[rank])
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < WORLD, reason="needs 2 GPUs")
+def test_sharded_kivi_decode_two_gpus_matches_single_gpu():
+    """Two ranks, each with half of the quantised rows (the second also the
+    16-bit recent rows), against one KIVICache over the whole context on one
+    GPU (same codes, since quantisation is per row) and a float64 attention
+    over the dequantised keys and values."""
+    import math
+    import torch.multiprocessing as mp
+    from halo_b200.baselines.kivi_cache import KIVICache, dequantize_packed
+    ctx = mp.get_context("spawn")
+    result_q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_kivi_rank_main, args=(r, port, result_q)) for r in range(WORLD)]
+    for p in procs:
+        p.start()
+    results = [result_q.get(timeout=300) for _ in range(WORLD)]
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    q, k, v, T = _kivi_inputs()
+    cache = KIVICache(bits=2, group_size=32, residual_length=128, fused_attention=True)
+    cache.update(k.cuda(), v.cuda(), layer_idx=0)
+    ref = cache.compute_attention(q.cuda().unsqueeze(2), layer_idx=0).squeeze(2).float().cpu()
+    kq, vq = cache._k_quant[0], cache._v_quant[0]
+    kd = dequantize_packed(kq.codes[:, :, :kq.T], kq.scale[:, :, :kq.T], kq.zero[:, :, :kq.T],
+                           bits=2, group_size=32)
+    vd = dequantize_packed(vq.codes[:, :, :vq.T], vq.scale[:, :, :vq.T], vq.zero[:, :, :vq.T],
+                           bits=2, group_size=32)
+    G = q.shape[1] // k.shape[1]
+    kf = torch.cat([kd, cache._k_recent[0]], 2).double().cpu().repeat_interleave(G, 1)
+    vf = torch.cat([vd, cache._v_recent[0]], 2).double().cpu().repeat_interleave(G, 1)
+    s = (q.double().unsqueeze(2) @ kf.transpose(-1, -2)).squeeze(2) / math.sqrt(q.shape[-1])
+    f64 = (torch.softmax(s, -1).unsqueeze(2) @ vf).squeeze(2)
+    lse64 = torch.logsumexp(s, -1)
+    for rank, outs, err in results:
+        assert err == 0
+        for out, lse in outs:
+            assert (out - ref).abs().max().item() <= 2e-3
+            assert (out.double() - f64).abs().max().item() <= 2e-3
+            assert (lse.double() - lse64).abs().max().item() <= 1e-4
