@@ -235,17 +235,24 @@ class ShardedKiviDecoder:
     the context may also pass the most recent rows in 16 bits
     (``recent_k`` / ``recent_v``).  A call attends this rank's rows with the
     fused packed kernel (and the recent rows with the split-KV kernel, folded
-    in by LSE), then all-gathers every rank's normalised fp32 ``(o, lse)``
-    and merges them, as :class:`ShardedDecoder` does with
-    ``exchange="nccl"``.  The keys are not causal-masked against each other:
-    every cached row precedes the decode query.
+    in by LSE), then merges every rank's normalised fp32 ``(o, lse)``:
+    ``exchange="p2p"`` in one kernel over NVLink peer memory
+    (``halo_sharded_merge`` with one normalised part per rank), ``"nccl"``
+    with an all-gather and the merge kernel, as :class:`ShardedDecoder`.
+    The keys are not causal-masked against each other: every cached row
+    precedes the decode query.
     """
 
     def __init__(self, k_shard: torch.Tensor, v_shard: torch.Tensor, *, bits: int = 2,
                  group_size: int = 32, recent_k: Optional[torch.Tensor] = None,
-                 recent_v: Optional[torch.Tensor] = None, group=None):
+                 recent_v: Optional[torch.Tensor] = None, group=None,
+                 exchange: str = "p2p"):
         import torch.distributed as dist
         from halo_b200.baselines.kivi_cache import _Packed
+        if exchange not in ("p2p", "nccl"):
+            raise ValueError(f"exchange must be 'p2p' or 'nccl', not {exchange!r}")
+        self.exchange = exchange
+        self._x = None
         if k_shard.shape[-2] % group_size:
             raise ValueError("rows per shard must be a multiple of group_size")
         self.group = group
@@ -310,5 +317,32 @@ class ShardedKiviDecoder:
         if self.world == 1:
             out.copy_(o_loc)
             return out, l_loc.clone()
+        if self.exchange == "p2p":
+            return self._p2p_merge(o_loc, l_loc, out)
         m_parts, o_parts = gather_partials(o_loc, l_loc, self.group, buffers=(local, gathered))
         return ops.lse_merge(m_parts, None, o_parts, out=out, parts_major=True)
+
+    def _p2p_merge(self, o_loc: torch.Tensor, l_loc: torch.Tensor, out: torch.Tensor):
+        from halo_b200 import _lib as L
+        B, H, D_v = o_loc.shape
+        if self._x is None or self._x_key != (B, H, D_v):
+            if self._x is not None:
+                self._x.close()
+            self._x = P2PExchange(B * H, D_v, self.group)
+            self._x_key = (B, H, D_v)
+        lse = torch.empty(B, H, dtype=torch.float32, device=o_loc.device)
+        # one normalised part per rank: m = its lse, l = 1 (NULL), o = its out
+        with torch.cuda.device(o_loc.device):
+            rc = L.lib().halo_sharded_merge(
+                B, H, D_v, 1, l_loc.data_ptr(), None, o_loc.data_ptr(), 1, 1, D_v, D_v,
+                self._x.world, self._x.rank, self._x.bufs, L.halo_dtype(out.dtype),
+                out.data_ptr(), out.stride(0), out.stride(1), lse.data_ptr(),
+                L.stream_handle(o_loc.device))
+        L.check(rc, "halo_sharded_merge")
+        return out, lse
+
+    def close(self) -> None:
+        """Release the peer mappings (call on every rank)."""
+        if self._x is not None:
+            self._x.close()
+            self._x = None

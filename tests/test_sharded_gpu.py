@@ -142,15 +142,18 @@ def _kivi_rank_main(rank: int, port: int, result_q):
         q, k, v, T = _kivi_inputs()
         lo, hi = rank * T // WORLD, (rank + 1) * T // WORLD
         last = rank == WORLD - 1
-        dec = ShardedKiviDecoder(k[..., lo:hi, :].to(dev), v[..., lo:hi, :].to(dev), bits=2,
-                                 group_size=32,
-                                 recent_k=k[..., T:, :].to(dev) if last else None,
-                                 recent_v=v[..., T:, :].to(dev) if last else None)
         outs = []
-        for _ in range(2):
-            out, lse = dec(q.to(dev))
-            torch.cuda.synchronize()
-            outs.append((out.float().cpu(), lse.cpu()))
+        for mode in ("p2p", "nccl"):
+            dec = ShardedKiviDecoder(k[..., lo:hi, :].to(dev), v[..., lo:hi, :].to(dev), bits=2,
+                                     group_size=32,
+                                     recent_k=k[..., T:, :].to(dev) if last else None,
+                                     recent_v=v[..., T:, :].to(dev) if last else None,
+                                     exchange=mode)
+            for _ in range(2):   # repeated calls cycle the exchange epochs
+                out, lse = dec(q.to(dev))
+                torch.cuda.synchronize()
+                outs.append((out.float().cpu(), lse.cpu()))
+            dec.close()
         from halo_b200 import _lib as L
         result_q.put((rank, outs, L.device_error()))
         dist.barrier(device_ids=[rank])
@@ -161,9 +164,10 @@ def _kivi_rank_main(rank: int, port: int, result_q):
 @pytest.mark.skipif(torch.cuda.device_count() < WORLD, reason="needs 2 GPUs")
 def test_sharded_kivi_decode_two_gpus_matches_single_gpu():
     """Two ranks, each with half of the quantised rows (the second also the
-    16-bit recent rows), against one KIVICache over the whole context on one
-    GPU (same codes, since quantisation is per row) and a float64 attention
-    over the dequantised keys and values."""
+    16-bit recent rows), with the NVLink and the NCCL exchange, against one
+    KIVICache over the whole context on one GPU (same codes, since
+    quantisation is per row) and a float64 attention over the dequantised
+    keys and values."""
     import math
     import torch.multiprocessing as mp
     from halo_b200.baselines.kivi_cache import KIVICache, dequantize_packed
