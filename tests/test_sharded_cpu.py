@@ -91,3 +91,16 @@ def test_two_gloo_ranks_gather_and_merge_equal_full_attention():
         # every rank holds the same merged result
         assert (o.double() - ro).abs().max().item() <= 1e-5
         assert (l.double() - rl).abs().max().item() <= 1e-5
+
+
+def test_sharded_kivi_decoder_rejects_bad_arguments():
+    """The sharded KIVI decoder checks its exchange and that each shard is a
+    whole number of quantisation groups before touching a device."""
+    import pytest
+    import torch
+    from halo_b200.sharded import ShardedKiviDecoder
+    k = torch.zeros(1, 2, 64, 128, dtype=torch.float16)
+    with pytest.raises(ValueError, match="exchange"):
+        ShardedKiviDecoder(k, k, exchange="mpi")
+    with pytest.raises(ValueError, match="group_size"):
+        ShardedKiviDecoder(k[..., :48, :], k[..., :48, :], group_size=32)
