@@ -44,6 +44,9 @@ constexpr int kBN = 128;            // keys per K/V tile and per score tile
 constexpr int kMaxSegs = 48;
 constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleLog2 = 8.f;
+// split-unit partial row: o[D], M, L, 2 floats of padding (16-byte rows)
+template <int D>
+constexpr int kPartStride = D + 4;
 constexpr int64_t kWsHeader = 256;  // workspace: flag word, then the fp16 V copies
 
 struct Seg {
@@ -72,6 +75,12 @@ struct alignas(64) Params {
   float* m;
   float* l;
   float* o;
+  // Split units (the last partial wave): CTAs blockIdx >= n_full take half
+  // of a unit's K/V walk each (2 CTAs per unit, first half then second) and
+  // write their rows' fp32 (M, L, o) to part instead of out; pf_merge_kernel
+  // folds the two halves.  n_full = all units and part = NULL: no split.
+  int32_t n_full;
+  float* part;
   unsigned int* err;
 };
 
@@ -104,7 +113,7 @@ __device__ __forceinline__ bool mbar_sleep_wait(uint64_t* bar, uint32_t parity, 
 }
 
 // K/V tiles of segment `sg` visible to query positions <= qmax.
-__device__ __forceinline__ int seg_tiles(const Seg& sg, int64_t qmax) {
+__host__ __device__ __forceinline__ int seg_tiles(const Seg& sg, int64_t qmax) {
   int n = (sg.len + kBN - 1) / kBN;
   if (sg.causal) {
     const int64_t lim = qmax - sg.start;   // last visible row
@@ -246,7 +255,9 @@ struct Bars {
   int abort_flag;
   int nU, nA;                        // K/V tiles of the walk, and tile A's share
   int16_t ntU[kMaxSegs], ntA[kMaxSegs];   // per segment: tiles B (the walk) / A see
+  int16_t t0[kMaxSegs];              // per segment: first tile of this CTA's window
 };
+static_assert(sizeof(Bars) <= 512, "barrier block");
 
 __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, Bars* bs,
                                          unsigned int* err) {
@@ -284,8 +295,16 @@ __global__ void __launch_bounds__(kThreads, 1) kp3_kernel(const __grid_constant_
 
   const int BH = p.B * p.H;
   const int n_pairs = (p.n_qtiles + 1) / 2;
-  const int pair = n_pairs - 1 - (int)(blockIdx.x / BH);   // heavy first
-  const int bh = (int)(blockIdx.x % BH);
+  // unit = (pair, bh), heaviest pairs first; units from n_full on are split
+  // into two CTAs (half 0: the first half of the walk, half 1: the rest)
+  int unit = (int)blockIdx.x, half = -1;
+  if (unit >= p.n_full) {
+    const int k = unit - p.n_full;
+    unit = p.n_full + (k >> 1);
+    half = k & 1;
+  }
+  const int pair = n_pairs - 1 - unit / BH;
+  const int bh = unit % BH;
   const int b = bh / p.H, h = bh % p.H, hk = h / p.G;
   const int qA0 = 2 * pair * kBM;
   const bool hasB = 2 * pair + 1 < p.n_qtiles;
@@ -314,13 +333,24 @@ __global__ void __launch_bounds__(kThreads, 1) kp3_kernel(const __grid_constant_
     }
     mbar_init(&bs->mma_done, 1);
     bs->abort_flag = 0;
-    int nu = 0, na = 0;
+    // this CTA's window [glo, ghi) of the union walk: all of it, or one
+    // half of a split unit's
+    int nfull = 0;
+    for (int s = 0; s < p.n_seg; ++s) nfull += seg_tiles(p.seg[s], qmaxU);
+    const int glo = half == 1 ? nfull / 2 : 0;
+    const int ghi = half == 0 ? nfull / 2 : nfull;
+    int nu = 0, na = 0, gb = 0;
     for (int s = 0; s < p.n_seg; ++s) {
       const int tu = seg_tiles(p.seg[s], qmaxU), ta = seg_tiles(p.seg[s], qmaxA);
-      bs->ntU[s] = (int16_t)tu;
-      bs->ntA[s] = (int16_t)ta;
-      nu += tu;
-      na += ta;
+      const int lo = min(max(glo - gb, 0), tu), hi = min(max(ghi - gb, 0), tu);
+      // tile A's tiles are a prefix of the segment's, so of the window too
+      const int wa = max(0, min(hi, ta) - lo);
+      bs->t0[s] = (int16_t)lo;
+      bs->ntU[s] = (int16_t)(hi - lo);
+      bs->ntA[s] = (int16_t)wa;
+      nu += hi - lo;
+      na += wa;
+      gb += tu;
     }
     bs->nU = nu;
     bs->nA = na;
@@ -370,14 +400,14 @@ __global__ void __launch_bounds__(kThreads, 1) kp3_kernel(const __grid_constant_
             mbar_arrive_expect_tx(&bs->k_full[st], Gm::kTileBytes);
             for (int blk = 0; blk < Gm::kBlocks; ++blk)
               tma_load_4d(smem + Gm::kOffK + st * Gm::kTileBytes + blk * Gm::kBlockBytes,
-                          &p.kmap[s], blk * 64, t * kBN, hk, bb, &bs->k_full[st]);
+                          &p.kmap[s], blk * 64, (bs->t0[s] + t) * kBN, hk, bb, &bs->k_full[st]);
             if (absent) mbar_arrive_n(&bs->k_empty[st], absent);
             ++nk;
             if (use > 0 && !(ok = wait_bar(&bs->v_empty[st], (use - 1) & 1, bs, p.err))) break;
             mbar_arrive_expect_tx(&bs->v_full[st], Gm::kTileBytes);
             for (int blk = 0; blk < Gm::kBlocks; ++blk)
               tma_load_4d(smem + Gm::kOffV + st * Gm::kTileBytes + blk * Gm::kBlockBytes,
-                          &vmaps[s], blk * 64, t * kBN, hk, bb, &bs->v_full[st]);
+                          &vmaps[s], blk * 64, (bs->t0[s] + t) * kBN, hk, bb, &bs->v_full[st]);
             if (absent) mbar_arrive_n(&bs->v_empty[st], absent);
             ++nv;
           }
@@ -574,7 +604,7 @@ __global__ void __launch_bounds__(kThreads, 1) kp3_kernel(const __grid_constant_
         ok = __all_sync(0xffffffffu, wait_bar(&bs->s_full[x], j & 1, bs, p.err));
         if (!ok) break;
         umma::fence_after_sync();
-        const int row0 = t * kBN;
+        const int row0 = (bs->t0[s] + t) * kBN;
         const int64_t kpos0 = sg.start + row0;
         const bool full = (row0 + kBN <= sg.len) && (!sg.causal || kpos0 + kBN - 1 <= qmin);
         const int lim_len = sg.len - row0;
@@ -645,7 +675,32 @@ __global__ void __launch_bounds__(kThreads, 1) kp3_kernel(const __grid_constant_
       if (ok) umma::fence_after_sync();
     }
     const int validX = x ? validB : validA;
-    if (active && ok) {
+    if (active && ok && half >= 0) {
+      // one half of a split unit: unnormalised o, M (natural log), L of the
+      // row, for pf_merge_kernel
+      float* pr = p.part + ((int64_t)((int)blockIdx.x - p.n_full) * 2 * kBM + x * kBM + r) *
+                               kPartStride<D>;
+      const bool live = r < validX;
+      if (live) {
+        pr[D] = (m == -INFINITY) ? -INFINITY : m * kLn2;
+        pr[D + 1] = l;
+      }
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        float ov[32];
+        if (nX > 0) {
+          umma::tmem_ld32(trow + ocol + c * 32, ov);   // warp-collective: every lane
+          umma::tmem_wait_ld();
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) ov[e] = 0.f;
+        }
+        if (!live) continue;
+        float4* od = reinterpret_cast<float4*>(pr + c * 32);
+#pragma unroll
+        for (int e = 0; e < 32; e += 4) od[e / 4] = make_float4(ov[e], ov[e + 1], ov[e + 2], ov[e + 3]);
+      }
+    } else if (active && ok) {
       const int t = qA0 + x * kBM + r;
       const bool live = r < validX;
       const int64_t row = ((int64_t)b * p.H + h) * p.T_q + t;
@@ -871,8 +926,56 @@ static bool pf_continues(const halo_kv_chunk_t& a, int64_t a_len, const halo_kv_
          a_len + c.len <= INT32_MAX;
 }
 
+namespace prefill {
+// Folds the two halves of each split unit: block (u, x) = query tile x of
+// split unit u, thread r = row; the same output contract as kp3_kernel's
+// finalising epilogue (out in out_dtype, lse in natural log).
 template <typename T, int D>
-static int launch_kp3(const prefill::Params& prm, int grid, cudaStream_t st) {
+__global__ void __launch_bounds__(kBM) pf_merge_kernel(const __grid_constant__ Params p) {
+  const int BH = p.B * p.H;
+  const int n_pairs = (p.n_qtiles + 1) / 2;
+  const int unit = p.n_full + (int)blockIdx.x;
+  const int pair = n_pairs - 1 - unit / BH, bh = unit % BH;
+  const int b = bh / p.H, h = bh % p.H;
+  const int x = (int)blockIdx.y, r = (int)threadIdx.x;
+  const int t = 2 * pair * kBM + x * kBM + r;
+  if (t >= p.T_q) return;
+  constexpr int kS = kPartStride<D>;
+  const float* p0 = p.part + ((int64_t)(2 * (int)blockIdx.x) * 2 * kBM + x * kBM + r) * kS;
+  const float* p1 = p0 + (int64_t)2 * kBM * kS;
+  const float M0 = p0[D], L0 = p0[D + 1], M1 = p1[D], L1 = p1[D + 1];
+  const float Mn = fmaxf(M0, M1);
+  const float w0 = (M0 == -INFINITY) ? 0.f : expf(M0 - Mn);
+  const float w1 = (M1 == -INFINITY) ? 0.f : expf(M1 - Mn);
+  const float L = L0 * w0 + L1 * w1;
+  const float inv = (L > 0.f) ? 1.f / L : 0.f;
+  const int64_t row = ((int64_t)b * p.H + h) * p.T_q + t;
+  if (p.lse) p.lse[row] = (L > 0.f) ? Mn + logf(L) : -INFINITY;
+  const int64_t off = (int64_t)b * p.out_sb + (int64_t)h * p.out_sh + (int64_t)t * p.out_st;
+  const float4* a4 = reinterpret_cast<const float4*>(p0);
+  const float4* c4 = reinterpret_cast<const float4*>(p1);
+#pragma unroll 4
+  for (int c = 0; c < D / 8; ++c) {
+    const float4 a0 = a4[2 * c], a1 = a4[2 * c + 1], c0 = c4[2 * c], c1 = c4[2 * c + 1];
+    const float v[8] = {(a0.x * w0 + c0.x * w1) * inv, (a0.y * w0 + c0.y * w1) * inv,
+                        (a0.z * w0 + c0.z * w1) * inv, (a0.w * w0 + c0.w * w1) * inv,
+                        (a1.x * w0 + c1.x * w1) * inv, (a1.y * w0 + c1.y * w1) * inv,
+                        (a1.z * w0 + c1.z * w1) * inv, (a1.w * w0 + c1.w * w1) * inv};
+    if (p.out_dtype == HALO_DTYPE_F32) {
+      float4* od = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + off + c * 8);
+      od[0] = make_float4(v[0], v[1], v[2], v[3]);
+      od[1] = make_float4(v[4], v[5], v[6], v[7]);
+    } else {
+      uint4* od = reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.out) + off + c * 8);
+      *od = make_uint4(Elem<T>::pack(v[0], v[1]), Elem<T>::pack(v[2], v[3]),
+                       Elem<T>::pack(v[4], v[5]), Elem<T>::pack(v[6], v[7]));
+    }
+  }
+}
+}  // namespace prefill
+
+template <typename T, int D>
+static int launch_kp3(const prefill::Params& prm, int grid, int n_split, cudaStream_t st) {
   using Gm = prefill::Geom<D>;
   static std::once_flag once[64];
   int dev = 0;
@@ -887,6 +990,12 @@ static int launch_kp3(const prefill::Params& prm, int grid, cudaStream_t st) {
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "kp3_kernel launch");
   count_launches();
+  if (n_split > 0) {
+    prefill::pf_merge_kernel<T, D><<<dim3((unsigned)n_split, 2), prefill::kBM, 0, st>>>(prm);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "pf_merge_kernel launch");
+    count_launches();
+  }
   return HALO_OK;
 }
 
@@ -982,8 +1091,47 @@ static int64_t pf_v16_bytes(const PfSeg& sg, const halo_prefill_problem_t* pb) {
   return align256((int64_t)(sg.bcast ? 1 : pb->B) * pb->H_kv * sg.len * pb->D * 2);
 }
 
+// Units of the last partial wave that run as two half-walk CTAs each (0:
+// none): the grid has more units than SMs (one CTA per SM), a remainder, and
+// the lightest unit (pair 0, the last in heavy-first order) walks at least
+// 8 K/V tiles.  Splitting those units fills the last wave with half-length
+// work instead of leaving SMs idle for a whole unit's time.
+static int pf_split_units(const PfSeg* segs, int n_seg, const halo_prefill_problem_t* pb) {
+  const int64_t n_qtiles = (pb->T_q + prefill::kBM - 1) / prefill::kBM;
+  const int64_t units = (n_qtiles + 1) / 2 * pb->B * pb->H;
+  const int W = device_sms();
+  if (n_seg == 0 || W <= 0 || units <= W || units % W == 0) return 0;
+  const int64_t qmax0 = pb->q_pos0 + std::min<int64_t>(2 * prefill::kBM, pb->T_q) - 1;
+  int tiles = 0;
+  for (int i = 0; i < n_seg; ++i) {
+    prefill::Seg sg;
+    sg.start = segs[i].c.start;
+    sg.len = (int32_t)segs[i].len;
+    sg.causal = segs[i].c.causal ? 1 : 0;
+    sg.bcast = segs[i].bcast ? 1 : 0;
+    tiles += prefill::seg_tiles(sg, qmax0);
+  }
+  return tiles >= 8 ? (int)(units % W) : 0;
+}
+
+// Workspace layout: [flag word, 256 B][fp16 V copies (bf16 inputs)][split
+// partials: per half-walk CTA 2 x 128 rows of kPartStride floats].
+static int64_t pf_part_offset(const PfSeg* segs, int n_seg, const halo_prefill_problem_t* pb) {
+  int64_t n = prefill::kWsHeader;
+  if (pb->dtype == HALO_DTYPE_BF16)
+    for (int i = 0; i < n_seg; ++i) n += pf_v16_bytes(segs[i], pb);
+  return align256(n);
+}
+
+static int64_t pf_part_bytes(int n_split, int D) {
+  return (int64_t)n_split * 2 * 2 * prefill::kBM * (D + 4) * 4;
+}
+
 static int64_t pf_workspace_bytes(const PfSeg* segs, int n_seg, const halo_prefill_problem_t* pb) {
-  if (pb->dtype != HALO_DTYPE_BF16 || n_seg == 0) return 0;
+  if (n_seg == 0) return 0;
+  const int n_split = pf_split_units(segs, n_seg, pb);
+  if (n_split > 0) return pf_part_offset(segs, n_seg, pb) + pf_part_bytes(n_split, pb->D);
+  if (pb->dtype != HALO_DTYPE_BF16) return 0;
   int64_t n = prefill::kWsHeader;
   for (int i = 0; i < n_seg; ++i) n += pf_v16_bytes(segs[i], pb);
   return n;
@@ -1004,7 +1152,13 @@ static int pf_run(const halo_prefill_problem_t* pb, const halo_kv_chunk_t* chunk
     return fail(HALO_ERR_MISALIGNED, "q must be 16-byte aligned with 16-byte row strides");
   const int D = pb->D;
   const bool v16 = workspace != nullptr && pb->dtype == HALO_DTYPE_BF16 && n_seg > 0;
-  if (v16) {
+  // split the last wave's units only for a finalising call without a
+  // caller running state (the halves' partials are merged into out here)
+  const int n_split = (workspace != nullptr && po->mode != HALO_MERGE_ACCUMULATE &&
+                       po->m == nullptr)
+                          ? pf_split_units(segs, n_seg, pb)
+                          : 0;
+  if (workspace != nullptr) {
     const int64_t need = pf_workspace_bytes(segs, n_seg, pb);
     if (workspace_bytes < need)
       return fail(HALO_ERR_WORKSPACE, "prefill workspace has %lld bytes, needs %lld",
@@ -1084,7 +1238,11 @@ static int pf_run(const halo_prefill_problem_t* pb, const halo_kv_chunk_t* chunk
   prm.l = po->l;
   prm.o = po->o;
   prm.err = device_error_ptr();
-  const int64_t grid = (int64_t)((prm.n_qtiles + 1) / 2) * pb->B * pb->H;
+  const int64_t units = (int64_t)((prm.n_qtiles + 1) / 2) * pb->B * pb->H;
+  prm.n_full = (int32_t)(units - n_split);
+  prm.part = n_split > 0 ? reinterpret_cast<float*>(ws + pf_part_offset(segs, n_seg, pb))
+                         : nullptr;
+  const int64_t grid = units + n_split;
   if (grid > INT32_MAX) return fail(HALO_ERR_UNSUPPORTED, "grid too large");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (pb->event_begin) cudaEventRecord(static_cast<cudaEvent_t>(pb->event_begin), st);
@@ -1109,11 +1267,11 @@ static int pf_run(const halo_prefill_problem_t* pb, const halo_kv_chunk_t* chunk
     count_launches();
   }
   if (pb->dtype == HALO_DTYPE_BF16)
-    rc = D == 128 ? launch_kp3<__nv_bfloat16, 128>(prm, (int)grid, st)
-                  : launch_kp3<__nv_bfloat16, 64>(prm, (int)grid, st);
+    rc = D == 128 ? launch_kp3<__nv_bfloat16, 128>(prm, (int)grid, n_split, st)
+                  : launch_kp3<__nv_bfloat16, 64>(prm, (int)grid, n_split, st);
   else
-    rc = D == 128 ? launch_kp3<__half, 128>(prm, (int)grid, st)
-                  : launch_kp3<__half, 64>(prm, (int)grid, st);
+    rc = D == 128 ? launch_kp3<__half, 128>(prm, (int)grid, n_split, st)
+                  : launch_kp3<__half, 64>(prm, (int)grid, n_split, st);
   if (rc == HALO_OK && pb->event_end) cudaEventRecord(static_cast<cudaEvent_t>(pb->event_end), st);
   return rc;
 }

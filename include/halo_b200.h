@@ -390,9 +390,13 @@ int32_t halo_prefill_attention(const halo_prefill_problem_t* problem,
                                const halo_prefill_out_t* out, halo_stream_t stream);
 
 /* Workspace bytes halo_prefill_attention_ws needs for this problem and chunk
- * list: 0 for fp16 inputs (nothing to stage), else 256 bytes of flags plus
- * an fp16 copy of V (B x H_kv x rows x D x 2 bytes per coalesced segment,
- * each rounded up to 256).  Negative status on bad arguments. */
+ * list: 256 bytes of flags, then for bf16 inputs an fp16 copy of V
+ * (B x H_kv x rows x D x 2 bytes per coalesced segment, each rounded up to
+ * 256), then, when there are more query-tile pairs x heads than SMs with a
+ * remainder, fp32 partials for the last wave's pairs, which run as two
+ * half-walk CTAs each (2 x 2 x 128 rows x (D + 4) floats per such pair).
+ * 0 when none of these apply (fp16 inputs, a single wave).  Negative status
+ * on bad arguments. */
 int64_t halo_prefill_workspace_bytes(const halo_prefill_problem_t* problem,
                                      const halo_kv_chunk_t* chunks, int32_t n_chunks);
 
@@ -403,8 +407,11 @@ int64_t halo_prefill_workspace_bytes(const halo_prefill_problem_t* problem,
  * two; max error well inside 2e-3).  If V holds a finite |v| >= 65536, which
  * fp16 cannot represent, the pre-pass raises a flag in the workspace and the
  * kernel takes the two-MMA bf16 route with the original V: same result
- * contract, no host round trip.  Same semantics as halo_prefill_attention
- * otherwise.  Same reference interface as halo_prefill_attention. */
+ * contract, no host round trip.  For a finalising call without a running
+ * state, the last partial wave's query-tile pairs run as two CTAs over half
+ * of their keys each, merged by one more launch (fills the SMs the last wave
+ * would leave idle).  Same semantics as halo_prefill_attention otherwise.
+ * Same reference interface as halo_prefill_attention. */
 int32_t halo_prefill_attention_ws(const halo_prefill_problem_t* problem,
                                   const halo_kv_chunk_t* chunks, int32_t n_chunks,
                                   const halo_prefill_out_t* out, void* workspace,

@@ -193,3 +193,48 @@ def test_multi_query_attention_uses_prefill_kernel():
     assert L.launch_count() - n0 == 2          # the fp16 copy of V + one kp3_kernel launch
     ro, rl = OA.full_attention_f64(q, k, v, q_pos=500)
     _check(out, lse, ro, rl)
+
+
+def _f64_causal_gpu(q, k, v, q_pos):
+    """Float64 causal attention on the GPU (query i sees keys <= q_pos + i)."""
+    import math
+    B, H, T_q, D = q.shape
+    G = H // k.shape[1]
+    kk = k.double().repeat_interleave(G, 1)
+    vv = v.double().repeat_interleave(G, 1)
+    s = (q.double() @ kk.transpose(-1, -2)) / math.sqrt(D)
+    qi = torch.arange(T_q, device=q.device)[:, None] + q_pos
+    kj = torch.arange(k.shape[-2], device=q.device)[None, :]
+    s = s.masked_fill(kj > qi, float("-inf"))
+    return torch.softmax(s, -1) @ vv, torch.logsumexp(s, -1)
+
+
+@pytest.mark.parametrize("dtype,D", [(torch.bfloat16, 128), (torch.float16, 128),
+                                     (torch.bfloat16, 64)])
+def test_prefill_split_last_wave_units(dtype, D):
+    """More query-tile units than SMs with a remainder: the lightest units of
+    the last wave run as two half-walk CTAs whose partials a merge kernel
+    folds; the result equals float64 attention like every other unit."""
+    from halo_b200 import _lib as L
+    ops = _ops()
+    B, H, H_kv, T_q, T = 1, 32, 8, 2048, 4096
+    units = (T_q // 256) * B * H
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    split = units > sms and units % sms != 0
+    q, k, v = _qkv(B, H, H_kv, T, T_q, D, dtype, seed=91)
+    qd, kd, vd = q.to(DEV), k.to(DEV), v.to(DEV)
+    chunks = [(kd[..., a:a + 1024, :], vd[..., a:a + 1024, :], a, True) for a in range(0, T, 1024)]
+    n0 = L.launch_count()
+    out, lse = ops.prefill_attention(qd, chunks, query_pos_offset=T - T_q,
+                                     out_dtype=torch.float32)
+    launches = L.launch_count() - n0
+    # v16 copy (bf16 only) + kp3, + the merge when units were split
+    assert launches == (1 if dtype == torch.bfloat16 else 0) + 1 + (1 if split else 0)
+    ro, rl = _f64_causal_gpu(qd, kd, vd, T - T_q)
+    assert (out.double() - ro).abs().max().item() <= OUT_TOL
+    assert (lse.double() - rl).abs().max().item() <= LSE_TOL
+    # a second call (workspace reused) gives the same result
+    out2, lse2 = ops.prefill_attention(qd, chunks, query_pos_offset=T - T_q,
+                                       out_dtype=torch.float32)
+    assert torch.equal(out, out2) and torch.equal(lse, lse2)
+    assert L.device_error() == 0
