@@ -5,6 +5,7 @@ There is no CPU fallback anywhere in the package.
 """
 from __future__ import annotations
 
+import contextlib
 import ctypes
 import os
 import threading
@@ -240,5 +241,23 @@ def launch_count() -> int:
     return int(lib().halo_launch_count())
 
 
+# The raw cudaStream_t of a device's current stream without building a
+# torch.cuda.Stream object (~0.3 us against ~2.5 us of host time per call).
+_raw_current_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def stream_handle(device: torch.device) -> int:
+    """The raw handle of ``device``'s current CUDA stream."""
+    if _raw_current_stream is not None:
+        idx = device.index if device.index is not None else torch.cuda.current_device()
+        return int(_raw_current_stream(idx))
     return torch.cuda.current_stream(device).cuda_stream
+
+
+def on_device(device: torch.device):
+    """``torch.cuda.device(device)``, or a no-op context when ``device`` is
+    already the current device (entering the torch context costs ~2 us of
+    host time, as much as the rest of a small decode call's set-up)."""
+    if device.index is None or device.index == torch.cuda.current_device():
+        return contextlib.nullcontext()
+    return torch.cuda.device(device)

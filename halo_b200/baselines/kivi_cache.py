@@ -136,6 +136,7 @@ class _Packed:
         self.bits, self.group = bits, group
         self.T = 0
         self.codes = self.scale = self.zero = None
+        self._view = None       # C-ABI description of the storage; reset when it moves
 
     def reserve(self, rows: int) -> None:
         cap = 0 if self.codes is None else self.codes.shape[2]
@@ -153,6 +154,7 @@ class _Packed:
             scale[:, :, :self.T].copy_(self.scale[:, :, :self.T])
             zero[:, :, :self.T].copy_(self.zero[:, :, :self.T])
         self.codes, self.scale, self.zero = codes, scale, zero
+        self._view = None
 
     def append(self, x) -> None:
         n = x.shape[2]
@@ -166,7 +168,11 @@ class _Packed:
                                  self.zero[:, :, :self.T], bits=self.bits, group_size=self.group)
 
     def view(self) -> L.KiviTensor:
-        t = L.KiviTensor()
+        """The storage's C-ABI description (pointers, strides, capacity); it
+        stays valid until ``reserve`` moves the storage."""
+        if self._view is not None:
+            return self._view
+        t = self._view = L.KiviTensor()
         t.codes, t.scale, t.zero = self.codes.data_ptr(), self.scale.data_ptr(), self.zero.data_ptr()
         t.codes_stride_b, t.codes_stride_h = self.codes.stride(0), self.codes.stride(1)
         t.sz_stride_b, t.sz_stride_h = self.scale.stride(0), self.scale.stride(1)
@@ -192,6 +198,11 @@ class KIVICache(_BaseCache):
         self._v_quant: list = []
         self._n_seen: list = []
         self._ones_cache: dict = {}
+        self._recent_tables: dict = {}   # layer -> ChunkTable of its recent rows
+        # fp32 (out, lse) of the packed prefix per (device, stream, B, H, D):
+        # written and consumed on that stream within one call, so stream
+        # order makes reuse across calls and layers safe
+        self._prefix_state: dict = {}
 
     @classmethod
     def from_memory_ratio(cls, *, memory_ratio: int, **kw) -> "KIVICache":
@@ -232,6 +243,7 @@ class KIVICache(_BaseCache):
                 kr = kr[..., oq:, :].contiguous()
                 vr = vr[..., oq:, :].contiguous()
         self._k_recent[layer_idx], self._v_recent[layer_idx] = kr, vr
+        self._recent_tables.pop(layer_idx, None)
         if self.fused_attention or self._k_quant[layer_idx] is None:
             return kr, vr
         return (torch.cat([self._k_quant[layer_idx].dequantized(), kr], dim=-2),
@@ -260,22 +272,32 @@ class KIVICache(_BaseCache):
             return out
         q3 = q.squeeze(2).contiguous()
         dev = q.device
-        recent = [(kr, vr, T_quant, False)] if (kr is not None and kr.shape[-2]) else []
+        recent = None
+        if kr is not None and kr.shape[-2]:
+            recent = self._recent_tables.get(layer_idx)
+            if recent is None:
+                recent = self._recent_tables[layer_idx] = ops.ChunkTable([(kr, vr, T_quant, False)])
         prior = None
         if T_quant:
             # The prefix's normalised (out, lse) is a running state with l = 1.
-            o32 = torch.empty(B, H, D, dtype=torch.float32, device=dev)
-            lse = torch.empty(B, H, dtype=torch.float32, device=dev)
+            key = (dev.index, L.stream_handle(dev), B, H, D)
+            st = self._prefix_state.get(key)
+            if st is None:
+                st = self._prefix_state[key] = (
+                    torch.empty(B, H, D, dtype=torch.float32, device=dev),
+                    torch.empty(B, H, dtype=torch.float32, device=dev))
+            o32, lse = st
             kivi_decode(q3, kq, vq, T_quant, self.bits, scale=scale, out=o32, lse=lse,
                         events=events)
-            if not recent:
-                return o32.to(q.dtype).unsqueeze(2)
+            if recent is None:
+                return o32.to(q.dtype, copy=True).unsqueeze(2)
             prior = (lse, self._ones(B, H, dev), o32)
-        out, _ = ops.chunked_decode(q3, recent, scale=scale, prior=prior)
+        out, _ = ops.chunked_decode(q3, recent if recent is not None else [], scale=scale,
+                                    prior=prior, want_lse=False)
         return out.unsqueeze(2)
 
     def _ones(self, B: int, H: int, dev) -> torch.Tensor:
-        key = (B, H, str(dev))
+        key = (B, H, dev.index)
         t = self._ones_cache.get(key)
         if t is None:
             t = self._ones_cache[key] = torch.ones(B, H, dtype=torch.float32, device=dev)
@@ -287,6 +309,7 @@ class KIVICache(_BaseCache):
         self._k_quant.clear()
         self._v_quant.clear()
         self._n_seen.clear()
+        self._recent_tables.clear()
 
 
 def kivi_decode(q3, kq: _Packed, vq: _Packed, rows: int, bits: int, *, scale: float,
@@ -302,7 +325,8 @@ def kivi_decode(q3, kq: _Packed, vq: _Packed, rows: int, bits: int, *, scale: fl
     need = lib.halo_kivi_decode_workspace_bytes(ctypes.byref(p), rows)
     if need < 0:
         L.check(int(need), "halo_kivi_decode_workspace_bytes")
-    ws = ops.WORKSPACES.get(q3.device, int(need))
+    sh = L.stream_handle(q3.device)
+    ws = ops.WORKSPACES.get(q3.device, int(need), sh)
     mg = L.MergeArgs()
     if state is not None:
         m, l, o = state
@@ -316,10 +340,9 @@ def kivi_decode(q3, kq: _Packed, vq: _Packed, rows: int, bits: int, *, scale: fl
         mg.out = out.data_ptr()
         mg.out_stride_b, mg.out_stride_h = out.stride(0), out.stride(1)
         mg.lse = lse.data_ptr()
-    with torch.cuda.device(q3.device):
+    with L.on_device(q3.device):
         rc = lib.halo_kivi_decode(ctypes.byref(p), ctypes.byref(kt), ctypes.byref(vt), rows, bits, 0,
-                                  0, ws.data_ptr(), ws.numel(), ctypes.byref(mg),
-                                  L.stream_handle(q3.device))
+                                  0, ws.data_ptr(), ws.numel(), ctypes.byref(mg), sh)
     L.check(rc, "halo_kivi_decode")
     return (out, lse) if state is None else None
 

@@ -24,8 +24,12 @@ class _Workspaces:
     def __init__(self):
         self._bufs: dict = {}
 
-    def get(self, device: torch.device, nbytes: int) -> torch.Tensor:
-        key = (device.index, torch.cuda.current_stream(device).cuda_stream)
+    def get(self, device: torch.device, nbytes: int, stream: Optional[int] = None) -> torch.Tensor:
+        """``stream``: the raw handle of the stream the buffer is used on
+        (default: ``device``'s current stream)."""
+        if stream is None:
+            stream = L.stream_handle(device)
+        key = (device.index, stream)
         buf = self._bufs.get(key)
         if buf is None or buf.numel() < nbytes:
             buf = torch.zeros(max(nbytes, 1 << 16), dtype=torch.uint8, device=device)
@@ -94,10 +98,11 @@ def decode_raw(q3: torch.Tensor, chunk_structs: Sequence[L.KVChunk], H_kv: int, 
     need = lib.halo_decode_workspace_bytes(ctypes.byref(prob), arr, n)
     if need < 0:
         L.check(int(need), "halo_decode_workspace_bytes")
-    ws = WORKSPACES.get(dev, int(need))
-    with torch.cuda.device(dev):
+    sh = L.stream_handle(dev)
+    ws = WORKSPACES.get(dev, int(need), sh)
+    with L.on_device(dev):
         rc = lib.halo_chunked_decode(ctypes.byref(prob), arr, n, ws.data_ptr(), ws.numel(),
-                                     ctypes.byref(merge), L.stream_handle(dev))
+                                     ctypes.byref(merge), sh)
     L.check(rc, "halo_chunked_decode")
 
 
@@ -146,10 +151,11 @@ def _decode_table(q3: torch.Tensor, table: ChunkTable, *, scale: float,
     need = lib.halo_decode_workspace_bytes(ctypes.byref(prob), table.arr, table.n)
     if need < 0:
         L.check(int(need), "halo_decode_workspace_bytes")
-    ws = WORKSPACES.get(dev, int(need))
-    with torch.cuda.device(dev):
+    sh = L.stream_handle(dev)
+    ws = WORKSPACES.get(dev, int(need), sh)
+    with L.on_device(dev):
         rc = lib.halo_chunked_decode(ctypes.byref(prob), table.arr, table.n, ws.data_ptr(),
-                                     ws.numel(), ctypes.byref(merge), L.stream_handle(dev))
+                                     ws.numel(), ctypes.byref(merge), sh)
     L.check(rc, "halo_chunked_decode")
 
 
@@ -169,13 +175,14 @@ def decode_partials(q3: torch.Tensor, table: ChunkTable, *, scale: float,
     need = lib.halo_decode_workspace_bytes(ctypes.byref(prob), table.arr, table.n)
     if need < 0:
         L.check(int(need), "halo_decode_workspace_bytes")
-    ws = WORKSPACES.get(dev, int(need))
+    sh = L.stream_handle(dev)
+    ws = WORKSPACES.get(dev, int(need), sh)
     n_parts = ctypes.c_int32(0)
     offs = (ctypes.c_int64 * 3)()
-    with torch.cuda.device(dev):
+    with L.on_device(dev):
         rc = lib.halo_chunked_decode_partials(ctypes.byref(prob), table.arr, table.n,
                                               ws.data_ptr(), ws.numel(), ctypes.byref(n_parts),
-                                              offs, L.stream_handle(dev))
+                                              offs, sh)
     L.check(rc, "halo_chunked_decode_partials")
     return ws, int(n_parts.value), (int(offs[0]), int(offs[1]), int(offs[2]))
 
@@ -197,13 +204,14 @@ def sharded_decode(q3: torch.Tensor, table: ChunkTable, exchange, *, scale: floa
     need = lib.halo_decode_workspace_bytes(ctypes.byref(prob), table.arr, table.n)
     if need < 0:
         L.check(int(need), "halo_decode_workspace_bytes")
-    ws = WORKSPACES.get(dev, int(need))
-    with torch.cuda.device(dev):
+    sh = L.stream_handle(dev)
+    ws = WORKSPACES.get(dev, int(need), sh)
+    with L.on_device(dev):
         rc = lib.halo_sharded_decode(ctypes.byref(prob), table.arr, table.n, ws.data_ptr(),
                                      ws.numel(), exchange.world, exchange.rank, exchange.bufs,
                                      L.halo_dtype(out.dtype), out.data_ptr(), out.stride(0),
                                      out.stride(1), lse.data_ptr() if lse is not None else None,
-                                     L.stream_handle(dev))
+                                     sh)
     L.check(rc, "halo_sharded_decode")
     return out, lse
 
@@ -212,10 +220,12 @@ def chunked_decode(q: torch.Tensor, chunks, *, scale: Optional[float] = None,
                    q_pos: Optional[torch.Tensor] = None, out_dtype: Optional[torch.dtype] = None,
                    out: Optional[torch.Tensor] = None, lse: Optional[torch.Tensor] = None,
                    prior: Optional[tuple] = None, max_split_rows: int = 0,
-                   events: Optional[tuple] = None):
+                   events: Optional[tuple] = None, want_lse: bool = True):
     """Attention of one decode query over ``chunks`` -- a list of
     ``(k, v, start, causal)`` tuples or a prepared :class:`ChunkTable` --
-    merged with log-sum-exp.  Returns ``(out (B, H, D_v), lse (B, H))``.
+    merged with log-sum-exp.  Returns ``(out (B, H, D_v), lse (B, H))``;
+    with ``want_lse=False`` and no ``lse`` given, the log-sum-exp is not
+    written and ``None`` is returned in its place.
 
     ``prior = (m, l, o)`` folds a running fp32 state in first.  ``q_pos``
     (device int64 ``(B,)``) defaults to ``total_T - 1`` as in
@@ -237,14 +247,14 @@ def chunked_decode(q: torch.Tensor, chunks, *, scale: Optional[float] = None,
         q_pos = q_pos.to(device=q3.device, dtype=torch.int64).contiguous()
     if out is None:
         out = torch.empty(B, H, D_v, dtype=out_dtype or q3.dtype, device=q3.device)
-    if lse is None:
+    if lse is None and want_lse:
         lse = torch.empty(B, H, dtype=torch.float32, device=q3.device)
     mg = L.MergeArgs()
     mg.mode = L.MERGE_FINALIZE
     mg.out_dtype = L.halo_dtype(out.dtype)
     mg.out = out.data_ptr()
     mg.out_stride_b, mg.out_stride_h = out.stride(0), out.stride(1)
-    mg.lse = lse.data_ptr()
+    mg.lse = lse.data_ptr() if lse is not None else None
     if prior is not None:
         m, l, o = prior
         mg.m, mg.l, mg.o = m.data_ptr(), l.data_ptr(), o.data_ptr()

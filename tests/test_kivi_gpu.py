@@ -184,3 +184,67 @@ def test_kivi_cache_fused_attention_matches_dequantised_attention():
     out = c.compute_attention(q, layer_idx=0)
     ro, _ = OA.full_attention_f64(q.cpu(), Kd.cpu(), Vd.cpu())
     assert (out.float().cpu() - ro.float()).abs().max().item() <= 2e-3 + 1e-3  # fp16 output rounding
+
+
+def test_kivi_cache_fused_decode_loop_tracks_updates():
+    """A decode loop on two layers: one-row updates, with the fused
+    attention after every one.  The updates cross quantisation boundaries
+    (the recent rows and the packed prefix change) and outgrow the packed
+    storage's first capacity, and some calls run on a side stream; each
+    output must match attention over the unfused cache's dequantised K/V."""
+    from halo_b200.baselines.kivi_cache import KIVICache
+    torch.manual_seed(5)
+    B, H, H_kv, D, steps = 2, 8, 2, 128, 260
+    c = KIVICache(bits=2, group_size=32, residual_length=128, fused_attention=True)
+    full = KIVICache(bits=2, group_size=32, residual_length=128, fused_attention=False)
+    k = torch.randn(2, B, H_kv, 200 + steps, D, device=DEV).half()
+    v = torch.randn(2, B, H_kv, 200 + steps, D, device=DEV).half()
+    side = torch.cuda.Stream()
+    caps = set()
+    for t in range(steps + 1):
+        a, b = (0, 200) if t == 0 else (199 + t, 200 + t)
+        for layer in range(2):
+            c.update(k[layer, ..., a:b, :], v[layer, ..., a:b, :], layer_idx=layer)
+            Kd, Vd = full.update(k[layer, ..., a:b, :], v[layer, ..., a:b, :], layer_idx=layer)
+            q = torch.randn(B, H, 1, D, device=DEV).half()
+            if t % 7 == 3:
+                side.wait_stream(torch.cuda.current_stream())
+                with torch.cuda.stream(side):
+                    out = c.compute_attention(q, layer_idx=layer)
+                torch.cuda.current_stream().wait_stream(side)
+            else:
+                out = c.compute_attention(q, layer_idx=layer)
+            if t % 13 == 0 or t == steps:
+                ro, _ = OA.full_attention_f64(q.cpu(), Kd.cpu(), Vd.cpu())
+                err = (out.float().cpu() - ro.float()).abs().max().item()
+                assert err <= 2e-3 + 1e-3, (t, layer, err)   # fp16 output rounding
+        caps.add(c._k_quant[0].codes.shape[2])
+    assert len(caps) >= 2, "the packed storage never grew"
+    assert c.get_seq_length(0) == 200 + steps
+
+
+def test_kivi_cache_fused_decode_without_recent_rows():
+    """residual_length 0 and a multiple of the group size: every row is
+    quantised and the fused call returns the packed prefix's attention
+    alone.  Two calls in a row: the first result must not change when the
+    second call reuses the cache's fp32 state buffers."""
+    from halo_b200.baselines.kivi_cache import KIVICache
+    torch.manual_seed(6)
+    B, H, H_kv, D = 2, 8, 2, 128
+    c = KIVICache(bits=2, group_size=32, residual_length=0, fused_attention=True)
+    full = KIVICache(bits=2, group_size=32, residual_length=0, fused_attention=False)
+    k = torch.randn(B, H_kv, 512, D, device=DEV).half()
+    v = torch.randn(B, H_kv, 512, D, device=DEV).half()
+    c.update(k, v, layer_idx=0)
+    Kd, Vd = full.update(k, v, layer_idx=0)
+    assert c._k_recent[0].shape[-2] == 0
+    q1 = torch.randn(B, H, 1, D, device=DEV).half()
+    q2 = torch.randn(B, H, 1, D, device=DEV).half()
+    out1 = c.compute_attention(q1, layer_idx=0)
+    keep = out1.clone()
+    out2 = c.compute_attention(q2, layer_idx=0)
+    torch.cuda.synchronize()
+    assert torch.equal(out1, keep)
+    for q, out in ((q1, out1), (q2, out2)):
+        ro, _ = OA.full_attention_f64(q.cpu(), Kd.cpu(), Vd.cpu())
+        assert (out.float().cpu() - ro.float()).abs().max().item() <= 2e-3 + 1e-3
