@@ -434,3 +434,30 @@ def test_decode_head_dims(cuda_device, dtype, D):
         ro, rl = OA.full_attention_f64(q[b:b + 1], k[b:b + 1], v[b:b + 1], q_pos=p)
         assert (out[b].cpu().double() - ro[0, :, 0]).abs().max().item() <= _tol(dtype)
         assert (lse[b].cpu().double() - rl[0, :, 0]).abs().max().item() <= LSE_TOL
+
+
+def test_decode_without_lse_output(cuda_device):
+    """``want_lse=False``: the output equals the one written alongside the
+    log-sum-exp (same launches, the merge skips the lse store), with and
+    without a prior running state, and ``None`` comes back for the lse."""
+    ops = _ops()
+    torch.manual_seed(3)
+    B, H, H_kv, D, T = 2, 16, 4, 128, 3000
+    q = torch.randn(B, H, 1, D, device=cuda_device).bfloat16()
+    k = torch.randn(B, H_kv, T, D, device=cuda_device).bfloat16()
+    v = torch.randn(B, H_kv, T, D, device=cuda_device).bfloat16()
+    chunks = [(k[..., a:b, :], v[..., a:b, :], a, False) for a, b in _bounds(T, 1024)]
+    ref_o, _ = OA.full_attention_f64(q.cpu(), k.cpu(), v.cpu())
+    out_l, lse = ops.chunked_decode(q, chunks)
+    out_n, none = ops.chunked_decode(q, chunks, want_lse=False)
+    assert none is None and lse is not None
+    assert torch.equal(out_l, out_n)
+    assert (out_n.float().cpu().double() - ref_o[:, :, 0]).abs().max().item() <= OUT_TOL_16
+    # a prior (m, l, o) from the first half folded into the second half
+    m = torch.full((B, H), -float("inf"), device=cuda_device)
+    l = torch.zeros(B, H, device=cuda_device)
+    o = torch.zeros(B, H, D, device=cuda_device)
+    ops.accumulate_decode(q, chunks[:2], m, l, o, scale=1.0 / math.sqrt(D), q_pos=None)
+    out_p, none_p = ops.chunked_decode(q, chunks[2:], prior=(m, l, o), want_lse=False)
+    assert none_p is None
+    assert (out_p.float().cpu().double() - ref_o[:, :, 0]).abs().max().item() <= OUT_TOL_16
