@@ -73,7 +73,7 @@ METRIC = "decode-attn tokens/s & achieved HBM GB/s at 32K-1M ctx, 1/2/4/8 B200"
 # (transposed tile math, K into MMA registers).  kd_kernel at cfg2: the hot
 # and selected launches of one layer.
 NCU_TRAFFIC_RATIO = 1.0040      # kd_dyn_kernel, ncu at 262144 tokens: (1073.795 + 4.311) MB read+write / 1073.742 MB algorithmic
-NCU_TRAFFIC_RATIO_KK = 1.0330      # kk_kernel, ncu of the cfg4 launch: (201.72 + 5.84) MB / 200.93 MB
+NCU_TRAFFIC_RATIO_KK = 1.0200      # kk_kernel, ncu of the cfg4 launch: (201.00 + 3.95) MB / 200.93 MB
 NCU_TRAFFIC_RATIO_KD_CFG2 = 1.0139  # kd_kernel, ncu of one layer's hot + selected launches (cfg2)
 
 
