@@ -71,6 +71,7 @@ constexpr int kConsumerWarps = 4;    // each owns 16 rows of every stage
 constexpr int kThreads = (kConsumerWarps + 1) * 32;
 constexpr int kMaxSegs = 48;         // tensor-map pairs per launch
 constexpr float kLazyMax = 8.f;      // KIVI decode: log2 headroom before the running max moves
+constexpr uint32_t kKiviWaitHintNs = 2000;  // KIVI decode: suspend-time hint of its ring waits
 constexpr int kMaxItems = 512;       // work items per launch
 // kCtrlBytes (halo_common.cuh): the control block at the start of every
 // decode workspace.
@@ -1376,7 +1377,7 @@ struct DequantTilesKD {
   KRegs<D> kr;
   __device__ __forceinline__ bool acquire(int t, int gt, uint32_t& kbase, uint32_t& vbase) {
     const int s = gt % KG::kStages;
-    if (!mbar_wait(&full[s], (gt / KG::kStages) & 1, err)) return false;
+    if (!mbar_wait_hint(&full[s], (gt / KG::kStages) & 1, err, kKiviWaitHintNs)) return false;
     const char* st = stages + s * KG::kStageBytes;
     load_k_regs<T, D>(st, KG::kCodeTile, KG::kSZTile, kr);
     dequant_rows<T, D, 2>(st + KG::kPackBytes, vdq);
@@ -1447,7 +1448,7 @@ __global__ void __launch_bounds__(kThreads, KGeom<T, D, BITS, TR>::kMinCtas)
         const int n_tiles = (it.rows + kBlockN - 1) / kBlockN;
         for (int t = 0; t < n_tiles; ++t, ++gt) {
           const int s = gt % STAGES;
-          if (gt >= STAGES && !mbar_wait(&empty[s], ((gt / STAGES) & 1) ^ 1, p.err)) return;
+          if (gt >= STAGES && !mbar_wait_hint(&empty[s], ((gt / STAGES) & 1) ^ 1, p.err, kKiviWaitHintNs)) return;
           const int64_t r0 = it.row0 + t * kBlockN;
           char* dst = stages + s * KG::kStageBytes;
           mbar_arrive_expect_tx(&full[s], KG::kStageBytes);

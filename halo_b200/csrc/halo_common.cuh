@@ -160,6 +160,37 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsign
   }
 }
 
+// The same bounded wait with mbarrier.try_wait's suspend-time hint: each
+// poll may block the thread in the barrier unit for up to `hint_ns` and
+// returns as soon as the phase completes, so a long wait takes fewer polls
+// (and fewer issue slots) than back-to-back polls.
+__device__ __forceinline__ bool mbar_try_wait_hint(uint64_t* bar, uint32_t parity,
+                                                   uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ bool mbar_wait_hint(uint64_t* bar, uint32_t parity, unsigned int* err,
+                                               uint32_t hint_ns) {
+  if (mbar_try_wait_hint(bar, parity, hint_ns)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+    for (int i = 0; i < 8; ++i)
+      if (mbar_try_wait_hint(bar, parity, hint_ns)) return true;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      set_device_error(err, static_cast<unsigned int>(-HALO_ERR_TIMEOUT));
+      return false;
+    }
+  }
+}
+
 // ---------------------------------------------------------------- bulk copy
 // One-dimensional bulk copy global -> shared through the async-copy (TMA)
 // engine; completion is signalled as transaction bytes on `bar`.  `src` and
