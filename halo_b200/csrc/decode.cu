@@ -1224,14 +1224,14 @@ struct alignas(64) KiviParams {
   float scale_log2;
 };
 
-// Packed-tile geometry of kk_kernel.  TR is the transposed tile math.  With
-// 2-bit codes it dequantises K straight into MMA registers (kKDirect) and
-// keeps only the V tile in shared memory, which leaves room for a 4-stage
-// packed ring; it runs 3 CTAs per SM at 128 registers, no spill (measured
-// 11 % faster than 4 CTAs at 96 registers with spills, 7 % faster than 2
-// CTAs).  With 4/8-bit codes both tiles are staged, the ring has 2 stages
-// and 4 CTAs run per SM.  The row-layout variant runs 2 CTAs per SM with 4
-// stages.
+// Packed-tile geometry of kk_kernel.  TR is the transposed tile math; it
+// runs 3 CTAs per SM at 128 registers, no spill (measured faster than 4
+// CTAs at 96 registers with spills by 11 % at 2 bits, 7 % at 4 bits and
+// 3 % at 8 bits, and than 2 CTAs by 7 % at 2 bits).  With 2-bit codes it
+// dequantises K straight into MMA registers (kKDirect) and keeps only the
+// V tile in shared memory, which leaves room for a 4-stage packed ring;
+// with 4/8-bit codes both tiles are staged and the ring has 2 stages.  The
+// row-layout variant runs 2 CTAs per SM with 4 stages.
 template <typename T, int D, int BITS, bool TR = false>
 struct KGeom {
   using Gm = Geom<T, D, 1>;
@@ -1242,7 +1242,7 @@ struct KGeom {
   static constexpr int kPackBytes = kCodeTile + 2 * kSZTile;
   static constexpr bool kKDirect = TR && BITS == 2;
   static constexpr int kStages = (TR && !kKDirect) ? 2 : 4;
-  static constexpr int kMinCtas = kKDirect ? 3 : (TR ? 4 : 2);   // per SM
+  static constexpr int kMinCtas = TR ? 3 : 2;   // per SM
   static constexpr int kStageBytes = 2 * kPackBytes;
   static constexpr int kDqBytes = (kKDirect ? 1 : 2) * Gm::kTileBytes;
   static constexpr int kSmemBytes =
