@@ -1248,6 +1248,7 @@ struct KGeom {
   static constexpr int kSmemBytes =
       kDqBytes + 2 * Gm::kQSlotBytes + kStages * kStageBytes + 128 + 1024;
   static_assert(kPackBytes % 16 == 0, "bulk copies need 16-byte multiples");
+  static_assert((2 * kStages + 4) * 8 <= 128, "full/empty/qfull/qempty barriers fit their 128 bytes");
 };
 
 // Warp w dequantises rows [16w, 16w+16) of one packed K or V tile into the
